@@ -1,0 +1,151 @@
+// Shared device helpers for libdct_cuda (sm_100a).
+//
+// Every kernel of the library is memory-bound fp32 work: 128-bit vector
+// loads/stores, streaming cache hints, float64 accumulation for every sum, and
+// grids sized as a multiple of the SM count.  Nothing here uses tensor cores.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <math.h>
+
+#define DCT_DEV __device__ __forceinline__
+
+namespace dct {
+
+// ---------------------------------------------------------------------------
+// launch geometry
+// ---------------------------------------------------------------------------
+struct DevInfo {
+  int device = -1;
+  int sm_count = 148;
+  int max_threads_per_sm = 2048;
+  size_t smem_optin = 227 * 1024;
+  size_t total_mem = 0;
+};
+const DevInfo& dev_info();   // defined in runtime.cu
+
+// Blocks for a grid-stride kernel of `threads`-thread blocks covering `work`
+// independent items: enough to fill every SM `waves` times, never more than
+// the work needs.
+inline unsigned grid_for(uint64_t work, int threads, int waves = 1) {
+  const DevInfo& d = dev_info();
+  uint64_t resident = (uint64_t)d.sm_count * (uint64_t)(d.max_threads_per_sm / threads) * waves;
+  uint64_t need = (work + threads - 1) / threads;
+  if (need < 1) need = 1;
+  return (unsigned)(need < resident ? need : resident);
+}
+
+// ---------------------------------------------------------------------------
+// memory access
+// ---------------------------------------------------------------------------
+// Streaming (evict-first) 128-bit accesses: every large tensor here is touched
+// exactly once per kernel, so it should not displace reusable lines in L2.
+DCT_DEV float4 ld_stream4(const float* p) { return __ldcs(reinterpret_cast<const float4*>(p)); }
+DCT_DEV void st_stream4(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+DCT_DEV float ld_stream(const float* p) { return __ldcs(p); }
+DCT_DEV void st_stream(float* p, float v) { __stcs(p, v); }
+// Small operands reused by many threads (biases, broadcast rows): keep cached.
+DCT_DEV float4 ld_keep4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+DCT_DEV float ld_keep(const float* p) { return __ldg(p); }
+
+DCT_DEV bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned16_h(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// warp / block reductions (fixed shuffle order => run-to-run deterministic)
+// ---------------------------------------------------------------------------
+DCT_DEV double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  return v;  // lane 0 holds the total
+}
+DCT_DEV float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;  // every lane holds the total
+}
+DCT_DEV float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// (value, index) arg-reductions with NumPy's rule: NaN is the maximum (and the
+// minimum), and among equal candidates the lowest index wins.
+struct ValIdx {
+  float v;
+  int64_t i;
+};
+DCT_DEV bool better_max(float av, int64_t ai, float bv, int64_t bi) {
+  bool an = isnan(av), bn = isnan(bv);
+  if (an || bn) {
+    if (an && bn) return ai < bi;
+    return an;
+  }
+  if (av != bv) return av > bv;
+  return ai < bi;
+}
+DCT_DEV bool better_min(float av, int64_t ai, float bv, int64_t bi) {
+  bool an = isnan(av), bn = isnan(bv);
+  if (an || bn) {
+    if (an && bn) return ai < bi;
+    return an;
+  }
+  if (av != bv) return av < bv;
+  return ai < bi;
+}
+template <bool IS_MAX>
+DCT_DEV bool better(float av, int64_t ai, float bv, int64_t bi) {
+  return IS_MAX ? better_max(av, ai, bv, bi) : better_min(av, ai, bv, bi);
+}
+template <bool IS_MAX>
+DCT_DEV void warp_argbest(float& v, int64_t& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int64_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better<IS_MAX>(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+}
+
+// Sum a per-thread double across a block of blockDim.x threads (<= 1024) in a
+// fixed order.  Returns the total in thread 0.  `sh` needs 32 doubles.
+DCT_DEV double block_sum(double v, double* sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sh[wid] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (wid == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    t = lane < nw ? sh[lane] : 0.0;
+    t = warp_sum(t);
+  }
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// fast unsigned division by a runtime-invariant divisor (round-up method of
+// Granlund & Montgomery, "Division by invariant integers using multiplication",
+// PLDI 1994): q = umulhi(n, m) + n >> s for n < 2^32.
+// ---------------------------------------------------------------------------
+struct FastDiv {
+  uint32_t d = 1, m = 0, s = 0;
+  FastDiv() = default;
+  explicit FastDiv(uint32_t div) : d(div) {
+    if (div == 1) { m = 0; s = 0; return; }
+    uint32_t l = 0;
+    while ((1ull << l) < div) ++l;               // l = ceil(log2(d))
+    uint64_t mm = ((1ull << 32) * ((1ull << l) - div)) / div + 1;
+    m = (uint32_t)mm;
+    s = l - 1;
+  }
+  DCT_DEV uint32_t div(uint32_t n) const {
+    if (d == 1) return n;
+    uint32_t hi = __umulhi(n, m);
+    return (hi + ((n - hi) >> 1)) >> s;
+  }
+};
+
+}  // namespace dct

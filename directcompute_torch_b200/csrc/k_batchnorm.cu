@@ -1,0 +1,283 @@
+// BatchNorm (NCHW, training and eval) kernels of libdct_cuda (sm_100a).
+//
+// The reference runs one 256-thread group per CHANNEL that walks N*S elements
+// with a divide and modulo per element (nn_batchnorm_mean_var.hlsl:19-60,
+// nn_batchnorm_backward_reduce.hlsl:21-60) and two per-element apply shaders
+// (nn_batchnorm_forward.hlsl:18-34, nn_batchnorm_backward_dx.hlsl:20-38).
+//
+// Here a warp owns one (n, c) plane of S contiguous floats, streams it with
+// 128-bit loads and leaves two float64 plane sums; a fold launch adds the N
+// plane sums of each channel in n order (deterministic; across GPUs the same
+// per-channel sums are what the NCCL exchange combines); a finalize launch turns
+// them into mean / biased var (+ the momentum update with the unbiased var) or
+// dgamma / dbeta.  The apply kernels are plane-wise too, so the channel's
+// constants sit in registers and the loop is a pure 128-bit stream.
+#include "dct_common.cuh"
+#include "kernels.h"
+
+namespace dct {
+
+namespace {
+
+DCT_DEV float rstd_of(float var, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));   // 1.0 / sqrt(v + eps)
+}
+
+// BWD == false: (sum x, sum x^2); BWD == true: (sum dy, sum dy*x)
+template <bool BWD, bool VEC>
+__global__ void __launch_bounds__(256) k_bn_plane_sums(const float* __restrict__ x, const float* __restrict__ dy,
+                                                       uint64_t planes, uint32_t S, double* out) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  for (uint64_t pl = gw; pl < planes; pl += nw) {
+    const float* px = x + pl * S;
+    const float* pd = BWD ? dy + pl * S : nullptr;
+    double a = 0.0, b = 0.0;
+    if (VEC) {
+      const uint32_t s4 = S >> 2;
+      uint32_t i = lane;
+      for (; i + 96 < s4; i += 128) {
+        float4 vx[4], vd[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          vx[k] = ld_stream4(px + 4 * (i + 32 * k));
+          if (BWD) vd[k] = ld_stream4(pd + 4 * (i + 32 * k));
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (BWD) {
+            a += (double)vd[k].x + (double)vd[k].y + (double)vd[k].z + (double)vd[k].w;
+            b += (double)vd[k].x * vx[k].x + (double)vd[k].y * vx[k].y + (double)vd[k].z * vx[k].z +
+                 (double)vd[k].w * vx[k].w;
+          } else {
+            a += (double)vx[k].x + (double)vx[k].y + (double)vx[k].z + (double)vx[k].w;
+            b += (double)vx[k].x * vx[k].x + (double)vx[k].y * vx[k].y + (double)vx[k].z * vx[k].z +
+                 (double)vx[k].w * vx[k].w;
+          }
+        }
+      }
+      for (; i < s4; i += 32) {
+        const float4 v = ld_stream4(px + 4 * i);
+        if (BWD) {
+          const float4 d = ld_stream4(pd + 4 * i);
+          a += (double)d.x + (double)d.y + (double)d.z + (double)d.w;
+          b += (double)d.x * v.x + (double)d.y * v.y + (double)d.z * v.z + (double)d.w * v.w;
+        } else {
+          a += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+          b += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+        }
+      }
+    } else {
+      for (uint32_t i = lane; i < S; i += 32) {
+        const double v = (double)px[i];
+        if (BWD) { const double d = (double)pd[i]; a += d; b += d * v; }
+        else { a += v; b += v * v; }
+      }
+    }
+    a = warp_sum(a);
+    b = warp_sum(b);
+    if (lane == 0) { out[2 * pl] = a; out[2 * pl + 1] = b; }
+  }
+}
+
+__global__ void k_bn_fold(const double* __restrict__ ps, uint32_t N, uint32_t C, double* chan) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;     // (c, j)
+  if (k >= 2 * C) return;
+  const uint32_t c = k >> 1, j = k & 1;
+  double acc = 0.0;
+  for (uint32_t n = 0; n < N; ++n) acc += ps[2 * ((uint64_t)n * C + c) + j];
+  chan[k] = acc;
+}
+
+__global__ void k_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rm,
+                                 float* rv, int training, float momentum) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const double m = chan[2 * c] / cnt;
+  const double v = fmax(0.0, chan[2 * c + 1] / cnt - m * m);
+  mean[c] = (float)m;
+  var[c] = (float)v;
+  if (training) {
+    const double mom = (double)momentum;
+    const double unb = v * (cnt / fmax(1.0, cnt - 1.0));
+    rm[c] = (float)((1.0 - mom) * (double)rm[c] + mom * m);
+    rv[c] = (float)((1.0 - mom) * (double)rv[c] + mom * unb);
+  }
+}
+
+__global__ void k_bn_bwd_final(const double* chan, uint32_t C, const float* mean, const float* var, float eps,
+                               float* dgamma, float* dbeta) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const double sdy = chan[2 * c], sdyx = chan[2 * c + 1];
+  const double rstd = (double)rstd_of(var[c], eps);
+  dgamma[c] = (float)((sdyx - (double)mean[c] * sdy) * rstd);
+  dbeta[c] = (float)sdy;
+}
+
+// y = ((x - m) * rstd) * g + b, one warp per plane; elements >= limit untouched
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_bn_forward(const float* __restrict__ x, const float* __restrict__ mean,
+                                                    const float* __restrict__ var, const float* __restrict__ gamma,
+                                                    const float* __restrict__ beta, float* __restrict__ y,
+                                                    uint64_t planes, uint32_t C, uint32_t S, float eps,
+                                                    uint64_t limit) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  for (uint64_t pl = gw; pl < planes; pl += nw) {
+    const uint32_t c = (uint32_t)(pl % C);
+    const float m = mean[c], r = rstd_of(var[c], eps), g = gamma[c], b = beta[c];
+    const uint64_t base = pl * S;
+    if (base >= limit) break;
+    const float* px = x + base;
+    float* py = y + base;
+    auto f = [&](float v) { return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, m), r), g), b); };
+    if (VEC && base + S <= limit) {
+      const uint32_t s4 = S >> 2;
+      uint32_t i = lane;
+      for (; i + 96 < s4; i += 128) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = ld_stream4(px + 4 * (i + 32 * k));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) st_stream4(py + 4 * (i + 32 * k), make_float4(f(v[k].x), f(v[k].y), f(v[k].z), f(v[k].w)));
+      }
+      for (; i < s4; i += 32) {
+        const float4 v = ld_stream4(px + 4 * i);
+        st_stream4(py + 4 * i, make_float4(f(v.x), f(v.y), f(v.z), f(v.w)));
+      }
+    } else {
+      for (uint32_t i = lane; i < S; i += 32)
+        if (base + i < limit) py[i] = f(px[i]);
+    }
+  }
+}
+
+// dx = (g*rstd) * (dy - (db + xhat*dg) / m)
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_bn_backward_dx(const float* __restrict__ x, const float* __restrict__ dy,
+                                                        const float* __restrict__ mean, const float* __restrict__ var,
+                                                        const float* __restrict__ gamma,
+                                                        const float* __restrict__ dgamma,
+                                                        const float* __restrict__ dbeta, float* __restrict__ dx,
+                                                        uint64_t planes, uint32_t C, uint32_t S, float eps, float mf,
+                                                        uint64_t limit) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  for (uint64_t pl = gw; pl < planes; pl += nw) {
+    const uint32_t c = (uint32_t)(pl % C);
+    const float m = mean[c], r = rstd_of(var[c], eps), dg = dgamma[c], db = dbeta[c];
+    const float k1 = __fmul_rn(gamma[c], r);
+    const uint64_t base = pl * S;
+    if (base >= limit) break;
+    auto f = [&](float xv, float d) {
+      const float xh = __fmul_rn(__fsub_rn(xv, m), r);
+      return __fmul_rn(k1, __fsub_rn(d, __fdiv_rn(__fadd_rn(db, __fmul_rn(xh, dg)), mf)));
+    };
+    const float* px = x + base;
+    const float* pd = dy + base;
+    float* po = dx + base;
+    if (VEC && base + S <= limit) {
+      const uint32_t s4 = S >> 2;
+      uint32_t i = lane;
+      for (; i + 32 < s4; i += 64) {
+        float4 a[2], d[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) { a[k] = ld_stream4(px + 4 * (i + 32 * k)); d[k] = ld_stream4(pd + 4 * (i + 32 * k)); }
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          st_stream4(po + 4 * (i + 32 * k), make_float4(f(a[k].x, d[k].x), f(a[k].y, d[k].y), f(a[k].z, d[k].z), f(a[k].w, d[k].w)));
+      }
+      for (; i < s4; i += 32) {
+        const float4 a = ld_stream4(px + 4 * i), d = ld_stream4(pd + 4 * i);
+        st_stream4(po + 4 * i, make_float4(f(a.x, d.x), f(a.y, d.y), f(a.z, d.z), f(a.w, d.w)));
+      }
+    } else {
+      for (uint32_t i = lane; i < S; i += 32)
+        if (base + i < limit) po[i] = f(px[i], pd[i]);
+    }
+  }
+}
+
+unsigned plane_blocks(uint64_t planes) {
+  const DevInfo& d = dev_info();
+  const uint64_t warps = planes;
+  uint64_t blocks = (warps + 7) / 8;
+  const uint64_t cap = (uint64_t)d.sm_count * (d.max_threads_per_sm / 256);
+  return (unsigned)(blocks < cap ? (blocks ? blocks : 1) : cap);
+}
+
+}  // namespace
+
+size_t bn_ws_bytes(uint32_t N, uint32_t C) {
+  return ((size_t)N * C * 2 + (size_t)C * 2) * sizeof(double);
+}
+
+cudaError_t launch_bn_plane_sums(const float* x, const float* dy, uint32_t N, uint32_t C, uint32_t S,
+                                 double* plane_sums, cudaStream_t st) {
+  const uint64_t planes = (uint64_t)N * C;
+  if (planes == 0) return cudaSuccess;
+  const bool vec = (S % 4 == 0) && aligned16_h(x) && (!dy || aligned16_h(dy));
+  const unsigned blocks = plane_blocks(planes);
+  if (dy) {
+    if (vec) k_bn_plane_sums<true, true><<<blocks, 256, 0, st>>>(x, dy, planes, S, plane_sums);
+    else k_bn_plane_sums<true, false><<<blocks, 256, 0, st>>>(x, dy, planes, S, plane_sums);
+  } else {
+    if (vec) k_bn_plane_sums<false, true><<<blocks, 256, 0, st>>>(x, nullptr, planes, S, plane_sums);
+    else k_bn_plane_sums<false, false><<<blocks, 256, 0, st>>>(x, nullptr, planes, S, plane_sums);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, double* chan, cudaStream_t st) {
+  if (C == 0) return cudaSuccess;
+  k_bn_fold<<<(2 * C + 255) / 256, 256, 0, st>>>(plane_sums, N, C, chan);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rmean,
+                                  float* rvar, bool training, float momentum, cudaStream_t st) {
+  if (C == 0) return cudaSuccess;
+  k_bn_stats_final<<<(C + 255) / 256, 256, 0, st>>>(chan, C, cnt, mean, var, rmean, rvar, training ? 1 : 0,
+                                                      momentum);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_bwd_final(const double* chan, uint32_t C, const float* mean, const float* var, float eps,
+                                float* dgamma, float* dbeta, cudaStream_t st) {
+  if (C == 0) return cudaSuccess;
+  k_bn_bwd_final<<<(C + 255) / 256, 256, 0, st>>>(chan, C, mean, var, eps, dgamma, dbeta);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_forward(const float* x, const float* mean, const float* var, const float* gamma,
+                              const float* beta, float* y, uint32_t N, uint32_t C, uint32_t S, float eps,
+                              uint64_t limit, cudaStream_t st) {
+  const uint64_t planes = (uint64_t)N * C;
+  if (planes == 0 || S == 0) return cudaSuccess;
+  const bool vec = (S % 4 == 0) && aligned16_h(x) && aligned16_h(y);
+  const unsigned blocks = plane_blocks(planes);
+  if (vec) k_bn_forward<true><<<blocks, 256, 0, st>>>(x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
+  else k_bn_forward<false><<<blocks, 256, 0, st>>>(x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* mean, const float* var,
+                                  const float* gamma, const float* dgamma, const float* dbeta, float* dx, uint32_t N,
+                                  uint32_t C, uint32_t S, float eps, uint64_t limit, cudaStream_t st) {
+  const uint64_t planes = (uint64_t)N * C;
+  if (planes == 0 || S == 0) return cudaSuccess;
+  const float mf = (float)((uint32_t)(N * S));     // HLSL: (float)(N * S) in uint arithmetic
+  const bool vec = (S % 4 == 0) && aligned16_h(x) && aligned16_h(dy) && aligned16_h(dx);
+  const unsigned blocks = plane_blocks(planes);
+  if (vec)
+    k_bn_backward_dx<true><<<blocks, 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C, S, eps, mf, limit);
+  else
+    k_bn_backward_dx<false><<<blocks, 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C, S, eps, mf, limit);
+  return cudaGetLastError();
+}
+
+}  // namespace dct

@@ -1,0 +1,370 @@
+// Row softmax / log-softmax / cross-entropy kernels of libdct_cuda (sm_100a).
+//
+// Replaces nn_softmax.hlsl:5-13 (one thread per row, three serial passes),
+// nn_loss.hlsl:11-43 (ONE 256-thread group for the whole batch),
+// nn_softmax_ce_grad.hlsl:6-11 (re-reads the stored probs) and
+// nn_argmax_correct.hlsl:10-26 with ONE fused pass: a warp owns a row, holds
+// it in registers (read from HBM once), and writes probs, dlogits =
+// (p - onehot) / B and optional log-probs from those registers; each row's
+// cross-entropy joins a per-block float64 partial that a second tiny launch
+// folds in block order (deterministic).
+//
+// Accuracy: x - max is formed with an error-free two-sum so the exponent's
+// argument is exact to first order (exp(s + t) = exp(s) * (1 + t)); the row
+// normaliser is summed in float64 and applied as a float64 product, so each
+// probability carries the error of one expf plus one rounding.  The loss and
+// log-probs are formed in float64 from log(sum).  dlogits follow the
+// reference formula (p - onehot) / B on the rounded p, bit for bit.
+#include "dct_common.cuh"
+#include "kernels.h"
+
+namespace dct {
+
+namespace {
+
+constexpr int kSmThreads = 256;
+constexpr int kSmWarps = kSmThreads / 32;
+
+// error-free transformation: a + b = s + t exactly (Knuth's TwoSum)
+DCT_DEV void two_sum(float a, float b, float& s, float& t) {
+  s = __fadd_rn(a, b);
+  float bb = __fsub_rn(s, a);
+  t = __fadd_rn(__fsub_rn(a, __fsub_rn(s, bb)), __fsub_rn(b, bb));
+}
+
+// exp(x - m) with the subtraction carried exactly to first order
+DCT_DEV float exp_diff(float x, float m) {
+  float s, t;
+  two_sum(x, -m, s, t);
+  float e = expf(s);
+  return __fmaf_rn(e, t, e);
+}
+
+DCT_DEV float label_of(const void* labels, bool is_int, uint32_t r, uint32_t K, bool& valid) {
+  (void)K;
+  if (is_int) {
+    int v = reinterpret_cast<const int*>(labels)[r];
+    valid = v >= 0;
+    return (float)(v < 0 ? 0 : v);
+  }
+  valid = true;
+  return reinterpret_cast<const float*>(labels)[r];
+}
+
+// (uint) cast of HLSL: truncation, NaN/negative -> 0, saturate
+DCT_DEV uint32_t hlsl_f2u(float f) { return __float2uint_rz(f); }
+
+struct RowCtx {
+  const float* __restrict__ logits;
+  const void* labels;
+  bool labels_int32;
+  uint32_t rows, K;
+  uint64_t total;          // elements in the logits buffer (label reads stay inside it)
+  float* probs;
+  float* dlogits;
+  float* logprobs;
+  double* part;            // per-block fp64 loss partials
+  float grad_div;
+  bool grad_div_pow2;
+  float grad_mul;
+  bool ref_max_init;
+  bool want_loss;
+};
+
+DCT_DEV float grad_of(float p, float oh, const RowCtx& c) {
+  const float d = __fsub_rn(p, oh);
+  return c.grad_div_pow2 ? __fmul_rn(d, c.grad_mul) : __fdiv_rn(d, c.grad_div);
+}
+
+// One warp per row, VPL float4 (VEC) or VPL*4 scalars per lane held in registers.
+template <int VPL, bool VEC>
+__global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_constant__ RowCtx c) {
+  __shared__ double wsum[kSmWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double block_loss = 0.0;
+  const uint32_t K = c.K;
+  for (uint32_t r = blockIdx.x * kSmWarps + warp; r < c.rows; r += gridDim.x * kSmWarps) {
+    const float* row = c.logits + (uint64_t)r * K;
+    float x[VPL * 4];
+    // ---- load the row (out-of-range slots = -inf)
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      if (VEC) {
+        const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+        float4 v = col < K ? ld_stream4(row + col) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        x[4 * j + 0] = v.x; x[4 * j + 1] = v.y; x[4 * j + 2] = v.z; x[4 * j + 3] = v.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t col = (uint32_t)(lane + 32 * (4 * j + q));
+          x[4 * j + q] = col < K ? ld_stream(row + col) : -INFINITY;
+        }
+      }
+    }
+    // ---- row max
+    float m = c.ref_max_init ? -1e30f : -INFINITY;
+#pragma unroll
+    for (int k = 0; k < VPL * 4; ++k) m = fmaxf(m, x[k]);
+    m = warp_max_f(m);
+    // ---- exp and float64 normaliser
+    double s = 0.0;
+#pragma unroll
+    for (int k = 0; k < VPL * 4; ++k) {
+      const float e = (x[k] == -INFINITY) ? 0.0f : exp_diff(x[k], m);
+      s += (double)e;
+      x[k] = e;                      // keep e, the logits are no longer needed except for the label
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const double inv = 1.0 / s;
+    const double lse = log(s);       // log sum exp(x - m)
+    // ---- label
+    bool lvalid = true;
+    float lab = 0.0f;
+    if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
+    const uint32_t lidx = !lvalid ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
+    // ---- outputs
+    float* prow = c.probs ? c.probs + (uint64_t)r * K : nullptr;
+    float* grow = c.dlogits ? c.dlogits + (uint64_t)r * K : nullptr;
+    float* lrow = c.logprobs ? c.logprobs + (uint64_t)r * K : nullptr;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      float p[4], g[4];
+      uint32_t col0 = VEC ? (uint32_t)(lane + 32 * j) * 4 : 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t col = VEC ? col0 + q : (uint32_t)(lane + 32 * (4 * j + q));
+        p[q] = (float)((double)x[4 * j + q] * inv);
+        const float oh = (c.labels && col == lidx) ? 1.0f : 0.0f;
+        g[q] = grad_of(p[q], oh, c);
+      }
+      if (VEC) {
+        if (col0 < K) {
+          if (prow) st_stream4(prow + col0, make_float4(p[0], p[1], p[2], p[3]));
+          if (grow) st_stream4(grow + col0, make_float4(g[0], g[1], g[2], g[3]));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t col = (uint32_t)(lane + 32 * (4 * j + q));
+          if (col < K) {
+            if (prow) st_stream(prow + col, p[q]);
+            if (grow) st_stream(grow + col, g[q]);
+          }
+        }
+      }
+    }
+    if (lrow) {
+      // log p = (x - m) - lse: re-read the row (L2-resident) and form it in fp64
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t col = VEC ? (uint32_t)(lane + 32 * j) * 4 + q : (uint32_t)(lane + 32 * (4 * j + q));
+          if (col < K) lrow[col] = (float)(((double)row[col] - (double)m) - lse);
+        }
+      }
+    }
+    if (c.want_loss && lane == 0 && lvalid) {
+      const uint64_t li = (uint64_t)r * K + lidx;
+      const double xl = li < c.total ? (double)row[lidx] : 0.0;
+      block_loss += -((xl - (double)m) - lse);
+    }
+  }
+  if (c.want_loss) {
+    if (lane == 0) wsum[warp] = block_loss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int w = 0; w < kSmWarps; ++w) t += wsum[w];
+      c.part[blockIdx.x] = t;
+    }
+  }
+}
+
+// Rows longer than 2048: one block per row, three streaming passes (L2 keeps the row).
+__global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_constant__ RowCtx c) {
+  __shared__ double shd[32];
+  __shared__ float shf[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double block_loss = 0.0;
+  const uint32_t K = c.K;
+  for (uint32_t r = blockIdx.x; r < c.rows; r += gridDim.x) {
+    const float* row = c.logits + (uint64_t)r * K;
+    float m = c.ref_max_init ? -1e30f : -INFINITY;
+    for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, row[k]);
+    m = warp_max_f(m);
+    __syncthreads();
+    if (lane == 0) shf[warp] = m;
+    __syncthreads();
+    m = shf[0];
+    for (int w = 1; w < kSmWarps; ++w) m = fmaxf(m, shf[w]);
+    double s = 0.0;
+    for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+      const float xv = row[k];
+      s += (xv == -INFINITY) ? 0.0 : (double)exp_diff(xv, m);
+    }
+    s = block_sum(s, shd);
+    __syncthreads();
+    if (threadIdx.x == 0) shd[0] = s;
+    __syncthreads();
+    s = shd[0];
+    const double inv = 1.0 / s, lse = log(s);
+    bool lvalid = true;
+    float lab = 0.0f;
+    if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
+    const uint32_t lidx = !lvalid ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
+    for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
+      const float xv = row[k];
+      const float e = (xv == -INFINITY) ? 0.0f : exp_diff(xv, m);
+      const float p = (float)((double)e * inv);
+      if (c.probs) c.probs[(uint64_t)r * K + k] = p;
+      if (c.dlogits) c.dlogits[(uint64_t)r * K + k] = grad_of(p, (c.labels && k == lidx) ? 1.0f : 0.0f, c);
+      if (c.logprobs) c.logprobs[(uint64_t)r * K + k] = (float)(((double)xv - (double)m) - lse);
+    }
+    if (c.want_loss && threadIdx.x == 0 && lvalid) {
+      const uint64_t li = (uint64_t)r * K + lidx;
+      const double xl = li < c.total ? (double)row[lidx] : 0.0;
+      block_loss += -((xl - (double)m) - lse);
+    }
+    __syncthreads();
+  }
+  if (c.want_loss && threadIdx.x == 0) c.part[blockIdx.x] = block_loss;
+}
+
+__global__ void k_loss_final(const double* part, int nparts, double div, float* loss, double* raw) {
+  __shared__ double sh[32];
+  double acc = 0.0;
+  for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
+  double t = block_sum(acc, sh);
+  if (threadIdx.x == 0) {
+    if (raw) raw[0] = t;
+    if (loss) loss[0] = (float)(t / div);
+  }
+}
+
+int softmax_blocks(uint32_t rows, uint32_t K) {
+  const DevInfo& d = dev_info();
+  if (K > 2048) {
+    int b = d.sm_count * 8;
+    return (int)(rows < (uint32_t)b ? (rows ? rows : 1) : b);
+  }
+  uint64_t need = ((uint64_t)rows + kSmWarps - 1) / kSmWarps;
+  uint64_t cap = (uint64_t)d.sm_count * 16;
+  uint64_t b = need < cap ? need : cap;
+  return (int)(b ? b : 1);
+}
+
+}  // namespace
+
+size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K) {
+  return (size_t)softmax_blocks(rows, K) * sizeof(double) + 64;
+}
+
+cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st) {
+  if (a.rows == 0) {
+    if (a.loss) { cudaError_t e = cudaMemsetAsync(a.loss, 0, sizeof(float), st); if (e) return e; }
+    if (a.loss_partial) return cudaMemsetAsync(a.loss_partial, 0, sizeof(double), st);
+    return cudaSuccess;
+  }
+  if (a.K == 0) return cudaErrorInvalidValue;
+  RowCtx c;
+  c.logits = a.logits;
+  c.labels = a.labels;
+  c.labels_int32 = a.labels_int32;
+  c.rows = a.rows;
+  c.K = a.K;
+  c.total = (uint64_t)a.rows * a.K;
+  c.probs = a.probs;
+  c.dlogits = a.dlogits;
+  c.logprobs = a.logprobs;
+  c.want_loss = (a.loss != nullptr || a.loss_partial != nullptr) && a.labels != nullptr;
+  c.part = (double*)ws;
+  if (c.want_loss && !ws) return cudaErrorInvalidValue;
+  c.grad_div = a.grad_div;
+  int ex = 0;
+  const float fr = frexpf(a.grad_div, &ex);
+  c.grad_div_pow2 = (fr == 0.5f) && a.grad_div > 0.0f && ex - 1 > -126 && ex - 1 < 127;
+  c.grad_mul = c.grad_div_pow2 ? ldexpf(1.0f, -(ex - 1)) : 1.0f;
+  c.ref_max_init = a.ref_max_init;
+  if (a.dlogits && !a.labels) return cudaErrorInvalidValue;
+  const int blocks = softmax_blocks(a.rows, a.K);
+  const bool vec = (a.K % 4 == 0) && aligned16_h(a.logits) && (!a.probs || aligned16_h(a.probs)) &&
+                   (!a.dlogits || aligned16_h(a.dlogits));
+  const uint32_t K = a.K;
+  if (K <= 128) {
+    if (vec) k_softmax_ce_warp<1, true><<<blocks, kSmThreads, 0, st>>>(c);
+    else k_softmax_ce_warp<1, false><<<blocks, kSmThreads, 0, st>>>(c);
+  } else if (K <= 256) {
+    if (vec) k_softmax_ce_warp<2, true><<<blocks, kSmThreads, 0, st>>>(c);
+    else k_softmax_ce_warp<2, false><<<blocks, kSmThreads, 0, st>>>(c);
+  } else if (K <= 512) {
+    if (vec) k_softmax_ce_warp<4, true><<<blocks, kSmThreads, 0, st>>>(c);
+    else k_softmax_ce_warp<4, false><<<blocks, kSmThreads, 0, st>>>(c);
+  } else if (K <= 1024) {
+    if (vec) k_softmax_ce_warp<8, true><<<blocks, kSmThreads, 0, st>>>(c);
+    else k_softmax_ce_warp<8, false><<<blocks, kSmThreads, 0, st>>>(c);
+  } else if (K <= 2048) {
+    if (vec) k_softmax_ce_warp<16, true><<<blocks, kSmThreads, 0, st>>>(c);
+    else k_softmax_ce_warp<16, false><<<blocks, kSmThreads, 0, st>>>(c);
+  } else {
+    k_softmax_ce_block<<<blocks, kSmThreads, 0, st>>>(c);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !c.want_loss) return e;
+  k_loss_final<<<1, 1024, 0, st>>>(c.part, blocks, a.loss_div, a.loss, a.loss_partial);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// reference argmax_correct (nn_argmax_correct.hlsl:10-26): strict '>' scan
+// from column 0; equivalent parallel rule: a NaN at column 0 gives index 0,
+// other NaNs are never chosen, ties keep the lowest index.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_argmax_correct(const float* __restrict__ logits,
+                                                        const float* __restrict__ labels, uint32_t rows, uint32_t K,
+                                                        uint32_t* counter) {
+  __shared__ uint32_t sc[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t hits = 0;
+  for (uint32_t r = blockIdx.x * 8 + warp; r < rows; r += gridDim.x * 8) {
+    const float* row = logits + (uint64_t)r * K;
+    float bv = 0.0f;
+    int64_t bi = -1;
+    for (uint32_t k = lane; k < K; k += 32) {
+      const float v = row[k];
+      if (isnan(v)) continue;
+      if (bi < 0 || v > bv) { bv = v; bi = k; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) {
+      const uint32_t idx = isnan(row[0]) ? 0u : (bi < 0 ? 0u : (uint32_t)bi);
+      if (idx == hlsl_f2u(labels[r])) ++hits;
+    }
+  }
+  if (lane == 0) sc[warp] = hits;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < 8; ++w) t += sc[w];
+    if (t) atomicAdd(counter, t);
+  }
+}
+
+cudaError_t launch_argmax_correct(const float* logits, const float* labels, uint32_t rows, uint32_t K,
+                                  uint32_t* counter, cudaStream_t st) {
+  if (rows == 0 || K == 0) return cudaSuccess;
+  const DevInfo& d = dev_info();
+  uint32_t blocks = (rows + 7) / 8;
+  const uint32_t cap = (uint32_t)d.sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  k_argmax_correct<<<blocks, 256, 0, st>>>(logits, labels, rows, K, counter);
+  return cudaGetLastError();
+}
+
+}  // namespace dct

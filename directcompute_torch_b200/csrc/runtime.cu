@@ -1,0 +1,1353 @@
+// libdct_cuda: the C-ABI drop-in for directcompute_torch's native engine.
+//
+// The reference binds `engine.dll` with ctypes (nn_engine.py:42-119) and drives
+// it through 32 extern "C" entry points (engine.cpp).  This file exports the
+// same names with the same argument meaning, on CUDA for one B200 per process:
+//
+//   device + stream      InitEngine / GetGPUInfo / FlushGPU / SyncGPU
+//   buffers              CreateBuffer / AddRefBuffer / UpdateBuffer / ReleaseBuffer /
+//                        ReleaseBufferBatch / ReadBuffer / ClearBuffer (refcounted
+//                        handles over cudaMallocAsync memory, size-keyed pool with
+//                        the reference's per-size caps, engine.cpp:181-290)
+//   kernels by name      CompileShader (name -> built-in CUDA kernel; the HLSL file
+//                        is not read) / RunShader / RunShaderRaw / RunShaderAlloc(2) /
+//                        ResolveShader / RunSequence(WithSGD)
+//   optimizers           SGDBatch / SGDBatchClipped as multi-tensor launches
+//   pool                 WarmPool / GetPoolStats / ResetPoolStats / GetPoolMemory / DrainPool
+//   out of scope         MatMulAlloc / Conv*Fused / MaxPool*Fused: exported stubs
+//                        (return null, record an error)
+//
+// and extension entry points prefixed dct_ (NumPy-broadcast binary ops, unary
+// ops, axis/full reductions, fused softmax+CE, fused Adam, BatchNorm, device
+// timing, errors, raw-pointer interop, NCCL sharding).
+//
+// Errors never cross the ABI as exceptions: like the reference, calls fail
+// quietly (null / false / no-op) -- and, unlike it, record a message that
+// dct_last_error() returns and dct_error_code() numbers.  Handles are checked
+// against the live-handle set before use, so a stale or foreign pointer is
+// rejected instead of dereferenced.  Every entry point holds one mutex
+// (ctypes drops the GIL during calls).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+#include "dct_common.cuh"
+#include "kernels.h"
+#include "../../include/dct_cuda.h"
+
+namespace dct {
+
+// ---------------------------------------------------------------------------
+// engine state
+// ---------------------------------------------------------------------------
+struct Buffer {
+  uint32_t magic;
+  int32_t ref;
+  uint64_t count;          // fp32 elements
+  float* d;
+  bool owned;              // false: wraps caller memory (dct_wrap_device_ptr)
+};
+constexpr uint32_t kBufMagic = 0xDC7B0F01u;
+
+struct Engine {
+  bool init = false;
+  DevInfo info;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  std::unordered_set<Buffer*> live;
+  std::unordered_map<uint64_t, std::vector<Buffer*>> pool;
+  uint64_t hits = 0, misses = 0, pool_bytes = 0;
+  void* ws = nullptr;             // reduction scratch
+  size_t ws_bytes = 0;
+  float* host_small = nullptr;    // pinned 64-byte staging for scalar readbacks
+  char name[128] = {0};
+  // error state
+  int err_code = 0;
+  std::string err;
+};
+
+static Engine g;
+static std::recursive_mutex g_mu;
+#define LOCK std::lock_guard<std::recursive_mutex> _lk(g_mu)
+
+const DevInfo& dev_info() { return g.info; }
+
+static void set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g.err_code = code;
+  g.err = buf;
+}
+
+static bool cuda_ok(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return true;
+  set_error(DCT_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+  return false;
+}
+
+static bool ensure_init();
+
+// ---------------------------------------------------------------------------
+// buffers and pool (engine.cpp:181-290 semantics)
+// ---------------------------------------------------------------------------
+static size_t max_pool_for_size(uint64_t count) {          // engine.cpp:186-197
+  const uint64_t bytes = count * sizeof(float);
+  const uint64_t usable = g.info.total_mem;
+  if (usable > 0 && bytes >= usable / 4) return 4;
+  if (bytes >= 4ull * 1024 * 1024) return 6;
+  if (bytes >= 256ull * 1024) return 8;
+  return 16;
+}
+
+static Buffer* buf_of(void* h) {
+  Buffer* b = static_cast<Buffer*>(h);
+  if (!b || g.live.find(b) == g.live.end() || b->magic != kBufMagic) return nullptr;
+  return b;
+}
+
+static Buffer* create_buffer(const float* host, uint64_t count) {
+  if (!ensure_init()) return nullptr;
+  if (count == 0) {
+    set_error(DCT_ERR_ARG, "CreateBuffer: zero-length buffer");
+    return nullptr;
+  }
+  Buffer* b = nullptr;
+  auto it = g.pool.find(count);
+  if (it != g.pool.end() && !it->second.empty()) {
+    b = it->second.back();
+    it->second.pop_back();
+    g.pool_bytes -= count * sizeof(float);
+    g.hits++;
+  } else {
+    g.misses++;
+    void* d = nullptr;
+    const size_t bytes = ((count * sizeof(float)) + 255) & ~size_t(255);
+    if (!cuda_ok(cudaMallocAsync(&d, bytes, g.stream), "CreateBuffer(cudaMallocAsync)")) return nullptr;
+    b = new Buffer{kBufMagic, 0, count, static_cast<float*>(d), true};
+  }
+  b->ref = 1;
+  g.live.insert(b);
+  if (host) {
+    cudaPointerAttributes at{};
+    const bool pinned = cudaPointerGetAttributes(&at, host) == cudaSuccess && at.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    cuda_ok(cudaMemcpyAsync(b->d, host, count * sizeof(float), cudaMemcpyHostToDevice, g.stream), "CreateBuffer(H2D)");
+    if (pinned) cudaStreamSynchronize(g.stream);   // caller may reuse its memory on return
+  }
+  return b;
+}
+
+static void destroy(Buffer* b) {
+  if (b->owned && b->d) cudaFreeAsync(b->d, g.stream);
+  b->magic = 0;
+  delete b;
+}
+
+static void release_internal(Buffer* b) {                   // engine.cpp:267-290
+  g.live.erase(b);
+  if (!b->owned) { destroy(b); return; }
+  auto& lst = g.pool[b->count];
+  if (lst.size() < max_pool_for_size(b->count)) {
+    lst.push_back(b);
+    g.pool_bytes += b->count * sizeof(float);
+  } else {
+    destroy(b);
+  }
+}
+
+static void release_handle(void* h) {
+  Buffer* b = buf_of(h);
+  if (!b) {
+    if (h) set_error(DCT_ERR_HANDLE, "ReleaseBuffer: unknown handle %p", h);
+    return;
+  }
+  if (--b->ref <= 0) release_internal(b);
+}
+
+static bool ensure_ws(size_t bytes) {
+  if (bytes <= g.ws_bytes) return true;
+  size_t want = std::max(bytes, g.ws_bytes * 2);
+  want = (want + (1 << 20) - 1) & ~size_t((1 << 20) - 1);
+  if (g.ws) cudaFreeAsync(g.ws, g.stream);
+  g.ws = nullptr;
+  g.ws_bytes = 0;
+  if (!cuda_ok(cudaMallocAsync(&g.ws, want, g.stream), "workspace(cudaMallocAsync)")) return false;
+  g.ws_bytes = want;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// init / device
+// ---------------------------------------------------------------------------
+static bool init_engine() {
+  if (g.init) return true;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    set_error(DCT_ERR_NO_DEVICE, "InitEngine: no CUDA device visible");
+    return false;
+  }
+  int dev = -1;
+  const char* e = getenv("DCT_DEVICE");
+  if (!e) e = getenv("LOCAL_RANK");
+  if (e) dev = atoi(e) % n;
+  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  if (!cuda_ok(cudaSetDevice(dev), "InitEngine(cudaSetDevice)")) return false;
+  cudaDeviceProp p{};
+  if (!cuda_ok(cudaGetDeviceProperties(&p, dev), "InitEngine(props)")) return false;
+  g.info.device = dev;
+  g.info.sm_count = p.multiProcessorCount;
+  g.info.max_threads_per_sm = p.maxThreadsPerMultiProcessor;
+  g.info.smem_optin = p.sharedMemPerBlockOptin;
+  g.info.total_mem = p.totalGlobalMem;
+  snprintf(g.name, sizeof(g.name), "%s", p.name);
+  if (!cuda_ok(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "InitEngine(stream)")) return false;
+  cudaEventCreate(&g.ev0);
+  cudaEventCreate(&g.ev1);
+  // keep freed blocks in the stream-ordered pool instead of returning them to the driver
+  cudaMemPool_t mp;
+  if (cudaDeviceGetDefaultMemPool(&mp, dev) == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;
+    cudaMemPoolSetAttribute(mp, cudaMemPoolAttrReleaseThreshold, &thr);
+  }
+  cudaGetLastError();
+  if (!cuda_ok(cudaMallocHost(&g.host_small, 64), "InitEngine(pinned staging)")) return false;
+  g.init = true;
+  return true;
+}
+
+static bool ensure_init() {
+  if (g.init) return true;
+  if (init_engine()) return true;
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// shader registry
+// ---------------------------------------------------------------------------
+struct Disp {
+  Buffer* srv[16];
+  uint32_t nsrv;
+  Buffer* uav[16];
+  uint32_t nuav;
+  uint32_t gx, gy, gz;
+  uint32_t u[16];          // cbuffer words, zero padded
+  uint32_t cbsize;
+  const char* name;
+};
+typedef bool (*Handler)(const Disp&);
+
+struct Shader {
+  const char* name;
+  Handler fn;
+  bool always;             // extension kernels: usable without CompileShader
+  bool compiled;
+  uint32_t magic;
+};
+constexpr uint32_t kShaderMagic = 0x5EADC0DEu;
+
+static float f_of(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static uint64_t lim(uint64_t count, uint32_t groups, uint32_t tpg = 256) {
+  return std::min<uint64_t>(count, (uint64_t)groups * tpg);
+}
+
+// argument checks: handles present and large enough
+static bool need(const Disp& d, uint32_t ns, uint32_t nu) {
+  if (d.nsrv < ns || d.nuav < nu) {
+    set_error(DCT_ERR_ARG, "%s: needs %u SRVs / %u UAVs, got %u / %u", d.name, ns, nu, d.nsrv, d.nuav);
+    return false;
+  }
+  for (uint32_t i = 0; i < ns; ++i)
+    if (!d.srv[i]) { set_error(DCT_ERR_HANDLE, "%s: SRV t%u is not a live buffer", d.name, i); return false; }
+  for (uint32_t i = 0; i < nu; ++i)
+    if (!d.uav[i]) { set_error(DCT_ERR_HANDLE, "%s: UAV u%u is not a live buffer", d.name, i); return false; }
+  return true;
+}
+static bool fits(const Disp& d, const Buffer* b, uint64_t n, const char* what) {
+  if (b->count >= n) return true;
+  set_error(DCT_ERR_SIZE, "%s: %s holds %llu floats, the dispatch touches %llu", d.name, what,
+            (unsigned long long)b->count, (unsigned long long)n);
+  return false;
+}
+#define FITS(b, n, what) if (!fits(d, b, n, what)) return false
+#define LAUNCH(expr) return cuda_ok((expr), d.name)
+
+// ---- elementwise -----------------------------------------------------------
+static bool h_add_bias_impl(const Disp& d, bool relu) {     // nn_add_bias.hlsl / nn_bias_relu.hlsl
+  if (!need(d, 2, 1)) return false;
+  const uint64_t M = d.u[0], N = d.u[1];
+  const uint64_t n = lim(M * N, d.gx);
+  if (n == 0 || N == 0) return true;
+  FITS(d.srv[0], n, "A"); FITS(d.uav[0], n, "C"); FITS(d.srv[1], std::min<uint64_t>(N, n), "B");
+  const uint64_t full = n / N, rem = n % N;
+  cudaError_t e = cudaSuccess;
+  if (full) e = launch_add_bias(d.srv[0]->d, d.srv[1]->d, d.uav[0]->d, full, N, relu, g.stream);
+  if (e == cudaSuccess && rem)
+    e = launch_add_bias(d.srv[0]->d + full * N, d.srv[1]->d, d.uav[0]->d + full * N, 1, rem, relu, g.stream);
+  LAUNCH(e);
+}
+static bool h_add_bias(const Disp& d) { return h_add_bias_impl(d, false); }
+static bool h_bias_relu(const Disp& d) { return h_add_bias_impl(d, true); }
+
+static bool h_relu(const Disp& d) {                           // nn_relu.hlsl: no cb, no bounds check
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n_out = lim(d.uav[0]->count, d.gx);
+  LAUNCH(launch_relu_bounded(d.srv[0]->d, d.srv[0]->count, d.uav[0]->d, n_out, g.stream));
+}
+
+static bool unary_n(const Disp& d, int op, float alpha) {
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n = lim(d.u[0], d.gx);
+  FITS(d.srv[0], n, "input"); FITS(d.uav[0], n, "output");
+  LAUNCH(launch_unary(op, d.srv[0]->d, d.uav[0]->d, n, alpha, g.stream));
+}
+static bool binary_n(const Disp& d, int op, uint64_t count, float al, float be) {
+  if (!need(d, 2, 1)) return false;
+  const uint64_t n = lim(count, d.gx);
+  FITS(d.srv[0], n, "t0"); FITS(d.srv[1], n, "t1"); FITS(d.uav[0], n, "u0");
+  LAUNCH(launch_binary_same(op, d.srv[0]->d, d.srv[1]->d, d.uav[0]->d, n, al, be, g.stream));
+}
+static bool h_relu6(const Disp& d) { return unary_n(d, EW_RELU6, 0.f); }
+static bool h_leaky_relu(const Disp& d) { return unary_n(d, EW_LEAKY_RELU, f_of(d.u[1])); }
+static bool h_sigmoid(const Disp& d) { return unary_n(d, EW_SIGMOID, 0.f); }
+static bool h_relu_grad(const Disp& d) { return binary_n(d, EW_RELU_GRAD, d.u[0], 0.f, 0.f); }
+static bool h_relu6_grad(const Disp& d) { return binary_n(d, EW_RELU6_GRAD, d.u[0], 0.f, 0.f); }
+static bool h_leaky_relu_grad(const Disp& d) { return binary_n(d, EW_LEAKY_RELU_GRAD, d.u[0], f_of(d.u[1]), 0.f); }
+static bool h_sigmoid_grad(const Disp& d) { return binary_n(d, EW_SIGMOID_GRAD, d.u[0], 0.f, 0.f); }
+static bool h_add(const Disp& d) { return binary_n(d, EW_ADD, (uint64_t)d.u[0] * d.u[1], 0.f, 0.f); }
+static bool h_scale_add(const Disp& d) { return binary_n(d, EW_SCALE_ADD, d.u[0], f_of(d.u[1]), f_of(d.u[2])); }
+
+static bool h_grad_accum(const Disp& d) {                     // accum = accum + grad
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n = lim(d.u[0], d.gx);
+  FITS(d.srv[0], n, "grad"); FITS(d.uav[0], n, "accum");
+  LAUNCH(launch_binary_same(EW_ADD, d.uav[0]->d, d.srv[0]->d, d.uav[0]->d, n, 0.f, 0.f, g.stream));
+}
+
+static bool h_gap_backward(const Disp& d) {
+  if (!need(d, 1, 1)) return false;
+  const uint64_t S = d.u[2];
+  const uint64_t n = lim((uint64_t)d.u[0] * d.u[1] * S, d.gx);
+  if (n == 0) return true;
+  FITS(d.uav[0], n, "dx"); FITS(d.srv[0], (n + S - 1) / S, "grad_output");
+  LAUNCH(launch_gap_backward(d.srv[0]->d, d.uav[0]->d, n, (uint32_t)S, g.stream));
+}
+
+static bool h_accumulate_scalar(const Disp& d) {
+  if (!need(d, 1, 1)) return false;
+  LAUNCH(launch_accumulate_scalar(d.srv[0]->d, d.uav[0]->d, g.stream));
+}
+
+// ---- reductions ------------------------------------------------------------
+static bool reduce_strided(const Disp& d, int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
+                           uint64_t so, uint64_t sl, uint64_t si, float* out, int32_t* idx) {
+  const size_t ws = reduce_strided_ws_bytes(outer, len, inner, so, sl, si);
+  if (ws && !ensure_ws(ws)) return false;
+  LAUNCH(launch_reduce_strided(op, x, outer, len, inner, so, sl, si, out, idx, g.ws, g.ws_bytes, g.stream));
+}
+
+static bool h_bias_grad(const Disp& d) {                      // nn_bias_grad.hlsl:8-29
+  if (!need(d, 1, 1)) return false;
+  const uint64_t B = d.u[0], K = std::min<uint64_t>(d.u[1], d.gx), si = d.u[2], sc = d.u[3];
+  if (K == 0) return true;
+  FITS(d.uav[0], K, "grad_bias");
+  if (B == 0) LAUNCH(cudaMemsetAsync(d.uav[0]->d, 0, K * sizeof(float), g.stream));
+  FITS(d.srv[0], (B - 1) * si + (K - 1) * sc + 1, "grad_out");
+  const float* x = d.srv[0]->d;
+  if (sc == 1) return reduce_strided(d, RED_SUM, x, 1, B, K, 0, si, 1, d.uav[0]->d, nullptr);
+  if (si == 1) return reduce_strided(d, RED_SUM, x, K, B, 1, sc, 1, 1, d.uav[0]->d, nullptr);
+  return reduce_strided(d, RED_SUM, x, 1, B, K, 0, si, sc, d.uav[0]->d, nullptr);
+}
+
+static bool h_gap(const Disp& d) {                            // nn_global_avg_pool.hlsl:16-35
+  if (!need(d, 1, 1)) return false;
+  const uint64_t S = d.u[2];
+  const uint64_t rows = std::min<uint64_t>((uint64_t)d.u[0] * d.u[1], d.gx);
+  if (rows == 0 || S == 0) return true;
+  FITS(d.srv[0], rows * S, "input"); FITS(d.uav[0], rows, "output");
+  return reduce_strided(d, RED_MEAN, d.srv[0]->d, rows, S, 1, S, 1, 1, d.uav[0]->d, nullptr);
+}
+
+static bool h_rms(const Disp& d) {                            // nn_rms.hlsl:7-24
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n = d.u[0];
+  FITS(d.srv[0], n, "A");
+  if (!ensure_ws(full_reduce_ws_bytes())) return false;
+  LAUNCH(launch_rms(d.srv[0]->d, n, d.uav[0]->d, g.ws, g.stream));
+}
+
+static bool h_grad_sq_reduce(const Disp& d) {                 // nn_grad_sq_reduce.hlsl:16-30
+  if (!need(d, 1, 1)) return false;
+  const uint64_t count = d.u[0], off = d.u[1], ng = d.gx;
+  FITS(d.srv[0], std::min<uint64_t>(count, ng * 256), "grad");
+  FITS(d.uav[0], off + ng, "partials");
+  LAUNCH(launch_grad_sq_reduce(d.srv[0]->d, std::min<uint64_t>(count, ng * 256), d.uav[0]->d, off, ng, g.stream));
+}
+
+static bool h_grad_norm_final(const Disp& d) {                // nn_grad_norm_final.hlsl:16-35
+  if (!need(d, 1, 1)) return false;
+  FITS(d.srv[0], d.u[0], "partials"); FITS(d.uav[0], 2, "normScale");
+  LAUNCH(launch_grad_norm_final(d.srv[0]->d, d.u[0], f_of(d.u[1]), d.uav[0]->d, g.stream));
+}
+
+static bool h_dice_loss(const Disp& d) {
+  if (!need(d, 2, 1)) return false;
+  const uint32_t b = std::min<uint32_t>(d.u[0], d.gx), size = d.u[1];
+  FITS(d.srv[0], (uint64_t)b * size, "Pred"); FITS(d.srv[1], (uint64_t)b * size, "Target"); FITS(d.uav[0], b, "Out");
+  LAUNCH(launch_dice_sums(d.srv[0]->d, d.srv[1]->d, b, size, d.uav[0]->d, 1, g.stream));
+}
+static bool h_dice_loss_sums(const Disp& d) {
+  if (!need(d, 2, 1)) return false;
+  const uint32_t b = std::min<uint32_t>(d.u[0], d.gx), size = d.u[1];
+  FITS(d.srv[0], (uint64_t)b * size, "Pred"); FITS(d.srv[1], (uint64_t)b * size, "Target");
+  FITS(d.uav[0], 3ull * b, "Sums");
+  LAUNCH(launch_dice_sums(d.srv[0]->d, d.srv[1]->d, b, size, d.uav[0]->d, 0, g.stream));
+}
+static bool h_dice_loss_grad(const Disp& d) {
+  if (!need(d, 3, 1)) return false;
+  const uint32_t batch = d.u[0], size = d.u[1];
+  const uint64_t n = lim((uint64_t)batch * size, d.gx);
+  if (n == 0) return true;
+  FITS(d.srv[0], n, "Pred"); FITS(d.srv[1], n, "Target"); FITS(d.uav[0], n, "DX");
+  FITS(d.srv[2], 3 * ((n - 1) / size + 1), "Sums");
+  LAUNCH(launch_dice_grad(d.srv[0]->d, d.srv[1]->d, d.srv[2]->d, d.uav[0]->d, batch, size, n, g.stream));
+}
+
+// ---- softmax / CE -------------------------------------------------------------
+static bool run_softmax_ce(const Disp& d, SoftmaxCEArgs a) {
+  const size_t ws = softmax_ce_ws_bytes(a.rows, a.K);
+  if (!ensure_ws(ws)) return false;
+  LAUNCH(launch_softmax_ce(a, g.ws, g.stream));
+}
+
+static bool h_softmax(const Disp& d) {                        // nn_softmax.hlsl:5-13 (16 rows / group)
+  if (!need(d, 1, 1)) return false;
+  const uint32_t K = d.u[1];
+  const uint32_t rows = (uint32_t)std::min<uint64_t>(d.u[0], (uint64_t)d.gx * 16);
+  FITS(d.srv[0], (uint64_t)rows * K, "input"); FITS(d.uav[0], (uint64_t)rows * K, "output");
+  SoftmaxCEArgs a;
+  a.logits = d.srv[0]->d; a.rows = rows; a.K = K; a.probs = d.uav[0]->d; a.ref_max_init = true;
+  return run_softmax_ce(d, a);
+}
+
+static bool h_loss(const Disp& d) {                           // nn_loss.hlsl:11-43
+  if (!need(d, 2, 1)) return false;
+  const uint32_t B = d.u[0], K = d.u[1];
+  FITS(d.srv[0], (uint64_t)B * K, "logits"); FITS(d.srv[1], B, "labels"); FITS(d.uav[0], 1, "loss");
+  SoftmaxCEArgs a;
+  a.logits = d.srv[0]->d; a.labels = d.srv[1]->d; a.rows = B; a.K = K;
+  a.loss = d.uav[0]->d; a.loss_div = (double)(float)B; a.ref_max_init = true;
+  return run_softmax_ce(d, a);
+}
+
+static bool h_softmax_ce_grad(const Disp& d) {                // nn_softmax_ce_grad.hlsl:6-11 (16x16 groups)
+  if (!need(d, 2, 1)) return false;
+  const uint32_t B = d.u[0], K = d.u[1];
+  const uint32_t cols = (uint32_t)std::min<uint64_t>(K, (uint64_t)d.gx * 16);
+  const uint32_t rows = (uint32_t)std::min<uint64_t>(B, (uint64_t)d.gy * 16);
+  FITS(d.srv[0], (uint64_t)B * K, "softmax_out"); FITS(d.srv[1], rows, "labels");
+  FITS(d.uav[0], (uint64_t)B * K, "grad_in");
+  LAUNCH(launch_softmax_ce_grad(d.srv[0]->d, d.srv[1]->d, d.uav[0]->d, B, K, rows, cols, g.stream));
+}
+
+static bool h_argmax_correct(const Disp& d) {                 // nn_argmax_correct.hlsl:10-26
+  if (!need(d, 2, 1)) return false;
+  const uint32_t K = d.u[1];
+  const uint32_t rows = (uint32_t)lim(d.u[0], d.gx);
+  FITS(d.srv[0], (uint64_t)rows * K, "logits"); FITS(d.srv[1], rows, "labels");
+  LAUNCH(launch_argmax_correct(d.srv[0]->d, d.srv[1]->d, rows, K, reinterpret_cast<uint32_t*>(d.uav[0]->d), g.stream));
+}
+
+// ---- optimizers ----------------------------------------------------------------
+static bool h_sgd(const Disp& d) {                            // nn_sgd.hlsl:5-11
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n = lim(d.u[0], d.gx);
+  FITS(d.srv[0], n, "grad"); FITS(d.uav[0], n, "weight");
+  LAUNCH(launch_sgd(d.uav[0]->d, d.srv[0]->d, n, f_of(d.u[1]), f_of(d.u[2]), g.stream));
+}
+
+static bool h_sgd_clipped(const Disp& d) {                    // nn_sgd_clipped.hlsl:15-20
+  if (!need(d, 2, 1)) return false;
+  const uint64_t n = lim(d.u[0], d.gx);
+  FITS(d.srv[0], n, "grad"); FITS(d.srv[1], 2, "normScale"); FITS(d.uav[0], n, "weight");
+  LAUNCH(launch_sgd_clipped(d.uav[0]->d, d.srv[0]->d, n, f_of(d.u[1]), d.srv[1]->d, g.stream));
+}
+
+static bool h_adam(const Disp& d) {                           // nn_adam.hlsl:18-34
+  if (!need(d, 1, 3)) return false;
+  const uint64_t n = lim(d.u[0], d.gx);
+  FITS(d.srv[0], n, "grad"); FITS(d.uav[0], n, "weight"); FITS(d.uav[1], n, "m"); FITS(d.uav[2], n, "v");
+  AdamParams p{f_of(d.u[1]), f_of(d.u[2]), f_of(d.u[3]), f_of(d.u[4]), f_of(d.u[5]), f_of(d.u[6])};
+  LAUNCH(launch_adam(d.uav[0]->d, d.uav[1]->d, d.uav[2]->d, d.srv[0]->d, n, p, g.stream));
+}
+
+// ---- batchnorm -------------------------------------------------------------------
+static bool bn_stats(const Disp& d, const float* x, uint32_t N, uint32_t C, uint32_t S, float* mean, float* var,
+                     float* rm, float* rv, bool training, float momentum, uint32_t c_eff);
+
+static bool h_bn_mean_var(const Disp& d) {                    // nn_batchnorm_mean_var.hlsl:19-60
+  if (!need(d, 1, 4)) return false;
+  const uint32_t N = d.u[0], C = d.u[1], S = d.u[2];
+  const bool training = d.u[3] == 1;
+  const uint32_t c_eff = std::min<uint32_t>(C, d.gx);
+  FITS(d.srv[0], (uint64_t)N * C * S, "x");
+  for (int i = 0; i < 4; ++i) FITS(d.uav[i], c_eff, "stats");
+  return bn_stats(d, d.srv[0]->d, N, C, S, d.uav[0]->d, d.uav[1]->d, d.uav[2]->d, d.uav[3]->d, training,
+                  f_of(d.u[4]), c_eff);
+}
+
+static bool h_bn_forward(const Disp& d) {                     // nn_batchnorm_forward.hlsl:18-34
+  if (!need(d, 5, 1)) return false;
+  const uint32_t N = d.u[0], C = d.u[1], S = d.u[2];
+  const uint64_t total = (uint64_t)N * C * S, n = lim(total, d.gx);
+  FITS(d.srv[0], n, "x"); FITS(d.uav[0], n, "y");
+  for (int i = 1; i < 5; ++i) FITS(d.srv[i], C, "per-channel");
+  LAUNCH(launch_bn_forward(d.srv[0]->d, d.srv[1]->d, d.srv[2]->d, d.srv[3]->d, d.srv[4]->d, d.uav[0]->d, N, C, S,
+                           f_of(d.u[3]), n, g.stream));
+}
+
+static bool h_bn_backward_reduce(const Disp& d) {             // nn_batchnorm_backward_reduce.hlsl:21-60
+  if (!need(d, 4, 2)) return false;
+  const uint32_t N = d.u[0], C = d.u[1], S = d.u[2];
+  const uint32_t c_eff = std::min<uint32_t>(C, d.gx);
+  FITS(d.srv[0], (uint64_t)N * C * S, "x"); FITS(d.srv[1], (uint64_t)N * C * S, "dy");
+  FITS(d.srv[2], C, "mean"); FITS(d.srv[3], C, "var"); FITS(d.uav[0], c_eff, "dgamma"); FITS(d.uav[1], c_eff, "dbeta");
+  if (!ensure_ws(bn_ws_bytes(N, C))) return false;
+  double* ps = (double*)g.ws;
+  double* chan = ps + (size_t)N * C * 2;
+  cudaError_t e = launch_bn_plane_sums(d.srv[0]->d, d.srv[1]->d, N, C, S, ps, g.stream);
+  if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, chan, g.stream);
+  if (e == cudaSuccess)
+    e = launch_bn_bwd_final(chan, c_eff, d.srv[2]->d, d.srv[3]->d, f_of(d.u[3]), d.uav[0]->d, d.uav[1]->d, g.stream);
+  LAUNCH(e);
+}
+
+static bool h_bn_backward_dx(const Disp& d) {                 // nn_batchnorm_backward_dx.hlsl:20-38
+  if (!need(d, 7, 1)) return false;
+  const uint32_t N = d.u[0], C = d.u[1], S = d.u[2];
+  const uint64_t total = (uint64_t)N * C * S, n = lim(total, d.gx);
+  FITS(d.srv[0], n, "x"); FITS(d.srv[1], n, "dy"); FITS(d.uav[0], n, "dx");
+  for (int i = 2; i < 7; ++i) FITS(d.srv[i], C, "per-channel");
+  LAUNCH(launch_bn_backward_dx(d.srv[0]->d, d.srv[1]->d, d.srv[2]->d, d.srv[3]->d, d.srv[4]->d, d.srv[5]->d,
+                               d.srv[6]->d, d.uav[0]->d, N, C, S, f_of(d.u[3]), n, g.stream));
+}
+
+// ---- extension kernels (new names, same RunShader signature) ---------------------
+// dct_unary      cb {op, count, alpha_bits}         t0 x        u0 y
+// dct_binary     cb {op, ndim, a_mask, b_mask, shape[ndim]} (ndim <= 8; a mask bit d = the
+//                operand has extent 1 along output dim d)  t0 a, t1 b  u0 out
+// dct_reduce     cb {op, outer, len, inner}          t0 x        u0 out [, u1 int32 idx]
+// dct_reduce_all cb {op, count}                      t0 x        u0 out[1]
+// dct_softmax_ce cb {rows, K, flags, loss_div_bits, grad_div_bits}  t0 logits, t1 labels
+//                u0 probs, u1 dlogits, u2 loss[1], u3 logprobs (any may be null);
+//                flags bit0: labels are int32
+static bool binary_from_masks(const Disp& d, int op, uint32_t ndim, uint32_t am, uint32_t bm, const uint32_t* shp,
+                              const Buffer* A, const Buffer* B, Buffer* O);
+
+static bool h_dct_unary(const Disp& d) {
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n = d.u[1];
+  FITS(d.srv[0], n, "x"); FITS(d.uav[0], n, "y");
+  LAUNCH(launch_unary((int)d.u[0], d.srv[0]->d, d.uav[0]->d, n, f_of(d.u[2]), g.stream));
+}
+
+static bool h_dct_binary(const Disp& d) {
+  if (!need(d, 2, 1)) return false;
+  const uint32_t ndim = d.u[1];
+  if (ndim > 8) { set_error(DCT_ERR_ARG, "dct_binary: ndim %u > 8", ndim); return false; }
+  return binary_from_masks(d, (int)d.u[0], ndim, d.u[2], d.u[3], &d.u[4], d.srv[0], d.srv[1], d.uav[0]);
+}
+
+static bool h_dct_reduce(const Disp& d) {
+  if (!need(d, 1, 1)) return false;
+  const int op = (int)d.u[0];
+  const uint64_t outer = d.u[1], len = d.u[2], inner = d.u[3];
+  FITS(d.srv[0], outer * len * inner, "x"); FITS(d.uav[0], outer * inner, "out");
+  int32_t* idx = nullptr;
+  if (d.nuav > 1 && d.uav[1]) { FITS(d.uav[1], outer * inner, "idx"); idx = reinterpret_cast<int32_t*>(d.uav[1]->d); }
+  float* out = d.uav[0]->d;
+  if (op == RED_ARGMAX || op == RED_ARGMIN) {
+    // the index is the product; values are not requested
+    if (!idx) { idx = reinterpret_cast<int32_t*>(out); out = nullptr; }
+  }
+  if (len > 0x7fffffffull && (op == RED_ARGMAX || op == RED_ARGMIN)) {
+    set_error(DCT_ERR_ARG, "dct_reduce: arg reductions need len < 2^31");
+    return false;
+  }
+  const size_t ws = reduce3d_ws_bytes(op, outer, len, inner);
+  if (ws && !ensure_ws(ws)) return false;
+  LAUNCH(launch_reduce3d(op, d.srv[0]->d, outer, len, inner, out, idx, g.ws, g.stream));
+}
+
+static bool h_dct_reduce_all(const Disp& d) {
+  if (!need(d, 1, 1)) return false;
+  const uint64_t n = d.u[1];
+  FITS(d.srv[0], n, "x"); FITS(d.uav[0], 1, "out");
+  if (!ensure_ws(full_reduce_ws_bytes())) return false;
+  LAUNCH(launch_full_reduce((int)d.u[0], d.srv[0]->d, n, d.uav[0]->d, nullptr, g.ws, g.stream));
+}
+
+static bool h_dct_softmax_ce(const Disp& d) {
+  if (d.nsrv < 1 || !d.srv[0]) { set_error(DCT_ERR_ARG, "dct_softmax_ce: logits missing"); return false; }
+  const uint32_t rows = d.u[0], K = d.u[1];
+  FITS(d.srv[0], (uint64_t)rows * K, "logits");
+  SoftmaxCEArgs a;
+  a.logits = d.srv[0]->d;
+  a.rows = rows; a.K = K;
+  if (d.nsrv > 1 && d.srv[1]) { FITS(d.srv[1], rows, "labels"); a.labels = d.srv[1]->d; }
+  a.labels_int32 = (d.u[2] & 1u) != 0;
+  Buffer* o[4] = {nullptr, nullptr, nullptr, nullptr};
+  for (uint32_t i = 0; i < 4 && i < d.nuav; ++i) o[i] = d.uav[i];
+  if (o[0]) { FITS(o[0], (uint64_t)rows * K, "probs"); a.probs = o[0]->d; }
+  if (o[1]) { FITS(o[1], (uint64_t)rows * K, "dlogits"); a.dlogits = o[1]->d; }
+  if (o[2]) { FITS(o[2], 1, "loss"); a.loss = o[2]->d; }
+  if (o[3]) { FITS(o[3], (uint64_t)rows * K, "logprobs"); a.logprobs = o[3]->d; }
+  a.loss_div = d.u[3] ? (double)f_of(d.u[3]) : (double)rows;
+  a.grad_div = d.u[4] ? f_of(d.u[4]) : (float)rows;
+  if ((a.dlogits || a.loss) && !a.labels) { set_error(DCT_ERR_ARG, "dct_softmax_ce: labels required"); return false; }
+  return run_softmax_ce(d, a);
+}
+
+static Shader g_shaders[] = {
+    {"add_bias", h_add_bias, false, false, kShaderMagic},
+    {"bias_relu", h_bias_relu, false, false, kShaderMagic},
+    {"relu", h_relu, false, false, kShaderMagic},
+    {"relu_grad", h_relu_grad, false, false, kShaderMagic},
+    {"relu6", h_relu6, false, false, kShaderMagic},
+    {"relu6_grad", h_relu6_grad, false, false, kShaderMagic},
+    {"leaky_relu", h_leaky_relu, false, false, kShaderMagic},
+    {"leaky_relu_grad", h_leaky_relu_grad, false, false, kShaderMagic},
+    {"sigmoid", h_sigmoid, false, false, kShaderMagic},
+    {"sigmoid_grad", h_sigmoid_grad, false, false, kShaderMagic},
+    {"add", h_add, false, false, kShaderMagic},
+    {"scale_add", h_scale_add, false, false, kShaderMagic},
+    {"grad_accum", h_grad_accum, false, false, kShaderMagic},
+    {"bias_grad", h_bias_grad, false, false, kShaderMagic},
+    {"global_avg_pool", h_gap, false, false, kShaderMagic},
+    {"global_avg_pool_backward", h_gap_backward, false, false, kShaderMagic},
+    {"softmax", h_softmax, false, false, kShaderMagic},
+    {"loss", h_loss, false, false, kShaderMagic},
+    {"softmax_ce_grad", h_softmax_ce_grad, false, false, kShaderMagic},
+    {"argmax_correct", h_argmax_correct, false, false, kShaderMagic},
+    {"accumulate_scalar", h_accumulate_scalar, false, false, kShaderMagic},
+    {"rms", h_rms, false, false, kShaderMagic},
+    {"grad_sq_reduce", h_grad_sq_reduce, false, false, kShaderMagic},
+    {"grad_norm_final", h_grad_norm_final, false, false, kShaderMagic},
+    {"sgd", h_sgd, false, false, kShaderMagic},
+    {"sgd_clipped", h_sgd_clipped, false, false, kShaderMagic},
+    {"adam", h_adam, false, false, kShaderMagic},
+    {"batchnorm_mean_var", h_bn_mean_var, false, false, kShaderMagic},
+    {"batchnorm_forward", h_bn_forward, false, false, kShaderMagic},
+    {"batchnorm_backward_reduce", h_bn_backward_reduce, false, false, kShaderMagic},
+    {"batchnorm_backward_dx", h_bn_backward_dx, false, false, kShaderMagic},
+    {"dice_loss", h_dice_loss, false, false, kShaderMagic},
+    {"dice_loss_sums", h_dice_loss_sums, false, false, kShaderMagic},
+    {"dice_loss_grad", h_dice_loss_grad, false, false, kShaderMagic},
+    {"dct_unary", h_dct_unary, true, false, kShaderMagic},
+    {"dct_binary", h_dct_binary, true, false, kShaderMagic},
+    {"dct_reduce", h_dct_reduce, true, false, kShaderMagic},
+    {"dct_reduce_all", h_dct_reduce_all, true, false, kShaderMagic},
+    {"dct_softmax_ce", h_dct_softmax_ce, true, false, kShaderMagic},
+};
+constexpr int kNumShaders = sizeof(g_shaders) / sizeof(g_shaders[0]);
+
+static Shader* find_shader(const char* name) {
+  if (!name) return nullptr;
+  for (int i = 0; i < kNumShaders; ++i)
+    if (strcmp(g_shaders[i].name, name) == 0) return &g_shaders[i];
+  return nullptr;
+}
+
+static bool is_shader_ptr(const void* p) {
+  const Shader* s = static_cast<const Shader*>(p);
+  return s >= g_shaders && s < g_shaders + kNumShaders && s->magic == kShaderMagic;
+}
+
+static bool dispatch(Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav, const uint32_t* groups,
+                     const void* cb, uint32_t cbsize) {
+  if (!ensure_init()) return false;
+  Disp d;
+  memset(&d, 0, sizeof(d));
+  d.name = s->name;
+  if (nsrv > 16 || nuav > 16) { set_error(DCT_ERR_ARG, "%s: too many views", s->name); return false; }
+  d.nsrv = nsrv;
+  d.nuav = nuav;
+  for (uint32_t i = 0; i < nsrv; ++i) {
+    d.srv[i] = srvs ? buf_of(srvs[i]) : nullptr;
+    if (srvs && srvs[i] && !d.srv[i]) { set_error(DCT_ERR_HANDLE, "%s: SRV t%u %p is not a live buffer", s->name, i, srvs[i]); return false; }
+  }
+  for (uint32_t i = 0; i < nuav; ++i) {
+    d.uav[i] = uavs ? buf_of(uavs[i]) : nullptr;
+    if (uavs && uavs[i] && !d.uav[i]) { set_error(DCT_ERR_HANDLE, "%s: UAV u%u %p is not a live buffer", s->name, i, uavs[i]); return false; }
+  }
+  d.gx = groups ? groups[0] : 1;
+  d.gy = groups ? groups[1] : 1;
+  d.gz = groups ? groups[2] : 1;
+  d.cbsize = cbsize;
+  if (cb && cbsize) memcpy(d.u, cb, std::min<uint32_t>(cbsize, sizeof(d.u)));
+  return s->fn(d);
+}
+
+// ---------------------------------------------------------------------------
+// BatchNorm statistics (shared by the reference name and dct_batchnorm_*)
+// ---------------------------------------------------------------------------
+typedef bool (*ChanAllreduce)(double* chan, uint32_t count);
+static ChanAllreduce g_chan_allreduce = nullptr;      // set when a sharded call is in progress
+
+static bool bn_stats(const Disp& d, const float* x, uint32_t N, uint32_t C, uint32_t S, float* mean, float* var,
+                     float* rm, float* rv, bool training, float momentum, uint32_t c_eff) {
+  if (!ensure_ws(bn_ws_bytes(N, C))) return false;
+  double* ps = (double*)g.ws;
+  double* chan = ps + (size_t)N * C * 2;
+  cudaError_t e = launch_bn_plane_sums(x, nullptr, N, C, S, ps, g.stream);
+  if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, chan, g.stream);
+  if (e != cudaSuccess) LAUNCH(e);
+  double cnt = (double)N * S;
+  LAUNCH(launch_bn_stats_final(chan, c_eff, cnt, mean, var, rm, rv, training, momentum, g.stream));
+}
+
+// ---------------------------------------------------------------------------
+// broadcast binary from output shape + operand masks
+// ---------------------------------------------------------------------------
+static bool binary_from_masks(const Disp& d, int op, uint32_t ndim, uint32_t am, uint32_t bm, const uint32_t* shp,
+                              const Buffer* A, const Buffer* B, Buffer* O) {
+  int64_t shape[8], as[8], bs[8];
+  uint64_t n = 1, na = 1, nb = 1;
+  for (uint32_t i = 0; i < ndim; ++i) {
+    shape[i] = shp[i];
+    n *= shp[i];
+    if (!((am >> i) & 1u)) na *= shp[i];
+    if (!((bm >> i) & 1u)) nb *= shp[i];
+  }
+  int64_t sa = 1, sb = 1;
+  for (int i = (int)ndim - 1; i >= 0; --i) {
+    const bool ab = (am >> i) & 1u, bb = (bm >> i) & 1u;
+    as[i] = ab ? 0 : sa;
+    bs[i] = bb ? 0 : sb;
+    if (!ab) sa *= shape[i];
+    if (!bb) sb *= shape[i];
+  }
+  if (n == 0) return true;
+  FITS(A, na, "a"); FITS(B, nb, "b"); FITS(O, n, "out");
+  LAUNCH(launch_binary_bcast(op, A->d, B->d, O->d, (int)ndim, shape, as, bs, g.stream));
+}
+
+}  // namespace dct
+
+using namespace dct;
+
+// ===========================================================================
+// exported C-ABI
+// ===========================================================================
+extern "C" {
+
+DCT_API bool InitEngine() {
+  LOCK;
+  return init_engine();
+}
+
+DCT_API void GetGPUInfo(DctGPUInfo* out) {
+  LOCK;
+  if (!out) return;
+  memset(out, 0, sizeof(*out));
+  if (!ensure_init()) return;
+  out->vendorId = 0x10DE;
+  out->deviceId = 0;
+  out->dedicatedVRAM = g.info.total_mem;
+  out->sharedMemory = 0;
+  out->isIntegrated = 0;
+  snprintf(out->description, sizeof(out->description), "%s", g.name);
+}
+
+DCT_API bool CompileShader(const char* name, const wchar_t* path) {
+  LOCK;
+  (void)path;
+  Shader* s = find_shader(name);
+  if (!s) return false;       // no CUDA kernel behind this name (outside the hot path)
+  s->compiled = true;
+  return true;
+}
+
+DCT_API bool CompileShaderEx(const char* name, const wchar_t* path, const char* entry) {
+  LOCK;
+  (void)path; (void)entry;
+  set_error(DCT_ERR_UNSUPPORTED, "CompileShaderEx(%s): HLSL source cannot run on CUDA", name ? name : "");
+  return false;
+}
+
+DCT_API void* CreateBuffer(float* data, uint32_t count) {
+  LOCK;
+  return create_buffer(data, count);
+}
+
+DCT_API void AddRefBuffer(void* h) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  if (b) b->ref++;
+  else if (h) set_error(DCT_ERR_HANDLE, "AddRefBuffer: unknown handle %p", h);
+}
+
+DCT_API void UpdateBuffer(void* h, float* data) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  if (!b || !data) {
+    if (h && !b) set_error(DCT_ERR_HANDLE, "UpdateBuffer: unknown handle %p", h);
+    return;
+  }
+  cudaPointerAttributes at{};
+  const bool pinned = cudaPointerGetAttributes(&at, data) == cudaSuccess && at.type == cudaMemoryTypeHost;
+  cudaGetLastError();
+  cuda_ok(cudaMemcpyAsync(b->d, data, b->count * sizeof(float), cudaMemcpyHostToDevice, g.stream), "UpdateBuffer");
+  if (pinned) cudaStreamSynchronize(g.stream);          // the caller may reuse its memory on return
+}
+
+DCT_API void ReleaseBuffer(void* h) {
+  LOCK;
+  if (h) release_handle(h);
+}
+
+DCT_API void ReleaseBufferBatch(void** hs, uint32_t count) {
+  LOCK;
+  if (!hs) return;
+  for (uint32_t i = 0; i < count; ++i)
+    if (hs[i]) release_handle(hs[i]);
+}
+
+DCT_API void ReadBuffer(void* h, float* dst) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  if (!b || !dst) {
+    if (h && !b) set_error(DCT_ERR_HANDLE, "ReadBuffer: unknown handle %p", h);
+    return;
+  }
+  cuda_ok(cudaMemcpyAsync(dst, b->d, b->count * sizeof(float), cudaMemcpyDeviceToHost, g.stream), "ReadBuffer");
+  cuda_ok(cudaStreamSynchronize(g.stream), "ReadBuffer(sync)");
+}
+
+DCT_API void ClearBuffer(void* h) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  if (!b) return;
+  cuda_ok(cudaMemsetAsync(b->d, 0, b->count * sizeof(float), g.stream), "ClearBuffer");
+}
+
+DCT_API void FlushGPU() {
+  LOCK;
+  if (g.init) cudaStreamQuery(g.stream);                 // submission only, never waits
+}
+
+DCT_API void SyncGPU() {
+  LOCK;
+  if (g.init) cuda_ok(cudaStreamSynchronize(g.stream), "SyncGPU");
+}
+
+DCT_API void RunShader(const char* name, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav, uint32_t* threads,
+                       void* cb, uint32_t cbsize) {
+  LOCK;
+  Shader* s = find_shader(name);
+  if (!s || !(s->compiled || s->always)) {
+    set_error(DCT_ERR_UNKNOWN_SHADER, "RunShader: '%s' is not a compiled kernel", name ? name : "");
+    return;                                              // engine.cpp:397-399: silent return
+  }
+  dispatch(s, srvs, nsrv, uavs, nuav, threads, cb, cbsize);
+}
+
+DCT_API void RunShaderRaw(const char* name, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav,
+                          uint32_t* threads, void* cb, uint32_t cbsize) {
+  RunShader(name, srvs, nsrv, uavs, nuav, threads, cb, cbsize);
+}
+
+DCT_API void* RunShaderAlloc(const char* name, void** srvs, uint32_t nsrv, uint32_t out_count, uint32_t* threads,
+                             void* cb, uint32_t cbsize) {
+  LOCK;
+  void* out = create_buffer(nullptr, out_count);
+  if (!out) return nullptr;
+  void* uavs[1] = {out};
+  RunShader(name, srvs, nsrv, uavs, 1, threads, cb, cbsize);
+  return out;
+}
+
+DCT_API void* RunShaderAlloc2(const char* name, void** srvs, uint32_t nsrv, uint32_t out_count, void* extra,
+                              uint32_t* threads, void* cb, uint32_t cbsize) {
+  LOCK;
+  void* out = create_buffer(nullptr, out_count);
+  if (!out) return nullptr;
+  void* uavs[2] = {out, extra};
+  RunShader(name, srvs, nsrv, uavs, 2, threads, cb, cbsize);
+  return out;
+}
+
+// -- optimizers ---------------------------------------------------------------
+static bool build_table(void** params, void** grads, uint32_t* sizes, uint32_t n, std::vector<MtTensor>& t,
+                        bool need_params) {
+  t.clear();
+  for (uint32_t i = 0; i < n; ++i) {
+    Buffer* w = params ? buf_of(params[i]) : nullptr;
+    Buffer* gr = grads ? buf_of(grads[i]) : nullptr;
+    if (!gr || (need_params && !w)) continue;            // engine.cpp:460 skips null pairs
+    uint64_t cnt = sizes ? sizes[i] : gr->count;
+    uint64_t cap = gr->count;
+    if (w) cap = std::min(cap, w->count);
+    if (cnt > cap) {
+      set_error(DCT_ERR_SIZE, "optimizer: sizes[%u]=%llu exceeds the buffers (%llu)", i, (unsigned long long)cnt,
+                (unsigned long long)cap);
+      cnt = cap;
+    }
+    t.push_back(MtTensor{w ? w->d : nullptr, gr->d, nullptr, nullptr, cnt});
+  }
+  return true;
+}
+
+DCT_API void SGDBatch(void** params, void** grads, uint32_t* sizes, uint32_t n, float lr, float clip) {
+  LOCK;
+  if (!ensure_init() || n == 0) return;
+  std::vector<MtTensor> t;
+  build_table(params, grads, sizes, n, t, true);
+  cuda_ok(launch_mt_sgd(t.data(), (int)t.size(), lr, clip, nullptr, g.stream), "SGDBatch");
+}
+
+DCT_API float SGDBatchClipped(void** params, void** grads, uint32_t* sizes, uint32_t n, float lr, float max_norm) {
+  LOCK;
+  if (!ensure_init() || n == 0) return 0.0f;
+  std::vector<MtTensor> t;
+  build_table(nullptr, grads, sizes, n, t, false);       // phase 1: every grad
+  const uint64_t parts = mt_sumsq_blocks(t.data(), (int)t.size());
+  if (!ensure_ws((parts + 8) * sizeof(double) + 64)) return 0.0f;
+  double* part = (double*)g.ws;
+  float* ns = (float*)((char*)g.ws + ((parts * sizeof(double) + 255) & ~size_t(255)));
+  if (!cuda_ok(launch_mt_sumsq(t.data(), (int)t.size(), part, (int)parts, g.stream), "SGDBatchClipped(sumsq)")) return 0.0f;
+  if (!cuda_ok(launch_norm_scale_from_parts(part, (int)parts, max_norm, ns, g.stream), "SGDBatchClipped(norm)")) return 0.0f;
+  std::vector<MtTensor> t3;
+  build_table(params, grads, sizes, n, t3, true);       // phase 3: param and grad present
+  if (!cuda_ok(launch_mt_sgd(t3.data(), (int)t3.size(), lr, 0.0f, ns, g.stream), "SGDBatchClipped(sgd)")) return 0.0f;
+  cuda_ok(cudaMemcpyAsync(g.host_small, ns, 2 * sizeof(float), cudaMemcpyDeviceToHost, g.stream), "SGDBatchClipped(D2H)");
+  cuda_ok(cudaStreamSynchronize(g.stream), "SGDBatchClipped(sync)");
+  return g.host_small[0];
+}
+
+// -- out-of-scope fused dense / layout ops: exported so the reference binds ----------
+DCT_API void* MatMulAlloc(void*, void*, uint32_t, uint32_t, uint32_t, uint32_t) {
+  LOCK;
+  set_error(DCT_ERR_UNSUPPORTED, "MatMulAlloc: dense matmul is outside libdct_cuda's scope");
+  return nullptr;
+}
+DCT_API void* ConvForwardFused(void*, void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
+                               uint32_t, uint32_t, uint32_t, uint32_t, void** pIm2col) {
+  LOCK;
+  if (pIm2col) *pIm2col = nullptr;
+  set_error(DCT_ERR_UNSUPPORTED, "ConvForwardFused: convolution is outside libdct_cuda's scope");
+  return nullptr;
+}
+DCT_API void ConvBackwardFused(void*, void*, void*, void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
+                               uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
+                               void** pDF, void** pDB, void** pDI) {
+  LOCK;
+  if (pDF) *pDF = nullptr;
+  if (pDB) *pDB = nullptr;
+  if (pDI) *pDI = nullptr;
+  set_error(DCT_ERR_UNSUPPORTED, "ConvBackwardFused: convolution is outside libdct_cuda's scope");
+}
+DCT_API void* MaxPoolForwardFused(void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, void** pIdx) {
+  LOCK;
+  if (pIdx) *pIdx = nullptr;
+  set_error(DCT_ERR_UNSUPPORTED, "MaxPoolForwardFused: pooling is outside libdct_cuda's scope");
+  return nullptr;
+}
+DCT_API void* MaxPoolBackwardFused(void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t) {
+  LOCK;
+  set_error(DCT_ERR_UNSUPPORTED, "MaxPoolBackwardFused: pooling is outside libdct_cuda's scope");
+  return nullptr;
+}
+
+// -- pool -------------------------------------------------------------------------
+DCT_API void WarmPool(uint32_t* sizes, uint32_t n, uint32_t copies) {   // engine.cpp:617-635
+  LOCK;
+  if (!ensure_init() || !sizes) return;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint64_t count = sizes[i];
+    if (count == 0) continue;
+    auto& lst = g.pool[count];
+    const size_t target = std::min<size_t>(copies, max_pool_for_size(count));
+    while (lst.size() < target) {
+      Buffer* b = create_buffer(nullptr, count);
+      if (!b) break;
+      release_internal(b);
+      if (g.misses > 0) g.misses--;
+    }
+  }
+}
+
+DCT_API void GetPoolStats(uint64_t* hits, uint64_t* misses) {
+  LOCK;
+  if (hits) *hits = g.hits;
+  if (misses) *misses = g.misses;
+}
+
+DCT_API void ResetPoolStats() {
+  LOCK;
+  g.hits = 0;
+  g.misses = 0;
+}
+
+DCT_API uint64_t GetPoolMemory() {
+  LOCK;
+  return g.pool_bytes;
+}
+
+DCT_API void DrainPool() {
+  LOCK;
+  for (auto& kv : g.pool)
+    for (Buffer* b : kv.second) destroy(b);
+  g.pool.clear();
+  g.pool_bytes = 0;
+  if (g.init) {
+    cudaStreamSynchronize(g.stream);
+    cudaMemPool_t mp;
+    if (cudaDeviceGetDefaultMemPool(&mp, g.info.device) == cudaSuccess) cudaMemPoolTrimTo(mp, 0);
+  }
+}
+
+// -- graph replay ------------------------------------------------------------------
+DCT_API void* ResolveShader(const char* name) {
+  LOCK;
+  Shader* s = find_shader(name);
+  return (s && (s->compiled || s->always)) ? s : nullptr;
+}
+
+DCT_API void RunSequence(DctSeqCmd* cmds, uint32_t count) {
+  LOCK;
+  if (!cmds) return;
+  for (uint32_t i = 0; i < count; ++i) {
+    DctSeqCmd& c = cmds[i];
+    if (!c.shader) continue;
+    if (!is_shader_ptr(c.shader)) {
+      set_error(DCT_ERR_ARG, "RunSequence: command %u has a foreign shader pointer", i);
+      continue;
+    }
+    Shader* s = static_cast<Shader*>(c.shader);
+    dispatch(s, c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs, std::min<uint32_t>(c.uavCount, 4), c.threads,
+             c.cbSize ? c.cbData : nullptr, std::min<uint32_t>(c.cbSize, 64));
+  }
+}
+
+DCT_API void RunSequenceWithSGD(DctSeqCmd* cmds, uint32_t count, void** params, void** grads, uint32_t* sizes,
+                                uint32_t n, float lr, float clip) {
+  LOCK;
+  RunSequence(cmds, count);
+  SGDBatch(params, grads, sizes, n, lr, clip);
+}
+
+// ===========================================================================
+// extension entry points
+// ===========================================================================
+DCT_API const char* dct_last_error() {
+  LOCK;
+  return g.err.c_str();
+}
+
+DCT_API int dct_error_code() {
+  LOCK;
+  return g.err_code;
+}
+
+DCT_API void dct_clear_error() {
+  LOCK;
+  g.err_code = 0;
+  g.err.clear();
+}
+
+DCT_API int dct_version() { return DCT_ABI_VERSION; }
+
+DCT_API int dct_device() {
+  LOCK;
+  return ensure_init() ? g.info.device : -1;
+}
+
+DCT_API int dct_sm_count() {
+  LOCK;
+  return ensure_init() ? g.info.sm_count : 0;
+}
+
+DCT_API void* dct_stream() {
+  LOCK;
+  return ensure_init() ? (void*)g.stream : nullptr;
+}
+
+DCT_API int dct_synchronize() {
+  LOCK;
+  if (!ensure_init()) return DCT_ERR_NO_DEVICE;
+  return cuda_ok(cudaStreamSynchronize(g.stream), "dct_synchronize") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_timer_start() {
+  LOCK;
+  if (!ensure_init()) return DCT_ERR_NO_DEVICE;
+  return cuda_ok(cudaEventRecord(g.ev0, g.stream), "dct_timer_start") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API float dct_timer_stop_ms() {
+  LOCK;
+  if (!ensure_init()) return -1.0f;
+  float ms = -1.0f;
+  if (!cuda_ok(cudaEventRecord(g.ev1, g.stream), "dct_timer_stop")) return -1.0f;
+  if (!cuda_ok(cudaEventSynchronize(g.ev1), "dct_timer_stop(sync)")) return -1.0f;
+  if (!cuda_ok(cudaEventElapsedTime(&ms, g.ev0, g.ev1), "dct_timer_stop(elapsed)")) return -1.0f;
+  return ms;
+}
+
+DCT_API void* dct_create_buffer(uint64_t count) {
+  LOCK;
+  return create_buffer(nullptr, count);
+}
+
+DCT_API void* dct_buffer_device_ptr(void* h) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  return b ? (void*)b->d : nullptr;
+}
+
+DCT_API uint64_t dct_buffer_count(void* h) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  return b ? b->count : 0;
+}
+
+DCT_API int dct_buffer_refcount(void* h) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  return b ? b->ref : 0;
+}
+
+DCT_API void* dct_wrap_device_ptr(void* dptr, uint64_t count) {
+  LOCK;
+  if (!ensure_init() || !dptr || count == 0) return nullptr;
+  Buffer* b = new Buffer{kBufMagic, 1, count, static_cast<float*>(dptr), false};
+  g.live.insert(b);
+  return b;
+}
+
+DCT_API int dct_copy_h2d(void* h, const void* src, uint64_t offset_floats, uint64_t count) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  if (!b || !src) return DCT_ERR_HANDLE;
+  if (offset_floats + count > b->count) return DCT_ERR_SIZE;
+  return cuda_ok(cudaMemcpyAsync(b->d + offset_floats, src, count * 4, cudaMemcpyHostToDevice, g.stream), "dct_copy_h2d") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_copy_d2h(void* h, void* dst, uint64_t offset_floats, uint64_t count) {
+  LOCK;
+  Buffer* b = buf_of(h);
+  if (!b || !dst) return DCT_ERR_HANDLE;
+  if (offset_floats + count > b->count) return DCT_ERR_SIZE;
+  if (!cuda_ok(cudaMemcpyAsync(dst, b->d + offset_floats, count * 4, cudaMemcpyDeviceToHost, g.stream), "dct_copy_d2h")) return DCT_ERR_CUDA;
+  return cuda_ok(cudaStreamSynchronize(g.stream), "dct_copy_d2h(sync)") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API void* dct_host_alloc(uint64_t bytes) {
+  LOCK;
+  if (!ensure_init()) return nullptr;
+  void* p = nullptr;
+  return cuda_ok(cudaMallocHost(&p, bytes), "dct_host_alloc") ? p : nullptr;
+}
+
+DCT_API void dct_host_free(void* p) {
+  LOCK;
+  if (p) cudaFreeHost(p);
+}
+
+DCT_API int dct_fill_random(void* h, uint64_t seed, uint64_t offset, int dist, float a, float b) {
+  LOCK;
+  Buffer* x = buf_of(h);
+  if (!x) return DCT_ERR_HANDLE;
+  return cuda_ok(launch_fill_random(x->d, x->count, seed, offset, dist, a, b, g.stream), "dct_fill_random") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_scatter(void* h, const int64_t* host_idx, const float* host_vals, uint64_t k) {
+  LOCK;
+  Buffer* x = buf_of(h);
+  if (!x) return DCT_ERR_HANDLE;
+  if (k == 0) return 0;
+  for (uint64_t i = 0; i < k; ++i)
+    if (host_idx[i] < 0 || (uint64_t)host_idx[i] >= x->count) return DCT_ERR_SIZE;
+  void* dmem = nullptr;
+  if (!cuda_ok(cudaMallocAsync(&dmem, k * 12, g.stream), "dct_scatter(alloc)")) return DCT_ERR_CUDA;
+  int64_t* di = (int64_t*)dmem;
+  float* dv = (float*)((char*)dmem + k * 8);
+  cudaMemcpyAsync(di, host_idx, k * 8, cudaMemcpyHostToDevice, g.stream);
+  cudaMemcpyAsync(dv, host_vals, k * 4, cudaMemcpyHostToDevice, g.stream);
+  cudaError_t e = launch_scatter_values(x->d, di, dv, k, g.stream);
+  cudaFreeAsync(dmem, g.stream);
+  cudaStreamSynchronize(g.stream);
+  return cuda_ok(e, "dct_scatter") ? 0 : DCT_ERR_CUDA;
+}
+
+// --- NumPy-semantics ops ------------------------------------------------------------
+static int run_ext(const char* name, void** srvs, uint32_t ns, void** uavs, uint32_t nu, const uint32_t* cb,
+                   uint32_t cbwords) {
+  Shader* s = find_shader(name);
+  const uint32_t groups[3] = {0xffffffffu, 1, 1};
+  dct_clear_error();
+  const bool ok = dispatch(s, srvs, ns, uavs, nu, groups, cb, cbwords * 4);
+  if (ok) return 0;
+  return g.err_code ? g.err_code : DCT_ERR_ARG;
+}
+
+DCT_API int dct_unary(int op, void* x, void* y, uint64_t n, float alpha) {
+  LOCK;
+  if (n > 0xffffffffull) {
+    Buffer* bx = buf_of(x); Buffer* by = buf_of(y);
+    if (!bx || !by) return DCT_ERR_HANDLE;
+    if (bx->count < n || by->count < n) return DCT_ERR_SIZE;
+    return cuda_ok(launch_unary(op, bx->d, by->d, n, alpha, g.stream), "dct_unary") ? 0 : DCT_ERR_CUDA;
+  }
+  uint32_t alpha_bits;
+  memcpy(&alpha_bits, &alpha, 4);
+  const uint32_t cb[3] = {(uint32_t)op, (uint32_t)n, alpha_bits};
+  void* s[1] = {x};
+  void* u[1] = {y};
+  return run_ext("dct_unary", s, 1, u, 1, cb, 3);
+}
+
+DCT_API int dct_binary(int op, void* a, const int64_t* a_shape, int a_ndim, void* b, const int64_t* b_shape,
+                       int b_ndim, void* out) {
+  LOCK;
+  if (a_ndim < 0 || b_ndim < 0 || a_ndim > 8 || b_ndim > 8) return DCT_ERR_ARG;
+  const int nd = std::max(a_ndim, b_ndim);
+  uint32_t cb[12] = {0};
+  cb[0] = (uint32_t)op;
+  cb[1] = (uint32_t)nd;
+  for (int i = 0; i < nd; ++i) {
+    const int ia = i - (nd - a_ndim), ib = i - (nd - b_ndim);
+    const int64_t ea = ia >= 0 ? a_shape[ia] : 1, eb = ib >= 0 ? b_shape[ib] : 1;
+    if (ea != eb && ea != 1 && eb != 1) {
+      set_error(DCT_ERR_ARG, "dct_binary: shapes do not broadcast at dim %d (%lld vs %lld)", i, (long long)ea,
+                (long long)eb);
+      return DCT_ERR_ARG;
+    }
+    const int64_t eo = ea == 1 ? eb : ea;
+    if (eo > 0xffffffffll) return DCT_ERR_ARG;
+    cb[4 + i] = (uint32_t)eo;
+    if (ea == 1 && eo != 1) cb[2] |= 1u << i;
+    if (eb == 1 && eo != 1) cb[3] |= 1u << i;
+  }
+  void* s[2] = {a, b};
+  void* u[1] = {out};
+  return run_ext("dct_binary", s, 2, u, 1, cb, 4 + nd);
+}
+
+DCT_API int dct_reduce(int op, void* x, uint64_t outer, uint64_t len, uint64_t inner, void* out, void* out_idx) {
+  LOCK;
+  if (outer > 0xffffffffull || len > 0xffffffffull || inner > 0xffffffffull) return DCT_ERR_ARG;
+  const uint32_t cb[4] = {(uint32_t)op, (uint32_t)outer, (uint32_t)len, (uint32_t)inner};
+  void* s[1] = {x};
+  void* u[2] = {out, out_idx};
+  return run_ext("dct_reduce", s, 1, u, out_idx ? 2 : 1, cb, 4);
+}
+
+DCT_API int dct_reduce_all(int op, void* x, uint64_t n, void* out, double* host_out64) {
+  LOCK;
+  Buffer* bx = buf_of(x);
+  Buffer* bo = buf_of(out);
+  if (!bx || !bo) return DCT_ERR_HANDLE;
+  if (bx->count < n) return DCT_ERR_SIZE;
+  if (!ensure_ws(full_reduce_ws_bytes() + 256)) return DCT_ERR_CUDA;
+  double* d64 = (double*)((char*)g.ws + full_reduce_ws_bytes());
+  if (!cuda_ok(launch_full_reduce(op, bx->d, n, bo->d, d64, g.ws, g.stream), "dct_reduce_all")) return DCT_ERR_CUDA;
+  if (host_out64) {
+    if (!cuda_ok(cudaMemcpyAsync(g.host_small, d64, 8, cudaMemcpyDeviceToHost, g.stream), "dct_reduce_all(D2H)")) return DCT_ERR_CUDA;
+    if (!cuda_ok(cudaStreamSynchronize(g.stream), "dct_reduce_all(sync)")) return DCT_ERR_CUDA;
+    memcpy(host_out64, g.host_small, 8);
+  }
+  return 0;
+}
+
+DCT_API int dct_softmax_ce(void* logits, void* labels, int labels_int32, uint32_t rows, uint32_t K, void* probs,
+                           void* dlogits, void* loss, void* logprobs, float loss_div, float grad_div) {
+  LOCK;
+  uint32_t ld, gd;
+  memcpy(&ld, &loss_div, 4);
+  memcpy(&gd, &grad_div, 4);
+  const uint32_t cb[5] = {rows, K, labels_int32 ? 1u : 0u, ld, gd};
+  void* s[2] = {logits, labels};
+  void* u[4] = {probs, dlogits, loss, logprobs};
+  return run_ext("dct_softmax_ce", s, labels ? 2 : 1, u, 4, cb, 5);
+}
+
+DCT_API int dct_adam(void* w, void* m, void* v, void* grad, uint64_t n, float step_size, float beta1, float beta2,
+                     float eps, float weight_decay, float clip) {
+  LOCK;
+  Buffer *bw = buf_of(w), *bm = buf_of(m), *bv = buf_of(v), *bg = buf_of(grad);
+  if (!bw || !bm || !bv || !bg) return DCT_ERR_HANDLE;
+  if (bw->count < n || bm->count < n || bv->count < n || bg->count < n) return DCT_ERR_SIZE;
+  AdamParams p{step_size, beta1, beta2, eps, weight_decay, clip};
+  return cuda_ok(launch_adam(bw->d, bm->d, bv->d, bg->d, n, p, g.stream), "dct_adam") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_adam_batch(void** w, void** m, void** v, void** grads, const uint32_t* sizes, uint32_t n,
+                           float step_size, float beta1, float beta2, float eps, float weight_decay, float clip) {
+  LOCK;
+  if (!ensure_init()) return DCT_ERR_NO_DEVICE;
+  std::vector<MtTensor> t;
+  for (uint32_t i = 0; i < n; ++i) {
+    Buffer *bw = buf_of(w[i]), *bm = buf_of(m[i]), *bv = buf_of(v[i]), *bg = buf_of(grads[i]);
+    if (!bw || !bg) continue;
+    if (!bm || !bv) return DCT_ERR_HANDLE;
+    uint64_t cnt = sizes ? sizes[i] : bw->count;
+    if (cnt > std::min({bw->count, bm->count, bv->count, bg->count})) return DCT_ERR_SIZE;
+    t.push_back(MtTensor{bw->d, bg->d, bm->d, bv->d, cnt});
+  }
+  AdamParams p{step_size, beta1, beta2, eps, weight_decay, clip};
+  return cuda_ok(launch_mt_adam(t.data(), (int)t.size(), p, g.stream), "dct_adam_batch") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_batchnorm_forward_train(void* x, void* gamma, void* beta, void* running_mean, void* running_var,
+                                        void* batch_mean, void* batch_var, void* y, uint32_t N, uint32_t C,
+                                        uint32_t S, float eps, float momentum) {
+  LOCK;
+  Buffer *bx = buf_of(x), *bg = buf_of(gamma), *bb = buf_of(beta), *rm = buf_of(running_mean),
+         *rv = buf_of(running_var), *bm = buf_of(batch_mean), *bvv = buf_of(batch_var), *by = buf_of(y);
+  if (!bx || !bg || !bb || !rm || !rv || !bm || !bvv || !by) return DCT_ERR_HANDLE;
+  const uint64_t n = (uint64_t)N * C * S;
+  if (bx->count < n || by->count < n || bg->count < C || bb->count < C || rm->count < C || rv->count < C ||
+      bm->count < C || bvv->count < C)
+    return DCT_ERR_SIZE;
+  Disp d;
+  memset(&d, 0, sizeof(d));
+  d.name = "dct_batchnorm_forward_train";
+  if (!bn_stats(d, bx->d, N, C, S, bm->d, bvv->d, rm->d, rv->d, true, momentum, C)) return g.err_code ? g.err_code : DCT_ERR_CUDA;
+  return cuda_ok(launch_bn_forward(bx->d, bm->d, bvv->d, bg->d, bb->d, by->d, N, C, S, eps, n, g.stream),
+                 "dct_batchnorm_forward_train") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_batchnorm_backward(void* x, void* dy, void* batch_mean, void* batch_var, void* gamma, void* dgamma,
+                                   void* dbeta, void* dx, uint32_t N, uint32_t C, uint32_t S, float eps) {
+  LOCK;
+  Buffer *bx = buf_of(x), *bd = buf_of(dy), *bm = buf_of(batch_mean), *bv = buf_of(batch_var), *bg = buf_of(gamma),
+         *dg = buf_of(dgamma), *db = buf_of(dbeta), *bo = buf_of(dx);
+  if (!bx || !bd || !bm || !bv || !bg || !dg || !db || !bo) return DCT_ERR_HANDLE;
+  const uint64_t n = (uint64_t)N * C * S;
+  if (bx->count < n || bd->count < n || bo->count < n) return DCT_ERR_SIZE;
+  if (!ensure_ws(bn_ws_bytes(N, C))) return DCT_ERR_CUDA;
+  double* ps = (double*)g.ws;
+  double* chan = ps + (size_t)N * C * 2;
+  cudaError_t e = launch_bn_plane_sums(bx->d, bd->d, N, C, S, ps, g.stream);
+  if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, chan, g.stream);
+  if (e == cudaSuccess) e = launch_bn_bwd_final(chan, C, bm->d, bv->d, eps, dg->d, db->d, g.stream);
+  if (e == cudaSuccess)
+    e = launch_bn_backward_dx(bx->d, bd->d, bm->d, bv->d, bg->d, dg->d, db->d, bo->d, N, C, S, eps, n, g.stream);
+  return cuda_ok(e, "dct_batchnorm_backward") ? 0 : DCT_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,236 @@
+/*
+ * dct_cuda.h -- C-ABI of libdct_cuda.so, the B200 (sm_100a) drop-in for the
+ * native engine of raviadi12/directcompute_torch.
+ *
+ * The reference Python (`nn_engine.py`) loads its engine with
+ * `ctypes.CDLL(_find_resource("engine.dll"))` (nn_engine.py:42) and binds the
+ * symbols below with the argtypes of nn_engine.py:43-119 and :133-134.  Each
+ * declaration names the reference definition it replaces (engine.cpp:line).
+ * Argument meaning, ownership and the quiet-failure error behaviour are the
+ * reference's; what each call does on the device is described beside it.
+ *
+ * Symbols prefixed `dct_` are extensions with no counterpart in engine.cpp:
+ * error reporting, device timing, raw-pointer interop, the NumPy-semantics ops
+ * (broadcast binary ops, exp/log/tanh, axis and full reductions, fused
+ * softmax+cross-entropy, fused Adam, fused BatchNorm) and multi-GPU sharding.
+ *
+ * Buffers are opaque handles to fp32 device arrays (labels and counters are
+ * stored as 32-bit words in the same buffers, as the reference does).  All
+ * work is enqueued in order on one CUDA stream per process; ReadBuffer,
+ * SGDBatchClipped, SyncGPU, dct_synchronize and dct_timer_stop_ms wait for it.
+ */
+#ifndef DCT_CUDA_H
+#define DCT_CUDA_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <wchar.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DCT_API __attribute__((visibility("default")))
+#define DCT_ABI_VERSION 1
+
+/* error codes returned by dct_* calls and by dct_error_code() */
+enum {
+  DCT_OK = 0,
+  DCT_ERR_NO_DEVICE = 1,      /* no CUDA device / InitEngine failed */
+  DCT_ERR_HANDLE = 2,         /* a handle is not a live buffer */
+  DCT_ERR_SIZE = 3,           /* a buffer is smaller than the dispatch touches */
+  DCT_ERR_ARG = 4,            /* bad shape / count / view list */
+  DCT_ERR_CUDA = 5,           /* a CUDA call or launch failed (message has the reason) */
+  DCT_ERR_UNKNOWN_SHADER = 6, /* RunShader of a name without a compiled kernel */
+  DCT_ERR_UNSUPPORTED = 7,    /* entry point outside this library's scope */
+  DCT_ERR_DIST = 8,           /* NCCL / sharding error or timeout */
+};
+
+/* engine.cpp:14-21 GPUInfo, read by nn_engine.py:124-140 */
+typedef struct DctGPUInfo {
+  uint32_t vendorId;       /* 0x10DE */
+  uint32_t deviceId;
+  uint64_t dedicatedVRAM;  /* cudaDeviceProp::totalGlobalMem */
+  uint64_t sharedMemory;
+  uint32_t isIntegrated;   /* 0: nn_engine.py selects its dGPU code paths */
+  char description[128];   /* device name */
+} DctGPUInfo;
+
+/* engine.cpp:940-950 SeqCmd (256 bytes), mirrored by nn_engine.py:2490-2502 */
+typedef struct DctSeqCmd {
+  void* shader;            /* pointer returned by ResolveShader */
+  void* srvs[8];
+  uint32_t srvCount;
+  void* uavs[4];
+  uint32_t uavCount;
+  uint32_t threads[3];
+  uint8_t cbData[64];
+  uint32_t cbSize;
+  uint32_t pad[1];
+} DctSeqCmd;
+
+/* ---- device ------------------------------------------------------------- */
+/* engine.cpp:61-129. Picks $DCT_DEVICE, else $LOCAL_RANK, else the current CUDA
+ * device; creates the stream. false when no device is visible. */
+DCT_API bool InitEngine(void);
+/* engine.cpp:131-133 */
+DCT_API void GetGPUInfo(DctGPUInfo* out);
+/* engine.cpp:135-151. Marks the built-in CUDA kernel `name` usable by RunShader;
+ * the HLSL file at `path` is not read. false for names with no kernel here. */
+DCT_API bool CompileShader(const char* name, const wchar_t* path);
+/* engine.cpp:153-169. Arbitrary HLSL cannot run on CUDA: always false. */
+DCT_API bool CompileShaderEx(const char* name, const wchar_t* path, const char* entryPoint);
+/* engine.cpp:325-328: submits queued work, never waits */
+DCT_API void FlushGPU(void);
+/* engine.cpp:332-347: waits for all queued work */
+DCT_API void SyncGPU(void);
+
+/* ---- buffers ------------------------------------------------------------- */
+/* engine.cpp:201-253. count fp32 elements (refcount 1), from the size-keyed
+ * pool when possible; `data` (nullable) is uploaded. null on count 0 / OOM. */
+DCT_API void* CreateBuffer(float* data, uint32_t count);
+/* engine.cpp:255-258 */
+DCT_API void AddRefBuffer(void* handle);
+/* engine.cpp:261-265: uploads `count` floats; `data` may be reused on return */
+DCT_API void UpdateBuffer(void* handle, float* data);
+/* engine.cpp:283-290: refcount--, at zero the buffer returns to the pool
+ * (per-size caps of engine.cpp:186-197) or is freed */
+DCT_API void ReleaseBuffer(void* handle);
+/* engine.cpp:676-685 */
+DCT_API void ReleaseBufferBatch(void** handles, uint32_t count);
+/* engine.cpp:292-321: blocking copy of all `count` floats to `dst` */
+DCT_API void ReadBuffer(void* handle, float* dst);
+/* engine.cpp:349-354: zero bits */
+DCT_API void ClearBuffer(void* handle);
+
+/* ---- kernels by name ------------------------------------------------------- */
+/* engine.cpp:396-401. `threads` are the reference's group counts; the CUDA
+ * kernels derive their own grid from the cbuffer fields and the groups'
+ * index space (groups x [numthreads]). Unknown names return silently and set
+ * DCT_ERR_UNKNOWN_SHADER. Names: add_bias bias_relu relu relu_grad relu6
+ * relu6_grad leaky_relu leaky_relu_grad sigmoid sigmoid_grad add scale_add
+ * grad_accum bias_grad global_avg_pool global_avg_pool_backward softmax loss
+ * softmax_ce_grad argmax_correct accumulate_scalar rms grad_sq_reduce
+ * grad_norm_final sgd sgd_clipped adam batchnorm_mean_var batchnorm_forward
+ * batchnorm_backward_reduce batchnorm_backward_dx dice_loss dice_loss_sums
+ * dice_loss_grad, plus the extension names dct_unary dct_binary dct_reduce
+ * dct_reduce_all dct_softmax_ce (cbuffer layouts in runtime.cu). */
+DCT_API void RunShader(const char* name, void** srvs, uint32_t srvCount, void** uavs, uint32_t uavCount,
+                       uint32_t* threads, void* cb, uint32_t cbSize);
+/* engine.cpp:404-406 (alias) */
+DCT_API void RunShaderRaw(const char* name, void** srvs, uint32_t srvCount, void** uavs, uint32_t uavCount,
+                          uint32_t* threads, void* cb, uint32_t cbSize);
+/* engine.cpp:409-416 */
+DCT_API void* RunShaderAlloc(const char* name, void** srvs, uint32_t srvCount, uint32_t outCount,
+                             uint32_t* threads, void* cb, uint32_t cbSize);
+/* engine.cpp:419-426 */
+DCT_API void* RunShaderAlloc2(const char* name, void** srvs, uint32_t srvCount, uint32_t outCount,
+                              void* extraUav, uint32_t* threads, void* cb, uint32_t cbSize);
+
+/* ---- optimizers ------------------------------------------------------------- */
+/* engine.cpp:436-485: w -= lr * clamp(g, +-clip) for every (param, grad) pair,
+ * one multi-tensor launch */
+DCT_API void SGDBatch(void** params, void** grads, uint32_t* sizes, uint32_t numParams, float lr, float clip);
+/* engine.cpp:494-614: global grad norm (float64), clip scale
+ * max/(norm+1e-6) when norm > max, w -= lr*g*scale; returns the norm (blocks) */
+DCT_API float SGDBatchClipped(void** params, void** grads, uint32_t* sizes, uint32_t numParams, float lr,
+                              float maxNorm);
+
+/* ---- outside the hot path: exported so nn_engine.py binds; null + DCT_ERR_UNSUPPORTED */
+DCT_API void* MatMulAlloc(void* a, void* b, uint32_t M, uint32_t K, uint32_t N, uint32_t flags); /* engine.cpp:741-747 */
+DCT_API void* ConvForwardFused(void* x, void* f, void* bias, uint32_t batch, uint32_t inC, uint32_t inH,
+                               uint32_t inW, uint32_t outC, uint32_t kH, uint32_t kW, uint32_t stride,
+                               uint32_t padding, uint32_t actType, void** pIm2col); /* engine.cpp:751-798 */
+DCT_API void ConvBackwardFused(void* go, void* fo, void* x, void* f, void* im2col, uint32_t batch, uint32_t inC,
+                               uint32_t inH, uint32_t inW, uint32_t outC, uint32_t kH, uint32_t kW,
+                               uint32_t stride, uint32_t padding, uint32_t actType, uint32_t xg, uint32_t fg,
+                               uint32_t bg, void** pDF, void** pDB, void** pDI); /* engine.cpp:802-876 */
+DCT_API void* MaxPoolForwardFused(void* x, uint32_t batch, uint32_t inC, uint32_t inH, uint32_t inW,
+                                  uint32_t pool, uint32_t stride, void** pIdx); /* engine.cpp:879-902 */
+DCT_API void* MaxPoolBackwardFused(void* go, void* idx, uint32_t batch, uint32_t inC, uint32_t outH,
+                                   uint32_t outW, uint32_t xSize); /* engine.cpp:905-930 */
+
+/* ---- pool -------------------------------------------------------------------- */
+DCT_API void WarmPool(uint32_t* sizes, uint32_t numSizes, uint32_t copies); /* engine.cpp:617-635 */
+DCT_API void GetPoolStats(uint64_t* hits, uint64_t* misses);                /* engine.cpp:638-641 */
+DCT_API void ResetPoolStats(void);                                          /* engine.cpp:643-646 */
+DCT_API uint64_t GetPoolMemory(void);                                       /* engine.cpp:649-651 */
+DCT_API void DrainPool(void);                                               /* engine.cpp:654-673 */
+
+/* ---- graph replay ---------------------------------------------------------------- */
+/* engine.cpp:934-937: a stable kernel-descriptor pointer for SeqCmd.shader */
+DCT_API void* ResolveShader(const char* name);
+/* engine.cpp:952-966 */
+DCT_API void RunSequence(DctSeqCmd* cmds, uint32_t count);
+/* engine.cpp:969-977 */
+DCT_API void RunSequenceWithSGD(DctSeqCmd* cmds, uint32_t cmdCount, void** params, void** grads,
+                                uint32_t* sizes, uint32_t numParams, float lr, float clip);
+
+/* ======================= extensions (no engine.cpp counterpart) ================= */
+DCT_API const char* dct_last_error(void);   /* message of the last failure ("" if none) */
+DCT_API int dct_error_code(void);           /* DCT_ERR_* of the last failure, 0 if none */
+DCT_API void dct_clear_error(void);
+DCT_API int dct_version(void);              /* DCT_ABI_VERSION */
+DCT_API int dct_device(void);               /* CUDA ordinal in use, -1 if none */
+DCT_API int dct_sm_count(void);
+DCT_API void* dct_stream(void);             /* the library's cudaStream_t */
+DCT_API int dct_synchronize(void);
+/* CUDA events on the library's stream: start, then stop returns elapsed ms (waits) */
+DCT_API int dct_timer_start(void);
+DCT_API float dct_timer_stop_ms(void);
+
+/* buffers beyond 2^32 elements, raw pointers, partial copies, pinned host memory */
+DCT_API void* dct_create_buffer(uint64_t count);
+DCT_API void* dct_buffer_device_ptr(void* handle);
+DCT_API uint64_t dct_buffer_count(void* handle);
+DCT_API int dct_buffer_refcount(void* handle);
+/* non-owning handle over caller device memory (released with ReleaseBuffer, never freed) */
+DCT_API void* dct_wrap_device_ptr(void* dptr, uint64_t count);
+DCT_API int dct_copy_h2d(void* handle, const void* src, uint64_t offset, uint64_t count);   /* async */
+DCT_API int dct_copy_d2h(void* handle, void* dst, uint64_t offset, uint64_t count);         /* waits */
+DCT_API void* dct_host_alloc(uint64_t bytes);   /* pinned */
+DCT_API void dct_host_free(void* p);
+
+/* synthetic data: Philox4x32-10 fill of the whole buffer; dist 0 = uniform [a,b),
+ * 1 = normal(mean a, std b); element i uses counter (i/4, offset), key seed */
+DCT_API int dct_fill_random(void* handle, uint64_t seed, uint64_t offset, int dist, float a, float b);
+/* x[idx[i]] = vals[i] (host arrays), e.g. outlier injection */
+DCT_API int dct_scatter(void* handle, const int64_t* idx, const float* vals, uint64_t k);
+
+/* unary ops: 0 relu 1 relu6 2 leaky_relu(alpha) 3 sigmoid 4 exp 5 log(|x|+1) 6 tanh 7 neg 8 abs */
+DCT_API int dct_unary(int op, void* x, void* y, uint64_t n, float alpha);
+/* NumPy-broadcast binary op: 20 add 21 sub 22 mul 23 div 24 maximum 25 minimum.
+ * Shapes are right-aligned; out has the broadcast shape (<= 8 dims). */
+DCT_API int dct_binary(int op, void* a, const int64_t* a_shape, int a_ndim, void* b, const int64_t* b_shape,
+                       int b_ndim, void* out);
+/* reduce x viewed as [outer, len, inner] over len: 0 sum 1 mean 2 max 3 argmax 4 min
+ * 5 argmin 6 sum of squares; float64 accumulation; arg ops write int32 to out_idx
+ * (or to out when out_idx is null); max/min also write indices when out_idx is set */
+DCT_API int dct_reduce(int op, void* x, uint64_t outer, uint64_t len, uint64_t inner, void* out, void* out_idx);
+/* full reduction of n elements (sum, mean, max, min, sumsq) into out[0]; the
+ * float64 value is returned in *host_out64 when non-null (waits) */
+DCT_API int dct_reduce_all(int op, void* x, uint64_t n, void* out, double* host_out64);
+/* fused row softmax + cross-entropy forward and backward in one pass:
+ * probs, dlogits = (p - onehot)/grad_div, loss[0] = sum(ce)/loss_div, logprobs;
+ * any output may be null; labels are float (reference layout) or int32 */
+DCT_API int dct_softmax_ce(void* logits, void* labels, int labels_int32, uint32_t rows, uint32_t K, void* probs,
+                           void* dlogits, void* loss, void* logprobs, float loss_div, float grad_div);
+/* nn_adam.hlsl semantics; step_size carries lr and the bias correction */
+DCT_API int dct_adam(void* w, void* m, void* v, void* grad, uint64_t n, float step_size, float beta1, float beta2,
+                     float eps, float weight_decay, float clip);
+DCT_API int dct_adam_batch(void** w, void** m, void** v, void** grads, const uint32_t* sizes, uint32_t n,
+                           float step_size, float beta1, float beta2, float eps, float weight_decay, float clip);
+/* BatchNorm training forward (stats + running-stat update + normalize) and
+ * backward (dgamma, dbeta, dx) over NCHW with S = H*W */
+DCT_API int dct_batchnorm_forward_train(void* x, void* gamma, void* beta, void* running_mean, void* running_var,
+                                        void* batch_mean, void* batch_var, void* y, uint32_t N, uint32_t C,
+                                        uint32_t S, float eps, float momentum);
+DCT_API int dct_batchnorm_backward(void* x, void* dy, void* batch_mean, void* batch_var, void* gamma,
+                                   void* dgamma, void* dbeta, void* dx, uint32_t N, uint32_t C, uint32_t S,
+                                   float eps);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DCT_CUDA_H */
