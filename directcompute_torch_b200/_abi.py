@@ -33,7 +33,7 @@ class GPUInfo(C.Structure):
 
 
 class SeqCmd(C.Structure):
-    """engine.cpp:940-950; nn_engine.py:2490-2502 (256 bytes)."""
+    """engine.cpp:940-950; nn_engine.py:2490-2502 (200 bytes on x86-64)."""
     _fields_ = [("shader", C.c_void_p), ("srvs", C.c_void_p * 8), ("srvCount", C.c_uint),
                 ("uavs", C.c_void_p * 4), ("uavCount", C.c_uint), ("threads", C.c_uint * 3),
                 ("cbData", C.c_ubyte * 64), ("cbSize", C.c_uint), ("pad", C.c_uint * 1)]

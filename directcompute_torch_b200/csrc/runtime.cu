@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <stdarg.h>
+#include <stddef.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -57,6 +58,9 @@ struct Buffer {
   bool owned;              // false: wraps caller memory (dct_wrap_device_ptr)
 };
 constexpr uint32_t kBufMagic = 0xDC7B0F01u;
+static_assert(sizeof(DctSeqCmd) == 200 && offsetof(DctSeqCmd, cbData) == 128 && offsetof(DctSeqCmd, cbSize) == 192,
+              "DctSeqCmd must match the reference's SeqCmd field layout");
+static_assert(sizeof(DctGPUInfo) == 160 && offsetof(DctGPUInfo, description) == 28, "GPUInfo layout");
 
 struct Engine {
   bool init = false;

@@ -57,7 +57,7 @@ typedef struct DctGPUInfo {
   char description[128];   /* device name */
 } DctGPUInfo;
 
-/* engine.cpp:940-950 SeqCmd (256 bytes), mirrored by nn_engine.py:2490-2502 */
+/* engine.cpp:940-950 SeqCmd, mirrored by nn_engine.py:2490-2502 (200 bytes on x86-64) */
 typedef struct DctSeqCmd {
   void* shader;            /* pointer returned by ResolveShader */
   void* srvs[8];
@@ -74,16 +74,16 @@ typedef struct DctSeqCmd {
 /* engine.cpp:61-129. Picks $DCT_DEVICE, else $LOCAL_RANK, else the current CUDA
  * device; creates the stream. false when no device is visible. */
 DCT_API bool InitEngine(void);
-/* engine.cpp:131-133 */
+/* engine.cpp:132-134 */
 DCT_API void GetGPUInfo(DctGPUInfo* out);
-/* engine.cpp:135-151. Marks the built-in CUDA kernel `name` usable by RunShader;
+/* engine.cpp:136-152. Marks the built-in CUDA kernel `name` usable by RunShader;
  * the HLSL file at `path` is not read. false for names with no kernel here. */
 DCT_API bool CompileShader(const char* name, const wchar_t* path);
-/* engine.cpp:153-169. Arbitrary HLSL cannot run on CUDA: always false. */
+/* engine.cpp:154-170. Arbitrary HLSL cannot run on CUDA: always false. */
 DCT_API bool CompileShaderEx(const char* name, const wchar_t* path, const char* entryPoint);
-/* engine.cpp:325-328: submits queued work, never waits */
+/* engine.cpp:325-327: submits queued work, never waits */
 DCT_API void FlushGPU(void);
-/* engine.cpp:332-347: waits for all queued work */
+/* engine.cpp:331-347: waits for all queued work */
 DCT_API void SyncGPU(void);
 
 /* ---- buffers ------------------------------------------------------------- */
@@ -94,7 +94,7 @@ DCT_API void* CreateBuffer(float* data, uint32_t count);
 DCT_API void AddRefBuffer(void* handle);
 /* engine.cpp:261-265: uploads `count` floats; `data` may be reused on return */
 DCT_API void UpdateBuffer(void* handle, float* data);
-/* engine.cpp:283-290: refcount--, at zero the buffer returns to the pool
+/* engine.cpp:284-290: refcount--, at zero the buffer returns to the pool
  * (per-size caps of engine.cpp:186-197) or is freed */
 DCT_API void ReleaseBuffer(void* handle);
 /* engine.cpp:676-685 */
@@ -141,21 +141,21 @@ DCT_API float SGDBatchClipped(void** params, void** grads, uint32_t* sizes, uint
 DCT_API void* MatMulAlloc(void* a, void* b, uint32_t M, uint32_t K, uint32_t N, uint32_t flags); /* engine.cpp:741-747 */
 DCT_API void* ConvForwardFused(void* x, void* f, void* bias, uint32_t batch, uint32_t inC, uint32_t inH,
                                uint32_t inW, uint32_t outC, uint32_t kH, uint32_t kW, uint32_t stride,
-                               uint32_t padding, uint32_t actType, void** pIm2col); /* engine.cpp:751-798 */
+                               uint32_t padding, uint32_t actType, void** pIm2col); /* engine.cpp:751-799 */
 DCT_API void ConvBackwardFused(void* go, void* fo, void* x, void* f, void* im2col, uint32_t batch, uint32_t inC,
                                uint32_t inH, uint32_t inW, uint32_t outC, uint32_t kH, uint32_t kW,
                                uint32_t stride, uint32_t padding, uint32_t actType, uint32_t xg, uint32_t fg,
                                uint32_t bg, void** pDF, void** pDB, void** pDI); /* engine.cpp:802-876 */
 DCT_API void* MaxPoolForwardFused(void* x, uint32_t batch, uint32_t inC, uint32_t inH, uint32_t inW,
-                                  uint32_t pool, uint32_t stride, void** pIdx); /* engine.cpp:879-902 */
+                                  uint32_t pool, uint32_t stride, void** pIdx); /* engine.cpp:881-903 */
 DCT_API void* MaxPoolBackwardFused(void* go, void* idx, uint32_t batch, uint32_t inC, uint32_t outH,
-                                   uint32_t outW, uint32_t xSize); /* engine.cpp:905-930 */
+                                   uint32_t outW, uint32_t xSize); /* engine.cpp:906-931 */
 
 /* ---- pool -------------------------------------------------------------------- */
 DCT_API void WarmPool(uint32_t* sizes, uint32_t numSizes, uint32_t copies); /* engine.cpp:617-635 */
-DCT_API void GetPoolStats(uint64_t* hits, uint64_t* misses);                /* engine.cpp:638-641 */
-DCT_API void ResetPoolStats(void);                                          /* engine.cpp:643-646 */
-DCT_API uint64_t GetPoolMemory(void);                                       /* engine.cpp:649-651 */
+DCT_API void GetPoolStats(uint64_t* hits, uint64_t* misses);                /* engine.cpp:637-640 */
+DCT_API void ResetPoolStats(void);                                          /* engine.cpp:642-645 */
+DCT_API uint64_t GetPoolMemory(void);                                       /* engine.cpp:648-650 */
 DCT_API void DrainPool(void);                                               /* engine.cpp:654-673 */
 
 /* ---- graph replay ---------------------------------------------------------------- */

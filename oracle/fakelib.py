@@ -34,7 +34,7 @@ F32 = np.float32
 
 
 class SeqCmd(ctypes.Structure):
-    """The reference's 256-byte packed dispatch command (engine.cpp:940-950)."""
+    """The reference's packed dispatch command (engine.cpp:940-950; 200 bytes on x86-64)."""
     _fields_ = [
         ("shader", ctypes.c_void_p),
         ("srvs", ctypes.c_void_p * 8),
