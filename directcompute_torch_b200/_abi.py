@@ -105,6 +105,7 @@ SIGNATURES = {
     "dct_adam_batch": ([PVP, PVP, PVP, PVP, PU32, U32, F32, F32, F32, F32, F32, F32], C.c_int),
     "dct_batchnorm_forward_train": ([VP] * 8 + [U32, U32, U32, F32, F32], C.c_int),
     "dct_batchnorm_backward": ([VP] * 8 + [U32, U32, U32, F32], C.c_int),
+    "dct_batchnorm_forward_train_noalloc": ([VP] * 8 + [U32, U32, U32, F32, F32, VP], C.c_int),
 }
 
 #: the 32 symbols of the reference engine (31 bound by nn_engine.py + SyncGPU)

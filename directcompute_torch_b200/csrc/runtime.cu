@@ -83,7 +83,23 @@ static Engine g;
 static std::recursive_mutex g_mu;
 #define LOCK std::lock_guard<std::recursive_mutex> _lk(g_mu)
 
-const DevInfo& dev_info() { return g.info; }
+// Launch geometry of the engine's device; before InitEngine (callers of the
+// allocation-free entry point may never initialise the engine) it is read
+// from the current device's attributes, which allocates nothing.
+const DevInfo& dev_info() {
+  if (g.init) return g.info;
+  static thread_local DevInfo local;
+  int d = 0;
+  if (cudaGetDevice(&d) == cudaSuccess && local.device != d) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, d) == cudaSuccess && v > 0) local.sm_count = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxThreadsPerMultiProcessor, d) == cudaSuccess && v > 0)
+      local.max_threads_per_sm = v;
+    local.device = d;
+  }
+  cudaGetLastError();
+  return local;
+}
 
 static void set_error(int code, const char* fmt, ...) {
   char buf[512];
@@ -93,6 +109,13 @@ static void set_error(int code, const char* fmt, ...) {
   va_end(ap);
   g.err_code = code;
   g.err = buf;
+}
+
+// error recording for entry points that live outside this file
+void note_error(int code, const char* msg) {
+  LOCK;
+  g.err_code = code;
+  g.err = msg ? msg : "";
 }
 
 static bool cuda_ok(cudaError_t e, const char* where) {

@@ -230,6 +230,23 @@ DCT_API int dct_batchnorm_backward(void* x, void* dy, void* batch_mean, void* ba
                                    void* dgamma, void* dbeta, void* dx, uint32_t N, uint32_t C, uint32_t S,
                                    float eps);
 
+/* BatchNorm training forward that allocates nothing.  No counterpart in the
+ * reference: it is for callers that cannot let this library allocate device
+ * memory (a process whose HBM is already owned by its own allocator or arena,
+ * or one held to a fixed memory budget).  Same math and kernels as
+ * dct_batchnorm_forward_train, but every buffer is a caller-owned device
+ * pointer, work goes on `stream` (null = the legacy default stream), and the
+ * float64 partial sums live in a fixed file-scope device array of 2 MiB +
+ * 64 KiB that every GPU loading the library keeps until exit.  Limit:
+ * N*C <= 131072 and C <= 4096, otherwise DCT_ERR_SIZE with a message and
+ * nothing is launched.  The first call on a device looks up the array's device
+ * address; make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race and must be serialised. */
+DCT_API int dct_batchnorm_forward_train_noalloc(const float* x, const float* gamma, const float* beta,
+                                                float* running_mean, float* running_var, float* batch_mean,
+                                                float* batch_var, float* y, uint32_t N, uint32_t C, uint32_t S,
+                                                float eps, float momentum, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
