@@ -114,52 +114,65 @@ class Ranks:
 
 
 # ---------------------------------------------------------------------------
-# clocks sampled during the timed region
+# clocks sampled during the timed region (NVML, every 2 ms, read-only)
 # ---------------------------------------------------------------------------
 class Clocks:
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, power and clock-event reasons of our GPU while timing."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, device):
-        self.device = device
-        self.proc = None
+    def __init__(self, pci_bus_id: str, period_s: float = 0.002):
+        self.pci = pci_bus_id
+        self.period = period_s
+        self.rows = []
+        self.max_mhz = None
+        self._stop = None
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml as N
+            N.nvmlInit()
+            try:
+                self.h = N.nvmlDeviceGetHandleByPciBusId(self.pci.encode() if isinstance(self.pci, str) else self.pci)
+            except Exception:
+                self.h = N.nvmlDeviceGetHandleByIndex(0)
+            self.N = N
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception as e:                      # no NVML: record why
+            self.err = repr(e)
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            N, h = self.N, self.h
+            get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self._stop.is_set():
+                try:
+                    self.rows.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
+                                      N.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
+                except Exception:
+                    pass
+                self._stop.wait(self.period)
+        self._t = threading.Thread(target=loop, daemon=True)
+        self._t.start()
         return self
 
     def __exit__(self, *a):
-        self.out = ""
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._stop is not None:
+            self._stop.set()
+            self._t.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                rows.append((float(f[1]), float(f[2]), float(f[3]) if f[3] not in ("[N/A]", "") else 0.0, f[5:9]))
-            except ValueError:
-                continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
-        busy = [r[0] for r in rows if r[2] > 300] or [r[0] for r in rows]
-        return {"sm_mhz": float(np.median(busy)), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
+                    "source": "nvml", "note": getattr(self, "err", "timed region shorter than one sample")}
+        reasons = sorted({name for _, _, r in self.rows for bit, name in self.REASONS.items() if r & bit})
+        sm = [r[0] for r in self.rows]
+        return {"sm_mhz": float(np.median(sm)), "sm_min_mhz": float(min(sm)), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "power_w_max": round(max(r[1] for r in self.rows), 1),
+                "source": "nvml, 2 ms"}
 
 
 # ---------------------------------------------------------------------------
@@ -213,7 +226,7 @@ class Lib:
 class C2:
     """The headline workload: BASELINE config C2 (seed 1), resident in HBM."""
 
-    def __init__(self, L: Lib, rank: int):
+    def __init__(self, L: Lib, rank: int, only: str | None = None):
         self.L = L
         n = A_ROWS * A_COLS
         self.A = L.new(n)
@@ -225,22 +238,25 @@ class C2:
         L.fill(self.B, seed, 1, 0, 0.5, 2.0)
         L.fill(self.Cc, seed, 2, 1, 0.0, 1.0)
         L.fill(self.D, seed, 3, 1, 0.0, 1.0)
-        self.out_b = {op: L.new(n) for op in C2_BINARY}
-        self.out_o = {op: L.new(OC_P * OC_R * OC_Q) for op in C2_OUTER}
-        self.out_u = {op: L.new(n) for op in C2_UNARY}
+        want = (lambda k: only is None or only == k)
+        self.out_b = {op: L.new(n) for op in C2_BINARY if want(f"c2_rowbcast_{op}")}
+        self.out_o = {op: L.new(OC_P * OC_R * OC_Q) for op in C2_OUTER if want(f"c2_outer_{op}")}
+        self.out_u = {op: L.new(n) for op in C2_UNARY if want(f"c2_unary_{op}")}
         self.sA = L.shape([A_ROWS, A_COLS])
         self.sB = L.shape([1, A_COLS])
         self.sC = L.shape([OC_P, 1, OC_Q])
         self.sD = L.shape([1, OC_R, OC_Q])
         self.ops = []
-        for op in C2_BINARY:
+        for op in self.out_b:
             self.ops.append((f"c2_rowbcast_{op}", ROWBCAST_BYTES,
                              lambda op=op: L.binary(op, self.A, self.sA, self.B, self.sB, self.out_b[op])))
-        for op in C2_OUTER:
+        for op in self.out_o:
             self.ops.append((f"c2_outer_{op}", OUTER_BYTES,
                              lambda op=op: L.binary(op, self.Cc, self.sC, self.D, self.sD, self.out_o[op])))
-        for op in C2_UNARY:
+        for op in self.out_u:
             self.ops.append((f"c2_unary_{op}", UNARY_BYTES, lambda op=op: L.unary(op, self.A, self.out_u[op], n)))
+        if not self.ops:
+            raise SystemExit(f"--only {only}: no such C2 op")
         self.step_bytes = sum(b for _, b, _ in self.ops)
         self.launches_per_step = len(self.ops)
 
@@ -296,14 +312,27 @@ def run_e2e(L: Lib, c2: C2, steps: int, warmup: int):
 # ---------------------------------------------------------------------------
 # per-op breakdown of the other BASELINE configs
 # ---------------------------------------------------------------------------
-def per_op_suite(L: Lib, rank: int, iters: int = 10):
-    """C3 / C4 / C5a / C5b ops: (name, algorithmic bytes, avg ms per call, launches per call)."""
+PER_OP_SECTIONS = {"c3": ("c3_sum_axis-1", "c3_sum_axis0", "c3_mean_axis-1", "c3_mean_axis0", "c3_max_axis-1",
+                           "c3_max_axis0", "c3_argmax_axis-1", "c3_argmax_axis0"),
+                   "c3f": ("c3_fullsum_2^30",), "c4": ("c4_softmax_ce_fused",), "c5a": ("c5a_adam_1.5e9",),
+                   "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd")}
+
+
+def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, warmup: int = 3):
+    """C3 / C4 / C5a / C5b ops: (name, algorithmic bytes, avg ms per call, launches per call).
+
+    With `only`, just that op is set up and run (`warmup` untimed + `iters` timed calls)."""
     C = L.C
     lib = L.lib
     res = {}
 
+    def section(key):
+        return only is None or only in PER_OP_SECTIONS[key]
+
     def measure(name, nbytes, fn, launches, it=iters):
-        for _ in range(3):
+        if only is not None and name != only:
+            return
+        for _ in range(warmup):
             fn()
         ms = L.time(fn, it) / it
         res[name] = {"gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4), "bytes": int(nbytes),
@@ -311,6 +340,30 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10):
 
     # C3: R[16384,4096] ~ N(0,1) + 0.1% +-1e4 outliers (seed 2)
     R_ROWS, R_COLS = 16384, 4096
+    out = L.new(R_ROWS)
+    oidx = L.new(R_ROWS)
+    if section("c3"):
+        _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS)
+    if section("c3f"):
+        V = L.new(1 << 30)
+        L.fill(V, 2 + 1000 * rank, 7, 0, -1.0, 1.0)
+        measure("c3_fullsum_2^30", 4 << 30, lambda: L.check(lib.dct_reduce_all(0, V, 1 << 30, out, None), "fullsum"),
+                2, it=5)
+        lib.ReleaseBuffer(V)
+    lib.ReleaseBuffer(out)
+    lib.ReleaseBuffer(oidx)
+    if section("c4"):
+        _c4(L, rank, measure)
+    if section("c5a"):
+        _c5a(L, rank, measure)
+    if section("c5b"):
+        _c5b(L, rank, measure)
+    lib.DrainPool()
+    return res
+
+
+def _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS):
+    C, lib = L.C, L.lib
     R = L.new(R_ROWS * R_COLS)
     L.fill(R, 2 + 1000 * rank, 0, 1, 0.0, 1.0)
     rng = np.random.default_rng(2 + 1000 * rank)
@@ -318,8 +371,6 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10):
     idx = rng.choice(R_ROWS * R_COLS, k, replace=False).astype(np.int64)
     vals = np.where(rng.integers(0, 2, k) == 1, 1e4, -1e4).astype(np.float32)
     L.check(lib.dct_scatter(R, idx.ctypes.data_as(C.POINTER(C.c_int64)), vals.ctypes.data_as(C.POINTER(C.c_float)), k), "scatter")
-    out = L.new(R_ROWS)
-    oidx = L.new(R_ROWS)
     rbytes = 4 * R_ROWS * R_COLS
     for op in ("sum", "mean", "max", "argmax"):
         measure(f"c3_{op}_axis-1", rbytes + 4 * R_ROWS,
@@ -327,15 +378,11 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10):
         measure(f"c3_{op}_axis0", rbytes + 4 * R_COLS,
                 lambda op=op: L.check(lib.dct_reduce(L.REDUCE[op], R, 1, R_ROWS, R_COLS, out, None), op), 2)
     lib.ReleaseBuffer(R)
-    # C3 full sum of 2^30 U(-1,1)
-    V = L.new(1 << 30)
-    L.fill(V, 2 + 1000 * rank, 7, 0, -1.0, 1.0)
-    measure("c3_fullsum_2^30", 4 << 30, lambda: L.check(lib.dct_reduce_all(0, V, 1 << 30, out, None), "fullsum"), 2,
-            it=5)
-    lib.ReleaseBuffer(V)
-    lib.ReleaseBuffer(out)
-    lib.ReleaseBuffer(oidx)
-    # C4: fused softmax + CE fwd+bwd on [65536,1000], int labels (seed 3)
+
+
+def _c4(L, rank, measure):
+    """C4: fused softmax + CE fwd+bwd on [65536,1000], int labels (seed 3)."""
+    lib = L.lib
     B, K = 65536, 1000
     X = L.new(B * K)
     L.fill(X, 3 + 1000 * rank, 0, 1, 0.0, 3.0)
@@ -347,7 +394,11 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10):
             lambda: L.check(lib.dct_softmax_ce(X, Lb, 1, B, K, P, G, LS, None, float(B), float(B)), "softmax_ce"), 2)
     for h in (X, Lb, P, G, LS):
         lib.ReleaseBuffer(h)
-    # C5a: Adam on 1.5e9 fp32 (seed 4), zero m/v
+
+
+def _c5a(L, rank, measure):
+    """C5a: Adam on 1.5e9 fp32 (seed 4), zero m/v."""
+    lib = L.lib
     n = 1_500_000_000
     W, Gr, M, Vv = L.new(n), L.new(n), L.new(n), L.new(n)
     L.fill(W, 4 + 1000 * rank, 0, 1, 0.0, 0.02)
@@ -363,7 +414,11 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10):
     measure("c5a_adam_1.5e9", 28 * n, adam, 1, it=10)
     for h in (W, Gr, M, Vv):
         lib.ReleaseBuffer(h)
-    # C5b: BatchNorm train fwd / bwd on [256,256,56,56] (seed 4)
+
+
+def _c5b(L, rank, measure):
+    """C5b: BatchNorm train fwd / bwd on [256,256,56,56] (seed 4)."""
+    lib = L.lib
     N, Cc, S = 256, 256, 56 * 56
     nx = N * Cc * S
     x, dy, y, dx = L.new(nx), L.new(nx), L.new(nx), L.new(nx)
@@ -380,8 +435,6 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10):
             lambda: L.check(lib.dct_batchnorm_backward(x, dy, bm, bv, gam, dg, db, dx, N, Cc, S, 1e-5), "bnb"), 4)
     for h in (x, dy, y, dx, gam, bet, rm, rv, bm, bv, dg, db):
         lib.ReleaseBuffer(h)
-    lib.DrainPool()
-    return res
 
 
 # ---------------------------------------------------------------------------
@@ -415,12 +468,14 @@ def reference_arm(args, ranks: Ranks):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="dct", choices=("dct", "reference"))
     ap.add_argument("--no-per-op", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--only", default=None, help="profiling mode: run one C2 op (e.g. c2_rowbcast_add) "
+                    "--warmup + --steps times and print its timing only")
     args = ap.parse_args()
     ranks = Ranks(args.gpus)
     if args.impl == "reference":
@@ -429,8 +484,22 @@ def main():
         return rc
     os.environ.setdefault("DCT_DEVICE", str(ranks.local))
     L = Lib()
-    c2 = C2(L, ranks.rank)
+    if args.only and not args.only.startswith("c2_"):
+        res = per_op_suite(L, ranks.rank, iters=args.steps, only=args.only, warmup=args.warmup)
+        print(json.dumps({"only": args.only, **res.get(args.only, {})}))
+        ranks.close()
+        return 0
+    c2 = C2(L, ranks.rank, only=args.only)
     lib = L.lib
+    if args.only:
+        name, nbytes, fn = c2.ops[0]
+        for _ in range(args.warmup):
+            fn()
+        ms = L.time(fn, args.steps) / max(1, args.steps)
+        print(json.dumps({"only": name, "ms": round(ms, 4), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                          "launches": args.warmup + args.steps}))
+        ranks.close()
+        return 0
     # per-op timing of the step's kernels (dominant kernel + roofline)
     ops = {}
     for name, nbytes, fn in c2.ops:
@@ -444,7 +513,9 @@ def main():
     L.launches = 0
     ranks.barrier()
     lib.dct_synchronize()
-    with Clocks(lib.dct_device()) as clk:
+    bus = L.C.create_string_buffer(64)
+    lib.dct_pci_bus_id(bus, 64)
+    with Clocks(bus.value.decode()) as clk:
         ms = L.time(c2.step, args.steps)
         lib.dct_synchronize()
     ranks.barrier()
@@ -454,12 +525,17 @@ def main():
     total_bytes = c2.step_bytes * args.steps * world
     value = total_bytes / (ms_max * 1e-3) / 1e9
     peak, peak_kind = _peaks()
-    dom = max(ops, key=lambda k: ops[k]["ms"] * (2 if "outer" in k else (5 if "rowbcast" in k else 4)))
-    dom_group = [k for k in ops if k.rsplit("_", 1)[0] == dom.rsplit("_", 1)[0]]
-    dom_ms = float(np.mean([ops[k]["ms"] for k in dom_group]))
-    dom_bytes = ops[dom]["bytes"]
+    # dominant kernel family: the one with the largest share of the step time
+    fams = {}
+    for name in ops:
+        fams.setdefault("_".join(name.split("_")[:2]), []).append(name)
+    dom_f = max(fams, key=lambda f: sum(ops[n]["ms"] for n in fams[f]))
+    dom_ms = sum(ops[n]["ms"] for n in fams[dom_f]) / len(fams[dom_f])
+    dom_bytes = ops[fams[dom_f][0]]["bytes"]
+    dom_share = sum(ops[n]["ms"] for n in fams[dom_f]) / sum(v["ms"] for v in ops.values())
+    dom = f"{dom_f} x{len(fams[dom_f])} ({', '.join(n.split('_', 2)[2] for n in fams[dom_f])})"
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-    traffic = NCU_TRAFFIC_BYTES.get(dom.rsplit("_", 1)[0])
+    traffic = NCU_TRAFFIC_BYTES.get(dom_f)
     e2e = None
     if not args.no_e2e:
         dt, h2d, d2h = run_e2e(L, c2, steps=max(1, min(args.steps, 3)), warmup=1)
@@ -502,7 +578,7 @@ def main():
             "frac_of_8TBs": round(value / (NOMINAL_HBM_GBS * world), 3),
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst)", "unit": "GB/s",
-                         "frac": round(achieved / peak, 3), "traffic": traffic,
+                         "frac": round(achieved / peak, 3), "traffic": traffic, "share_of_step": round(dom_share, 3),
                          "algorithmic_bytes_per_launch": dom_bytes},
             "cpu_baseline": cpu,
             "e2e": e2e,

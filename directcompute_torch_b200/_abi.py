@@ -82,6 +82,7 @@ SIGNATURES = {
     "dct_device": ([], C.c_int),
     "dct_sm_count": ([], C.c_int),
     "dct_stream": ([], VP),
+    "dct_pci_bus_id": ([C.c_char_p, C.c_int], C.c_int),
     "dct_synchronize": ([], C.c_int),
     "dct_timer_start": ([], C.c_int),
     "dct_timer_stop_ms": ([], C.c_float),

@@ -116,8 +116,85 @@ __global__ void k_bn_bwd_final(const double* chan, uint32_t C, const float* mean
   dbeta[c] = (float)sdy;
 }
 
-// y = ((x - m) * rstd) * g + b, one warp per plane; elements >= limit untouched
-template <bool VEC>
+// Apply kernels: chunked schedule over the flat NCHW array (one contiguous
+// 16 KB slice per block, loads first); with S % 4 == 0 each float4 lies in one
+// (n, c) plane, whose channel c = (i4 / (S/4)) % C comes from two fast
+// divisions.  The per-channel constants are re-read through L1.  Elements at
+// or beyond `limit` (the reference's groups*256 index space) are untouched.
+constexpr int kBnU = 4;
+constexpr uint64_t kBnChunk4 = 256ull * kBnU;
+
+DCT_DEV float bn_fwd1(float v, float m, float r, float g, float b) {
+  return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, m), r), g), b);
+}
+DCT_DEV float bn_dx1(float xv, float d, float m, float r, float k1, float db, float dg, float mf) {
+  const float xh = __fmul_rn(__fsub_rn(xv, m), r);
+  return __fmul_rn(k1, __fsub_rn(d, __fdiv_rn(__fadd_rn(db, __fmul_rn(xh, dg)), mf)));
+}
+
+__global__ void __launch_bounds__(256) k_bn_forward_chunk(const float* __restrict__ x, const float* __restrict__ mean,
+                                                          const float* __restrict__ var,
+                                                          const float* __restrict__ gamma,
+                                                          const float* __restrict__ beta, float* __restrict__ y,
+                                                          uint32_t n4, FastDiv s4, FastDiv cdiv, float eps) {
+  const uint64_t base = (uint64_t)blockIdx.x * kBnChunk4 + threadIdx.x;
+  float4 v[kBnU];
+  uint32_t ch[kBnU];
+#pragma unroll
+  for (int k = 0; k < kBnU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) {
+      v[k] = ld_stream4(x + 4 * i);
+      const uint32_t pl = s4.div((uint32_t)i);
+      ch[k] = pl - cdiv.div(pl) * cdiv.d;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kBnU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i >= n4) continue;
+    const uint32_t c = ch[k];
+    const float m = ld_keep(mean + c), r = rstd_of(ld_keep(var + c), eps), g = ld_keep(gamma + c), b = ld_keep(beta + c);
+    st_stream4(y + 4 * i, make_float4(bn_fwd1(v[k].x, m, r, g, b), bn_fwd1(v[k].y, m, r, g, b),
+                                      bn_fwd1(v[k].z, m, r, g, b), bn_fwd1(v[k].w, m, r, g, b)));
+  }
+}
+
+__global__ void __launch_bounds__(256) k_bn_dx_chunk(const float* __restrict__ x, const float* __restrict__ dy,
+                                                     const float* __restrict__ mean, const float* __restrict__ var,
+                                                     const float* __restrict__ gamma,
+                                                     const float* __restrict__ dgamma,
+                                                     const float* __restrict__ dbeta, float* __restrict__ dx,
+                                                     uint32_t n4, FastDiv s4, FastDiv cdiv, float eps, float mf) {
+  const uint64_t base = (uint64_t)blockIdx.x * kBnChunk4 + threadIdx.x;
+  float4 a[kBnU], d[kBnU];
+  uint32_t ch[kBnU];
+#pragma unroll
+  for (int k = 0; k < kBnU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) {
+      a[k] = ld_stream4(x + 4 * i);
+      d[k] = ld_stream4(dy + 4 * i);
+      const uint32_t pl = s4.div((uint32_t)i);
+      ch[k] = pl - cdiv.div(pl) * cdiv.d;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kBnU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i >= n4) continue;
+    const uint32_t c = ch[k];
+    const float m = ld_keep(mean + c), r = rstd_of(ld_keep(var + c), eps);
+    const float k1 = __fmul_rn(ld_keep(gamma + c), r), dg = ld_keep(dgamma + c), db = ld_keep(dbeta + c);
+    st_stream4(dx + 4 * i, make_float4(bn_dx1(a[k].x, d[k].x, m, r, k1, db, dg, mf),
+                                       bn_dx1(a[k].y, d[k].y, m, r, k1, db, dg, mf),
+                                       bn_dx1(a[k].z, d[k].z, m, r, k1, db, dg, mf),
+                                       bn_dx1(a[k].w, d[k].w, m, r, k1, db, dg, mf)));
+  }
+}
+
+// Scalar fallbacks (S % 4 != 0, unaligned, or > 2^34 elements): one warp per
+// plane; elements >= limit untouched.
 __global__ void __launch_bounds__(256) k_bn_forward(const float* __restrict__ x, const float* __restrict__ mean,
                                                     const float* __restrict__ var, const float* __restrict__ gamma,
                                                     const float* __restrict__ beta, float* __restrict__ y,
@@ -131,32 +208,11 @@ __global__ void __launch_bounds__(256) k_bn_forward(const float* __restrict__ x,
     const float m = mean[c], r = rstd_of(var[c], eps), g = gamma[c], b = beta[c];
     const uint64_t base = pl * S;
     if (base >= limit) break;
-    const float* px = x + base;
-    float* py = y + base;
-    auto f = [&](float v) { return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, m), r), g), b); };
-    if (VEC && base + S <= limit) {
-      const uint32_t s4 = S >> 2;
-      uint32_t i = lane;
-      for (; i + 96 < s4; i += 128) {
-        float4 v[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = ld_stream4(px + 4 * (i + 32 * k));
-#pragma unroll
-        for (int k = 0; k < 4; ++k) st_stream4(py + 4 * (i + 32 * k), make_float4(f(v[k].x), f(v[k].y), f(v[k].z), f(v[k].w)));
-      }
-      for (; i < s4; i += 32) {
-        const float4 v = ld_stream4(px + 4 * i);
-        st_stream4(py + 4 * i, make_float4(f(v.x), f(v.y), f(v.z), f(v.w)));
-      }
-    } else {
-      for (uint32_t i = lane; i < S; i += 32)
-        if (base + i < limit) py[i] = f(px[i]);
-    }
+    for (uint32_t i = lane; i < S; i += 32)
+      if (base + i < limit) y[base + i] = bn_fwd1(x[base + i], m, r, g, b);
   }
 }
 
-// dx = (g*rstd) * (dy - (db + xhat*dg) / m)
-template <bool VEC>
 __global__ void __launch_bounds__(256) k_bn_backward_dx(const float* __restrict__ x, const float* __restrict__ dy,
                                                         const float* __restrict__ mean, const float* __restrict__ var,
                                                         const float* __restrict__ gamma,
@@ -173,32 +229,8 @@ __global__ void __launch_bounds__(256) k_bn_backward_dx(const float* __restrict_
     const float k1 = __fmul_rn(gamma[c], r);
     const uint64_t base = pl * S;
     if (base >= limit) break;
-    auto f = [&](float xv, float d) {
-      const float xh = __fmul_rn(__fsub_rn(xv, m), r);
-      return __fmul_rn(k1, __fsub_rn(d, __fdiv_rn(__fadd_rn(db, __fmul_rn(xh, dg)), mf)));
-    };
-    const float* px = x + base;
-    const float* pd = dy + base;
-    float* po = dx + base;
-    if (VEC && base + S <= limit) {
-      const uint32_t s4 = S >> 2;
-      uint32_t i = lane;
-      for (; i + 32 < s4; i += 64) {
-        float4 a[2], d[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) { a[k] = ld_stream4(px + 4 * (i + 32 * k)); d[k] = ld_stream4(pd + 4 * (i + 32 * k)); }
-#pragma unroll
-        for (int k = 0; k < 2; ++k)
-          st_stream4(po + 4 * (i + 32 * k), make_float4(f(a[k].x, d[k].x), f(a[k].y, d[k].y), f(a[k].z, d[k].z), f(a[k].w, d[k].w)));
-      }
-      for (; i < s4; i += 32) {
-        const float4 a = ld_stream4(px + 4 * i), d = ld_stream4(pd + 4 * i);
-        st_stream4(po + 4 * i, make_float4(f(a.x, d.x), f(a.y, d.y), f(a.z, d.z), f(a.w, d.w)));
-      }
-    } else {
-      for (uint32_t i = lane; i < S; i += 32)
-        if (base + i < limit) po[i] = f(px[i], pd[i]);
-    }
+    for (uint32_t i = lane; i < S; i += 32)
+      if (base + i < limit) dx[base + i] = bn_dx1(x[base + i], dy[base + i], m, r, k1, db, dg, mf);
   }
 }
 
@@ -258,10 +290,16 @@ cudaError_t launch_bn_forward(const float* x, const float* mean, const float* va
                               uint64_t limit, cudaStream_t st) {
   const uint64_t planes = (uint64_t)N * C;
   if (planes == 0 || S == 0) return cudaSuccess;
-  const bool vec = (S % 4 == 0) && aligned16_h(x) && aligned16_h(y);
-  const unsigned blocks = plane_blocks(planes);
-  if (vec) k_bn_forward<true><<<blocks, 256, 0, st>>>(x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
-  else k_bn_forward<false><<<blocks, 256, 0, st>>>(x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
+  const uint64_t total = planes * S;
+  if (limit > total) limit = total;
+  const bool vec = (S % 4 == 0) && (limit % 4 == 0) && limit / 4 < 0xffffffffull && aligned16_h(x) && aligned16_h(y);
+  if (vec) {
+    const uint32_t n4 = (uint32_t)(limit / 4);
+    k_bn_forward_chunk<<<(unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4), 256, 0, st>>>(
+        x, mean, var, gamma, beta, y, n4, FastDiv(S / 4), FastDiv(C), eps);
+  } else {
+    k_bn_forward<<<plane_blocks(planes), 256, 0, st>>>(x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
+  }
   return cudaGetLastError();
 }
 
@@ -270,13 +308,19 @@ cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* 
                                   uint32_t C, uint32_t S, float eps, uint64_t limit, cudaStream_t st) {
   const uint64_t planes = (uint64_t)N * C;
   if (planes == 0 || S == 0) return cudaSuccess;
+  const uint64_t total = planes * S;
+  if (limit > total) limit = total;
   const float mf = (float)((uint32_t)(N * S));     // HLSL: (float)(N * S) in uint arithmetic
-  const bool vec = (S % 4 == 0) && aligned16_h(x) && aligned16_h(dy) && aligned16_h(dx);
-  const unsigned blocks = plane_blocks(planes);
-  if (vec)
-    k_bn_backward_dx<true><<<blocks, 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C, S, eps, mf, limit);
-  else
-    k_bn_backward_dx<false><<<blocks, 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C, S, eps, mf, limit);
+  const bool vec = (S % 4 == 0) && (limit % 4 == 0) && limit / 4 < 0xffffffffull && aligned16_h(x) &&
+                   aligned16_h(dy) && aligned16_h(dx);
+  if (vec) {
+    const uint32_t n4 = (uint32_t)(limit / 4);
+    k_bn_dx_chunk<<<(unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4), 256, 0, st>>>(
+        x, dy, mean, var, gamma, dgamma, dbeta, dx, n4, FastDiv(S / 4), FastDiv(C), eps, mf);
+  } else {
+    k_bn_backward_dx<<<plane_blocks(planes), 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C,
+                                                            S, eps, mf, limit);
+  }
   return cudaGetLastError();
 }
 

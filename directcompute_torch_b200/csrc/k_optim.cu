@@ -45,39 +45,39 @@ DCT_DEV float sgd_scaled1(float w, float g, float lr, float scale) {
   return __fsub_rn(w, __fmul_rn(__fmul_rn(lr, g), scale));
 }
 
+// Chunked schedule (one contiguous 16 KB slice of each array per block, all
+// loads before any store): the block scheduler then walks the four streams in
+// address order, which keeps DRAM pages open (see k_elementwise.cu).
+constexpr int kOptU = 4;
+constexpr uint64_t kOptChunk4 = 256ull * kOptU;
+
 __global__ void __launch_bounds__(256) k_adam(float* __restrict__ w, float* __restrict__ m, float* __restrict__ v,
                                               const float* __restrict__ g, uint64_t n, AdamK p) {
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const uint64_t n4 = n >> 2;
-  uint64_t i = tid;
-  for (; i + stride < n4; i += 2 * stride) {
-    float4 W[2], M[2], V[2], G[2];
+  const uint64_t base = (uint64_t)blockIdx.x * kOptChunk4 + threadIdx.x;
+  float4 W[kOptU], M[kOptU], V[kOptU], G[kOptU];
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint64_t o = 4 * (i + k * stride);
-      W[k] = ld_stream4(w + o); M[k] = ld_stream4(m + o); V[k] = ld_stream4(v + o); G[k] = ld_stream4(g + o);
+  for (int k = 0; k < kOptU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) {
+      W[k] = ld_stream4(w + 4 * i); M[k] = ld_stream4(m + 4 * i);
+      V[k] = ld_stream4(v + 4 * i); G[k] = ld_stream4(g + 4 * i);
     }
+  }
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+  for (int k = 0; k < kOptU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) {
       adam1(W[k].x, M[k].x, V[k].x, G[k].x, p); adam1(W[k].y, M[k].y, V[k].y, G[k].y, p);
       adam1(W[k].z, M[k].z, V[k].z, G[k].z, p); adam1(W[k].w, M[k].w, V[k].w, G[k].w, p);
-      const uint64_t o = 4 * (i + k * stride);
-      st_stream4(w + o, W[k]); st_stream4(m + o, M[k]); st_stream4(v + o, V[k]);
+      st_stream4(w + 4 * i, W[k]); st_stream4(m + 4 * i, M[k]); st_stream4(v + 4 * i, V[k]);
     }
   }
-  for (; i < n4; i += stride) {
-    const uint64_t o = 4 * i;
-    float4 W = ld_stream4(w + o), M = ld_stream4(m + o), V = ld_stream4(v + o), G = ld_stream4(g + o);
-    adam1(W.x, M.x, V.x, G.x, p); adam1(W.y, M.y, V.y, G.y, p);
-    adam1(W.z, M.z, V.z, G.z, p); adam1(W.w, M.w, V.w, G.w, p);
-    st_stream4(w + o, W); st_stream4(m + o, M); st_stream4(v + o, V);
-  }
-  const uint64_t t = 4 * n4 + tid;
-  if (t < n) {
-    float W = w[t], M = m[t], V = v[t];
-    adam1(W, M, V, g[t], p);
-    w[t] = W; m[t] = M; v[t] = V;
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const uint64_t t = 4 * n4 + threadIdx.x;
+    float Wt = w[t], Mt = m[t], Vt = v[t];
+    adam1(Wt, Mt, Vt, g[t], p);
+    w[t] = Wt; m[t] = Mt; v[t] = Vt;
   }
 }
 
@@ -94,27 +94,41 @@ template <bool SCALED>
 __global__ void __launch_bounds__(256) k_sgd(float* w, const float* __restrict__ g, uint64_t n, float lr, float clip,
                                              const float* ns) {
   const float scale = SCALED ? ns[1] : 1.0f;
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (aligned16(w) && aligned16(g)) {
-    const uint64_t n4 = n >> 2;
-    for (uint64_t i = tid; i < n4; i += stride) {
-      float4 W = ld_stream4(w + 4 * i), G = ld_stream4(g + 4 * i);
-      if (SCALED) {
-        W.x = sgd_scaled1(W.x, G.x, lr, scale); W.y = sgd_scaled1(W.y, G.y, lr, scale);
-        W.z = sgd_scaled1(W.z, G.z, lr, scale); W.w = sgd_scaled1(W.w, G.w, lr, scale);
-      } else {
-        W.x = sgd1(W.x, G.x, lr, clip); W.y = sgd1(W.y, G.y, lr, clip);
-        W.z = sgd1(W.z, G.z, lr, clip); W.w = sgd1(W.w, G.w, lr, clip);
-      }
-      st_stream4(w + 4 * i, W);
-    }
-    const uint64_t t = 4 * n4 + tid;
-    if (t < n) w[t] = SCALED ? sgd_scaled1(w[t], g[t], lr, scale) : sgd1(w[t], g[t], lr, clip);
-  } else {
-    for (uint64_t i = tid; i < n; i += stride)
-      w[i] = SCALED ? sgd_scaled1(w[i], g[i], lr, scale) : sgd1(w[i], g[i], lr, clip);
+  const uint64_t n4 = n >> 2;
+  const uint64_t base = (uint64_t)blockIdx.x * kOptChunk4 + threadIdx.x;
+  float4 W[kOptU], G[kOptU];
+#pragma unroll
+  for (int k = 0; k < kOptU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) { W[k] = ld_stream4(w + 4 * i); G[k] = ld_stream4(g + 4 * i); }
   }
+#pragma unroll
+  for (int k = 0; k < kOptU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i >= n4) continue;
+    float4 o = W[k];
+    if (SCALED) {
+      o.x = sgd_scaled1(o.x, G[k].x, lr, scale); o.y = sgd_scaled1(o.y, G[k].y, lr, scale);
+      o.z = sgd_scaled1(o.z, G[k].z, lr, scale); o.w = sgd_scaled1(o.w, G[k].w, lr, scale);
+    } else {
+      o.x = sgd1(o.x, G[k].x, lr, clip); o.y = sgd1(o.y, G[k].y, lr, clip);
+      o.z = sgd1(o.z, G[k].z, lr, clip); o.w = sgd1(o.w, G[k].w, lr, clip);
+    }
+    st_stream4(w + 4 * i, o);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const uint64_t t = 4 * n4 + threadIdx.x;
+    w[t] = SCALED ? sgd_scaled1(w[t], g[t], lr, scale) : sgd1(w[t], g[t], lr, clip);
+  }
+}
+
+template <bool SCALED>
+__global__ void __launch_bounds__(256) k_sgd_scalar(float* w, const float* g, uint64_t n, float lr, float clip,
+                                                    const float* ns) {
+  const float scale = SCALED ? ns[1] : 1.0f;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    w[i] = SCALED ? sgd_scaled1(w[i], g[i], lr, scale) : sgd1(w[i], g[i], lr, clip);
 }
 
 // ---------------------------------------------------------------------------
@@ -256,23 +270,32 @@ cudaError_t launch_adam(float* w, float* m, float* v, const float* g, uint64_t n
                         cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   const AdamK k = to_k(p);
-  if (aligned16_h(w) && aligned16_h(m) && aligned16_h(v) && aligned16_h(g))
-    k_adam<<<grid_for((n + 3) / 4, 256), 256, 0, st>>>(w, m, v, g, n, k);
+  const uint64_t blocks = ((n >> 2) + kOptChunk4 - 1) / kOptChunk4;
+  if (aligned16_h(w) && aligned16_h(m) && aligned16_h(v) && aligned16_h(g) && blocks < (1ull << 31))
+    k_adam<<<(unsigned)(blocks ? blocks : 1), 256, 0, st>>>(w, m, v, g, n, k);
   else
     k_adam_scalar<<<grid_for(n, 256), 256, 0, st>>>(w, m, v, g, n, k);
   return cudaGetLastError();
 }
 
-cudaError_t launch_sgd(float* w, const float* g, uint64_t n, float lr, float clip, cudaStream_t st) {
+template <bool SCALED>
+static cudaError_t run_sgd(float* w, const float* g, uint64_t n, float lr, float clip, const float* ns,
+                           cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  k_sgd<false><<<grid_for((n + 3) / 4, 256), 256, 0, st>>>(w, g, n, lr, clip, nullptr);
+  const uint64_t blocks = ((n >> 2) + kOptChunk4 - 1) / kOptChunk4;
+  if (aligned16_h(w) && aligned16_h(g) && blocks < (1ull << 31))
+    k_sgd<SCALED><<<(unsigned)(blocks ? blocks : 1), 256, 0, st>>>(w, g, n, lr, clip, ns);
+  else
+    k_sgd_scalar<SCALED><<<grid_for(n, 256), 256, 0, st>>>(w, g, n, lr, clip, ns);
   return cudaGetLastError();
 }
 
+cudaError_t launch_sgd(float* w, const float* g, uint64_t n, float lr, float clip, cudaStream_t st) {
+  return run_sgd<false>(w, g, n, lr, clip, nullptr, st);
+}
+
 cudaError_t launch_sgd_clipped(float* w, const float* g, uint64_t n, float lr, const float* ns, cudaStream_t st) {
-  if (n == 0) return cudaSuccess;
-  k_sgd<true><<<grid_for((n + 3) / 4, 256), 256, 0, st>>>(w, g, n, lr, 0.0f, ns);
-  return cudaGetLastError();
+  return run_sgd<true>(w, g, n, lr, 0.0f, ns, st);
 }
 
 cudaError_t launch_mt_sgd(const MtTensor* t, int count, float lr, float clip, const float* ns, cudaStream_t st) {

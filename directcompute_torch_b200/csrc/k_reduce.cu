@@ -31,19 +31,42 @@ namespace {
 constexpr int kRedThreads = 256;
 constexpr int kRedWarps = kRedThreads / 32;
 
-DCT_DEV bool is_arg(int op) { return op == RED_MAX || op == RED_ARGMAX || op == RED_MIN || op == RED_ARGMIN; }
+// max / min that return NaN if either operand is NaN (one instruction)
+DCT_DEV float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+DCT_DEV float fmin_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
 
 // Partial accumulator of one reduction lane.
+//  * sums: float64;
+//  * MAX / MIN: value only, NaN propagates (NumPy);
+//  * ARGMAX / ARGMIN: (value, int32 index); within one lane indices only grow,
+//    so a later candidate replaces the current one only if strictly better
+//    (a first NaN beats every number); merges of lanes, warps and chunks use
+//    the full rule, ties going to the lower index.
 template <int OP>
 struct Acc {
-  static constexpr bool kArg = (OP == RED_MAX || OP == RED_ARGMAX || OP == RED_MIN || OP == RED_ARGMIN);
+  static constexpr bool kArg = (OP == RED_ARGMAX || OP == RED_ARGMIN);
+  static constexpr bool kExt = (OP == RED_MAX || OP == RED_MIN);
   static constexpr bool kMax = (OP == RED_MAX || OP == RED_ARGMAX);
   double s = 0.0;
-  float v = 0.0f;
-  int64_t i = -1;
+  float v = kMax ? -INFINITY : INFINITY;
+  int32_t i = -1;
   DCT_DEV void add(float x, int64_t idx) {
     if constexpr (kArg) {
-      if (i < 0 || better<kMax>(x, idx, v, i)) { v = x; i = idx; }
+      // common path: one compare (x <= v is false for a better x and for any NaN)
+      if (i < 0 || !(kMax ? (x <= v) : (x >= v))) {
+        const bool take = (i < 0) | (kMax ? (x > v) : (x < v)) | ((x != x) & (v == v));
+        if (take) { v = x; i = (int32_t)idx; }
+      }
+    } else if constexpr (kExt) {
+      v = kMax ? fmax_nan(v, x) : fmin_nan(v, x);
     } else if constexpr (OP == RED_SUMSQ) {
       double d = (double)x;
       s += d * d;
@@ -54,6 +77,8 @@ struct Acc {
   DCT_DEV void merge(const Acc& o) {
     if constexpr (kArg) {
       if (o.i >= 0 && (i < 0 || better<kMax>(o.v, o.i, v, i))) { v = o.v; i = o.i; }
+    } else if constexpr (kExt) {
+      v = ((kMax ? (o.v > v) : (o.v < v)) || (o.v != o.v)) && !(v != v) ? o.v : v;
     } else {
       s += o.s;
     }
@@ -62,9 +87,17 @@ struct Acc {
     if constexpr (kArg) {
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
-        float ov = __shfl_down_sync(0xffffffffu, v, off);
-        int64_t oi = __shfl_down_sync(0xffffffffu, i, off);
-        if (oi >= 0 && (i < 0 || better<kMax>(ov, oi, v, i))) { v = ov; i = oi; }
+        Acc o;
+        o.v = __shfl_down_sync(0xffffffffu, v, off);
+        o.i = __shfl_down_sync(0xffffffffu, i, off);
+        merge(o);
+      }
+    } else if constexpr (kExt) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        Acc o;
+        o.v = __shfl_down_sync(0xffffffffu, v, off);
+        merge(o);
       }
     } else {
       s = warp_sum(s);
@@ -72,14 +105,14 @@ struct Acc {
   }
   // packed 8-byte partial
   DCT_DEV unsigned long long pack() const {
-    if constexpr (kArg) {
-      return ((unsigned long long)(uint32_t)__float_as_uint(v) << 32) | (uint32_t)(int32_t)i;
+    if constexpr (kArg || kExt) {
+      return ((unsigned long long)(uint32_t)__float_as_uint(v) << 32) | (uint32_t)i;
     } else {
       return (unsigned long long)__double_as_longlong(s);
     }
   }
   DCT_DEV void unpack(unsigned long long w) {
-    if constexpr (kArg) {
+    if constexpr (kArg || kExt) {
       v = __uint_as_float((uint32_t)(w >> 32));
       i = (int32_t)(uint32_t)(w & 0xffffffffu);
     } else {
@@ -89,7 +122,9 @@ struct Acc {
   DCT_DEV void store(float* out, int32_t* out_idx, uint64_t k, uint64_t len) const {
     if constexpr (kArg) {
       if (out) out[k] = v;
-      if (out_idx) out_idx[k] = (int32_t)i;
+      if (out_idx) out_idx[k] = i;
+    } else if constexpr (kExt) {
+      out[k] = v;
     } else if constexpr (OP == RED_MEAN) {
       out[k] = (float)(s / (double)len);
     } else {
@@ -209,6 +244,70 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
   }
 }
 
+// ---------------------------------------------------------------------------
+// COLUMN-SWEEP kernel (inner <= 4096, contiguous): block (chunk, o) streams
+// whole rows l0..l1 of x[o] -- each row one contiguous run, two rows in
+// flight -- and thread t owns float4 columns t, t+256, ... (VPT of them), so
+// the block's reads sweep memory in address order like the chunked
+// elementwise kernels.  Per-chunk partials are folded in chunk order.
+// ---------------------------------------------------------------------------
+template <int OP, int VPT>
+__global__ void __launch_bounds__(256) k_reduce_colsweep(const float* __restrict__ x, uint64_t len, uint64_t inner,
+                                                         uint64_t so, uint64_t sl, uint32_t chunks,
+                                                         uint64_t chunk_len, float* out, int32_t* out_idx,
+                                                         unsigned long long* part) {
+  const uint32_t w4 = (uint32_t)(inner >> 2);
+  const uint32_t ch = blockIdx.x;
+  const uint64_t o = blockIdx.y;
+  const uint64_t l0 = (uint64_t)ch * chunk_len;
+  const uint64_t l1 = min(len, l0 + chunk_len);
+  const float* base = x + o * so;
+  Acc<OP> acc[VPT][4];
+  uint64_t l = l0;
+  for (; l + 1 < l1; l += 2) {
+    float4 v[2][VPT];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const uint32_t c4 = threadIdx.x + 256 * j;
+        if (c4 < w4) v[r][j] = ld_stream4(base + (l + r) * sl + 4ull * c4);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        if (threadIdx.x + 256 * j < w4) {
+          const int64_t li = (int64_t)(l + r);
+          acc[j][0].add(v[r][j].x, li); acc[j][1].add(v[r][j].y, li);
+          acc[j][2].add(v[r][j].z, li); acc[j][3].add(v[r][j].w, li);
+        }
+      }
+  }
+  if (l < l1) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const uint32_t c4 = threadIdx.x + 256 * j;
+      if (c4 < w4) {
+        const float4 v = ld_stream4(base + l * sl + 4ull * c4);
+        acc[j][0].add(v.x, (int64_t)l); acc[j][1].add(v.y, (int64_t)l);
+        acc[j][2].add(v.z, (int64_t)l); acc[j][3].add(v.w, (int64_t)l);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const uint32_t c4 = threadIdx.x + 256 * j;
+    if (c4 >= w4) continue;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint64_t c = 4ull * c4 + q;
+      if (chunks == 1) acc[j][q].store(out, out_idx, o * inner + c, len);
+      else part[(o * chunks + ch) * inner + c] = acc[j][q].pack();
+    }
+  }
+}
+
 // fold chunk partials: out[k] = combine(part[k*stride_k ... with chunk stride])
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
@@ -244,8 +343,10 @@ __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict_
   }
 }
 
+constexpr bool kColSweep = false;    // column-sweep plan (kind 3) off: under-occupied without a cluster combine
+
 struct Plan {
-  int kind;           // 0 rows, 1 cols, 2 generic
+  int kind;           // 0 rows, 1 cols, 2 generic, 3 column sweep
   bool vec;
   uint32_t chunks;
   uint64_t chunk_len;
@@ -276,6 +377,21 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
     uint64_t blocks = (warps + kRedWarps - 1) / kRedWarps;
     if (blocks > target_blocks * 4) blocks = target_blocks * 4;
     p.grid = dim3((unsigned)blocks, 1, 1);
+  } else if (kColSweep && si == 1 && inner % 4 == 0 && inner <= 4096 && sl % 4 == 0 && so % 4 == 0 &&
+             aligned16_h(x) && len >= 64 && outer <= 65535) {
+    p.kind = 3;
+    p.vec = true;
+    // about two blocks per SM in total, at least 8 rows per chunk
+    const uint64_t target = (uint64_t)d.sm_count * 2;
+    uint64_t chunks = (target + outer - 1) / outer;
+    const uint64_t max_chunks = len / 8;
+    if (chunks > max_chunks) chunks = max_chunks;
+    if (chunks < 1) chunks = 1;
+    const uint64_t cl = (len + chunks - 1) / chunks;
+    chunks = (len + cl - 1) / cl;
+    p.chunks = (uint32_t)chunks;
+    p.chunk_len = cl;
+    p.grid = dim3((unsigned)chunks, (unsigned)outer, 1);
   } else if (si == 1) {
     p.kind = 1;
     p.vec = (inner % 4 == 0) && (sl % 4 == 0) && (so % 4 == 0) && aligned16_h(x);
@@ -321,6 +437,14 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
   } else if (p.kind == 1) {
     if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
     else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
+  } else if (p.kind == 3) {
+    const uint64_t w4 = inner / 4;
+    if (w4 <= 256)
+      k_reduce_colsweep<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
+    else if (w4 <= 512)
+      k_reduce_colsweep<OP, 2><<<p.grid, kRedThreads, 0, st>>>(x, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
+    else
+      k_reduce_colsweep<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
   } else {
     k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, out, out_idx);
   }

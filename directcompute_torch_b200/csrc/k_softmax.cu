@@ -11,11 +11,15 @@
 //
 // Accuracy: x - max is formed with an error-free two-sum so the exponent's
 // argument is exact to first order (exp(s + t) = exp(s) * (1 + t)); the row
-// normaliser is summed in float64 and applied as a float64 product, so each
-// probability carries the error of one expf plus one rounding.  The loss and
+// normaliser is summed in float64, rounded once to its fp32 reciprocal and
+// applied as one fp32 product, so each probability carries the error of one
+// expf plus two roundings (held to 4 ulp).  The loss and
 // log-probs are formed in float64 from log(sum).  dlogits follow the
 // reference formula (p - onehot) / B on the rounded p, bit for bit.
+#include <algorithm>
+
 #include "dct_common.cuh"
+#include "dct_tma.cuh"
 #include "kernels.h"
 
 namespace dct {
@@ -116,7 +120,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_con
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const double inv = 1.0 / s;
+    const float invf = (float)(1.0 / s);   // p = e * (1/s): <= 1 ulp on top of exp's
     const double lse = log(s);       // log sum exp(x - m)
     // ---- label
     bool lvalid = true;
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_con
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint32_t col = VEC ? col0 + q : (uint32_t)(lane + 32 * (4 * j + q));
-        p[q] = (float)((double)x[4 * j + q] * inv);
+        p[q] = __fmul_rn(x[4 * j + q], invf);
         const float oh = (c.labels && col == lidx) ? 1.0f : 0.0f;
         g[q] = grad_of(p[q], oh, c);
       }
@@ -182,6 +186,130 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_con
   }
 }
 
+// TMA-staged variant (K % 4 == 0, row <= 8 KB, no log-probs): each warp owns
+// a two-stage ring of row buffers in shared memory filled by 1-D bulk copies
+// completing on per-stage mbarriers, so row r+2 streams in while row r is
+// computed and the row costs no registers.  Three passes over shared memory:
+// max; exp written back in place with the float64 sum; probabilities and
+// gradients streamed out.  Every mbarrier wait is bounded (dct_tma.cuh).
+template <int VPL, int WPB>
+__global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_constant__ RowCtx c, uint32_t buf_bytes,
+                                                             uint32_t* err) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ double wsum[WPB];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + 2 * warp;
+  float* const buf0 = reinterpret_cast<float*>(smem + 128 + (size_t)(2 * warp) * buf_bytes);
+  float* const buf1 = reinterpret_cast<float*>(smem + 128 + (size_t)(2 * warp + 1) * buf_bytes);
+  const uint32_t K = c.K;
+  const uint32_t rb = K * 4u;
+  if (lane == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  const uint32_t r0 = blockIdx.x * WPB + warp;
+  const uint32_t rstep = gridDim.x * WPB;
+  if (lane == 0) {
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const uint32_t r = r0 + s2 * rstep;
+      if (r < c.rows) {
+        mbar_arrive_expect_tx(&bars[s2], rb);
+        bulk_load(s2 ? buf1 : buf0, c.logits + (uint64_t)r * K, rb, &bars[s2]);
+      }
+    }
+  }
+  __syncwarp();
+  double block_loss = 0.0;
+  uint32_t k = 0;
+  for (uint32_t r = r0; r < c.rows; r += rstep, ++k) {
+    const int st = k & 1;
+    float* row = st ? buf1 : buf0;
+    mbar_wait(&bars[st], (k >> 1) & 1u, err);
+    bool lvalid = true;
+    float lab = 0.0f;
+    if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
+    const uint32_t lidx = !lvalid ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
+    // pass 1: row max
+    float m = c.ref_max_init ? -1e30f : -INFINITY;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+      if (col < K) {
+        const float4 v = *reinterpret_cast<const float4*>(row + col);
+        m = fmaxf(fmaxf(m, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
+      }
+    }
+    m = warp_max_f(m);
+    // pass 2: e = exp(x - m) in place, float64 normaliser
+    double sacc = 0.0;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+      if (col < K) {
+        float4 v = *reinterpret_cast<const float4*>(row + col);
+        v.x = (v.x == -INFINITY) ? 0.0f : exp_diff(v.x, m);
+        v.y = (v.y == -INFINITY) ? 0.0f : exp_diff(v.y, m);
+        v.z = (v.z == -INFINITY) ? 0.0f : exp_diff(v.z, m);
+        v.w = (v.w == -INFINITY) ? 0.0f : exp_diff(v.w, m);
+        sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
+        *reinterpret_cast<float4*>(row + col) = v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+    const float invf = (float)(1.0 / sacc);
+    __syncwarp();
+    // pass 3: probabilities and gradients
+    float* prow = c.probs ? c.probs + (uint64_t)r * K : nullptr;
+    float* grow = c.dlogits ? c.dlogits + (uint64_t)r * K : nullptr;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+      if (col < K) {
+        const float4 e = *reinterpret_cast<const float4*>(row + col);
+        const float4 p = make_float4(__fmul_rn(e.x, invf), __fmul_rn(e.y, invf), __fmul_rn(e.z, invf),
+                                     __fmul_rn(e.w, invf));
+        if (prow) st_stream4(prow + col, p);
+        if (grow) {
+          const float4 g = make_float4(grad_of(p.x, (c.labels && col == lidx) ? 1.0f : 0.0f, c),
+                                       grad_of(p.y, (c.labels && col + 1 == lidx) ? 1.0f : 0.0f, c),
+                                       grad_of(p.z, (c.labels && col + 2 == lidx) ? 1.0f : 0.0f, c),
+                                       grad_of(p.w, (c.labels && col + 3 == lidx) ? 1.0f : 0.0f, c));
+          st_stream4(grow + col, g);
+        }
+      }
+    }
+    if (c.want_loss && lane == 0 && lvalid) {
+      const uint64_t li = (uint64_t)r * K + lidx;
+      const double xl = li < c.total ? (double)c.logits[li] : 0.0;
+      block_loss += -((xl - (double)m) - log(sacc));
+    }
+    // hand the stage back to the bulk-copy engine for row r + 2*rstep
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t nr = r + 2 * rstep;
+      if (nr < c.rows) {
+        mbar_arrive_expect_tx(&bars[st], rb);
+        bulk_load(row, c.logits + (uint64_t)nr * K, rb, &bars[st]);
+      }
+    }
+    __syncwarp();
+  }
+  if (c.want_loss) {
+    if (lane == 0) wsum[warp] = block_loss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int w = 0; w < WPB; ++w) t += wsum[w];
+      c.part[blockIdx.x] = t;
+    }
+  }
+}
+
 // Rows longer than 2048: one block per row, three streaming passes (L2 keeps the row).
 __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_constant__ RowCtx c) {
   __shared__ double shd[32];
@@ -209,7 +337,8 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_co
     if (threadIdx.x == 0) shd[0] = s;
     __syncthreads();
     s = shd[0];
-    const double inv = 1.0 / s, lse = log(s);
+    const float invf = (float)(1.0 / s);
+    const double lse = log(s);
     bool lvalid = true;
     float lab = 0.0f;
     if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
@@ -217,7 +346,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_co
     for (uint32_t k = threadIdx.x; k < K; k += blockDim.x) {
       const float xv = row[k];
       const float e = (xv == -INFINITY) ? 0.0f : exp_diff(xv, m);
-      const float p = (float)((double)e * inv);
+      const float p = __fmul_rn(e, invf);
       if (c.probs) c.probs[(uint64_t)r * K + k] = p;
       if (c.dlogits) c.dlogits[(uint64_t)r * K + k] = grad_of(p, (c.labels && k == lidx) ? 1.0f : 0.0f, c);
       if (c.logprobs) c.logprobs[(uint64_t)r * K + k] = (float)(((double)xv - (double)m) - lse);
@@ -257,8 +386,21 @@ int softmax_blocks(uint32_t rows, uint32_t K) {
 
 }  // namespace
 
+// blocks of the TMA-staged kernel: up to 3 per SM (shared memory bound), one
+// row per warp per step
+int tma_blocks(uint32_t rows, uint32_t K) {
+  const uint32_t buf_bytes = ((K * 4u) + 127u) & ~127u;
+  const int wpb = buf_bytes <= 4096 ? 8 : 4;
+  const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
+  const DevInfo& di = dev_info();
+  const int per_sm = std::min<int>(3, std::max<int>(1, (int)((228u * 1024u) / (smem + 1024))));
+  const uint64_t need = ((uint64_t)rows + wpb - 1) / wpb;
+  const uint64_t cap = (uint64_t)di.sm_count * per_sm;
+  return (int)std::max<uint64_t>(1, std::min(need, cap));
+}
+
 size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K) {
-  return (size_t)softmax_blocks(rows, K) * sizeof(double) + 64;
+  return (size_t)std::max(softmax_blocks(rows, K), tma_blocks(rows, K)) * sizeof(double) + 64;
 }
 
 cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st) {
@@ -288,10 +430,37 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
   c.grad_mul = c.grad_div_pow2 ? ldexpf(1.0f, -(ex - 1)) : 1.0f;
   c.ref_max_init = a.ref_max_init;
   if (a.dlogits && !a.labels) return cudaErrorInvalidValue;
-  const int blocks = softmax_blocks(a.rows, a.K);
   const bool vec = (a.K % 4 == 0) && aligned16_h(a.logits) && (!a.probs || aligned16_h(a.probs)) &&
                    (!a.dlogits || aligned16_h(a.dlogits));
   const uint32_t K = a.K;
+  if (vec && !a.logprobs && K <= 2048 && K >= 128) {
+    const uint32_t buf_bytes = ((K * 4u) + 127u) & ~127u;
+    const int wpb = buf_bytes <= 4096 ? 8 : 4;
+    const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
+    const int blocks_t = tma_blocks(a.rows, K);
+    cudaError_t e = cudaSuccess;
+#define DCT_SM_TMA(VPL, WPB)                                                                                  \
+  do {                                                                                                        \
+    static bool attr_set = false;                                                                             \
+    if (!attr_set) {                                                                                          \
+      e = cudaFuncSetAttribute(k_softmax_ce_tma<VPL, WPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                               (int)(128 + 2 * WPB * 8192));                                                   \
+      attr_set = (e == cudaSuccess);                                                                          \
+    }                                                                                                         \
+    if (e == cudaSuccess) k_softmax_ce_tma<VPL, WPB><<<blocks_t, WPB * 32, smem, st>>>(c, buf_bytes, a.err);  \
+  } while (0)
+    if (K <= 256) DCT_SM_TMA(2, 8);
+    else if (K <= 512) DCT_SM_TMA(4, 8);
+    else if (K <= 1024) DCT_SM_TMA(8, 8);
+    else DCT_SM_TMA(16, 4);
+#undef DCT_SM_TMA
+    if (e != cudaSuccess) return e;
+    e = cudaGetLastError();
+    if (e != cudaSuccess || !c.want_loss) return e;
+    k_loss_final<<<1, 1024, 0, st>>>(c.part, blocks_t, a.loss_div, a.loss, a.loss_partial);
+    return cudaGetLastError();
+  }
+  const int blocks = softmax_blocks(a.rows, a.K);
   if (K <= 128) {
     if (vec) k_softmax_ce_warp<1, true><<<blocks, kSmThreads, 0, st>>>(c);
     else k_softmax_ce_warp<1, false><<<blocks, kSmThreads, 0, st>>>(c);

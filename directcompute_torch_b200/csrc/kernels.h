@@ -91,6 +91,7 @@ struct SoftmaxCEArgs {
   double loss_div = 1.0;
   float grad_div = 1.0f;
   bool ref_max_init = false;       // true: max starts at -1e30 (nn_softmax.hlsl:8)
+  uint32_t* err = nullptr;         // device-visible error word (bounded waits)
 };
 size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K);
 cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st);

@@ -73,6 +73,8 @@ struct Engine {
   void* ws = nullptr;             // reduction scratch
   size_t ws_bytes = 0;
   float* host_small = nullptr;    // pinned 64-byte staging for scalar readbacks
+  uint32_t* dev_err_host = nullptr;   // mapped error word written by device code
+  uint32_t* dev_err_dev = nullptr;
   char name[128] = {0};
   // error state
   int err_code = 0;
@@ -125,6 +127,17 @@ static bool cuda_ok(cudaError_t e, const char* where) {
 }
 
 static bool ensure_init();
+
+// Device code reports bounded-wait timeouts through a mapped host word; surface
+// them after every wait on the stream.
+static bool check_device_errors() {
+  if (!g.dev_err_host) return true;
+  const uint32_t e = *(volatile uint32_t*)g.dev_err_host;
+  if (!e) return true;
+  *(volatile uint32_t*)g.dev_err_host = 0;
+  set_error(DCT_ERR_CUDA, "device: a bounded wait in a kernel timed out (error bits 0x%x); results are invalid", e);
+  return false;
+}
 
 // ---------------------------------------------------------------------------
 // buffers and pool (engine.cpp:181-290 semantics)
@@ -251,6 +264,10 @@ static bool init_engine() {
   }
   cudaGetLastError();
   if (!cuda_ok(cudaMallocHost(&g.host_small, 64), "InitEngine(pinned staging)")) return false;
+  if (!cuda_ok(cudaHostAlloc((void**)&g.dev_err_host, 64, cudaHostAllocMapped), "InitEngine(error word)")) return false;
+  *g.dev_err_host = 0;
+  if (!cuda_ok(cudaHostGetDevicePointer((void**)&g.dev_err_dev, g.dev_err_host, 0), "InitEngine(error word)"))
+    return false;
   g.init = true;
   return true;
 }
@@ -454,6 +471,7 @@ static bool h_dice_loss_grad(const Disp& d) {
 
 // ---- softmax / CE -------------------------------------------------------------
 static bool run_softmax_ce(const Disp& d, SoftmaxCEArgs a) {
+  a.err = g.dev_err_dev;
   const size_t ws = softmax_ce_ws_bytes(a.rows, a.K);
   if (!ensure_ws(ws)) return false;
   LAUNCH(launch_softmax_ce(a, g.ws, g.stream));
@@ -605,9 +623,12 @@ static bool h_dct_reduce(const Disp& d) {
   int32_t* idx = nullptr;
   if (d.nuav > 1 && d.uav[1]) { FITS(d.uav[1], outer * inner, "idx"); idx = reinterpret_cast<int32_t*>(d.uav[1]->d); }
   float* out = d.uav[0]->d;
+  int op_run = op;
   if (op == RED_ARGMAX || op == RED_ARGMIN) {
     // the index is the product; values are not requested
     if (!idx) { idx = reinterpret_cast<int32_t*>(out); out = nullptr; }
+  } else if ((op == RED_MAX || op == RED_MIN) && idx) {
+    op_run = op == RED_MAX ? RED_ARGMAX : RED_ARGMIN;       // values and indices in one pass
   }
   if (len > 0x7fffffffull && (op == RED_ARGMAX || op == RED_ARGMIN)) {
     set_error(DCT_ERR_ARG, "dct_reduce: arg reductions need len < 2^31");
@@ -615,7 +636,7 @@ static bool h_dct_reduce(const Disp& d) {
   }
   const size_t ws = reduce3d_ws_bytes(op, outer, len, inner);
   if (ws && !ensure_ws(ws)) return false;
-  LAUNCH(launch_reduce3d(op, d.srv[0]->d, outer, len, inner, out, idx, g.ws, g.stream));
+  LAUNCH(launch_reduce3d(op_run, d.srv[0]->d, outer, len, inner, out, idx, g.ws, g.stream));
 }
 
 static bool h_dct_reduce_all(const Disp& d) {
@@ -861,6 +882,7 @@ DCT_API void ReadBuffer(void* h, float* dst) {
   }
   cuda_ok(cudaMemcpyAsync(dst, b->d, b->count * sizeof(float), cudaMemcpyDeviceToHost, g.stream), "ReadBuffer");
   cuda_ok(cudaStreamSynchronize(g.stream), "ReadBuffer(sync)");
+  check_device_errors();
 }
 
 DCT_API void ClearBuffer(void* h) {
@@ -877,7 +899,7 @@ DCT_API void FlushGPU() {
 
 DCT_API void SyncGPU() {
   LOCK;
-  if (g.init) cuda_ok(cudaStreamSynchronize(g.stream), "SyncGPU");
+  if (g.init && cuda_ok(cudaStreamSynchronize(g.stream), "SyncGPU")) check_device_errors();
 }
 
 DCT_API void RunShader(const char* name, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav, uint32_t* threads,
@@ -1107,6 +1129,12 @@ DCT_API int dct_sm_count() {
   return ensure_init() ? g.info.sm_count : 0;
 }
 
+DCT_API int dct_pci_bus_id(char* out, int len) {
+  LOCK;
+  if (!out || len <= 0 || !ensure_init()) return DCT_ERR_NO_DEVICE;
+  return cuda_ok(cudaDeviceGetPCIBusId(out, len, g.info.device), "dct_pci_bus_id") ? 0 : DCT_ERR_CUDA;
+}
+
 DCT_API void* dct_stream() {
   LOCK;
   return ensure_init() ? (void*)g.stream : nullptr;
@@ -1115,7 +1143,8 @@ DCT_API void* dct_stream() {
 DCT_API int dct_synchronize() {
   LOCK;
   if (!ensure_init()) return DCT_ERR_NO_DEVICE;
-  return cuda_ok(cudaStreamSynchronize(g.stream), "dct_synchronize") ? 0 : DCT_ERR_CUDA;
+  if (!cuda_ok(cudaStreamSynchronize(g.stream), "dct_synchronize")) return DCT_ERR_CUDA;
+  return check_device_errors() ? 0 : DCT_ERR_CUDA;
 }
 
 DCT_API int dct_timer_start() {
@@ -1131,6 +1160,7 @@ DCT_API float dct_timer_stop_ms() {
   if (!cuda_ok(cudaEventRecord(g.ev1, g.stream), "dct_timer_stop")) return -1.0f;
   if (!cuda_ok(cudaEventSynchronize(g.ev1), "dct_timer_stop(sync)")) return -1.0f;
   if (!cuda_ok(cudaEventElapsedTime(&ms, g.ev0, g.ev1), "dct_timer_stop(elapsed)")) return -1.0f;
+  if (!check_device_errors()) return -1.0f;
   return ms;
 }
 

@@ -175,6 +175,7 @@ DCT_API int dct_version(void);              /* DCT_ABI_VERSION */
 DCT_API int dct_device(void);               /* CUDA ordinal in use, -1 if none */
 DCT_API int dct_sm_count(void);
 DCT_API void* dct_stream(void);             /* the library's cudaStream_t */
+DCT_API int dct_pci_bus_id(char* out, int len);   /* "0000:xx:00.0" of the device in use */
 DCT_API int dct_synchronize(void);
 /* CUDA events on the library's stream: start, then stop returns elapsed ms (waits) */
 DCT_API int dct_timer_start(void);
