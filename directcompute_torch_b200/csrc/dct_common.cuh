@@ -23,6 +23,9 @@ struct DevInfo {
   size_t total_mem = 0;
 };
 const DevInfo& dev_info();   // defined in runtime.cu
+// device-visible error word for bounded waits (mapped host memory; null before
+// InitEngine, then kernels skip the report)
+uint32_t* device_error_word();   // defined in runtime.cu
 
 // Blocks for a grid-stride kernel of `threads`-thread blocks covering `work`
 // independent items: enough to fill every SM `waves` times, never more than

@@ -21,6 +21,8 @@
 //    8 per-warp accumulators combine through shared memory; the reduced axis is
 //    split into chunks when there are too few column tiles to fill the GPU;
 //  * anything else: one thread per output.
+#include <algorithm>
+
 #include "dct_common.cuh"
 #include "kernels.h"
 
@@ -58,6 +60,17 @@ struct Acc {
   double s = 0.0;
   float v = kMax ? -INFINITY : INFINITY;
   int32_t i = -1;
+  // the identity element (also the state of a lane that saw no input)
+  DCT_DEV void reset() {
+    s = 0.0;
+    v = kMax ? -INFINITY : INFINITY;
+    i = -1;
+  }
+  DCT_DEV static unsigned long long identity_pack() {
+    Acc a;
+    a.reset();
+    return a.pack();
+  }
   DCT_DEV void add(float x, int64_t idx) {
     if constexpr (kArg) {
       // common path: one compare (x <= v is false for a better x and for any NaN)
@@ -152,6 +165,7 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
     const uint64_t l1 = min(len, l0 + chunk_len);
     const float* p = x + row * so;
     Acc<OP> acc;
+    acc.reset();
     if (VEC) {
       uint64_t l = l0 + 4 * (uint64_t)lane;
       for (; l + 3 * 128 + 3 < l1; l += 4 * 128) {
@@ -244,70 +258,6 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
   }
 }
 
-// ---------------------------------------------------------------------------
-// COLUMN-SWEEP kernel (inner <= 4096, contiguous): block (chunk, o) streams
-// whole rows l0..l1 of x[o] -- each row one contiguous run, two rows in
-// flight -- and thread t owns float4 columns t, t+256, ... (VPT of them), so
-// the block's reads sweep memory in address order like the chunked
-// elementwise kernels.  Per-chunk partials are folded in chunk order.
-// ---------------------------------------------------------------------------
-template <int OP, int VPT>
-__global__ void __launch_bounds__(256) k_reduce_colsweep(const float* __restrict__ x, uint64_t len, uint64_t inner,
-                                                         uint64_t so, uint64_t sl, uint32_t chunks,
-                                                         uint64_t chunk_len, float* out, int32_t* out_idx,
-                                                         unsigned long long* part) {
-  const uint32_t w4 = (uint32_t)(inner >> 2);
-  const uint32_t ch = blockIdx.x;
-  const uint64_t o = blockIdx.y;
-  const uint64_t l0 = (uint64_t)ch * chunk_len;
-  const uint64_t l1 = min(len, l0 + chunk_len);
-  const float* base = x + o * so;
-  Acc<OP> acc[VPT][4];
-  uint64_t l = l0;
-  for (; l + 1 < l1; l += 2) {
-    float4 v[2][VPT];
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        const uint32_t c4 = threadIdx.x + 256 * j;
-        if (c4 < w4) v[r][j] = ld_stream4(base + (l + r) * sl + 4ull * c4);
-      }
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        if (threadIdx.x + 256 * j < w4) {
-          const int64_t li = (int64_t)(l + r);
-          acc[j][0].add(v[r][j].x, li); acc[j][1].add(v[r][j].y, li);
-          acc[j][2].add(v[r][j].z, li); acc[j][3].add(v[r][j].w, li);
-        }
-      }
-  }
-  if (l < l1) {
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const uint32_t c4 = threadIdx.x + 256 * j;
-      if (c4 < w4) {
-        const float4 v = ld_stream4(base + l * sl + 4ull * c4);
-        acc[j][0].add(v.x, (int64_t)l); acc[j][1].add(v.y, (int64_t)l);
-        acc[j][2].add(v.z, (int64_t)l); acc[j][3].add(v.w, (int64_t)l);
-      }
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const uint32_t c4 = threadIdx.x + 256 * j;
-    if (c4 >= w4) continue;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint64_t c = 4ull * c4 + q;
-      if (chunks == 1) acc[j][q].store(out, out_idx, o * inner + c, len);
-      else part[(o * chunks + ch) * inner + c] = acc[j][q].pack();
-    }
-  }
-}
-
 // fold chunk partials: out[k] = combine(part[k*stride_k ... with chunk stride])
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
@@ -338,15 +288,14 @@ __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict_
     const uint64_t o = k / inner, c = k - o * inner;
     const float* p = x + o * so + c * si;
     Acc<OP> acc;
+    acc.reset();
     for (uint64_t l = 0; l < len; ++l) acc.add(p[l * sl], (int64_t)l);
     acc.store(out, out_idx, k, len);
   }
 }
 
-constexpr bool kColSweep = false;    // column-sweep plan (kind 3) off: under-occupied without a cluster combine
-
 struct Plan {
-  int kind;           // 0 rows, 1 cols, 2 generic, 3 column sweep
+  int kind;           // 0 rows, 1 cols, 2 generic
   bool vec;
   uint32_t chunks;
   uint64_t chunk_len;
@@ -377,21 +326,6 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
     uint64_t blocks = (warps + kRedWarps - 1) / kRedWarps;
     if (blocks > target_blocks * 4) blocks = target_blocks * 4;
     p.grid = dim3((unsigned)blocks, 1, 1);
-  } else if (kColSweep && si == 1 && inner % 4 == 0 && inner <= 4096 && sl % 4 == 0 && so % 4 == 0 &&
-             aligned16_h(x) && len >= 64 && outer <= 65535) {
-    p.kind = 3;
-    p.vec = true;
-    // about two blocks per SM in total, at least 8 rows per chunk
-    const uint64_t target = (uint64_t)d.sm_count * 2;
-    uint64_t chunks = (target + outer - 1) / outer;
-    const uint64_t max_chunks = len / 8;
-    if (chunks > max_chunks) chunks = max_chunks;
-    if (chunks < 1) chunks = 1;
-    const uint64_t cl = (len + chunks - 1) / chunks;
-    chunks = (len + cl - 1) / cl;
-    p.chunks = (uint32_t)chunks;
-    p.chunk_len = cl;
-    p.grid = dim3((unsigned)chunks, (unsigned)outer, 1);
   } else if (si == 1) {
     p.kind = 1;
     p.vec = (inner % 4 == 0) && (sl % 4 == 0) && (so % 4 == 0) && aligned16_h(x);
@@ -427,8 +361,9 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
   if (len == 0) return cudaErrorInvalidValue;
   Plan p = make_plan(outer, len, inner, so, sl, si, x);
   unsigned long long* part = (unsigned long long*)ws;
-  if (p.chunks > 1) {
-    const size_t need = (size_t)outer * inner * p.chunks * sizeof(unsigned long long);
+  const uint32_t nparts = p.chunks;
+  if (nparts > 1) {
+    const size_t need = (size_t)outer * inner * nparts * sizeof(unsigned long long);
     if (!ws || ws_bytes < need) return cudaErrorInvalidValue;
   }
   if (p.kind == 0) {
@@ -437,21 +372,13 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
   } else if (p.kind == 1) {
     if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
     else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
-  } else if (p.kind == 3) {
-    const uint64_t w4 = inner / 4;
-    if (w4 <= 256)
-      k_reduce_colsweep<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
-    else if (w4 <= 512)
-      k_reduce_colsweep<OP, 2><<<p.grid, kRedThreads, 0, st>>>(x, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
-    else
-      k_reduce_colsweep<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
   } else {
     k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, out, out_idx);
   }
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess || p.chunks == 1) return e;
+  if (e != cudaSuccess || nparts == 1) return e;
   const uint64_t nout = outer * inner;
-  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(part, nout, p.chunks, inner, len, out, out_idx);
+  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(part, nout, nparts, inner, len, out, out_idx);
   return cudaGetLastError();
 }
 
@@ -480,8 +407,9 @@ size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uin
   const float* probes[2] = {nullptr, reinterpret_cast<const float*>(4)};
   for (const float* pr : probes) {
     Plan p = make_plan(outer, len, inner, so, sl, si, pr);
-    if (p.chunks > 1) {
-      size_t b = (size_t)outer * inner * p.chunks * sizeof(unsigned long long);
+    const uint64_t nparts = p.chunks;
+    if (nparts > 1) {
+      size_t b = (size_t)outer * inner * nparts * sizeof(unsigned long long);
       if (b > best) best = b;
     }
   }

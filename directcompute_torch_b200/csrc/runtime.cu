@@ -35,7 +35,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <chrono>
 #include <mutex>
+#include <thread>
 #include <string>
 #include <unordered_map>
 #include <unordered_set>
@@ -43,6 +45,7 @@
 
 #include "dct_common.cuh"
 #include "kernels.h"
+#include "runtime_internal.h"
 #include "../../include/dct_cuda.h"
 
 namespace dct {
@@ -50,13 +53,6 @@ namespace dct {
 // ---------------------------------------------------------------------------
 // engine state
 // ---------------------------------------------------------------------------
-struct Buffer {
-  uint32_t magic;
-  int32_t ref;
-  uint64_t count;          // fp32 elements
-  float* d;
-  bool owned;              // false: wraps caller memory (dct_wrap_device_ptr)
-};
 constexpr uint32_t kBufMagic = 0xDC7B0F01u;
 static_assert(sizeof(DctSeqCmd) == 200 && offsetof(DctSeqCmd, cbData) == 128 && offsetof(DctSeqCmd, cbSize) == 192,
               "DctSeqCmd must match the reference's SeqCmd field layout");
@@ -112,6 +108,8 @@ static void set_error(int code, const char* fmt, ...) {
   g.err_code = code;
   g.err = buf;
 }
+
+uint32_t* device_error_word() { return g.dev_err_dev; }
 
 // error recording for entry points that live outside this file
 void note_error(int code, const char* msg) {
@@ -184,7 +182,7 @@ static Buffer* create_buffer(const float* host, uint64_t count) {
     const bool pinned = cudaPointerGetAttributes(&at, host) == cudaSuccess && at.type == cudaMemoryTypeHost;
     cudaGetLastError();
     cuda_ok(cudaMemcpyAsync(b->d, host, count * sizeof(float), cudaMemcpyHostToDevice, g.stream), "CreateBuffer(H2D)");
-    if (pinned) cudaStreamSynchronize(g.stream);   // caller may reuse its memory on return
+    if (pinned) rt_wait_stream("CreateBuffer");      // caller may reuse its memory on return
   }
   return b;
 }
@@ -226,6 +224,47 @@ static bool ensure_ws(size_t bytes) {
   if (!cuda_ok(cudaMallocAsync(&g.ws, want, g.stream), "workspace(cudaMallocAsync)")) return false;
   g.ws_bytes = want;
   return true;
+}
+
+// ---------------------------------------------------------------------------
+// internal API for the other translation units (runtime_internal.h)
+// ---------------------------------------------------------------------------
+static DistHooks g_hooks;
+DistHooks& rt_dist_hooks() { return g_hooks; }
+std::recursive_mutex& rt_mutex() { return g_mu; }
+Buffer* rt_buf(void* h) { return buf_of(h); }
+cudaStream_t rt_stream() { return g.stream; }
+bool rt_ensure_ws(size_t bytes) { return ensure_ws(bytes); }
+void* rt_ws() { return g.ws; }
+double* rt_host_scratch() { return reinterpret_cast<double*>(g.host_small); }
+bool rt_cuda_ok(cudaError_t e, const char* where) { return cuda_ok(e, where); }
+
+bool rt_wait_stream(const char* where) {
+  if (!g_hooks.async_error) {
+    if (!cuda_ok(cudaStreamSynchronize(g.stream), where)) return false;
+    return check_device_errors();
+  }
+  // a peer that died must not hang this process: poll with a deadline
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(g.stream);
+    if (q == cudaSuccess) return check_device_errors();
+    if (q != cudaErrorNotReady) return cuda_ok(q, where);
+    char msg[256] = {0};
+    if (g_hooks.async_error(msg, sizeof(msg))) {
+      if (g_hooks.abort) g_hooks.abort();
+      set_error(DCT_ERR_DIST, "%s: communicator failed: %s", where, msg);
+      return false;
+    }
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > g_hooks.timeout_s) {
+      if (g_hooks.abort) g_hooks.abort();
+      set_error(DCT_ERR_DIST, "%s: no progress within %.0f s (a peer rank is gone?); communicator aborted", where,
+                g_hooks.timeout_s);
+      return false;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -276,6 +315,10 @@ static bool ensure_init() {
   if (g.init) return true;
   if (init_engine()) return true;
   return false;
+}
+bool rt_init() {
+  LOCK;
+  return ensure_init();
 }
 
 // ---------------------------------------------------------------------------
@@ -858,7 +901,7 @@ DCT_API void UpdateBuffer(void* h, float* data) {
   const bool pinned = cudaPointerGetAttributes(&at, data) == cudaSuccess && at.type == cudaMemoryTypeHost;
   cudaGetLastError();
   cuda_ok(cudaMemcpyAsync(b->d, data, b->count * sizeof(float), cudaMemcpyHostToDevice, g.stream), "UpdateBuffer");
-  if (pinned) cudaStreamSynchronize(g.stream);          // the caller may reuse its memory on return
+  if (pinned) rt_wait_stream("UpdateBuffer");            // the caller may reuse its memory on return
 }
 
 DCT_API void ReleaseBuffer(void* h) {
@@ -881,8 +924,7 @@ DCT_API void ReadBuffer(void* h, float* dst) {
     return;
   }
   cuda_ok(cudaMemcpyAsync(dst, b->d, b->count * sizeof(float), cudaMemcpyDeviceToHost, g.stream), "ReadBuffer");
-  cuda_ok(cudaStreamSynchronize(g.stream), "ReadBuffer(sync)");
-  check_device_errors();
+  rt_wait_stream("ReadBuffer");
 }
 
 DCT_API void ClearBuffer(void* h) {
@@ -899,7 +941,7 @@ DCT_API void FlushGPU() {
 
 DCT_API void SyncGPU() {
   LOCK;
-  if (g.init && cuda_ok(cudaStreamSynchronize(g.stream), "SyncGPU")) check_device_errors();
+  if (g.init) rt_wait_stream("SyncGPU");
 }
 
 DCT_API void RunShader(const char* name, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav, uint32_t* threads,
@@ -982,7 +1024,7 @@ DCT_API float SGDBatchClipped(void** params, void** grads, uint32_t* sizes, uint
   build_table(params, grads, sizes, n, t3, true);       // phase 3: param and grad present
   if (!cuda_ok(launch_mt_sgd(t3.data(), (int)t3.size(), lr, 0.0f, ns, g.stream), "SGDBatchClipped(sgd)")) return 0.0f;
   cuda_ok(cudaMemcpyAsync(g.host_small, ns, 2 * sizeof(float), cudaMemcpyDeviceToHost, g.stream), "SGDBatchClipped(D2H)");
-  cuda_ok(cudaStreamSynchronize(g.stream), "SGDBatchClipped(sync)");
+  rt_wait_stream("SGDBatchClipped");
   return g.host_small[0];
 }
 
@@ -1062,7 +1104,7 @@ DCT_API void DrainPool() {
   g.pool.clear();
   g.pool_bytes = 0;
   if (g.init) {
-    cudaStreamSynchronize(g.stream);
+    rt_wait_stream("DrainPool");
     cudaMemPool_t mp;
     if (cudaDeviceGetDefaultMemPool(&mp, g.info.device) == cudaSuccess) cudaMemPoolTrimTo(mp, 0);
   }
@@ -1143,8 +1185,8 @@ DCT_API void* dct_stream() {
 DCT_API int dct_synchronize() {
   LOCK;
   if (!ensure_init()) return DCT_ERR_NO_DEVICE;
-  if (!cuda_ok(cudaStreamSynchronize(g.stream), "dct_synchronize")) return DCT_ERR_CUDA;
-  return check_device_errors() ? 0 : DCT_ERR_CUDA;
+  if (rt_wait_stream("dct_synchronize")) return 0;
+  return g.err_code ? g.err_code : DCT_ERR_CUDA;
 }
 
 DCT_API int dct_timer_start() {
@@ -1158,7 +1200,7 @@ DCT_API float dct_timer_stop_ms() {
   if (!ensure_init()) return -1.0f;
   float ms = -1.0f;
   if (!cuda_ok(cudaEventRecord(g.ev1, g.stream), "dct_timer_stop")) return -1.0f;
-  if (!cuda_ok(cudaEventSynchronize(g.ev1), "dct_timer_stop(sync)")) return -1.0f;
+  if (!rt_wait_stream("dct_timer_stop")) return -1.0f;
   if (!cuda_ok(cudaEventElapsedTime(&ms, g.ev0, g.ev1), "dct_timer_stop(elapsed)")) return -1.0f;
   if (!check_device_errors()) return -1.0f;
   return ms;
@@ -1209,7 +1251,7 @@ DCT_API int dct_copy_d2h(void* h, void* dst, uint64_t offset_floats, uint64_t co
   if (!b || !dst) return DCT_ERR_HANDLE;
   if (offset_floats + count > b->count) return DCT_ERR_SIZE;
   if (!cuda_ok(cudaMemcpyAsync(dst, b->d + offset_floats, count * 4, cudaMemcpyDeviceToHost, g.stream), "dct_copy_d2h")) return DCT_ERR_CUDA;
-  return cuda_ok(cudaStreamSynchronize(g.stream), "dct_copy_d2h(sync)") ? 0 : DCT_ERR_CUDA;
+  return rt_wait_stream("dct_copy_d2h") ? 0 : (g.err_code ? g.err_code : DCT_ERR_CUDA);
 }
 
 DCT_API void* dct_host_alloc(uint64_t bytes) {
@@ -1246,7 +1288,7 @@ DCT_API int dct_scatter(void* h, const int64_t* host_idx, const float* host_vals
   cudaMemcpyAsync(dv, host_vals, k * 4, cudaMemcpyHostToDevice, g.stream);
   cudaError_t e = launch_scatter_values(x->d, di, dv, k, g.stream);
   cudaFreeAsync(dmem, g.stream);
-  cudaStreamSynchronize(g.stream);
+  rt_wait_stream("dct_scatter");
   return cuda_ok(e, "dct_scatter") ? 0 : DCT_ERR_CUDA;
 }
 
@@ -1324,7 +1366,7 @@ DCT_API int dct_reduce_all(int op, void* x, uint64_t n, void* out, double* host_
   if (!cuda_ok(launch_full_reduce(op, bx->d, n, bo->d, d64, g.ws, g.stream), "dct_reduce_all")) return DCT_ERR_CUDA;
   if (host_out64) {
     if (!cuda_ok(cudaMemcpyAsync(g.host_small, d64, 8, cudaMemcpyDeviceToHost, g.stream), "dct_reduce_all(D2H)")) return DCT_ERR_CUDA;
-    if (!cuda_ok(cudaStreamSynchronize(g.stream), "dct_reduce_all(sync)")) return DCT_ERR_CUDA;
+    if (!rt_wait_stream("dct_reduce_all")) return g.err_code ? g.err_code : DCT_ERR_CUDA;
     memcpy(host_out64, g.host_small, 8);
   }
   return 0;

@@ -192,3 +192,22 @@ def test_adam_bitexact(dev):
     _same(dev.read(hm), m)
     _same(dev.read(hv), v)
     dev.free(hw, hm, hv, hg)
+
+
+@pytest.mark.parametrize("shape", [(6, 40, 512), (3, 1000, 4096), (2, 9, 8192), (5, 64, 12)])
+def test_middle_axis_reductions(dev, shape):
+    """[outer, len, inner] reduced over the middle axis (column kernels with outer > 1)."""
+    P, L, Q = shape
+    x = _R(P * L, Q, seed=P + L + Q).reshape(P, L, Q)
+    hx = dev.buf(x)
+    ho, hi = dev.empty(P * Q), dev.empty(P * Q)
+    x64 = x.astype(np.float64)
+    dev.reduce("sum", hx, P, L, Q, ho)
+    want = x64.sum(axis=1).ravel()
+    err = np.abs(dev.read(ho) - want) / np.maximum(np.abs(want), 1.0)
+    assert err.max() < 1e-6
+    dev.reduce("argmax", hx, P, L, Q, hi)
+    assert np.array_equal(dev.read(hi, np.int32), x.argmax(axis=1).ravel())
+    dev.reduce("min", hx, P, L, Q, ho)
+    _same(dev.read(ho), x.min(axis=1).ravel())
+    dev.free(hx, ho, hi)
