@@ -54,9 +54,10 @@ C2_BINARY = ("add", "sub", "mul", "div", "maximum")
 C2_OUTER = ("mul", "add")
 C2_UNARY = ("exp", "log_abs1p", "tanh", "sigmoid")
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from the ncu capture
-# summarised in profiles/c2_rowbcast_add_ncu.md (small case scaled to a full launch)
-NCU_TRAFFIC_BYTES = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one full-size launch, from the
+# ncu capture summarised in profiles/k_rowvec_chunk_c2_rowbcast_add.md (the
+# bench's own workload: 512 MB on the device, one launch captured)
+NCU_TRAFFIC_BYTES = {"c2_rowbcast": 483_056_128}
 
 
 def _peaks():
