@@ -319,10 +319,14 @@ PER_OP_SECTIONS = {"c3": ("c3_sum_axis-1", "c3_sum_axis0", "c3_mean_axis-1", "c3
                    "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd")}
 
 
-def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, warmup: int = 3):
+def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, warmup: int = 3, comm=None):
     """C3 / C4 / C5a / C5b ops: (name, algorithmic bytes, avg ms per call, launches per call).
 
-    With `only`, just that op is set up and run (`warmup` untimed + `iters` timed calls)."""
+    With `only`, just that op is set up and run (`warmup` untimed + `iters` timed calls).
+    With a communicator (N > 1) every rank holds the single-GPU shard (weak
+    scaling) and the ops whose result spans shards -- axis-0 and full
+    reductions, the softmax-CE loss, BatchNorm statistics -- run through the
+    sharded dct_dist_* entry points (one NCCL all-gather each)."""
     C = L.C
     lib = L.lib
     res = {}
@@ -344,26 +348,29 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, wa
     out = L.new(R_ROWS)
     oidx = L.new(R_ROWS)
     if section("c3"):
-        _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS)
+        _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS, comm)
     if section("c3f"):
         V = L.new(1 << 30)
         L.fill(V, 2 + 1000 * rank, 7, 0, -1.0, 1.0)
-        measure("c3_fullsum_2^30", 4 << 30, lambda: L.check(lib.dct_reduce_all(0, V, 1 << 30, out, None), "fullsum"),
-                2, it=5)
+        if comm is None:
+            fs = lambda: L.check(lib.dct_reduce_all(0, V, 1 << 30, out, None), "fullsum")  # noqa: E731
+        else:
+            fs = lambda: comm.reduce_all("sum", V, 1 << 30, out)  # noqa: E731
+        measure("c3_fullsum_2^30", 4 << 30, fs, 2 if comm is None else 5, it=5)
         lib.ReleaseBuffer(V)
     lib.ReleaseBuffer(out)
     lib.ReleaseBuffer(oidx)
     if section("c4"):
-        _c4(L, rank, measure)
+        _c4(L, rank, measure, comm)
     if section("c5a"):
         _c5a(L, rank, measure)
     if section("c5b"):
-        _c5b(L, rank, measure)
+        _c5b(L, rank, measure, comm)
     lib.DrainPool()
     return res
 
 
-def _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS):
+def _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS, comm=None):
     C, lib = L.C, L.lib
     R = L.new(R_ROWS * R_COLS)
     L.fill(R, 2 + 1000 * rank, 0, 1, 0.0, 1.0)
@@ -376,13 +383,18 @@ def _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS):
     for op in ("sum", "mean", "max", "argmax"):
         measure(f"c3_{op}_axis-1", rbytes + 4 * R_ROWS,
                 lambda op=op: L.check(lib.dct_reduce(L.REDUCE[op], R, R_ROWS, R_COLS, 1, out, None), op), 1)
-        measure(f"c3_{op}_axis0", rbytes + 4 * R_COLS,
-                lambda op=op: L.check(lib.dct_reduce(L.REDUCE[op], R, 1, R_ROWS, R_COLS, out, None), op), 2)
+        if comm is None:
+            measure(f"c3_{op}_axis0", rbytes + 4 * R_COLS,
+                    lambda op=op: L.check(lib.dct_reduce(L.REDUCE[op], R, 1, R_ROWS, R_COLS, out, None), op), 2)
+        else:                      # rows of a [R_ROWS * world, R_COLS] matrix, reduced over all of them
+            total = R_ROWS * comm.world
+            measure(f"c3_{op}_axis0", rbytes + 4 * R_COLS,
+                    lambda op=op: comm.reduce(op, R, 1, R_ROWS, R_COLS, R_ROWS * comm.rank, total, out), 5)
     lib.ReleaseBuffer(R)
 
 
-def _c4(L, rank, measure):
-    """C4: fused softmax + CE fwd+bwd on [65536,1000], int labels (seed 3)."""
+def _c4(L, rank, measure, comm=None):
+    """C4: fused softmax + CE fwd+bwd on [65536,1000] per rank, int labels (seed 3)."""
     lib = L.lib
     B, K = 65536, 1000
     X = L.new(B * K)
@@ -391,8 +403,13 @@ def _c4(L, rank, measure):
     Lb = L.new(B)
     L.check(lib.dct_copy_h2d(Lb, lab.ctypes.data, 0, B), "labels")
     P, G, LS = L.new(B * K), L.new(B * K), L.new(1)
-    measure("c4_softmax_ce_fused", 4 * (3 * B * K + B) + 4,
-            lambda: L.check(lib.dct_softmax_ce(X, Lb, 1, B, K, P, G, LS, None, float(B), float(B)), "softmax_ce"), 2)
+    if comm is None:
+        measure("c4_softmax_ce_fused", 4 * (3 * B * K + B) + 4,
+                lambda: L.check(lib.dct_softmax_ce(X, Lb, 1, B, K, P, G, LS, None, float(B), float(B)), "smce"), 2)
+    else:
+        measure("c4_softmax_ce_fused", 4 * (3 * B * K + B) + 4,
+                lambda: comm.softmax_ce(X, Lb, B, K, probs=P, dlogits=G, loss=LS, global_rows=B * comm.world,
+                                        labels_int32=True), 6)
     for h in (X, Lb, P, G, LS):
         lib.ReleaseBuffer(h)
 
@@ -417,8 +434,8 @@ def _c5a(L, rank, measure):
         lib.ReleaseBuffer(h)
 
 
-def _c5b(L, rank, measure):
-    """C5b: BatchNorm train fwd / bwd on [256,256,56,56] (seed 4)."""
+def _c5b(L, rank, measure, comm=None):
+    """C5b: BatchNorm train fwd / bwd on [256,256,56,56] per rank (seed 4)."""
     lib = L.lib
     N, Cc, S = 256, 256, 56 * 56
     nx = N * Cc * S
@@ -430,10 +447,17 @@ def _c5b(L, rank, measure):
         arr = np.full(Cc, v, np.float32)
         L.check(lib.dct_copy_h2d(h, arr.ctypes.data, 0, Cc), "bn init")
     lib.dct_synchronize()
-    measure("c5b_batchnorm_fwd", 4 * 3 * nx,
-            lambda: L.check(lib.dct_batchnorm_forward_train(x, gam, bet, rm, rv, bm, bv, y, N, Cc, S, 1e-5, 0.1), "bnf"), 4)
-    measure("c5b_batchnorm_bwd", 4 * 5 * nx,
-            lambda: L.check(lib.dct_batchnorm_backward(x, dy, bm, bv, gam, dg, db, dx, N, Cc, S, 1e-5), "bnb"), 4)
+    if comm is None:
+        measure("c5b_batchnorm_fwd", 4 * 3 * nx,
+                lambda: L.check(lib.dct_batchnorm_forward_train(x, gam, bet, rm, rv, bm, bv, y, N, Cc, S, 1e-5, 0.1),
+                                "bnf"), 4)
+        measure("c5b_batchnorm_bwd", 4 * 5 * nx,
+                lambda: L.check(lib.dct_batchnorm_backward(x, dy, bm, bv, gam, dg, db, dx, N, Cc, S, 1e-5), "bnb"), 4)
+    else:
+        measure("c5b_batchnorm_fwd", 4 * 3 * nx,
+                lambda: comm.batchnorm_forward_train(x, gam, bet, rm, rv, bm, bv, y, N, Cc, S, 1e-5, 0.1), 7)
+        measure("c5b_batchnorm_bwd", 4 * 5 * nx,
+                lambda: comm.batchnorm_backward(x, dy, bm, bv, gam, dg, db, dx, N, Cc, S, 1e-5), 7)
     for h in (x, dy, y, dx, gam, bet, rm, rv, bm, bv, dg, db):
         lib.ReleaseBuffer(h)
 
@@ -545,7 +569,13 @@ def main():
         e2e = {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
     per_op = {}
     if not args.no_per_op:
-        per_op = per_op_suite(L, ranks.rank)
+        comm = None
+        if world > 1:
+            from directcompute_torch_b200.dist import Communicator
+            comm = Communicator.from_process_group(timeout_s=120)
+        per_op = per_op_suite(L, ranks.rank, comm=comm)
+        if comm is not None:
+            comm.close()
         if world > 1:
             for k in per_op:
                 per_op[k]["ms"] = ranks.max(per_op[k]["ms"])

@@ -107,6 +107,24 @@ SIGNATURES = {
     "dct_batchnorm_forward_train": ([VP] * 8 + [U32, U32, U32, F32, F32], C.c_int),
     "dct_batchnorm_backward": ([VP] * 8 + [U32, U32, U32, F32], C.c_int),
     "dct_batchnorm_forward_train_noalloc": ([VP] * 8 + [U32, U32, U32, F32, F32, VP], C.c_int),
+    # sharding over NCCL
+    "dct_dist_available": ([], C.c_int),
+    "dct_dist_nccl_version": ([], C.c_int),
+    "dct_dist_shard": ([U64, C.c_int, C.c_int, C.POINTER(U64), C.POINTER(U64)], C.c_int),
+    "dct_dist_unique_id": ([VP, C.c_int], C.c_int),
+    "dct_dist_init": ([VP, C.c_int, C.c_int, C.c_int, C.c_double], C.c_int),
+    "dct_dist_finalize": ([], C.c_int),
+    "dct_dist_rank": ([], C.c_int),
+    "dct_dist_world": ([], C.c_int),
+    "dct_dist_allreduce": ([VP, U64, C.c_int], C.c_int),
+    "dct_dist_broadcast": ([VP, U64, C.c_int], C.c_int),
+    "dct_dist_barrier": ([], C.c_int),
+    "dct_dist_reduce": ([C.c_int, VP, U64, U64, U64, U64, U64, VP, VP], C.c_int),
+    "dct_dist_reduce_all": ([C.c_int, VP, U64, VP, C.POINTER(C.c_double)], C.c_int),
+    "dct_dist_softmax_ce": ([VP, VP, C.c_int, U32, U32, VP, VP, VP, VP, F32, F32], C.c_int),
+    "dct_dist_batchnorm_forward_train": ([VP] * 8 + [U32, U32, U32, F32, F32], C.c_int),
+    "dct_dist_batchnorm_backward": ([VP] * 8 + [U32, U32, U32, F32], C.c_int),
+    "dct_selftest_bounded_wait": ([U32], C.c_int),
 }
 
 #: the 32 symbols of the reference engine (31 bound by nn_engine.py + SyncGPU)

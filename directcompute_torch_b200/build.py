@@ -24,11 +24,28 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libdct_cuda.so")
 INCLUDE = os.path.join(ROOT, "include")
 
+
+
+def _nccl_include() -> list[str]:
+    """nccl.h for the sharding layer (types and the config initializer only: the
+    library itself is dlopen'ed at run time).  The copy shipped with the NCCL
+    that PyTorch loads comes first, then the system one."""
+    try:
+        import nvidia.nccl as _n  # the wheel PyTorch's CUDA build depends on
+        for base in list(getattr(_n, "__path__", [])):
+            inc = os.path.join(base, "include")
+            if os.path.exists(os.path.join(inc, "nccl.h")):
+                return ["-I" + inc]
+    except ImportError:
+        pass
+    return []
+
+
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3", "-lineinfo", "-std=c++17", "--fmad=false", "-prec-div=true", "-prec-sqrt=true",
     "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3", "--expt-relaxed-constexpr",
-    "-I" + INCLUDE, "-I" + CSRC,
+    "-I" + INCLUDE, "-I" + CSRC, *_nccl_include(),
 ]
 
 

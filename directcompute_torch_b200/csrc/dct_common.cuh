@@ -23,8 +23,12 @@ struct DevInfo {
   size_t total_mem = 0;
 };
 const DevInfo& dev_info();   // defined in runtime.cu
-// device-visible error word for bounded waits (mapped host memory; null before
-// InitEngine, then kernels skip the report)
+// device-visible error word (mapped host memory; null before InitEngine, then
+// kernels skip the report).  Bits:
+enum : uint32_t {
+  DCT_DEVERR_WAIT_TIMEOUT = 1u,    // a bounded wait in a kernel ran out
+  DCT_DEVERR_PEER_INVALID = 2u,    // a rank's shard of a sharded op was invalid
+};
 uint32_t* device_error_word();   // defined in runtime.cu
 
 // Blocks for a grid-stride kernel of `threads`-thread blocks covering `work`

@@ -13,9 +13,6 @@
 
 namespace dct {
 
-// error word set by device code (mapped host memory; DCT_DEVERR_* bits)
-enum : uint32_t { DCT_DEVERR_WAIT_TIMEOUT = 1u };
-
 DCT_DEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 DCT_DEV void mbar_init(uint64_t* bar, uint32_t count) {
@@ -42,9 +39,10 @@ DCT_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`; false (and the error bit set) on timeout.
-DCT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-  for (uint32_t spins = 0; spins < (1u << 22); ++spins)
+// Bounded wait for phase `parity` of `bar`: at most `limit` polls; false (and
+// the error bit set) when they run out.
+DCT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t limit = 1u << 22) {
+  for (uint32_t spins = 0; spins < limit; ++spins)
     if (mbar_try_wait(bar, parity)) return true;
   if (err) atomicOr(err, DCT_DEVERR_WAIT_TIMEOUT);
   return false;

@@ -1,0 +1,661 @@
+// Sharding layer of libdct_cuda: one process per GPU, NCCL over NVLink/NVSwitch.
+//
+// The reference drives a single D3D11 device and has no multi-GPU path
+// (engine.cpp:61-129 creates one device and one immediate context).  These
+// dct_dist_* entry points are the data-parallel extension of its hot path.
+// Each rank holds one contiguous shard of the sharded axis (rows of C2/C3/C4,
+// the batch N of C5b, a flat slice of C5a), and the ops whose result depends on
+// other shards make exactly one exchange:
+//
+//   axis reduction over the sharded axis   one packed 8-byte partial per output
+//   full reduction                          (float64 value, count)
+//   softmax-CE loss                         (float64 sum of row losses, rows)
+//   BatchNorm statistics / backward sums    C x 2 float64 channel sums + count
+//
+// Every exchange is one ncclAllGather of fixed-size records into a [world]
+// array, folded on the device in rank order: results are identical on every
+// rank and from run to run, and at world size 1 bit-identical to the
+// single-GPU entry points.  Each record ends with a header (shard offset,
+// count, validity); a rank whose arguments are bad still takes part with an
+// invalid header, so all ranks take the same collective steps and all of them
+// report the failure (DCT_ERR_DIST at the next wait) instead of hanging.
+//
+// NCCL is loaded with dlopen (DCT_NCCL_LIB, else an already-loaded
+// libnccl.so.2, else the loader's libnccl.so.2), so the library loads and runs
+// single-GPU work where NCCL is absent.  With an NCCL at least as new as the
+// headers this file was built with, the communicator is non-blocking: init and
+// every collective are polled against the deadline given to dct_dist_init, and
+// while a communicator is active every wait of the library polls the stream,
+// the communicator's asynchronous error and the deadline, and aborts the
+// communicator on failure (a peer that died cannot hang this process).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <chrono>
+#include <mutex>
+#include <string>
+#include <thread>
+
+#include "dct_common.cuh"
+#include "kernels.h"
+#include "runtime_internal.h"
+#include "../../include/dct_cuda.h"
+
+namespace dct {
+namespace {
+
+struct NcclApi {
+  void* h = nullptr;
+  int version = 0;
+  decltype(&ncclGetVersion) GetVersion = nullptr;
+  decltype(&ncclGetUniqueId) GetUniqueId = nullptr;
+  decltype(&ncclCommInitRank) CommInitRank = nullptr;
+  decltype(&ncclCommInitRankConfig) CommInitRankConfig = nullptr;
+  decltype(&ncclCommGetAsyncError) CommGetAsyncError = nullptr;
+  decltype(&ncclCommAbort) CommAbort = nullptr;
+  decltype(&ncclCommFinalize) CommFinalize = nullptr;
+  decltype(&ncclCommDestroy) CommDestroy = nullptr;
+  decltype(&ncclAllGather) AllGather = nullptr;
+  decltype(&ncclAllReduce) AllReduce = nullptr;
+  decltype(&ncclBroadcast) Broadcast = nullptr;
+  decltype(&ncclGetErrorString) GetErrorString = nullptr;
+  decltype(&ncclGetLastError) GetLastError = nullptr;
+};
+
+struct DistState {
+  NcclApi api;
+  std::string load_error;
+  ncclComm_t comm = nullptr;
+  bool nonblocking = false;
+  int world = 0, rank = -1;
+  double timeout_s = 120.0;
+  bool aborted = false;
+  // exchange buffers (device, stream-ordered)
+  void* send = nullptr;
+  size_t send_bytes = 0;
+  void* recv = nullptr;
+  size_t recv_bytes = 0;
+  double* fold = nullptr;          // folded sums / counts (float64)
+  size_t fold_bytes = 0;
+};
+DistState D;
+
+#define DLOCK std::lock_guard<std::recursive_mutex> _dlk(rt_mutex())
+
+template <class F>
+bool sym(F& f, const char* name) {
+  f = reinterpret_cast<F>(dlsym(D.api.h, name));
+  return f != nullptr;
+}
+
+bool load_nccl() {
+  if (D.api.h) return true;
+  void* h = nullptr;
+  const char* env = getenv("DCT_NCCL_LIB");
+  if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_LOCAL);
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+  if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+  if (!h) {
+    const char* e = dlerror();
+    D.load_error = std::string("NCCL not found (set DCT_NCCL_LIB): ") + (e ? e : "");
+    return false;
+  }
+  D.api.h = h;
+  bool ok = sym(D.api.GetVersion, "ncclGetVersion") && sym(D.api.GetUniqueId, "ncclGetUniqueId") &&
+            sym(D.api.CommInitRank, "ncclCommInitRank") && sym(D.api.CommGetAsyncError, "ncclCommGetAsyncError") &&
+            sym(D.api.CommAbort, "ncclCommAbort") && sym(D.api.CommDestroy, "ncclCommDestroy") &&
+            sym(D.api.AllGather, "ncclAllGather") && sym(D.api.AllReduce, "ncclAllReduce") &&
+            sym(D.api.Broadcast, "ncclBroadcast") && sym(D.api.GetErrorString, "ncclGetErrorString");
+  sym(D.api.CommInitRankConfig, "ncclCommInitRankConfig");
+  sym(D.api.CommFinalize, "ncclCommFinalize");
+  sym(D.api.GetLastError, "ncclGetLastError");
+  if (!ok) {
+    D.load_error = "the NCCL library lacks a required symbol";
+    dlclose(h);
+    D.api = NcclApi{};
+    return false;
+  }
+  D.api.GetVersion(&D.api.version);
+  return true;
+}
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+void fail(const char* where, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void fail(const char* where, const char* fmt, ...) {
+  char body[384], msg[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(body, sizeof(body), fmt, ap);
+  va_end(ap);
+  snprintf(msg, sizeof(msg), "%s: %s", where, body);
+  note_error(DCT_ERR_DIST, msg);
+}
+
+void abort_comm() {
+  if (D.comm) D.api.CommAbort(D.comm);
+  D.comm = nullptr;
+  D.aborted = true;
+  rt_dist_hooks() = DistHooks{};
+}
+
+const char* nccl_msg(ncclResult_t r) {
+  static thread_local char buf[320];
+  const char* last = (D.comm && D.api.GetLastError) ? D.api.GetLastError(D.comm) : "";
+  snprintf(buf, sizeof(buf), "%s%s%s", D.api.GetErrorString(r), last && *last ? " / " : "", last ? last : "");
+  return buf;
+}
+
+// Bring an NCCL call to completion of its enqueue (non-blocking communicators
+// answer ncclInProgress); on failure or past the deadline abort the communicator.
+bool settle(ncclResult_t r, const char* where) {
+  if (r == ncclSuccess) return true;
+  if (r == ncclInProgress && D.comm) {
+    const double t0 = now_s();
+    for (;;) {
+      ncclResult_t st = ncclSuccess;
+      D.api.CommGetAsyncError(D.comm, &st);
+      if (st == ncclSuccess) return true;
+      if (st != ncclInProgress) { r = st; break; }
+      if (now_s() - t0 > D.timeout_s) {
+        fail(where, "NCCL did not complete within %.0f s; communicator aborted", D.timeout_s);
+        abort_comm();
+        return false;
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+  }
+  fail(where, "NCCL error: %s; communicator aborted", nccl_msg(r));
+  abort_comm();
+  return false;
+}
+
+bool hook_async_error(char* msg, int len) {
+  if (!D.comm) return false;
+  ncclResult_t st = ncclSuccess;
+  if (D.api.CommGetAsyncError(D.comm, &st) != ncclSuccess) return false;
+  if (st == ncclSuccess || st == ncclInProgress) return false;
+  snprintf(msg, len, "%s", nccl_msg(st));
+  return true;
+}
+void hook_abort() { abort_comm(); }
+
+bool need_comm(const char* where) {
+  if (D.comm) return true;
+  fail(where, "%s", D.aborted ? "the communicator was aborted after a failure; dct_dist_finalize, then dct_dist_init"
+                              : "no communicator (call dct_dist_init)");
+  return false;
+}
+
+bool grow(void*& p, size_t& have, size_t want, const char* where) {
+  if (have >= want) return true;
+  cudaStream_t st = rt_stream();
+  if (p) cudaFreeAsync(p, st);
+  p = nullptr;
+  have = 0;
+  want = (want + 255) & ~size_t(255);
+  if (!rt_cuda_ok(cudaMallocAsync(&p, want, st), where)) return false;
+  have = want;
+  return true;
+}
+
+bool buffers(size_t send, size_t recv, size_t fold, const char* where) {
+  return grow(D.send, D.send_bytes, send, where) && grow(D.recv, D.recv_bytes, recv, where) &&
+         grow(reinterpret_cast<void*&>(D.fold), D.fold_bytes, fold, where);
+}
+
+bool all_gather(const void* send, void* recv, size_t count_u64, const char* where) {
+  return settle(D.api.AllGather(send, recv, count_u64, ncclUint64, D.comm, rt_stream()), where);
+}
+
+// ---------------------------------------------------------------------------
+// record headers and rank-order folds
+// ---------------------------------------------------------------------------
+// header of a reduction shard record: [offset, len, len_total, valid]
+__global__ void k_put_header_u64(unsigned long long* h, unsigned long long a, unsigned long long b,
+                                 unsigned long long c, unsigned long long d) {
+  if (threadIdx.x == 0) { h[0] = a; h[1] = b; h[2] = c; h[3] = d; }
+}
+// writes the first n (<= 4) of a, b, c, d to h
+__global__ void k_put_f64(double* h, int n, double a, double b, double c, double d) {
+  if (threadIdx.x != 0) return;
+  const double v[4] = {a, b, c, d};
+  for (int i = 0; i < n && i < 4; ++i) h[i] = v[i];
+}
+
+// Shards of an axis reduction must tile [0, len_total) in rank order and agree
+// on len_total; any invalid or inconsistent header marks the result invalid.
+__global__ void k_check_axis_shards(const unsigned long long* all, int world, uint64_t stride, uint64_t nout,
+                                    uint32_t* err) {
+  if (threadIdx.x != 0) return;
+  unsigned long long expect = 0, total = all[nout + 2];
+  bool ok = true;
+  for (int r = 0; r < world; ++r) {
+    const unsigned long long* h = all + (uint64_t)r * stride + nout;
+    ok &= (h[3] == 1ull) && (h[0] == expect) && (h[2] == total);
+    expect += h[1];
+  }
+  ok &= (expect == total);
+  if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
+}
+
+// Full reduction records [value, count, valid, -]: fold in rank order.
+// post: 0 none, 1 mean (divide by the total count).
+__global__ void k_fold_full(const double* all, int world, int op, int post, float* out32, double* out64,
+                            uint32_t* err) {
+  if (threadIdx.x != 0) return;
+  double acc = 0.0, cnt = 0.0;
+  bool ok = true, first = true;
+  const bool ext = (op == RED_MAX || op == RED_MIN);
+  for (int r = 0; r < world; ++r) {
+    const double* rec = all + 4 * r;
+    ok &= (rec[2] == 1.0);
+    cnt += rec[1];
+    if (ext) {
+      if (rec[1] == 0.0) continue;                       // empty shard: no candidate
+      const double v = rec[0];
+      if (first || isnan(v) || (!isnan(acc) && (op == RED_MAX ? v > acc : v < acc))) acc = v;
+      first = false;
+    } else {
+      acc = first ? rec[0] : acc + rec[0];
+      first = false;
+    }
+  }
+  if (ext && first) ok = false;                          // max / min of nothing
+  if (post == 1) acc = acc / cnt;
+  if (!ok) {
+    acc = (double)NAN;
+    if (err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
+  }
+  if (out32) out32[0] = (float)acc;
+  if (out64) out64[0] = acc;
+}
+
+// Softmax-CE records [sum of row losses, rows, valid, -] -> loss = sum / div
+__global__ void k_fold_loss(const double* all, int world, double div, float* loss, uint32_t* err) {
+  if (threadIdx.x != 0) return;
+  double acc = 0.0;
+  bool ok = true;
+  for (int r = 0; r < world; ++r) {
+    ok &= (all[4 * r + 2] == 1.0);
+    acc = r == 0 ? all[0] : acc + all[4 * r];
+  }
+  if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
+  if (loss) loss[0] = ok ? (float)(acc / div) : NAN;
+}
+
+// Channel-sum records [nsum sums][count, valid, nsum, -]: out[j] = sum over
+// ranks in rank order; out[nsum] = total count.
+__global__ void k_fold_sums(const double* all, int world, uint32_t nsum, double* out, uint32_t* err) {
+  const uint64_t stride = (uint64_t)nsum + 4;
+  const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j < nsum) {
+    double acc = all[j];
+    for (int r = 1; r < world; ++r) acc += all[(uint64_t)r * stride + j];
+    out[j] = acc;
+  } else if (j == nsum) {
+    double cnt = 0.0;
+    bool ok = true;
+    for (int r = 0; r < world; ++r) {
+      const double* h = all + (uint64_t)r * stride + nsum;
+      cnt += h[0];
+      ok &= (h[1] == 1.0) && (h[2] == (double)nsum);
+    }
+    out[nsum] = cnt;
+    if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
+  }
+}
+
+Buffer* live(void* h) { return h ? rt_buf(h) : nullptr; }
+
+}  // namespace
+}  // namespace dct
+
+using namespace dct;
+
+extern "C" {
+
+DCT_API int dct_dist_available(void) {
+  DLOCK;
+  return load_nccl() ? 1 : 0;
+}
+
+DCT_API int dct_dist_nccl_version(void) {
+  DLOCK;
+  return load_nccl() ? D.api.version : 0;
+}
+
+DCT_API int dct_dist_shard(uint64_t n, int world, int rank, uint64_t* offset, uint64_t* count) {
+  if (world < 1 || rank < 0 || rank >= world || !offset || !count) return DCT_ERR_ARG;
+  const uint64_t base = n / (uint64_t)world, rem = n % (uint64_t)world;
+  const uint64_t r = (uint64_t)rank;
+  *count = base + (r < rem ? 1 : 0);
+  *offset = r * base + (r < rem ? r : rem);
+  return 0;
+}
+
+DCT_API int dct_dist_unique_id(void* out, int len) {
+  DLOCK;
+  if (!out || len < (int)sizeof(ncclUniqueId)) {
+    note_error(DCT_ERR_ARG, "dct_dist_unique_id: the output needs 128 bytes");
+    return DCT_ERR_ARG;
+  }
+  if (!load_nccl()) { note_error(DCT_ERR_DIST, D.load_error.c_str()); return DCT_ERR_DIST; }
+  ncclUniqueId id;
+  const ncclResult_t r = D.api.GetUniqueId(&id);
+  if (r != ncclSuccess) {
+    fail("dct_dist_unique_id", "%s", D.api.GetErrorString(r));
+    return DCT_ERR_DIST;
+  }
+  memcpy(out, &id, sizeof(id));
+  return 0;
+}
+
+DCT_API int dct_dist_init(const void* id, int len, int nranks, int rank, double timeout_s) {
+  DLOCK;
+  if (!id || len < (int)sizeof(ncclUniqueId) || nranks < 1 || rank < 0 || rank >= nranks) {
+    note_error(DCT_ERR_ARG, "dct_dist_init: need a 128-byte id and 0 <= rank < nranks");
+    return DCT_ERR_ARG;
+  }
+  if (D.comm) { note_error(DCT_ERR_DIST, "dct_dist_init: already initialised (dct_dist_finalize first)"); return DCT_ERR_DIST; }
+  if (!load_nccl()) { note_error(DCT_ERR_DIST, D.load_error.c_str()); return DCT_ERR_DIST; }
+  if (!rt_init()) return DCT_ERR_NO_DEVICE;
+  if (!rt_cuda_ok(cudaSetDevice(dev_info().device), "dct_dist_init(cudaSetDevice)")) return DCT_ERR_CUDA;
+  D.timeout_s = timeout_s > 0 ? timeout_s : 120.0;
+  D.aborted = false;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclComm_t comm = nullptr;
+  ncclResult_t r;
+  D.nonblocking = D.api.CommInitRankConfig && D.api.version >= NCCL_VERSION_CODE;
+  if (D.nonblocking) {
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    r = D.api.CommInitRankConfig(&comm, nranks, uid, rank, &cfg);
+  } else {
+    r = D.api.CommInitRank(&comm, nranks, uid, rank);   // blocking: no init deadline with this NCCL
+  }
+  D.comm = comm;
+  if (!settle(r, "dct_dist_init")) return DCT_ERR_DIST;
+  D.world = nranks;
+  D.rank = rank;
+  DistHooks& hk = rt_dist_hooks();
+  hk.async_error = &hook_async_error;
+  hk.abort = &hook_abort;
+  hk.timeout_s = D.timeout_s;
+  return 0;
+}
+
+DCT_API int dct_dist_finalize(void) {
+  DLOCK;
+  int rc = 0;
+  if (D.comm) {
+    if (!rt_wait_stream("dct_dist_finalize")) rc = DCT_ERR_DIST;
+    if (D.comm && D.api.CommFinalize) {
+      if (!settle(D.api.CommFinalize(D.comm), "dct_dist_finalize")) rc = DCT_ERR_DIST;
+    }
+    if (D.comm) D.api.CommDestroy(D.comm);
+  }
+  D.comm = nullptr;
+  rt_dist_hooks() = DistHooks{};
+  D.world = 0;
+  D.rank = -1;
+  D.aborted = false;
+  cudaStream_t st = rt_stream();
+  for (void** p : {&D.send, &D.recv, reinterpret_cast<void**>(&D.fold)})
+    if (*p) { cudaFreeAsync(*p, st); *p = nullptr; }
+  D.send_bytes = D.recv_bytes = D.fold_bytes = 0;
+  return rc;
+}
+
+DCT_API int dct_dist_rank(void) { DLOCK; return D.comm ? D.rank : -1; }
+DCT_API int dct_dist_world(void) { DLOCK; return D.comm ? D.world : 0; }
+
+DCT_API int dct_dist_allreduce(void* buf, uint64_t count, int op) {
+  DLOCK;
+  if (!need_comm("dct_dist_allreduce")) return DCT_ERR_DIST;
+  Buffer* b = live(buf);
+  if (!b) { note_error(DCT_ERR_HANDLE, "dct_dist_allreduce: not a live buffer"); return DCT_ERR_HANDLE; }
+  if (b->count < count) { note_error(DCT_ERR_SIZE, "dct_dist_allreduce: buffer too small"); return DCT_ERR_SIZE; }
+  ncclRedOp_t o;
+  switch (op) {
+    case RED_SUM: o = ncclSum; break;
+    case RED_MEAN: o = ncclAvg; break;
+    case RED_MAX: o = ncclMax; break;
+    case RED_MIN: o = ncclMin; break;
+    default: note_error(DCT_ERR_ARG, "dct_dist_allreduce: op must be 0 sum, 1 mean, 2 max or 4 min"); return DCT_ERR_ARG;
+  }
+  return settle(D.api.AllReduce(b->d, b->d, count, ncclFloat32, o, D.comm, rt_stream()), "dct_dist_allreduce")
+             ? 0 : DCT_ERR_DIST;
+}
+
+DCT_API int dct_dist_broadcast(void* buf, uint64_t count, int root) {
+  DLOCK;
+  if (!need_comm("dct_dist_broadcast")) return DCT_ERR_DIST;
+  Buffer* b = live(buf);
+  if (!b) { note_error(DCT_ERR_HANDLE, "dct_dist_broadcast: not a live buffer"); return DCT_ERR_HANDLE; }
+  if (b->count < count) { note_error(DCT_ERR_SIZE, "dct_dist_broadcast: buffer too small"); return DCT_ERR_SIZE; }
+  if (root < 0 || root >= D.world) { note_error(DCT_ERR_ARG, "dct_dist_broadcast: bad root"); return DCT_ERR_ARG; }
+  return settle(D.api.Broadcast(b->d, b->d, count, ncclFloat32, root, D.comm, rt_stream()), "dct_dist_broadcast")
+             ? 0 : DCT_ERR_DIST;
+}
+
+DCT_API int dct_dist_barrier(void) {
+  DLOCK;
+  if (!need_comm("dct_dist_barrier")) return DCT_ERR_DIST;
+  if (!buffers(8, 8 * (size_t)D.world, 8, "dct_dist_barrier")) return DCT_ERR_CUDA;
+  if (!all_gather(D.send, D.recv, 1, "dct_dist_barrier")) return DCT_ERR_DIST;
+  return rt_wait_stream("dct_dist_barrier") ? 0 : DCT_ERR_DIST;
+}
+
+// x viewed as [outer, len, inner], this rank's slice [len_offset, len_offset + len)
+// of a middle axis of global extent len_total; out / out_idx get the reduction
+// over the whole axis on every rank.
+DCT_API int dct_dist_reduce(int op, void* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t len_offset,
+                            uint64_t len_total, void* out, void* out_idx) {
+  DLOCK;
+  const char* W = "dct_dist_reduce";
+  if (!need_comm(W)) return DCT_ERR_DIST;
+  if (op < RED_SUM || op > RED_SUMSQ) { note_error(DCT_ERR_ARG, "dct_dist_reduce: unknown op"); return DCT_ERR_ARG; }
+  const uint64_t nout = outer * inner;
+  if (nout == 0 || len_total > 0x7fffffffull) {
+    note_error(DCT_ERR_ARG, "dct_dist_reduce: need outer*inner > 0 and len_total < 2^31");
+    return DCT_ERR_ARG;
+  }
+  const uint64_t stride = nout + 4;
+  if (!buffers(stride * 8, stride * 8 * (size_t)D.world, 8, W)) return DCT_ERR_CUDA;
+  Buffer *bx = live(x), *bo = live(out), *bi = live(out_idx);
+  const bool arg = (op == RED_ARGMAX || op == RED_ARGMIN);
+  int op_run = op;                                    // max / min with indices: values and indices in one pass
+  if ((op == RED_MAX || op == RED_MIN) && out_idx) op_run = op == RED_MAX ? RED_ARGMAX : RED_ARGMIN;
+  bool valid = bx && (bo || (arg && bi)) && (!out_idx || bi) && bx->count >= outer * len * inner &&
+               (!bo || bo->count >= nout) && (!bi || bi->count >= nout) && len_offset + len <= len_total;
+  unsigned long long* send = (unsigned long long*)D.send;
+  cudaStream_t st = rt_stream();
+  if (valid && !rt_ensure_ws(reduce3d_ws_bytes(op_run, outer, len, inner))) return DCT_ERR_CUDA;
+  if (valid && !rt_cuda_ok(launch_reduce3d_packed(op_run, bx->d, outer, len, inner, (int32_t)len_offset, send,
+                                                  rt_ws(), st), W))
+    valid = false;
+  k_put_header_u64<<<1, 32, 0, st>>>(send + nout, len_offset, len, len_total, valid ? 1ull : 0ull);
+  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  if (!all_gather(send, D.recv, stride, W)) return DCT_ERR_DIST;
+  const unsigned long long* all = (const unsigned long long*)D.recv;
+  k_check_axis_shards<<<1, 32, 0, st>>>(all, D.world, stride, nout, device_error_word());
+  float* o32 = bo ? bo->d : nullptr;
+  int32_t* oi = bi ? reinterpret_cast<int32_t*>(bi->d) : nullptr;
+  if (arg && !oi) { oi = reinterpret_cast<int32_t*>(o32); o32 = nullptr; }   // indices into out (dct_reduce rule)
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && valid)
+    e = launch_fold_packed(op_run, all, (uint32_t)D.world, nout, stride, len_total, o32, oi, st);
+  if (!rt_cuda_ok(e, W)) return DCT_ERR_CUDA;
+  if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_reduce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
+  return 0;
+}
+
+// full reduction (0 sum, 1 mean, 2 max, 4 min, 6 sum of squares) of this
+// rank's n elements, combined over all ranks into out[0] on every rank;
+// *host_out64 gets the float64 value (waits) when non-null
+DCT_API int dct_dist_reduce_all(int op, void* x, uint64_t n, void* out, double* host_out64) {
+  DLOCK;
+  const char* W = "dct_dist_reduce_all";
+  if (!need_comm(W)) return DCT_ERR_DIST;
+  if (!(op == RED_SUM || op == RED_MEAN || op == RED_MAX || op == RED_MIN || op == RED_SUMSQ)) {
+    note_error(DCT_ERR_ARG, "dct_dist_reduce_all: op must be 0 sum, 1 mean, 2 max, 4 min or 6 sumsq");
+    return DCT_ERR_ARG;
+  }
+  if (!buffers(32 + 8, 32 * (size_t)D.world, 16, W)) return DCT_ERR_CUDA;
+  Buffer *bx = live(x), *bo = live(out);
+  bool valid = bx && bo && bx->count >= n && bo->count >= 1;
+  cudaStream_t st = rt_stream();
+  double* rec = (double*)D.send;
+  const int local_op = op == RED_MEAN ? RED_SUM : op;
+  // record [value, n, valid, 0]; value = float64 sum (mean: the raw sum) or extreme
+  k_put_f64<<<1, 32, 0, st>>>(rec, 4, 0.0, (double)n, 0.0, 0.0);
+  if (valid && n > 0) {
+    if (!rt_ensure_ws(full_reduce_ws_bytes() + 256)) return DCT_ERR_CUDA;
+    float* scratch32 = reinterpret_cast<float*>(rec + 4);              // float copy of the local result, unused
+    if (!rt_cuda_ok(launch_full_reduce(local_op, bx->d, n, scratch32, rec, rt_ws(), st), W)) valid = false;
+  }
+  k_put_f64<<<1, 32, 0, st>>>(rec + 2, 1, valid ? 1.0 : 0.0, 0.0, 0.0, 0.0);
+  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  if (!all_gather(rec, D.recv, 4, W)) return DCT_ERR_DIST;
+  k_fold_full<<<1, 32, 0, st>>>((const double*)D.recv, D.world, local_op, op == RED_MEAN ? 1 : 0,
+                                valid ? bo->d : nullptr, D.fold, device_error_word());
+  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  if (host_out64) {
+    double* hs = rt_host_scratch();
+    if (!rt_cuda_ok(cudaMemcpyAsync(hs, D.fold, 8, cudaMemcpyDeviceToHost, st), W)) return DCT_ERR_CUDA;
+    if (!rt_wait_stream(W)) return DCT_ERR_DIST;
+    *host_out64 = hs[0];
+  }
+  if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_reduce_all: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
+  return 0;
+}
+
+// fused softmax + CE over this rank's rows; dlogits use grad_div (the global
+// batch), loss[0] = (sum of every rank's row losses) / loss_div on every rank
+DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, uint32_t rows, uint32_t K, void* probs,
+                                void* dlogits, void* loss, void* logprobs, float loss_div, float grad_div) {
+  DLOCK;
+  const char* W = "dct_dist_softmax_ce";
+  if (!need_comm(W)) return DCT_ERR_DIST;
+  if (!buffers(32, 32 * (size_t)D.world, 8, W)) return DCT_ERR_CUDA;
+  Buffer *bl = live(logits), *bt = live(labels), *bp = live(probs), *bd = live(dlogits), *bs = live(loss),
+         *bq = live(logprobs);
+  const uint64_t n = (uint64_t)rows * K;
+  bool valid = bl && bl->count >= n && K > 0 && (!labels || (bt && bt->count >= rows)) &&
+               (!probs || (bp && bp->count >= n)) && (!dlogits || (bd && bd->count >= n && labels)) &&
+               (!loss || (bs && bs->count >= 1)) && (!logprobs || (bq && bq->count >= n));
+  cudaStream_t st = rt_stream();
+  double* rec = (double*)D.send;
+  k_put_f64<<<1, 32, 0, st>>>(rec, 4, 0.0, (double)rows, 0.0, 0.0);            // [loss sum, rows, valid, 0]
+  if (valid && rows > 0) {
+    SoftmaxCEArgs a;
+    a.logits = bl->d;
+    a.labels = bt ? bt->d : nullptr;
+    a.labels_int32 = labels_int32 != 0;
+    a.rows = rows;
+    a.K = K;
+    a.probs = bp ? bp->d : nullptr;
+    a.dlogits = bd ? bd->d : nullptr;
+    a.logprobs = bq ? bq->d : nullptr;
+    a.loss_partial = bt ? rec : nullptr;
+    a.grad_div = grad_div;
+    a.err = device_error_word();
+    if (!rt_ensure_ws(softmax_ce_ws_bytes(rows, K))) return DCT_ERR_CUDA;
+    if (!rt_cuda_ok(launch_softmax_ce(a, rt_ws(), st), W)) valid = false;
+  }
+  k_put_f64<<<1, 32, 0, st>>>(rec + 2, 1, valid ? 1.0 : 0.0, 0.0, 0.0, 0.0);
+  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  if (!all_gather(rec, D.recv, 4, W)) return DCT_ERR_DIST;
+  k_fold_loss<<<1, 32, 0, st>>>((const double*)D.recv, D.world, (double)loss_div, bs && valid ? bs->d : nullptr,
+                                device_error_word());
+  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_softmax_ce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
+  return 0;
+}
+
+namespace {
+// Channel sums of this rank's x (BWD: dy, dy*x) into the send record, the
+// exchange, and the rank-order fold into D.fold = [2C sums][total count].
+bool bn_exchange(const float* x, const float* dy, uint32_t N, uint32_t C, uint32_t S, bool valid, const char* W,
+                 int* rc) {
+  const uint32_t nsum = 2 * C;
+  const uint64_t stride = (uint64_t)nsum + 4;
+  if (!buffers(stride * 8, stride * 8 * (size_t)D.world, ((size_t)nsum + 1) * 8, W)) { *rc = DCT_ERR_CUDA; return false; }
+  cudaStream_t st = rt_stream();
+  double* rec = (double*)D.send;
+  if (valid) {
+    if (!rt_ensure_ws(bn_ws_bytes(N, C))) { *rc = DCT_ERR_CUDA; return false; }
+    double* ps = (double*)rt_ws();
+    cudaError_t e = launch_bn_plane_sums(x, dy, N, C, S, ps, st);
+    if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, rec, st);     // [C][2] sums straight into the record
+    if (!rt_cuda_ok(e, W)) valid = false;
+  }
+  k_put_f64<<<1, 32, 0, st>>>(rec + nsum, 4, (double)N * (double)S, valid ? 1.0 : 0.0, (double)nsum, 0.0);
+  if (!rt_cuda_ok(cudaGetLastError(), W)) { *rc = DCT_ERR_CUDA; return false; }
+  if (!all_gather(rec, D.recv, stride, W)) { *rc = DCT_ERR_DIST; return false; }
+  k_fold_sums<<<(nsum + 1 + 255) / 256, 256, 0, st>>>((const double*)D.recv, D.world, nsum, D.fold, device_error_word());
+  if (!rt_cuda_ok(cudaGetLastError(), W)) { *rc = DCT_ERR_CUDA; return false; }
+  return true;
+}
+}  // namespace
+
+// BatchNorm training forward over this rank's N samples: statistics over all
+// ranks' samples (global count), running stats updated identically on every rank
+DCT_API int dct_dist_batchnorm_forward_train(void* x, void* gamma, void* beta, void* running_mean,
+                                             void* running_var, void* batch_mean, void* batch_var, void* y,
+                                             uint32_t N, uint32_t C, uint32_t S, float eps, float momentum) {
+  DLOCK;
+  const char* W = "dct_dist_batchnorm_forward_train";
+  if (!need_comm(W)) return DCT_ERR_DIST;
+  if (C == 0) { note_error(DCT_ERR_ARG, "dct_dist_batchnorm_forward_train: C == 0"); return DCT_ERR_ARG; }
+  Buffer *bx = live(x), *bg = live(gamma), *bb = live(beta), *rm = live(running_mean), *rv = live(running_var),
+         *bm = live(batch_mean), *bvv = live(batch_var), *by = live(y);
+  const uint64_t n = (uint64_t)N * C * S;
+  const bool valid = bx && bg && bb && rm && rv && bm && bvv && by && bx->count >= n && by->count >= n &&
+                     bg->count >= C && bb->count >= C && rm->count >= C && rv->count >= C && bm->count >= C &&
+                     bvv->count >= C;
+  int rc = 0;
+  if (!bn_exchange(valid ? bx->d : nullptr, nullptr, N, C, S, valid, W, &rc)) return rc;
+  if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_batchnorm_forward_train: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
+  cudaStream_t st = rt_stream();
+  cudaError_t e = launch_bn_stats_final(D.fold, C, 0.0, bm->d, bvv->d, rm->d, rv->d, true, momentum, st, D.fold + 2 * C);
+  if (e == cudaSuccess) e = launch_bn_forward(bx->d, bm->d, bvv->d, bg->d, bb->d, by->d, N, C, S, eps, n, st);
+  return rt_cuda_ok(e, W) ? 0 : DCT_ERR_CUDA;
+}
+
+// BatchNorm backward over this rank's N samples: dgamma / dbeta summed over
+// all ranks (identical everywhere), dx of the local samples with m = global N*S
+DCT_API int dct_dist_batchnorm_backward(void* x, void* dy, void* batch_mean, void* batch_var, void* gamma,
+                                        void* dgamma, void* dbeta, void* dx, uint32_t N, uint32_t C, uint32_t S,
+                                        float eps) {
+  DLOCK;
+  const char* W = "dct_dist_batchnorm_backward";
+  if (!need_comm(W)) return DCT_ERR_DIST;
+  if (C == 0) { note_error(DCT_ERR_ARG, "dct_dist_batchnorm_backward: C == 0"); return DCT_ERR_ARG; }
+  Buffer *bx = live(x), *bd = live(dy), *bm = live(batch_mean), *bv = live(batch_var), *bg = live(gamma),
+         *dg = live(dgamma), *db = live(dbeta), *bo = live(dx);
+  const uint64_t n = (uint64_t)N * C * S;
+  const bool valid = bx && bd && bm && bv && bg && dg && db && bo && bx->count >= n && bd->count >= n &&
+                     bo->count >= n && bm->count >= C && bv->count >= C && bg->count >= C && dg->count >= C &&
+                     db->count >= C;
+  int rc = 0;
+  if (!bn_exchange(valid ? bx->d : nullptr, valid ? bd->d : nullptr, N, C, S, valid, W, &rc)) return rc;
+  if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_batchnorm_backward: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
+  cudaStream_t st = rt_stream();
+  cudaError_t e = launch_bn_bwd_final(D.fold, C, bm->d, bv->d, eps, dg->d, db->d, st);
+  if (e == cudaSuccess)
+    e = launch_bn_backward_dx(bx->d, bd->d, bm->d, bv->d, bg->d, dg->d, db->d, bo->d, N, C, S, eps, n, st,
+                              D.fold + 2 * C);
+  return rt_cuda_ok(e, W) ? 0 : DCT_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -10,8 +10,8 @@
 // plane sums of each channel in n order (deterministic; across GPUs the same
 // per-channel sums are what the NCCL exchange combines); a finalize launch turns
 // them into mean / biased var (+ the momentum update with the unbiased var) or
-// dgamma / dbeta.  The apply kernels are plane-wise too, so the channel's
-// constants sit in registers and the loop is a pure 128-bit stream.
+// dgamma / dbeta.  The apply kernels stream the flat array in 16 KB chunks per
+// block and find each float4's channel with two fast divisions.
 #include "dct_common.cuh"
 #include "kernels.h"
 
@@ -91,9 +91,10 @@ __global__ void k_bn_fold(const double* __restrict__ ps, uint32_t N, uint32_t C,
 }
 
 __global__ void k_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rm,
-                                 float* rv, int training, float momentum) {
+                                 float* rv, int training, float momentum, const double* cnt_dev) {
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
+  if (cnt_dev) cnt = *cnt_dev;
   const double m = chan[2 * c] / cnt;
   const double v = fmax(0.0, chan[2 * c + 1] / cnt - m * m);
   mean[c] = (float)m;
@@ -165,7 +166,9 @@ __global__ void __launch_bounds__(256) k_bn_dx_chunk(const float* __restrict__ x
                                                      const float* __restrict__ gamma,
                                                      const float* __restrict__ dgamma,
                                                      const float* __restrict__ dbeta, float* __restrict__ dx,
-                                                     uint32_t n4, FastDiv s4, FastDiv cdiv, float eps, float mf) {
+                                                     uint32_t n4, FastDiv s4, FastDiv cdiv, float eps, float mf,
+                                                     const double* __restrict__ cnt_dev) {
+  if (cnt_dev) mf = (float)*cnt_dev;
   const uint64_t base = (uint64_t)blockIdx.x * kBnChunk4 + threadIdx.x;
   float4 a[kBnU], d[kBnU];
   uint32_t ch[kBnU];
@@ -219,7 +222,8 @@ __global__ void __launch_bounds__(256) k_bn_backward_dx(const float* __restrict_
                                                         const float* __restrict__ dgamma,
                                                         const float* __restrict__ dbeta, float* __restrict__ dx,
                                                         uint64_t planes, uint32_t C, uint32_t S, float eps, float mf,
-                                                        uint64_t limit) {
+                                                        uint64_t limit, const double* __restrict__ cnt_dev) {
+  if (cnt_dev) mf = (float)*cnt_dev;
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -271,10 +275,10 @@ cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, dou
 }
 
 cudaError_t launch_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rmean,
-                                  float* rvar, bool training, float momentum, cudaStream_t st) {
+                                  float* rvar, bool training, float momentum, cudaStream_t st, const double* cnt_dev) {
   if (C == 0) return cudaSuccess;
   k_bn_stats_final<<<(C + 255) / 256, 256, 0, st>>>(chan, C, cnt, mean, var, rmean, rvar, training ? 1 : 0,
-                                                      momentum);
+                                                      momentum, cnt_dev);
   return cudaGetLastError();
 }
 
@@ -305,7 +309,8 @@ cudaError_t launch_bn_forward(const float* x, const float* mean, const float* va
 
 cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* mean, const float* var,
                                   const float* gamma, const float* dgamma, const float* dbeta, float* dx, uint32_t N,
-                                  uint32_t C, uint32_t S, float eps, uint64_t limit, cudaStream_t st) {
+                                  uint32_t C, uint32_t S, float eps, uint64_t limit, cudaStream_t st,
+                                  const double* cnt_dev) {
   const uint64_t planes = (uint64_t)N * C;
   if (planes == 0 || S == 0) return cudaSuccess;
   const uint64_t total = planes * S;
@@ -316,10 +321,10 @@ cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* 
   if (vec) {
     const uint32_t n4 = (uint32_t)(limit / 4);
     k_bn_dx_chunk<<<(unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4), 256, 0, st>>>(
-        x, dy, mean, var, gamma, dgamma, dbeta, dx, n4, FastDiv(S / 4), FastDiv(C), eps, mf);
+        x, dy, mean, var, gamma, dgamma, dbeta, dx, n4, FastDiv(S / 4), FastDiv(C), eps, mf, cnt_dev);
   } else {
     k_bn_backward_dx<<<plane_blocks(planes), 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C,
-                                                            S, eps, mf, limit);
+                                                            S, eps, mf, limit, cnt_dev);
   }
   return cudaGetLastError();
 }

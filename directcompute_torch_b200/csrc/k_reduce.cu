@@ -45,6 +45,16 @@ DCT_DEV float fmin_nan(float a, float b) {
   return r;
 }
 
+// Where a finished reduction goes: float values (+ int32 indices), or, for a
+// shard of a reduction split across ranks, one packed 8-byte partial per output
+// with the shard's global index offset applied to arg indices.
+struct RedOut {
+  float* out = nullptr;
+  int32_t* idx = nullptr;
+  unsigned long long* packed = nullptr;
+  int32_t idx_off = 0;
+};
+
 // Partial accumulator of one reduction lane.
 //  * sums: float64;
 //  * MAX / MIN: value only, NaN propagates (NumPy);
@@ -132,6 +142,15 @@ struct Acc {
       s = __longlong_as_double((long long)w);
     }
   }
+  DCT_DEV void emit(const RedOut& o, uint64_t k, uint64_t len) const {
+    if (o.packed) {
+      Acc t = *this;
+      if constexpr (kArg) { if (t.i >= 0) t.i += o.idx_off; }
+      o.packed[k] = t.pack();
+    } else {
+      store(o.out, o.idx, k, len);
+    }
+  }
   DCT_DEV void store(float* out, int32_t* out_idx, uint64_t k, uint64_t len) const {
     if constexpr (kArg) {
       if (out) out[k] = v;
@@ -152,8 +171,7 @@ struct Acc {
 template <int OP, bool VEC>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __restrict__ x, uint64_t rows, uint64_t len,
                                                              uint64_t so, uint32_t chunks, uint64_t chunk_len,
-                                                             float* out, int32_t* out_idx,
-                                                             unsigned long long* part) {
+                                                             RedOut ro, unsigned long long* part) {
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -187,7 +205,7 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
     }
     acc.warp_reduce();
     if (lane == 0) {
-      if (chunks == 1) acc.store(out, out_idx, row, len);
+      if (chunks == 1) acc.emit(ro, row, len);
       else part[pr] = acc.pack();
     }
   }
@@ -200,8 +218,8 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
 template <int OP, int VEC>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                              uint64_t inner, uint64_t so, uint64_t sl,
-                                                             uint32_t chunks, uint64_t chunk_len, float* out,
-                                                             int32_t* out_idx, unsigned long long* part) {
+                                                             uint32_t chunks, uint64_t chunk_len, RedOut ro,
+                                                             unsigned long long* part) {
   constexpr int W = 32 * VEC;
   __shared__ unsigned long long sh[kRedWarps][W];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -250,7 +268,7 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
         if (w == 0) tot = t; else tot.merge(t);
       }
       if (c < inner) {
-        if (chunks == 1) tot.store(out, out_idx, o * inner + c, len);
+        if (chunks == 1) tot.emit(ro, o * inner + c, len);
         else part[(o * chunks + ch) * inner + c] = tot.pack();
       }
     }
@@ -261,8 +279,7 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 // fold chunk partials: out[k] = combine(part[k*stride_k ... with chunk stride])
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
-                                                     uint32_t chunks, uint64_t inner, uint64_t len, float* out,
-                                                     int32_t* out_idx) {
+                                                     uint32_t chunks, uint64_t inner, uint64_t len, RedOut ro) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += stride) {
     // k = o*inner + c ; partial index = (o*chunks + ch)*inner + c
@@ -273,7 +290,7 @@ __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* _
       t.unpack(part[(o * chunks + ch) * inner + c]);
       if (ch == 0) tot = t; else tot.merge(t);
     }
-    tot.store(out, out_idx, k, len);
+    tot.emit(ro, k, len);
   }
 }
 
@@ -281,7 +298,7 @@ __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* _
 template <int OP>
 __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                         uint64_t inner, uint64_t so, uint64_t sl, uint64_t si,
-                                                        float* out, int32_t* out_idx) {
+                                                        RedOut ro) {
   const uint64_t nout = outer * inner;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += stride) {
@@ -290,7 +307,7 @@ __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict_
     Acc<OP> acc;
     acc.reset();
     for (uint64_t l = 0; l < len; ++l) acc.add(p[l * sl], (int64_t)l);
-    acc.store(out, out_idx, k, len);
+    acc.emit(ro, k, len);
   }
 }
 
@@ -356,7 +373,7 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
 
 template <int OP>
 cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
-                       uint64_t si, float* out, int32_t* out_idx, void* ws, size_t ws_bytes, cudaStream_t st) {
+                       uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (outer == 0 || inner == 0) return cudaSuccess;
   if (len == 0) return cudaErrorInvalidValue;
   Plan p = make_plan(outer, len, inner, so, sl, si, x);
@@ -367,34 +384,50 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
     if (!ws || ws_bytes < need) return cudaErrorInvalidValue;
   }
   if (p.kind == 0) {
-    if (p.vec) k_reduce_rows<OP, true><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, out, out_idx, part);
-    else k_reduce_rows<OP, false><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, out, out_idx, part);
+    if (p.vec) k_reduce_rows<OP, true><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
+    else k_reduce_rows<OP, false><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
   } else if (p.kind == 1) {
-    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
-    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, out, out_idx, part);
+    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
+    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
   } else {
-    k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, out, out_idx);
+    k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, ro);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nparts == 1) return e;
   const uint64_t nout = outer * inner;
-  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(part, nout, nparts, inner, len, out, out_idx);
+  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(part, nout, nparts, inner, len, ro);
   return cudaGetLastError();
 }
 
 cudaError_t dispatch_reduce(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t so,
-                            uint64_t sl, uint64_t si, float* out, int32_t* out_idx, void* ws, size_t ws_bytes,
-                            cudaStream_t st) {
+                            uint64_t sl, uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st) {
   switch (op) {
-    case RED_SUM: return run_reduce<RED_SUM>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
-    case RED_MEAN: return run_reduce<RED_MEAN>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
-    case RED_MAX: return run_reduce<RED_MAX>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
-    case RED_ARGMAX: return run_reduce<RED_ARGMAX>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
-    case RED_MIN: return run_reduce<RED_MIN>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
-    case RED_ARGMIN: return run_reduce<RED_ARGMIN>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
-    case RED_SUMSQ: return run_reduce<RED_SUMSQ>(x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
+    case RED_SUM: return run_reduce<RED_SUM>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_MEAN: return run_reduce<RED_MEAN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_MAX: return run_reduce<RED_MAX>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_ARGMAX: return run_reduce<RED_ARGMAX>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_MIN: return run_reduce<RED_MIN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_ARGMIN: return run_reduce<RED_ARGMIN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_SUMSQ: return run_reduce<RED_SUMSQ>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// identity partials (a shard with nothing to reduce)
+template <int OP>
+__global__ void k_identity_packed(unsigned long long* packed, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += stride)
+    packed[k] = Acc<OP>::identity_pack();
+}
+
+template <int OP>
+cudaError_t run_fold_packed(const unsigned long long* parts, uint32_t nparts, uint64_t nout, uint64_t stride,
+                            uint64_t len_total, const RedOut& ro, cudaStream_t st) {
+  // parts[p * stride + k]: the chunk-fold layout with outer = 1, inner = stride
+  // (k < nout <= stride, so the fold's outer index is always 0)
+  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(parts, nout, nparts, stride, len_total, ro);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -419,7 +452,10 @@ size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uin
 cudaError_t launch_reduce_strided(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
                                   uint64_t so, uint64_t sl, uint64_t si, float* out, int32_t* out_idx, void* ws,
                                   size_t ws_bytes, cudaStream_t st) {
-  return dispatch_reduce(op, x, outer, len, inner, so, sl, si, out, out_idx, ws, ws_bytes, st);
+  RedOut ro;
+  ro.out = out;
+  ro.idx = out_idx;
+  return dispatch_reduce(op, x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
 }
 
 size_t reduce3d_ws_bytes(int op, uint64_t outer, uint64_t len, uint64_t inner) {
@@ -431,8 +467,56 @@ size_t reduce3d_ws_bytes(int op, uint64_t outer, uint64_t len, uint64_t inner) {
 cudaError_t launch_reduce3d(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner, float* out,
                             int32_t* out_idx, void* ws, cudaStream_t st) {
   const size_t need = reduce3d_ws_bytes(op, outer, len, inner);
-  if (inner == 1) return dispatch_reduce(op, x, outer, len, 1, len, 1, 1, out, out_idx, ws, need, st);
-  return dispatch_reduce(op, x, outer, len, inner, len * inner, inner, 1, out, out_idx, ws, need, st);
+  RedOut ro;
+  ro.out = out;
+  ro.idx = out_idx;
+  if (inner == 1) return dispatch_reduce(op, x, outer, len, 1, len, 1, 1, ro, ws, need, st);
+  return dispatch_reduce(op, x, outer, len, inner, len * inner, inner, 1, ro, ws, need, st);
+}
+
+cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
+                                   int32_t idx_off, unsigned long long* packed, void* ws, cudaStream_t st) {
+  RedOut ro;
+  ro.packed = packed;
+  ro.idx_off = idx_off;
+  const uint64_t nout = outer * inner;
+  if (nout == 0) return cudaSuccess;
+  if (len == 0) {
+    const unsigned b = grid_for(nout, 256);
+    switch (op) {
+      case RED_SUM: k_identity_packed<RED_SUM><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_MEAN: k_identity_packed<RED_MEAN><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_MAX: k_identity_packed<RED_MAX><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_ARGMAX: k_identity_packed<RED_ARGMAX><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_MIN: k_identity_packed<RED_MIN><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_ARGMIN: k_identity_packed<RED_ARGMIN><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_SUMSQ: k_identity_packed<RED_SUMSQ><<<b, 256, 0, st>>>(packed, nout); break;
+      default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
+  const size_t need = reduce3d_ws_bytes(op, outer, len, inner);
+  if (inner == 1) return dispatch_reduce(op, x, outer, len, 1, len, 1, 1, ro, ws, need, st);
+  return dispatch_reduce(op, x, outer, len, inner, len * inner, inner, 1, ro, ws, need, st);
+}
+
+cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,
+                               uint64_t stride, uint64_t len_total, float* out, int32_t* out_idx, cudaStream_t st) {
+  if (nout == 0) return cudaSuccess;
+  if (stride < nout) return cudaErrorInvalidValue;
+  RedOut ro;
+  ro.out = out;
+  ro.idx = out_idx;
+  switch (op) {
+    case RED_SUM: return run_fold_packed<RED_SUM>(parts, nparts, nout, stride, len_total, ro, st);
+    case RED_MEAN: return run_fold_packed<RED_MEAN>(parts, nparts, nout, stride, len_total, ro, st);
+    case RED_MAX: return run_fold_packed<RED_MAX>(parts, nparts, nout, stride, len_total, ro, st);
+    case RED_ARGMAX: return run_fold_packed<RED_ARGMAX>(parts, nparts, nout, stride, len_total, ro, st);
+    case RED_MIN: return run_fold_packed<RED_MIN>(parts, nparts, nout, stride, len_total, ro, st);
+    case RED_ARGMIN: return run_fold_packed<RED_ARGMIN>(parts, nparts, nout, stride, len_total, ro, st);
+    case RED_SUMSQ: return run_fold_packed<RED_SUMSQ>(parts, nparts, nout, stride, len_total, ro, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -54,6 +54,17 @@ enum RedOp : int { RED_SUM = 0, RED_MEAN, RED_MAX, RED_ARGMAX, RED_MIN, RED_ARGM
 size_t reduce3d_ws_bytes(int op, uint64_t outer, uint64_t len, uint64_t inner);
 cudaError_t launch_reduce3d(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
                             float* out, int32_t* out_idx, void* ws, cudaStream_t st);
+// One shard of a reduction whose middle axis is split across ranks: instead of
+// final values, one packed 8-byte partial per output (float64 sum, or float
+// value << 32 | int32 index with idx_off added to the shard-local index).
+// len == 0 writes identity partials.  Fold the ranks' partials, laid out
+// parts[p * stride + k] (k < nout = outer*inner <= stride), with
+// launch_fold_packed (merge in part order, ties to the lower index, mean
+// divides by len_total).
+cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
+                                   int32_t idx_off, unsigned long long* packed, void* ws, cudaStream_t st);
+cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,
+                               uint64_t stride, uint64_t len_total, float* out, int32_t* out_idx, cudaStream_t st);
 // General strided form: out[o*inner + i] = reduce_l x[o*so + l*sl + i*si].
 size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
                                uint64_t si);
@@ -128,9 +139,11 @@ cudaError_t launch_bn_plane_sums(const float* x, const float* dy, uint32_t N, ui
 cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, double* chan,
                            cudaStream_t st);
 // Finalize the forward statistics from per-channel (sum, sumsq) over cnt elements.
+// cnt_dev (optional): element count per channel read on the device instead of
+// `cnt` (a count combined across ranks)
 cudaError_t launch_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean,
                                   float* var, float* rmean, float* rvar, bool training,
-                                  float momentum, cudaStream_t st);
+                                  float momentum, cudaStream_t st, const double* cnt_dev = nullptr);
 // Finalize backward: dgamma = (sum dy*x - mean*sum dy) * rstd, dbeta = sum dy.
 cudaError_t launch_bn_bwd_final(const double* chan, uint32_t C, const float* mean, const float* var,
                                 float eps, float* dgamma, float* dbeta, cudaStream_t st);
@@ -140,7 +153,7 @@ cudaError_t launch_bn_forward(const float* x, const float* mean, const float* va
 cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* mean, const float* var,
                                   const float* gamma, const float* dgamma, const float* dbeta, float* dx,
                                   uint32_t N, uint32_t C, uint32_t S, float eps, uint64_t limit,
-                                  cudaStream_t st);
+                                  cudaStream_t st, const double* cnt_dev = nullptr);
 
 // ---- synthetic data (k_rng.cu) --------------------------------------------------
 // Philox4x32-10 counter-based fills.  dist 0: uniform [lo, hi); 1: normal(mean=lo, std=hi)

@@ -133,7 +133,11 @@ static bool check_device_errors() {
   const uint32_t e = *(volatile uint32_t*)g.dev_err_host;
   if (!e) return true;
   *(volatile uint32_t*)g.dev_err_host = 0;
-  set_error(DCT_ERR_CUDA, "device: a bounded wait in a kernel timed out (error bits 0x%x); results are invalid", e);
+  if (e & DCT_DEVERR_PEER_INVALID)
+    set_error(DCT_ERR_DIST, "sharded op: a rank's shard was invalid (bad handle, size or count on that rank; "
+              "error bits 0x%x); results are invalid", e);
+  else
+    set_error(DCT_ERR_CUDA, "device: a bounded wait in a kernel timed out (error bits 0x%x); results are invalid", e);
   return false;
 }
 
@@ -251,16 +255,17 @@ bool rt_wait_stream(const char* where) {
     if (q == cudaSuccess) return check_device_errors();
     if (q != cudaErrorNotReady) return cuda_ok(q, where);
     char msg[256] = {0};
+    const double limit = g_hooks.timeout_s;
     if (g_hooks.async_error(msg, sizeof(msg))) {
-      if (g_hooks.abort) g_hooks.abort();
+      if (g_hooks.abort) g_hooks.abort();       // clears the hooks
       set_error(DCT_ERR_DIST, "%s: communicator failed: %s", where, msg);
       return false;
     }
     const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    if (el > g_hooks.timeout_s) {
+    if (el > limit) {
       if (g_hooks.abort) g_hooks.abort();
       set_error(DCT_ERR_DIST, "%s: no progress within %.0f s (a peer rank is gone?); communicator aborted", where,
-                g_hooks.timeout_s);
+                limit);
       return false;
     }
     std::this_thread::sleep_for(std::chrono::microseconds(200));

@@ -248,6 +248,59 @@ DCT_API int dct_batchnorm_forward_train_noalloc(const float* x, const float* gam
                                                 float* batch_var, float* y, uint32_t N, uint32_t C, uint32_t S,
                                                 float eps, float momentum, void* stream);
 
+/* ======================= sharding over NCCL (one process per GPU) ==============
+ * No counterpart in the reference, which drives one D3D11 device
+ * (engine.cpp:61-129).  Each rank holds one contiguous shard of the sharded
+ * axis; ops whose result depends on other shards make one NCCL all-gather of
+ * small fixed-size records, folded on the device in rank order (identical
+ * results on every rank; at world size 1 bit-identical to the single-GPU
+ * entry points).  Every rank must make the same dct_dist_* calls in the same
+ * order with the same outer/inner/C/S/op.  A rank whose own arguments are bad
+ * still takes part in the exchange and returns DCT_ERR_ARG; the other ranks
+ * get DCT_ERR_DIST at their next wait.  While a communicator is active every
+ * wait of the library is bounded by the init timeout and aborts the
+ * communicator when it expires or NCCL reports an asynchronous error.
+ * Other ops (elementwise, axis -1 reductions, Adam) shard with no exchange. */
+DCT_API int dct_dist_available(void);          /* 1 if an NCCL library can be loaded */
+DCT_API int dct_dist_nccl_version(void);       /* NCCL_VERSION_CODE of that library, 0 if none */
+/* balanced contiguous split: shard `rank` of n items is [*offset, *offset + *count) */
+DCT_API int dct_dist_shard(uint64_t n, int world, int rank, uint64_t* offset, uint64_t* count);
+DCT_API int dct_dist_unique_id(void* out, int len);   /* rank 0: 128-byte id to send to every rank */
+DCT_API int dct_dist_init(const void* id, int len, int nranks, int rank, double timeout_s);
+DCT_API int dct_dist_finalize(void);
+DCT_API int dct_dist_rank(void);    /* -1 without a communicator */
+DCT_API int dct_dist_world(void);   /* 0 without a communicator */
+/* in-place fp32 all-reduce of buf[0:count]: op 0 sum, 1 mean, 2 max, 4 min */
+DCT_API int dct_dist_allreduce(void* buf, uint64_t count, int op);
+DCT_API int dct_dist_broadcast(void* buf, uint64_t count, int root);
+DCT_API int dct_dist_barrier(void);
+/* dct_reduce over a sharded middle axis: x is [outer, len, inner], this rank's
+ * slice [len_offset, len_offset + len) of an axis of extent len_total (the
+ * ranks' slices tile it in rank order; checked on the device).  out / out_idx
+ * as dct_reduce, identical on every rank; indices are global (< 2^31). */
+DCT_API int dct_dist_reduce(int op, void* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t len_offset,
+                            uint64_t len_total, void* out, void* out_idx);
+/* dct_reduce_all over every rank's n elements (0 sum, 1 mean, 2 max, 4 min, 6 sumsq) */
+DCT_API int dct_dist_reduce_all(int op, void* x, uint64_t n, void* out, double* host_out64);
+/* dct_softmax_ce over this rank's rows; pass the global batch as grad_div and
+ * loss_div: loss[0] = (sum of every rank's row losses) / loss_div */
+DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, uint32_t rows, uint32_t K,
+                                void* probs, void* dlogits, void* loss, void* logprobs, float loss_div,
+                                float grad_div);
+/* BatchNorm over this rank's N samples with statistics of all ranks' samples */
+DCT_API int dct_dist_batchnorm_forward_train(void* x, void* gamma, void* beta, void* running_mean,
+                                             void* running_var, void* batch_mean, void* batch_var, void* y,
+                                             uint32_t N, uint32_t C, uint32_t S, float eps, float momentum);
+DCT_API int dct_dist_batchnorm_backward(void* x, void* dy, void* batch_mean, void* batch_var, void* gamma,
+                                        void* dgamma, void* dbeta, void* dx, uint32_t N, uint32_t C, uint32_t S,
+                                        float eps);
+
+/* self-test of the device-side bounded wait: one block waits on a barrier
+ * phase that nothing completes, gives up after `spins` polls, sets the device
+ * error word and exits; the next wait returns DCT_ERR_CUDA and the context
+ * stays usable */
+DCT_API int dct_selftest_bounded_wait(uint32_t spins);
+
 #ifdef __cplusplus
 }
 #endif

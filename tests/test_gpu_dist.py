@@ -1,0 +1,364 @@
+"""The sharded (dct_dist_*) entry points on the GPU.
+
+World size 1 (a one-rank NCCL communicator, always runnable): every sharded op
+is bit-identical to its single-GPU entry point, which is itself held to the
+oracle elsewhere (and here, for the BatchNorm extension entry points).  The
+host-made failures: an inconsistent shard header makes the next wait return
+DCT_ERR_DIST, and a device-side bounded wait that runs out makes it return
+DCT_ERR_CUDA; the context stays usable after both.
+
+World size 2 (only with two GPUs): two processes, one GPU each, shard the
+rows / batch; every rank's result equals the unsharded oracle on the whole
+input (bit-exact for max/min/argmax/argmin and the dlogits formula, rel 1e-5
+for sums, means, losses and BatchNorm statistics).
+"""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+import time
+import traceback
+
+import numpy as np
+import pytest
+
+from oracle import newops as O
+from oracle import shaders as S
+
+pytestmark = pytest.mark.gpu
+
+REDUCE_OPS = ("sum", "mean", "max", "argmax", "min", "argmin", "sumsq")
+
+
+def _same(a, b):
+    a = np.asarray(a)
+    b = np.asarray(b)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    av, bv = a.view(np.uint32), b.view(np.uint32)
+    eq = (av == bv) | (np.isnan(a.view(np.float32)) & np.isnan(b.view(np.float32)))
+    assert eq.all(), f"{(~eq).sum()} mismatches, first at {np.flatnonzero(~eq.ravel())[:5]}"
+
+
+@pytest.fixture(scope="module")
+def comm(dev):
+    from directcompute_torch_b200.dist import Communicator
+    c = Communicator.single(timeout_s=30)
+    yield c
+    c.close()
+
+
+def _reduce_local(dev, op, hx, outer, n, inner, want_idx):
+    lib = dev.lib
+    hout = dev.empty(outer * inner)
+    hidx = dev.empty(outer * inner) if want_idx else None
+    from directcompute_torch_b200._abi import REDUCE
+    assert lib.dct_reduce(REDUCE[op], hx, outer, n, inner, hout, hidx) == 0, dev.error()
+    return hout, hidx
+
+
+@pytest.mark.parametrize("shape", [(1, 1000, 4096), (1, 333, 37), (6, 40, 512), (64, 1, 1), (3, 100, 1)])
+def test_world1_reduce_matches_local(dev, comm, shape):
+    outer, n, inner = shape
+    r = np.random.default_rng(31)
+    x = r.standard_normal(shape).astype(np.float32)
+    x.ravel()[r.choice(x.size, size=max(1, x.size // 500), replace=False)] = 1e4
+    hx = dev.buf(x)
+    for op in REDUCE_OPS:
+        for want_idx in ((False, True) if op in ("max", "min", "argmax") else (False,)):
+            ha, hai = _reduce_local(dev, op, hx, outer, n, inner, want_idx)
+            hb = dev.empty(outer * inner)
+            hbi = dev.empty(outer * inner) if want_idx else None
+            comm.reduce(op, hx, outer, n, inner, 0, n, hb, hbi)
+            dev.sync()
+            _same(dev.read(hb), dev.read(ha))
+            if want_idx:
+                _same(dev.read(hbi), dev.read(hai))
+            dev.free(ha, hb, *(h for h in (hai, hbi) if h))
+    dev.free(hx)
+
+
+def test_world1_reduce_all_matches_local(dev, comm):
+    r = np.random.default_rng(32)
+    for n in (1, 1000, (1 << 22) + 3):
+        x = r.uniform(-1, 1, n).astype(np.float32)
+        hx = dev.buf(x)
+        for op in ("sum", "mean", "max", "min", "sumsq"):
+            ha, hb = dev.empty(1), dev.empty(1)
+            va = dev.reduce_all(op, hx, n, ha)
+            vb = comm.reduce_all(op, hx, n, hb, want_host=True)
+            assert va == vb or (np.isnan(va) and np.isnan(vb)), (op, n, va, vb)
+            _same(dev.read(hb), dev.read(ha))
+            dev.free(ha, hb)
+        dev.free(hx)
+
+
+@pytest.mark.parametrize("BK", [(4096, 1000), (300, 37), (64, 3000)])
+def test_world1_softmax_ce_matches_local(dev, comm, BK):
+    B, K = BK
+    r = np.random.default_rng(33)
+    x = (3 * r.standard_normal((B, K))).astype(np.float32)
+    lab = r.integers(0, K, B).astype(np.float32)
+    hx, hl = dev.buf(x), dev.buf(lab)
+    outs = []
+    for sharded in (False, True):
+        hp, hg, hloss = dev.empty(B * K), dev.empty(B * K), dev.empty(1)
+        if sharded:
+            comm.softmax_ce(hx, hl, B, K, probs=hp, dlogits=hg, loss=hloss, global_rows=B)
+        else:
+            assert dev.lib.dct_softmax_ce(hx, hl, 0, B, K, hp, hg, hloss, None, float(B), float(B)) == 0, dev.error()
+        dev.sync()
+        outs.append([dev.read(h) for h in (hp, hg, hloss)])
+        dev.free(hp, hg, hloss)
+    for a, b in zip(*outs):
+        _same(b, a)
+    p, loss, _ = O.softmax_ce_f64(x, lab.astype(np.int64))
+    assert abs(float(outs[1][2][0]) - float(loss)) <= 1e-5 * abs(float(loss))
+    dev.free(hx, hl)
+
+
+def _bn_inputs(shape, seed):
+    r = np.random.default_rng(seed)
+    N, C, H, W = shape
+    x = (0.5 + 2 * r.standard_normal(shape)).astype(np.float32)
+    dy = r.standard_normal(shape).astype(np.float32)
+    gamma = r.random(C, dtype=np.float32)
+    beta = r.random(C, dtype=np.float32)
+    rm0 = (0.1 * r.standard_normal(C)).astype(np.float32)
+    rv0 = (1.0 + r.random(C, dtype=np.float32)).astype(np.float32)
+    return x, dy, gamma, beta, rm0, rv0
+
+
+def _bn_dx_global(x, dy, mean, var, gamma, dg, db, C, S_, m_count, eps):
+    """nn_batchnorm_backward_dx.hlsl:20-38 with m = the global element count per channel."""
+    n = x.size
+    c = (np.arange(n, dtype=np.int64) // S_) % C
+    rstd = (np.float32(1.0) / np.sqrt(var[:C] + np.float32(eps))).astype(np.float32)
+    xhat = ((x.ravel() - mean[c]) * rstd[c]).astype(np.float32)
+    inner = ((db[c] + xhat * dg[c]) / np.float32(m_count)).astype(np.float32)
+    return ((gamma[c] * rstd[c]) * (dy.ravel() - inner)).astype(np.float32)
+
+
+@pytest.mark.parametrize("shape", [(8, 16, 7, 7), (16, 64, 28, 28), (3, 5, 3, 3)])
+def test_world1_batchnorm_matches_local_and_oracle(dev, comm, shape):
+    N, C, H, W = shape
+    S_ = H * W
+    eps = 1e-5
+    x, dy, gamma, beta, rm0, rv0 = _bn_inputs(shape, 34)
+    hx, hdy, hg, hb = dev.buf(x), dev.buf(dy), dev.buf(gamma), dev.buf(beta)
+    res = []
+    lib = dev.lib
+    for sharded in (False, True):
+        hrm, hrv, hm, hv, hy = dev.buf(rm0), dev.buf(rv0), dev.empty(C), dev.empty(C), dev.empty(x.size)
+        hdg, hdb, hdx = dev.empty(C), dev.empty(C), dev.empty(x.size)
+        if sharded:
+            comm.batchnorm_forward_train(hx, hg, hb, hrm, hrv, hm, hv, hy, N, C, S_, eps, 0.1)
+            comm.batchnorm_backward(hx, hdy, hm, hv, hg, hdg, hdb, hdx, N, C, S_, eps)
+        else:
+            assert lib.dct_batchnorm_forward_train(hx, hg, hb, hrm, hrv, hm, hv, hy, N, C, S_, eps, 0.1) == 0
+            assert lib.dct_batchnorm_backward(hx, hdy, hm, hv, hg, hdg, hdb, hdx, N, C, S_, eps) == 0
+        dev.sync()
+        res.append([dev.read(h) for h in (hrm, hrv, hm, hv, hy, hdg, hdb, hdx)])
+        dev.free(hrm, hrv, hm, hv, hy, hdg, hdb, hdx)
+    for a, b in zip(*res):
+        _same(b, a)
+    rm, rv, mean, var, y, dg, db, dx = res[1]
+    mean64, var64 = S.batchnorm_mean_var(x.ravel(), N, C, S_)
+    assert np.allclose(mean, mean64, rtol=1e-6, atol=1e-7) and np.allclose(var, var64, rtol=1e-6)
+    rm_o, rv_o = S.batchnorm_running(rm0, rv0, mean64, var64, N, S_, 0.1)
+    assert np.allclose(rm, rm_o, rtol=1e-6, atol=1e-8) and np.allclose(rv, rv_o, rtol=1e-6)
+    _same(y, S.batchnorm_forward(x.ravel(), mean, var, gamma, beta, N, C, S_, np.float32(eps)))
+    dg_o, db_o = S.batchnorm_backward_reduce(x.ravel(), dy.ravel(), mean, var, N, C, S_, np.float32(eps))
+    tol = 1e-6 * np.sqrt(N * S_)
+    assert np.allclose(dg, dg_o, rtol=1e-5, atol=tol) and np.allclose(db, db_o, rtol=1e-5, atol=tol)
+    _same(dx, S.batchnorm_backward_dx(x.ravel(), dy.ravel(), mean, var, gamma, dg, db, N, C, S_, np.float32(eps)))
+    dev.free(hx, hdy, hg, hb)
+
+
+def test_world1_allreduce_broadcast_barrier(dev, comm):
+    v = np.arange(1000, dtype=np.float32) - 300.5
+    h = dev.buf(v)
+    for op in ("sum", "mean", "max", "min"):
+        comm.allreduce(h, v.size, op)
+    comm.broadcast(h, v.size, 0)
+    comm.barrier()
+    _same(dev.read(h), v)
+    dev.free(h)
+
+
+def test_world1_inconsistent_shards_fail_on_every_wait(dev, comm):
+    """A shard header that does not tile [0, len_total) is caught on the device."""
+    x = np.ones((1, 100, 8), np.float32)
+    hx, ho = dev.buf(x), dev.empty(8)
+    comm.reduce("sum", hx, 1, 100, 8, 0, 200, ho)          # claims a 200-row axis, holds 100 rows
+    rc = dev.lib.dct_synchronize()
+    code, msg = dev.error()
+    assert rc == 8 and code == 8 and "shard" in msg, (rc, code, msg)
+    dev.clear_error()
+    comm.reduce("sum", hx, 1, 100, 8, 0, 100, ho)          # the same call, consistent: fine
+    dev.sync()
+    _same(dev.read(ho), np.full(8, 100.0, np.float32))
+    dev.free(hx, ho)
+
+
+def test_bounded_wait_times_out_and_context_survives(dev):
+    """A kernel waits on a barrier phase that nothing completes; the wait gives
+    up after its poll budget, reports through the error word, and the next op works."""
+    lib = dev.lib
+    dev.sync()
+    t0 = time.perf_counter()
+    assert lib.dct_selftest_bounded_wait(4096) == 0, dev.error()
+    rc = lib.dct_synchronize()
+    secs = time.perf_counter() - t0
+    code, msg = dev.error()
+    assert rc == 5 and code == 5 and "bounded wait" in msg, (rc, code, msg)
+    assert secs < 30, secs
+    dev.clear_error()
+    a = np.arange(4096, dtype=np.float32)
+    ha, hb = dev.buf(a), dev.empty(a.size)
+    dev.unary("neg", ha, hb, a.size)
+    dev.sync()
+    _same(dev.read(hb), -a)
+    dev.free(ha, hb)
+    print(f"bounded wait of 4096 polls gave up after {secs * 1e3:.1f} ms (host-observed)")
+
+
+# ---------------------------------------------------------------------------
+# two GPUs, two processes
+# ---------------------------------------------------------------------------
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _world2_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), DCT_DEVICE=str(rank),
+                      NCCL_NVLS_ENABLE="0")
+    try:
+        import torch  # noqa: F401  (loads PyTorch's NCCL first)
+        import torch.distributed as td
+        td.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        from tests.devhelp import Dev
+        from directcompute_torch_b200.dist import Communicator, shard_range
+        dev = Dev()
+        comm = Communicator.from_process_group(timeout_s=60)
+        errs = {}
+        r = np.random.default_rng(40)
+        # C3-style axis-0 reductions, rows sharded (uneven split)
+        R, Cc = 1001, 640
+        x = r.standard_normal((R, Cc)).astype(np.float32)
+        x[r.integers(0, R, 50), r.integers(0, Cc, 50)] = 1e4
+        b = shard_range(R, world, 1)[0]
+        x[b - 1, 5] = x[b, 5] = 2e4                        # tie across the boundary
+        x[b + 3, 7] = np.nan
+        off, cnt = shard_range(R, world, rank)
+        hx = dev.buf(x[off:off + cnt])
+        for op in ("sum", "mean", "max", "argmax", "min", "argmin"):
+            ho = dev.empty(Cc)
+            comm.reduce(op, hx, 1, cnt, Cc, off, R, ho)
+            dev.sync()
+            got = dev.read(ho, np.int32 if op.startswith("arg") else np.float32)
+            want = O.reduce(op, x, axis=0)
+            if op in ("sum", "mean"):
+                fin = np.isfinite(want)
+                errs[op] = float(np.max(np.abs(got[fin] - want[fin]) / np.maximum(np.abs(want[fin]), 1.0)))
+            else:
+                errs[op] = int(np.sum(~((got == want) | (np.isnan(got.astype(np.float32)) & np.isnan(
+                    want.astype(np.float32))))))
+            dev.free(ho)
+        dev.free(hx)
+        # full reduction of a flat vector
+        n = (1 << 21) + 5
+        v = r.uniform(-1, 1, n).astype(np.float32)
+        o2, c2 = shard_range(n, world, rank)
+        hv, ho = dev.buf(v[o2:o2 + c2]), dev.empty(1)
+        s = comm.reduce_all("sum", hv, c2, ho, want_host=True)
+        errs["full_sum"] = abs(s - float(v.astype(np.float64).sum())) / abs(float(v.astype(np.float64).sum()))
+        mx = comm.reduce_all("max", hv, c2, ho, want_host=True)
+        errs["full_max"] = int(mx != float(v.max()))
+        dev.free(hv, ho)
+        # softmax + CE, rows sharded, global divisor
+        B, K = 3000, 1000
+        lg = (3 * r.standard_normal((B, K))).astype(np.float32)
+        lab = r.integers(0, K, B)
+        o3, c3 = shard_range(B, world, rank)
+        hl, ht = dev.buf(lg[o3:o3 + c3]), dev.buf(lab[o3:o3 + c3].astype(np.float32))
+        hp, hg, hloss = dev.empty(c3 * K), dev.empty(c3 * K), dev.empty(1)
+        comm.softmax_ce(hl, ht, c3, K, probs=hp, dlogits=hg, loss=hloss, global_rows=B)
+        dev.sync()
+        _, loss64, _ = O.softmax_ce_f64(lg, lab)
+        errs["loss"] = abs(float(dev.read(hloss)[0]) - float(loss64)) / abs(float(loss64))
+        p_dev = dev.read(hp).reshape(c3, K)
+        want_g = O.softmax_ce_dlogits(p_dev, lab[o3:o3 + c3], B)
+        errs["dlogits"] = int(np.sum(dev.read(hg).view(np.uint32) != want_g.ravel().view(np.uint32)))
+        dev.free(hl, ht, hp, hg, hloss)
+        # BatchNorm, batch sharded
+        shape = (10, 32, 14, 14)
+        N, C, H, W = shape
+        S_ = H * W
+        x, dy, gamma, beta, rm0, rv0 = _bn_inputs(shape, 41)
+        o4, c4 = shard_range(N, world, rank)
+        hx, hdy = dev.buf(x[o4:o4 + c4]), dev.buf(dy[o4:o4 + c4])
+        hgm, hbt, hrm, hrv = dev.buf(gamma), dev.buf(beta), dev.buf(rm0), dev.buf(rv0)
+        hm, hvv, hy = dev.empty(C), dev.empty(C), dev.empty(c4 * C * S_)
+        hdg, hdb, hdx = dev.empty(C), dev.empty(C), dev.empty(c4 * C * S_)
+        comm.batchnorm_forward_train(hx, hgm, hbt, hrm, hrv, hm, hvv, hy, c4, C, S_, 1e-5, 0.1)
+        comm.batchnorm_backward(hx, hdy, hm, hvv, hgm, hdg, hdb, hdx, c4, C, S_, 1e-5)
+        dev.sync()
+        mean64, var64 = S.batchnorm_mean_var(x.ravel(), N, C, S_)
+        mean, var = dev.read(hm), dev.read(hvv)
+        errs["bn_mean"] = float(np.max(np.abs(mean - mean64) / np.maximum(np.abs(mean64), 1e-3)))
+        errs["bn_var"] = float(np.max(np.abs(var - var64) / var64))
+        rm_o, rv_o = S.batchnorm_running(rm0, rv0, mean64, var64, N, S_, 0.1)
+        errs["bn_running"] = float(max(np.max(np.abs(dev.read(hrm) - rm_o)), np.max(np.abs(dev.read(hrv) - rv_o) / rv_o)))
+        y_o = S.batchnorm_forward(x[o4:o4 + c4].ravel(), mean, var, gamma, beta, c4, C, S_, np.float32(1e-5))
+        errs["bn_y"] = int(np.sum(dev.read(hy).view(np.uint32) != y_o.view(np.uint32)))
+        dg_o, db_o = S.batchnorm_backward_reduce(x.ravel(), dy.ravel(), mean, var, N, C, S_, np.float32(1e-5))
+        dg, db = dev.read(hdg), dev.read(hdb)
+        errs["bn_dgamma"] = float(np.max(np.abs(dg - dg_o) / np.maximum(np.abs(dg_o), np.sqrt(N * S_) * 1e-6)))
+        errs["bn_dbeta"] = float(np.max(np.abs(db - db_o) / np.maximum(np.abs(db_o), np.sqrt(N * S_) * 1e-6)))
+        dx_o = _bn_dx_global(x[o4:o4 + c4], dy[o4:o4 + c4], mean, var, gamma, dg, db, C, S_, N * S_, 1e-5)
+        errs["bn_dx"] = int(np.sum(dev.read(hdx).view(np.uint32) != dx_o.view(np.uint32)))
+        dev.free(hx, hdy, hgm, hbt, hrm, hrv, hm, hvv, hy, hdg, hdb, hdx)
+        # fp32 all-reduce
+        a = np.full(4099, rank + 1.0, np.float32)
+        ha = dev.buf(a)
+        comm.allreduce(ha, a.size, "sum")
+        dev.sync()
+        errs["allreduce"] = int(np.sum(dev.read(ha) != sum(range(1, world + 1))))
+        dev.free(ha)
+        comm.close()
+        td.destroy_process_group()
+        q.put((rank, True, errs))
+    except BaseException:
+        q.put((rank, False, traceback.format_exc()))
+
+
+def test_world2_sharded_ops_match_unsharded_oracle():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_world2_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, ok, payload = q.get(timeout=600)
+            res[r] = (ok, payload)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in (0, 1):
+        ok, e = res[r]
+        assert ok, e
+        print(f"rank {r}: {e}")
+        for k in ("max", "argmax", "min", "argmin", "full_max", "dlogits", "bn_y", "bn_dx", "allreduce"):
+            assert e[k] == 0, (r, k, e[k])
+        for k in ("sum", "mean", "full_sum", "loss", "bn_mean", "bn_var", "bn_running", "bn_dgamma", "bn_dbeta"):
+            assert e[k] <= 1e-5, (r, k, e[k])
