@@ -581,7 +581,9 @@ def main():
                 per_op[k]["ms"] = ranks.max(per_op[k]["ms"])
                 per_op[k]["gbs"] = round(per_op[k]["bytes"] * world / (per_op[k]["ms"] * 1e-3) / 1e9, 1)
     for k, v in ops.items():
-        per_op[k] = {"gbs": round(v["gbs"], 1), "ms": round(v["ms"], 4), "bytes": v["bytes"], "launches": 1}
+        ms_k = ranks.max(v["ms"]) if world > 1 else v["ms"]     # every rank ran its shard: whole-job rate
+        per_op[k] = {"gbs": round(v["bytes"] * world / (ms_k * 1e-3) / 1e9, 1), "ms": round(ms_k, 4),
+                     "bytes": v["bytes"], "launches": 1}
     for k, v in per_op.items():
         v["frac_of_measured_hbm"] = round(v["gbs"] / (peak * world), 3)
         v["frac_of_8TBs"] = round(v["gbs"] / (NOMINAL_HBM_GBS * world), 3)

@@ -268,7 +268,9 @@ bool rt_wait_stream(const char* where) {
                 limit);
       return false;
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    // poll hot for the first 2 ms (short waits stay short), then back off
+    if (el < 2e-3) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
 
