@@ -222,6 +222,50 @@ def test_bounded_wait_times_out_and_context_survives(dev):
     print(f"bounded wait of 4096 polls gave up after {secs * 1e3:.1f} ms (host-observed)")
 
 
+def _lonely_rank(q):
+    """Rank 0 of a 2-rank communicator that rank 1 never joins (one GPU, one process)."""
+    try:
+        import torch  # noqa: F401
+        from directcompute_torch_b200 import load_library
+        from directcompute_torch_b200.dist import Communicator
+        lib = load_library()
+        assert lib.InitEngine()
+        t0 = time.monotonic()
+        try:
+            Communicator(0, 2, Communicator.new_unique_id(), timeout_s=3)
+            q.put(("returned", time.monotonic() - t0, ""))
+        except RuntimeError as e:
+            q.put(("raised", time.monotonic() - t0, str(e)))
+        # work on the device still runs after the failed init
+        h = lib.dct_create_buffer(1024)
+        lib.ClearBuffer(h)
+        q.put(("sync", lib.dct_synchronize(), ""))
+    except BaseException:
+        q.put(("crash", 0.0, traceback.format_exc()))
+    q.close()
+    q.join_thread()    # flush the queue's feeder thread before leaving
+    os._exit(0)        # the abandoned init helper is still waiting for rank 1: skip exit-time teardown
+
+
+def test_init_gives_up_when_a_rank_never_joins():
+    """Host-made failure: the peer never calls init.  dct_dist_init returns
+    DCT_ERR_DIST at its deadline instead of blocking the caller."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely_rank, args=(q,))
+    p.start()
+    try:
+        what, secs, msg = q.get(timeout=120)
+        assert what == "raised", (what, msg)
+        assert "not every rank joined" in msg and 2.5 < secs < 30, (secs, msg)
+        what, rc, msg = q.get(timeout=60)
+        assert what == "sync" and rc == 0, (what, rc, msg)
+    finally:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+
+
 # ---------------------------------------------------------------------------
 # two GPUs, two processes
 # ---------------------------------------------------------------------------
