@@ -19,7 +19,10 @@ PF32 = C.POINTER(C.c_float)
 # op codes (include/dct_cuda.h)
 UNARY = {"relu": 0, "relu6": 1, "leaky_relu": 2, "sigmoid": 3, "exp": 4, "log_abs1p": 5, "tanh": 6,
          "neg": 7, "abs": 8}
-BINARY = {"add": 20, "sub": 21, "mul": 22, "div": 23, "maximum": 24, "minimum": 25}
+BINARY = {"add": 20, "sub": 21, "mul": 22, "div": 23, "maximum": 24, "minimum": 25,
+          # gradient helpers (same shapes except the pick masks, which broadcast)
+          "sigmoid_grad": 19, "pick_max": 27, "pick_min": 28, "exp_grad": 29, "tanh_grad": 30,
+          "log_abs1p_grad": 31, "copy": 32}
 REDUCE = {"sum": 0, "mean": 1, "max": 2, "argmax": 3, "min": 4, "argmin": 5, "sumsq": 6}
 
 ERRORS = {0: "OK", 1: "NO_DEVICE", 2: "HANDLE", 3: "SIZE", 4: "ARG", 5: "CUDA", 6: "UNKNOWN_SHADER",
@@ -107,6 +110,8 @@ SIGNATURES = {
     "dct_batchnorm_forward_train": ([VP] * 8 + [U32, U32, U32, F32, F32], C.c_int),
     "dct_batchnorm_backward": ([VP] * 8 + [U32, U32, U32, F32], C.c_int),
     "dct_batchnorm_forward_train_noalloc": ([VP] * 8 + [U32, U32, U32, F32, F32, VP], C.c_int),
+    "dct_sum_to_shape": ([VP, C.POINTER(C.c_int64), C.c_int, C.POINTER(C.c_int64), C.c_int, VP], C.c_int),
+    "dct_broadcast_to": ([VP, C.POINTER(C.c_int64), C.c_int, C.POINTER(C.c_int64), C.c_int, VP], C.c_int),
     # sharding over NCCL
     "dct_dist_available": ([], C.c_int),
     "dct_dist_nccl_version": ([], C.c_int),

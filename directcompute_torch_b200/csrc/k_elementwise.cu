@@ -70,6 +70,19 @@ DCT_DEV float binary_op(float a, float b, float alpha, float beta) {
     return __fmul_rn(a, b > 0.0f ? 1.0f : alpha);
   } else if constexpr (OP == EW_SIGMOID_GRAD) {        // (dy, y): dy*y*(1-y)
     return __fmul_rn(__fmul_rn(a, b), __fsub_rn(1.0f, b));
+  } else if constexpr (OP == EW_PICK_MAX) {            // maximum's gradient goes to a
+    return (a >= b || isnan(a)) ? 1.0f : 0.0f;
+  } else if constexpr (OP == EW_PICK_MIN) {
+    return (a <= b || isnan(a)) ? 1.0f : 0.0f;
+  } else if constexpr (OP == EW_EXP_GRAD) {            // (g, y = exp(x)): g*y
+    return __fmul_rn(a, b);
+  } else if constexpr (OP == EW_TANH_GRAD) {           // (g, y = tanh(x)): g*(1-y*y)
+    return __fmul_rn(a, __fsub_rn(1.0f, __fmul_rn(b, b)));
+  } else if constexpr (OP == EW_LOG_ABS1P_GRAD) {      // (g, x): g*sign(x)/(|x|+1)
+    const float q = __fdiv_rn(a, __fadd_rn(fabsf(b), 1.0f));
+    return b > 0.0f ? q : (b < 0.0f ? -q : (b == 0.0f ? 0.0f : b));
+  } else if constexpr (OP == EW_FIRST) {               // broadcast copy of a
+    return a;
   } else {                                             // EW_SCALE_ADD
     return __fadd_rn(__fmul_rn(alpha, a), __fmul_rn(beta, b));
   }
@@ -332,8 +345,10 @@ __global__ void __launch_bounds__(256) k_add_bias_scalar(const float* A, const f
 #define DCT_UNARY_CASES(X) X(EW_RELU) X(EW_RELU6) X(EW_LEAKY_RELU) X(EW_SIGMOID) X(EW_EXP) \
   X(EW_LOG_ABS1P) X(EW_TANH) X(EW_NEG) X(EW_ABS)
 #define DCT_BINARY_CASES(X) X(EW_ADD) X(EW_SUB) X(EW_MUL) X(EW_DIV) X(EW_MAXIMUM) X(EW_MINIMUM) \
-  X(EW_RELU_GRAD) X(EW_RELU6_GRAD) X(EW_LEAKY_RELU_GRAD) X(EW_SIGMOID_GRAD) X(EW_SCALE_ADD)
-#define DCT_BCAST_CASES(X) X(EW_ADD) X(EW_SUB) X(EW_MUL) X(EW_DIV) X(EW_MAXIMUM) X(EW_MINIMUM)
+  X(EW_RELU_GRAD) X(EW_RELU6_GRAD) X(EW_LEAKY_RELU_GRAD) X(EW_SIGMOID_GRAD) X(EW_SCALE_ADD)     \
+  X(EW_PICK_MAX) X(EW_PICK_MIN) X(EW_EXP_GRAD) X(EW_TANH_GRAD) X(EW_LOG_ABS1P_GRAD) X(EW_FIRST)
+#define DCT_BCAST_CASES(X) X(EW_ADD) X(EW_SUB) X(EW_MUL) X(EW_DIV) X(EW_MAXIMUM) X(EW_MINIMUM) \
+  X(EW_PICK_MAX) X(EW_PICK_MIN) X(EW_FIRST)
 
 constexpr uint64_t kMaxChunkN4 = (1ull << 31) * kChunk4;   // grid.x limit
 

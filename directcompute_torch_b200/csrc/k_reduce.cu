@@ -31,6 +31,7 @@ namespace dct {
 namespace {
 
 constexpr int kRedThreads = 256;
+constexpr int kSumMaxDims = 8;
 constexpr int kRedWarps = kRedThreads / 32;
 
 // max / min that return NaN if either operand is NaN (one instruction)
@@ -517,6 +518,167 @@ cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t
     case RED_SUMSQ: return run_fold_packed<RED_SUMSQ>(parts, nparts, nout, stride, len_total, ro, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// ---------------------------------------------------------------------------
+// broadcast gradient (sum over the dims an operand was broadcast along)
+// ---------------------------------------------------------------------------
+namespace {
+
+// Collapsed view of g: alternating groups of kept / reduced dims.
+struct SumPlan {
+  int ng = 0;
+  uint64_t ext[kSumMaxDims];
+  bool red[kSumMaxDims];
+};
+
+SumPlan plan_sum(int ndim, const int64_t* gshape, const int64_t* tshape) {
+  SumPlan p;
+  for (int d = 0; d < ndim; ++d) {
+    const uint64_t e = (uint64_t)gshape[d];
+    if (e == 1) continue;                                   // carries nothing
+    const bool r = tshape[d] == 1;
+    if (p.ng > 0 && p.red[p.ng - 1] == r) { p.ext[p.ng - 1] *= e; continue; }
+    p.ext[p.ng] = e;
+    p.red[p.ng] = r;
+    ++p.ng;
+  }
+  return p;
+}
+
+// Generic form (two or more reduced groups): one thread per output element and
+// chunk of the reduced index space, walked with an odometer; fp64 sums, folded
+// over chunks in order by k_fold_chunks.
+struct SumMap {
+  int nk, nr;
+  uint64_t kext[kSumMaxDims];
+  uint64_t kstr[kSumMaxDims];
+  uint64_t rext[kSumMaxDims];
+  uint64_t rstr[kSumMaxDims];
+};
+
+__global__ void __launch_bounds__(256) k_sum_generic(const float* __restrict__ g, SumMap m, uint64_t nout,
+                                                     uint64_t rtot, uint64_t cl, float* out,
+                                                     unsigned long long* part) {
+  const uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= nout) return;
+  uint64_t rem = k, base = 0;
+  for (int i = m.nk - 1; i >= 0; --i) {
+    const uint64_t q = rem / m.kext[i];
+    base += (rem - q * m.kext[i]) * m.kstr[i];
+    rem = q;
+  }
+  const uint64_t r0 = (uint64_t)blockIdx.y * cl;
+  const uint64_t r1 = min(rtot, r0 + cl);
+  uint64_t ridx[kSumMaxDims];
+  uint64_t off = 0;
+  rem = r0;
+  for (int j = m.nr - 1; j >= 0; --j) {
+    const uint64_t q = rem / m.rext[j];
+    ridx[j] = rem - q * m.rext[j];
+    off += ridx[j] * m.rstr[j];
+    rem = q;
+  }
+  double s = 0.0;
+  for (uint64_t r = r0; r < r1; ++r) {
+    s += (double)g[base + off];
+    for (int j = m.nr - 1; j >= 0; --j) {                   // odometer step, last group fastest
+      off += m.rstr[j];
+      if (++ridx[j] < m.rext[j]) break;
+      off -= m.rstr[j] * m.rext[j];
+      ridx[j] = 0;
+    }
+  }
+  if (gridDim.y == 1) out[k] = (float)s;
+  else part[(uint64_t)blockIdx.y * nout + k] = (unsigned long long)__double_as_longlong(s);
+}
+
+struct GenericSplit {
+  uint64_t nout, rtot, chunks, cl;
+};
+
+GenericSplit split_generic(const SumPlan& p) {
+  GenericSplit s{1, 1, 1, 1};
+  for (int i = 0; i < p.ng; ++i) (p.red[i] ? s.rtot : s.nout) *= p.ext[i];
+  const DevInfo& d = dev_info();
+  const uint64_t target = (uint64_t)d.sm_count * d.max_threads_per_sm * 2;
+  if (s.nout < target && s.rtot > 256) {
+    s.chunks = std::min<uint64_t>((target + s.nout - 1) / s.nout, (s.rtot + 255) / 256);
+    s.chunks = std::min<uint64_t>(s.chunks, 65535);
+  }
+  s.cl = (s.rtot + s.chunks - 1) / s.chunks;
+  s.chunks = (s.rtot + s.cl - 1) / s.cl;
+  return s;
+}
+
+}  // namespace
+
+size_t sum_to_shape_ws_bytes(int ndim, const int64_t* gshape, const int64_t* tshape) {
+  if (ndim < 0 || ndim > kSumMaxDims) return 0;
+  const SumPlan p = plan_sum(ndim, gshape, tshape);
+  int nred = 0;
+  for (int i = 0; i < p.ng; ++i) nred += p.red[i];
+  if (nred == 0) return 0;
+  if (nred == 1 && p.ng <= 3) {                             // [K][R][K]: one 3-D reduction
+    uint64_t o = 1, l = 1, in = 1;
+    int i = 0;
+    if (!p.red[0]) o = p.ext[i++];
+    l = p.ext[i++];
+    if (i < p.ng) in = p.ext[i];
+    return reduce3d_ws_bytes(RED_SUM, o, l, in);
+  }
+  const GenericSplit s = split_generic(p);
+  return s.chunks > 1 ? (size_t)(s.nout * s.chunks * sizeof(unsigned long long)) : 0;
+}
+
+cudaError_t launch_sum_to_shape(const float* g, int ndim, const int64_t* gshape, const int64_t* tshape,
+                                float* out, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (ndim < 0 || ndim > kSumMaxDims) return cudaErrorInvalidValue;
+  uint64_t n = 1;
+  for (int d = 0; d < ndim; ++d) {
+    if (gshape[d] < 0 || !(tshape[d] == 1 || tshape[d] == gshape[d])) return cudaErrorInvalidValue;
+    n *= (uint64_t)gshape[d];
+  }
+  const SumPlan p = plan_sum(ndim, gshape, tshape);
+  uint64_t nout = 1;
+  int nred = 0;
+  for (int i = 0; i < p.ng; ++i) {
+    if (p.red[i]) ++nred;
+    else nout *= p.ext[i];
+  }
+  if (n == 0) {                                             // empty input: sums of nothing
+    uint64_t tn = 1;
+    for (int d = 0; d < ndim; ++d) tn *= (uint64_t)tshape[d];
+    return tn ? cudaMemsetAsync(out, 0, tn * sizeof(float), st) : cudaSuccess;
+  }
+  if (nred == 0) return cudaMemcpyAsync(out, g, n * sizeof(float), cudaMemcpyDeviceToDevice, st);
+  if (nred == 1 && p.ng <= 3) {
+    uint64_t o = 1, l = 1, in = 1;
+    int i = 0;
+    if (!p.red[0]) o = p.ext[i++];
+    l = p.ext[i++];
+    if (i < p.ng) in = p.ext[i];
+    return launch_reduce3d(RED_SUM, g, o, l, in, out, nullptr, ws, st);
+  }
+  // generic: strides of each group in g (row-major, contiguous)
+  SumMap m{};
+  uint64_t stride = 1;
+  uint64_t gstr[kSumMaxDims];
+  for (int i = p.ng - 1; i >= 0; --i) { gstr[i] = stride; stride *= p.ext[i]; }
+  for (int i = 0; i < p.ng; ++i) {
+    if (p.red[i]) { m.rext[m.nr] = p.ext[i]; m.rstr[m.nr] = gstr[i]; ++m.nr; }
+    else { m.kext[m.nk] = p.ext[i]; m.kstr[m.nk] = gstr[i]; ++m.nk; }
+  }
+  const GenericSplit sp = split_generic(p);
+  unsigned long long* part = (unsigned long long*)ws;
+  if (sp.chunks > 1 && (!ws || ws_bytes < sp.nout * sp.chunks * sizeof(unsigned long long)))
+    return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)((sp.nout + 255) / 256), (unsigned)sp.chunks, 1);
+  if (grid.x == 0 || (sp.nout + 255) / 256 > 0x7fffffffull) return cudaErrorInvalidValue;
+  k_sum_generic<<<grid, 256, 0, st>>>(g, m, sp.nout, sp.rtot, sp.cl, out, part);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || sp.chunks == 1) return e;
+  return launch_fold_packed(RED_SUM, part, (uint32_t)sp.chunks, sp.nout, sp.nout, sp.rtot, out, nullptr, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -15,6 +15,10 @@ enum EwOp : int {
   EW_NEG, EW_ABS,
   EW_RELU_GRAD = 16, EW_RELU6_GRAD, EW_LEAKY_RELU_GRAD, EW_SIGMOID_GRAD,
   EW_ADD, EW_SUB, EW_MUL, EW_DIV, EW_MAXIMUM, EW_MINIMUM, EW_SCALE_ADD,
+  // gradient helpers: masks of where maximum / minimum(a, b) routes the
+  // gradient to a (a >= b resp. a <= b, or a is NaN: 1.0 else 0.0), the
+  // unary ops' backward (g, saved tensor), and a broadcast copy of a
+  EW_PICK_MAX = 27, EW_PICK_MIN, EW_EXP_GRAD, EW_TANH_GRAD, EW_LOG_ABS1P_GRAD, EW_FIRST,
   EW_GAP_BWD = 40,
 };
 // y[i] = op(x[i]) for i < n (unary ops; alpha = leaky slope)
@@ -65,6 +69,12 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
                                    int32_t idx_off, unsigned long long* packed, void* ws, cudaStream_t st);
 cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,
                                uint64_t stride, uint64_t len_total, float* out, int32_t* out_idx, cudaStream_t st);
+// Broadcast gradient: out (shape t) = g (shape gshape, ndim <= 8) summed over
+// every dim where t has extent 1 and g does not (t right-aligned and padded
+// with 1s to ndim).  float64 accumulation, rounded once.
+size_t sum_to_shape_ws_bytes(int ndim, const int64_t* gshape, const int64_t* tshape);
+cudaError_t launch_sum_to_shape(const float* g, int ndim, const int64_t* gshape, const int64_t* tshape,
+                                float* out, void* ws, size_t ws_bytes, cudaStream_t st);
 // General strided form: out[o*inner + i] = reduce_l x[o*so + l*sl + i*si].
 size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
                                uint64_t si);

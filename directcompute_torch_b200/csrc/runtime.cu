@@ -1353,6 +1353,63 @@ DCT_API int dct_binary(int op, void* a, const int64_t* a_shape, int a_ndim, void
   return run_ext("dct_binary", s, 2, u, 1, cb, 4 + nd);
 }
 
+// Right-align `t` against `g` (ndim = g_ndim), padding with 1s; false if t does
+// not broadcast to g.
+static bool align_target(const int64_t* g_shape, int g_ndim, const int64_t* t_shape, int t_ndim, int64_t* t_out,
+                         const char* where) {
+  if (g_ndim < 0 || g_ndim > 8 || t_ndim < 0 || t_ndim > g_ndim || (g_ndim && !g_shape) || (t_ndim && !t_shape)) {
+    set_error(DCT_ERR_ARG, "%s: need 0 <= ndim(target) <= ndim(full) <= 8", where);
+    return false;
+  }
+  for (int d = 0; d < g_ndim; ++d) {
+    const int td = d - (g_ndim - t_ndim);
+    t_out[d] = td >= 0 ? t_shape[td] : 1;
+    if (g_shape[d] < 0 || !(t_out[d] == 1 || t_out[d] == g_shape[d])) {
+      set_error(DCT_ERR_ARG, "%s: shape of the target does not broadcast to the full shape at dim %d", where, d);
+      return false;
+    }
+  }
+  return true;
+}
+
+DCT_API int dct_sum_to_shape(void* grad, const int64_t* g_shape, int g_ndim, const int64_t* t_shape, int t_ndim,
+                             void* out) {
+  LOCK;
+  if (!ensure_init()) return DCT_ERR_NO_DEVICE;
+  int64_t t[8];
+  if (!align_target(g_shape, g_ndim, t_shape, t_ndim, t, "dct_sum_to_shape")) return DCT_ERR_ARG;
+  Buffer *bg = buf_of(grad), *bo = buf_of(out);
+  if (!bg || !bo) { set_error(DCT_ERR_HANDLE, "dct_sum_to_shape: not a live buffer"); return DCT_ERR_HANDLE; }
+  uint64_t n = 1, tn = 1;
+  for (int d = 0; d < g_ndim; ++d) { n *= (uint64_t)g_shape[d]; tn *= (uint64_t)t[d]; }
+  if (bg->count < n || bo->count < tn) { set_error(DCT_ERR_SIZE, "dct_sum_to_shape: buffer too small"); return DCT_ERR_SIZE; }
+  const size_t ws = sum_to_shape_ws_bytes(g_ndim, g_shape, t);
+  if (ws && !ensure_ws(ws)) return DCT_ERR_CUDA;
+  return cuda_ok(launch_sum_to_shape(bg->d, g_ndim, g_shape, t, bo->d, g.ws, g.ws_bytes, g.stream),
+                 "dct_sum_to_shape") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_broadcast_to(void* x, const int64_t* x_shape, int x_ndim, const int64_t* out_shape, int out_ndim,
+                             void* out) {
+  LOCK;
+  if (!ensure_init()) return DCT_ERR_NO_DEVICE;
+  int64_t xs[8];
+  if (!align_target(out_shape, out_ndim, x_shape, x_ndim, xs, "dct_broadcast_to")) return DCT_ERR_ARG;
+  Buffer *bx = buf_of(x), *bo = buf_of(out);
+  if (!bx || !bo) { set_error(DCT_ERR_HANDLE, "dct_broadcast_to: not a live buffer"); return DCT_ERR_HANDLE; }
+  int64_t str[8];
+  uint64_t n = 1, xn = 1;
+  int64_t s = 1;
+  for (int d = out_ndim - 1; d >= 0; --d) {
+    str[d] = xs[d] == 1 ? 0 : s;
+    s *= xs[d];
+  }
+  for (int d = 0; d < out_ndim; ++d) { n *= (uint64_t)out_shape[d]; xn *= (uint64_t)xs[d]; }
+  if (bx->count < xn || bo->count < n) { set_error(DCT_ERR_SIZE, "dct_broadcast_to: buffer too small"); return DCT_ERR_SIZE; }
+  return cuda_ok(launch_binary_bcast(EW_FIRST, bx->d, bx->d, bo->d, out_ndim, out_shape, str, str, g.stream),
+                 "dct_broadcast_to") ? 0 : DCT_ERR_CUDA;
+}
+
 DCT_API int dct_reduce(int op, void* x, uint64_t outer, uint64_t len, uint64_t inner, void* out, void* out_idx) {
   LOCK;
   if (outer > 0xffffffffull || len > 0xffffffffull || inner > 0xffffffffull) return DCT_ERR_ARG;

@@ -201,10 +201,23 @@ DCT_API int dct_scatter(void* handle, const int64_t* idx, const float* vals, uin
 
 /* unary ops: 0 relu 1 relu6 2 leaky_relu(alpha) 3 sigmoid 4 exp 5 log(|x|+1) 6 tanh 7 neg 8 abs */
 DCT_API int dct_unary(int op, void* x, void* y, uint64_t n, float alpha);
-/* NumPy-broadcast binary op: 20 add 21 sub 22 mul 23 div 24 maximum 25 minimum.
+/* NumPy-broadcast binary op: 20 add 21 sub 22 mul 23 div 24 maximum 25 minimum;
+ * gradient masks 27 pick_max / 28 pick_min = 1.0 where maximum / minimum(a, b)
+ * routes the gradient to a (a >= b resp. a <= b, or a is NaN), else 0.0.
+ * Same shapes only: 19 sigmoid_grad(dy, y) = dy*y*(1-y), 29 exp_grad(g, y) = g*y,
+ * 30 tanh_grad(g, y) = g*(1-y*y), 31 log_abs1p_grad(g, x) = g*sign(x)/(|x|+1),
+ * 32 copy (out = a broadcast to the output shape; b is not used but must be valid).
  * Shapes are right-aligned; out has the broadcast shape (<= 8 dims). */
 DCT_API int dct_binary(int op, void* a, const int64_t* a_shape, int a_ndim, void* b, const int64_t* b_shape,
                        int b_ndim, void* out);
+/* broadcast gradient: out (t_shape) = g (g_shape) summed over the dims where
+ * t_shape (right-aligned, padded with 1s) has extent 1 and g does not; float64
+ * accumulation rounded once (the reverse of NumPy broadcasting) */
+DCT_API int dct_sum_to_shape(void* g, const int64_t* g_shape, int g_ndim, const int64_t* t_shape, int t_ndim,
+                             void* out);
+/* out (out_shape) = x (x_shape) broadcast NumPy-style (the reverse of dct_sum_to_shape) */
+DCT_API int dct_broadcast_to(void* x, const int64_t* x_shape, int x_ndim, const int64_t* out_shape, int out_ndim,
+                             void* out);
 /* reduce x viewed as [outer, len, inner] over len: 0 sum 1 mean 2 max 3 argmax 4 min
  * 5 argmin 6 sum of squares; float64 accumulation; arg ops write int32 to out_idx
  * (or to out when out_idx is null); max/min also write indices when out_idx is set */
