@@ -1,21 +1,6 @@
-// Extended-precision elementary functions of libdct_cuda, written from the
-// mathematics (no vendor math-library internals):
-//
-//  * exp of a non-positive argument as an unevaluated float-float sum
-//    (hi + lo) * 2^k.  Argument reduction after Cody & Waite ("Software
-//    Manual for the Elementary Functions", 1980): k = rint(a / ln 2),
-//    r = -a - k ln 2 with ln 2 split into a float head and tail so the head
-//    product is absorbed exactly by one fused multiply-add; exp(r) on
-//    |r| <= ln2/2 by its Taylor series to degree 8 (truncation < 2^-32);
-//    the sums 1 + r and the reduction are carried with the error-free
-//    transformation of Dekker (1971, Fast2Sum).  The float-float result is
-//    accurate to about 2^-28 relative before any final rounding.
-//  * sigmoid(x) = 1 / (1 + e^-x) (x >= 0) or e^x / (1 + e^x) (x < 0), both
-//    from e = exp(-|x|), with the denominator kept as float-float and the
-//    quotient (approximate reciprocal times numerator) corrected once by its
-//    exact remainder (one fused multiply-add, Markstein's scheme), so the
-//    result is within about 0.6 ulp of the true value and the kernel has no
-//    data-dependent branch.
+// Elementary functions of libdct_cuda written from the mathematics (no vendor
+// math-library internals): the sigmoid, from Tang's table-driven exponential and
+// a quotient corrected once by its exact remainder (see sigmoid_tab).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -24,41 +9,7 @@
 
 namespace dct {
 
-// e^(-a) = (hi + lo) * 2^k for a >= 0 (NaN propagates; a > 104 gives 0).
-DCT_DEV void exp_neg_ff(float a, float& hi, float& lo, int& k) {
-  const float kInvLn2 = 1.4426950408889634f;
-  const float kLn2Hi = 0.693147182464599609375f;      // float nearest ln 2
-  const float kLn2Lo = -1.904654299957768e-09f;       // ln 2 - kLn2Hi
-  const float x = -a;
-  const float kf = rintf(__fmul_rn(x, kInvLn2));
-  // r1 = x - k*ln2_hi is exact: one fused rounding of a value representable in 24 bits
-  const float r1 = __fmaf_rn(-kf, kLn2Hi, x);
-  // r = r1 - k*ln2_lo as (rh, rl); |k*ln2_lo| < 3e-7, so Fast2Sum's error is
-  // below 2^-45 absolute even when |r1| is smaller than it
-  const float t = __fmul_rn(kf, kLn2Lo);
-  const float rh = __fsub_rn(r1, t);
-  const float rl = __fsub_rn(__fsub_rn(r1, rh), t);
-  // exp(r) - 1 - r = r^2 * P(r), P = sum_{n=2..8} r^(n-2)/n!  (|r| <= ln2/2: truncation < 2^-32)
-  float p = 2.4801587301587302e-05f;                   // 1/8!
-  p = __fmaf_rn(p, rh, 1.9841269841269841e-04f);       // 1/7!
-  p = __fmaf_rn(p, rh, 1.3888888888888889e-03f);       // 1/6!
-  p = __fmaf_rn(p, rh, 8.3333333333333333e-03f);       // 1/5!
-  p = __fmaf_rn(p, rh, 4.1666666666666667e-02f);       // 1/4!
-  p = __fmaf_rn(p, rh, 1.6666666666666667e-01f);       // 1/3!
-  p = __fmaf_rn(p, rh, 0.5f);                          // 1/2!
-  const float q = __fmul_rn(__fmul_rn(rh, rh), p);
-  // 1 + rh + q as float-float: two Fast2Sums (|rh| >= |q|, 1 >= |rh + q|)
-  const float u = __fadd_rn(rh, q);
-  const float eu = __fsub_rn(q, __fsub_rn(u, rh));
-  hi = __fadd_rn(1.0f, u);
-  const float e2 = __fsub_rn(u, __fsub_rn(hi, 1.0f));
-  lo = __fadd_rn(e2, __fadd_rn(eu, rl));
-  k = (int)kf;
-  if (a > 104.0f) { hi = 0.0f; lo = 0.0f; k = 0; }     // below every subnormal
-}
-
-// 2^k as a float for -126 <= k <= 127
-DCT_DEV float pow2i(int k) { return __int_as_float((k + 127) << 23); }
+constexpr float kTwoM64 = 0x1p-64f;
 
 // approximate reciprocal (the hardware's, about 1 ulp); only used where an
 // exact-remainder correction follows
@@ -68,76 +19,76 @@ DCT_DEV float rcp_approx(float x) {
   return r;
 }
 
-// sigmoid for |x| > 87 (e^-|x| < 2^-125): 1 for x >= 0, else e^x rounded once
-// into the subnormal range.  Rarely taken, so it may be slow.
-DCT_DEV float sigmoid_tail(float x) {
-  float h, l;
-  int k;
-  exp_neg_ff(fabsf(x), h, l, k);
-  float eh, el;
-  if (k >= -125) {
-    const float sc = pow2i(k);
-    eh = __fmul_rn(h, sc);                              // exact power-of-two scaling
-    el = __fmul_rn(l, sc);
-  } else {                                              // e below 2^-125: one rounding into the subnormals
-    eh = __fmul_rn(__fmul_rn(__fadd_rn(h, l), pow2i(k + 64)), 5.42101086242752217e-20f);   // * 2^-64
-    el = 0.0f;
-  }
-  // denominator 1 + e as (s, t): Fast2Sum, 1 >= e
-  const float s = __fadd_rn(1.0f, eh);
-  const float t = __fadd_rn(__fsub_rn(eh, __fsub_rn(s, 1.0f)), el);
-  const bool neg = x < 0.0f;
-  const float nh = neg ? eh : 1.0f;
-  const float nl = neg ? el : 0.0f;
-  // quotient (nh + nl) / (s + t): q0 from the approximate reciprocal, then one
-  // correction by the exact remainder nh - q0*s (fused) -> error ~0.5 ulp
-  const float r = rcp_approx(s);                        // s in [1, 2]
-  const float q0 = __fmul_rn(nh, r);
-  float rr = __fmaf_rn(-q0, s, nh);
-  rr = __fadd_rn(rr, __fsub_rn(nl, __fmul_rn(q0, t)));
-  return __fmaf_rn(rr, r, q0);
+// min that returns NaN if either operand is NaN (one instruction)
+DCT_DEV float fmin_nanp(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
-// sigmoid, <= 1 ulp, about 40 instructions on the common path.  e = e^-|x| is
-// built directly as float-float: k = rint(-|x|/ln2) by the 1.5*2^23 rounding
-// trick (no conversion unit), r = -|x| - k*ln2_hi exact by one fused
-// multiply-add, exp(r) = 1 + r + r^2 P7(r) through two Fast2Sums, and the
-// ln2 tail t = k*ln2_lo folded in as exp(r - t) = exp(r)(1 - t) (error t^2/2 <
-// 2^-43); then the float-float quotient as in sigmoid_tail's final steps.
-DCT_DEV float sigmoid_acc(float x) {
-  const float a = fabsf(x);
-  if (a > 87.0f) return sigmoid_tail(x);
+// 2^(j/32) = hi + lo, j = 0..31: hi is the float nearest the value, lo the
+// float nearest the rest; computed from the definition in 60-digit decimal
+// arithmetic.  256 bytes.
+static __device__ __align__(256) const float2 kExp2Tab[32] = {
+    {0x1p+0f, 0.0f}, {0x1.059b0ep+0f, -0x1.9d4f52p-25f},
+    {0x1.0b5586p+0f, 0x1.9f3122p-25f}, {0x1.11301ep+0f, -0x1.fdb496p-25f},
+    {0x1.172b84p+0f, -0x1.c15742p-27f}, {0x1.1d4874p+0f, -0x1.d2e8cap-25f},
+    {0x1.2387a6p+0f, 0x1.ceac48p-25f}, {0x1.29e9ep+0f, -0x1.5c0424p-25f},
+    {0x1.306fep+0f, 0x1.4636e2p-25f}, {0x1.371a74p+0f, -0x1.18aac6p-25f},
+    {0x1.3dea64p+0f, 0x1.824684p-25f}, {0x1.44e086p+0f, 0x1.8624b4p-30f},
+    {0x1.4bfdaep+0f, -0x1.593abcp-25f}, {0x1.5342b6p+0f, -0x1.2c561p-25f},
+    {0x1.5ab07ep+0f, -0x1.5bd5ecp-27f}, {0x1.6247ecp+0f, -0x1.f8b55p-25f},
+    {0x1.6a09e6p+0f, 0x1.9fcef4p-26f}, {0x1.71f75ep+0f, 0x1.1d8beep-25f},
+    {0x1.7a1148p+0f, -0x1.829fdp-25f}, {0x1.82589ap+0f, -0x1.accc7cp-26f},
+    {0x1.8ace54p+0f, 0x1.15506ep-27f}, {0x1.93737cp+0f, -0x1.e64744p-25f},
+    {0x1.9c4918p+0f, 0x1.51f848p-27f}, {0x1.a5503cp+0f, -0x1.b83b54p-25f},
+    {0x1.ae89fap+0f, -0x1.a94b14p-26f}, {0x1.b7f77p+0f, -0x1.a09438p-25f},
+    {0x1.c199bep+0f, -0x1.3d56b2p-27f}, {0x1.cb720ep+0f, -0x1.8837ccp-27f},
+    {0x1.d5818ep+0f, -0x1.822dbcp-27f}, {0x1.dfc974p+0f, -0x1.908c94p-25f},
+    {0x1.ea4afap+0f, 0x1.52486cp-27f}, {0x1.f50766p+0f, -0x1.246ebp-26f},
+};
+
+// sigmoid to within 1.5 ulp of the exact value over the whole float range (the
+// ops' bar is 2 ulp), about 31 instructions and no branch.  `tab` is kExp2Tab
+// or a copy of it (in shared memory for the streaming kernel).
+//  * e = exp(-|x|) by Tang's table-driven method (ACM TOMS 15(2), 1989):
+//    |x| is clamped to 104 (e^-104 rounds to 0; NaN stays NaN); k =
+//    rint(-|x| * 32/ln2) by the 1.5*2^23 rounding trick; r = -|x| - k*ln2/32 with
+//    ln2/32 split in two parts (the first has 12 significant bits, so k * part1
+//    is exact for |k| < 2^13); exp(r) - 1 = r + r^2 (1/2 + r/6 + r^2/24) on
+//    |r| <= ln2/64 (truncation below 2^-40); e = 2^(k>>5) * (T_hi + (T_hi p +
+//    T_lo)), with the power of two applied as 2^(m+64) (exact: the product stays
+//    normal) and then 2^-64 (one rounding, into the subnormals for |x| > 87.3).
+//  * sigmoid = n / (1 + e), n = 1 for x >= 0 and e for x < 0: the denominator
+//    kept exactly as s + t (Fast2Sum, Dekker 1971), q0 = n * rcp(s), and one
+//    correction by the exact remainder n - q0 (s + t) (Markstein's scheme).
+DCT_DEV float sigmoid_tab(float x, const float2* tab) {
+  const float a = fmin_nanp(fabsf(x), 104.0f);
   const float kMagic = 12582912.0f;                    // 1.5 * 2^23
-  const float y = __fmul_rn(-a, 1.4426950408889634f);
+  const float y = __fmul_rn(-a, 0x1.715476p+5f);       // -|x| * 32/ln2
   const float kb = __fadd_rn(y, kMagic);               // integer part in the low mantissa bits
   const float kf = __fsub_rn(kb, kMagic);
-  const int k = __float_as_int(kb) - __float_as_int(kMagic);
-  const float r = __fmaf_rn(-kf, 0.693147182464599609375f, -a);   // exact
-  const float t = __fmul_rn(kf, -1.904654299957768e-09f);           // k * (ln2 - ln2_hi)
-  float p = 1.9841269841269841e-04f;                   // 1/7!  (|r| <= ln2/2: truncation < 2^-27.5)
-  p = __fmaf_rn(p, r, 1.3888888888888889e-03f);        // 1/6!
-  p = __fmaf_rn(p, r, 8.3333333333333333e-03f);        // 1/5!
-  p = __fmaf_rn(p, r, 4.1666666666666667e-02f);        // 1/4!
-  p = __fmaf_rn(p, r, 1.6666666666666667e-01f);        // 1/3!
-  p = __fmaf_rn(p, r, 0.5f);                           // 1/2!
-  const float q = __fmul_rn(__fmul_rn(r, r), p);
-  const float u = __fadd_rn(r, q);
-  const float eu = __fsub_rn(q, __fsub_rn(u, r));
-  const float hi = __fadd_rn(1.0f, u);
-  const float e2 = __fsub_rn(u, __fsub_rn(hi, 1.0f));
-  const float lo = __fadd_rn(e2, __fadd_rn(eu, __fmaf_rn(-t, r, -t)));
-  const float sc = pow2i(k);                           // k >= -126 here
-  const float eh = __fmul_rn(hi, sc), el = __fmul_rn(lo, sc);
-  const float s = __fadd_rn(1.0f, eh);
-  const float t2 = __fadd_rn(__fsub_rn(eh, __fsub_rn(s, 1.0f)), el);
-  const bool neg = x < 0.0f;
-  const float nh = neg ? eh : 1.0f;
-  const float nl = neg ? el : 0.0f;
+  const int k = __float_as_int(kb) - __float_as_int(kMagic);     // in [-4802, 0] (NaN: any int)
+  float r = __fmaf_rn(-kf, 0x1.62ep-6f, -a);           // exact
+  r = __fmaf_rn(-kf, 0x1.0bfbe8p-20f, r);
+  const float w = __fmaf_rn(__fmaf_rn(r, 0x1.555556p-5f, 0x1.555556p-3f), r, 0.5f);   // 1/2 + r/6 + r^2/24
+  const float p = __fmaf_rn(w, __fmul_rn(r, r), r);    // exp(r) - 1
+  const float2 t2 = tab[k & 31];
+  const float ef = __fadd_rn(t2.x, __fmaf_rn(t2.x, p, t2.y));
+  // ef * 2^(m + 64) * 2^-64, m = k >> 5 in [-151, 0]: 2^(m + 64) has exponent
+  // field m + 191 in [40, 191]; multiplies (not exponent arithmetic) keep NaN
+  const float sc = __int_as_float(((k >> 5) + 191) << 23);
+  const float e = __fmul_rn(__fmul_rn(ef, sc), kTwoM64);
+  const float s = __fadd_rn(1.0f, e);
+  const float t = __fsub_rn(e, __fsub_rn(s, 1.0f));    // 1 + e = s + t exactly (1 >= e)
+  const float n = x < 0.0f ? e : 1.0f;
   const float rc = rcp_approx(s);
-  const float q0 = __fmul_rn(nh, rc);
-  float rr = __fmaf_rn(-q0, s, nh);
-  rr = __fadd_rn(rr, __fmaf_rn(-q0, t2, nl));
-  return __fmaf_rn(rr, rc, q0);
+  const float q0 = __fmul_rn(n, rc);
+  float rho = __fmaf_rn(-q0, s, n);
+  rho = __fmaf_rn(-q0, t, rho);
+  return __fmaf_rn(rho, rc, q0);
 }
+
+DCT_DEV float sigmoid_acc(float x) { return sigmoid_tab(x, kExp2Tab); }
 
 }  // namespace dct

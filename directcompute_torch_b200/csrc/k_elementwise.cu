@@ -126,10 +126,24 @@ __global__ void __launch_bounds__(256) k_unary_chunk(const float* x, float* y, u
     const uint64_t i = base + 256ull * k;
     if (i < n4) v[k] = ld_stream4(x + 4 * i);
   }
+  if constexpr (OP == EW_SIGMOID) {
+    // the sigmoid's 2^(j/32) table in shared memory: one 8-byte load per element
+    __shared__ float2 tab[32];
+    if (threadIdx.x < 32) tab[threadIdx.x] = kExp2Tab[threadIdx.x];
+    __syncthreads();
 #pragma unroll
-  for (int k = 0; k < kChunkU; ++k) {
-    const uint64_t i = base + 256ull * k;
-    if (i < n4) st_stream4(y + 4 * i, unary4<OP>(v[k], al));
+    for (int k = 0; k < kChunkU; ++k) {
+      const uint64_t i = base + 256ull * k;
+      if (i < n4)
+        st_stream4(y + 4 * i, make_float4(sigmoid_tab(v[k].x, tab), sigmoid_tab(v[k].y, tab),
+                                          sigmoid_tab(v[k].z, tab), sigmoid_tab(v[k].w, tab)));
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kChunkU; ++k) {
+      const uint64_t i = base + 256ull * k;
+      if (i < n4) st_stream4(y + 4 * i, unary4<OP>(v[k], al));
+    }
   }
   if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
     const uint64_t t = 4 * n4 + threadIdx.x;

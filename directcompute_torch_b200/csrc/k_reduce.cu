@@ -166,6 +166,67 @@ struct Acc {
   }
 };
 
+// Streaming state of one column in the column kernel's hot loop, cheaper per
+// element than Acc: sums add in float64; max / min use the NaN-propagating
+// instruction; arg reductions keep (value, row) updated only on a strictly
+// better value -- rows arrive in increasing order, so that is the first
+// occurrence -- and a NaN flag.  A lane that saw a NaN rescans its own rows for
+// the first NaN afterwards (NaN is the maximum and the minimum).  The lane
+// starts at its first row, so an all -inf (+inf) column still names that row.
+template <int OP>
+struct ColLane {
+  static constexpr bool kArg = Acc<OP>::kArg;
+  static constexpr bool kExt = Acc<OP>::kExt;
+  static constexpr bool kMax = Acc<OP>::kMax;
+  double s;
+  float v, nanf;
+  int32_t i;
+  DCT_DEV void reset(int32_t first_row) {
+    s = 0.0;
+    v = kMax ? -INFINITY : INFINITY;
+    nanf = -INFINITY;
+    i = first_row;
+  }
+  DCT_DEV void add(float x, int32_t row) {
+    if constexpr (kArg) {
+      const bool u = kMax ? (x > v) : (x < v);
+      v = u ? x : v;
+      i = u ? row : i;
+      nanf = fmax_nan(nanf, x);
+    } else if constexpr (kExt) {
+      v = kMax ? fmax_nan(v, x) : fmin_nan(v, x);
+    } else if constexpr (OP == RED_SUMSQ) {
+      const double d = (double)x;
+      s = fma(d, d, s);
+    } else {
+      s += (double)x;
+    }
+  }
+  // Acc form of this lane; `col` is the lane's column pointer (row 0), rows
+  // first_row, first_row + step, ... < end were visited (`seen` false: none).
+  DCT_DEV Acc<OP> finish(const float* col, uint64_t sl, uint64_t first_row, uint64_t step, uint64_t end,
+                         bool seen) const {
+    Acc<OP> a;
+    a.reset();
+    if (!seen) return a;
+    if constexpr (kArg) {
+      a.v = v;
+      a.i = i;
+      if (nanf != nanf) {                                 // rare: find this lane's first NaN
+        for (uint64_t r = first_row; r < end; r += step) {
+          const float x = col[r * sl];
+          if (x != x) { a.v = x; a.i = (int32_t)r; break; }
+        }
+      }
+    } else if constexpr (kExt) {
+      a.v = v;
+    } else {
+      a.s = s;
+    }
+    return a;
+  }
+};
+
 // ---------------------------------------------------------------------------
 // ROW kernel: (row, chunk) per warp, contiguous along the reduced axis.
 // ---------------------------------------------------------------------------
@@ -232,24 +293,32 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
     Acc<OP> acc[VEC];
     const float* base = x + o * so;
     if (VEC == 4 && c0 + 3 < inner) {
-      uint64_t l = l0 + warp;
-      for (; l + 3 * kRedWarps < l1; l += 4 * kRedWarps) {
-        float4 v[4];
+      // 8 rows (8 x 512 B per warp) in flight per batch: the loop is bound by
+      // memory latency, not by the per-element work
+      constexpr int U = 8;
+      const uint64_t first = l0 + warp;
+      ColLane<OP> ln[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = ld_stream4(base + (l + k * kRedWarps) * sl + c0);
+      for (int j = 0; j < 4; ++j) ln[j].reset((int32_t)first);
+      uint64_t l = first;
+      for (; l + (U - 1) * kRedWarps < l1; l += U * kRedWarps) {
+        float4 v[U];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int64_t li = (int64_t)(l + k * kRedWarps);
-          acc[0].add(v[k].x, li); acc[VEC > 1 ? 1 : 0].add(v[k].y, li);
-          acc[VEC > 2 ? 2 : 0].add(v[k].z, li); acc[VEC > 3 ? 3 : 0].add(v[k].w, li);
+        for (int k = 0; k < U; ++k) v[k] = ld_stream4(base + (l + k * kRedWarps) * sl + c0);
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int32_t li = (int32_t)(l + k * kRedWarps);
+          ln[0].add(v[k].x, li); ln[1].add(v[k].y, li); ln[2].add(v[k].z, li); ln[3].add(v[k].w, li);
         }
       }
       for (; l < l1; l += kRedWarps) {
-        float4 v = ld_stream4(base + l * sl + c0);
-        const int64_t li = (int64_t)l;
-        acc[0].add(v.x, li); acc[VEC > 1 ? 1 : 0].add(v.y, li);
-        acc[VEC > 2 ? 2 : 0].add(v.z, li); acc[VEC > 3 ? 3 : 0].add(v.w, li);
+        const float4 v = ld_stream4(base + l * sl + c0);
+        const int32_t li = (int32_t)l;
+        ln[0].add(v.x, li); ln[1].add(v.y, li); ln[2].add(v.z, li); ln[3].add(v.w, li);
       }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        acc[j < VEC ? j : 0] = ln[j].finish(base + c0 + j, sl, first, kRedWarps, l1, first < l1);
     } else {
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
@@ -320,11 +389,16 @@ struct Plan {
   dim3 grid;
 };
 
+// cols_per_sm: resident blocks per SM of the column kernel that will run (its
+// occupancy); the column plan fills exactly that many blocks per SM in one wave.
+// Workspace sizing passes the largest possible value (every block resident).
 Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl, uint64_t si,
-               const float* x) {
+               const float* x, int cols_per_sm = 0) {
   Plan p{};
   const DevInfo& d = dev_info();
   const uint64_t target_blocks = (uint64_t)d.sm_count * (d.max_threads_per_sm / kRedThreads);
+  const uint64_t col_blocks =
+      (uint64_t)d.sm_count * (cols_per_sm > 0 ? (uint64_t)cols_per_sm : (uint64_t)(d.max_threads_per_sm / kRedThreads));
   if (inner == 1 && sl == 1) {
     p.kind = 0;
     p.vec = (len % 4 == 0) && (so % 4 == 0) && aligned16_h(x);
@@ -352,8 +426,9 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
     uint64_t gy = outer < 65535 ? outer : 65535;
     uint64_t chunks = 1;
     const uint64_t have = tiles * gy;
-    if (have < target_blocks && len > 64) {
-      chunks = (target_blocks + have - 1) / have;
+    if (have < col_blocks && len > 64) {
+      chunks = col_blocks / have;                           // whole waves: no half-empty last wave
+      if (chunks < 1) chunks = 1;
       const uint64_t max_chunks = (len + 63) / 64;          // >= 64 rows per chunk
       if (chunks > max_chunks) chunks = max_chunks;
       if (chunks > 65535) chunks = 65535;
@@ -377,7 +452,21 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
                        uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (outer == 0 || inner == 0) return cudaSuccess;
   if (len == 0) return cudaErrorInvalidValue;
+  static int cols_occ[2] = {0, 0};                        // per instantiation: VEC 1 / 4
+  for (int vi = 0; vi < 2; ++vi) {
+    if (cols_occ[vi] == 0) {
+      int b = 0;
+      const cudaError_t e = vi ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 4>, kRedThreads, 0)
+                               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 1>, kRedThreads, 0);
+      cols_occ[vi] = (e == cudaSuccess && b > 0) ? b : -1;
+      cudaGetLastError();
+    }
+  }
   Plan p = make_plan(outer, len, inner, so, sl, si, x);
+  if (p.kind == 1) {
+    const int occ = cols_occ[p.vec ? 1 : 0];
+    if (occ > 0) p = make_plan(outer, len, inner, so, sl, si, x, occ);
+  }
   unsigned long long* part = (unsigned long long*)ws;
   const uint32_t nparts = p.chunks;
   if (nparts > 1) {

@@ -83,6 +83,30 @@ def test_unary_2ulp(dev, op, n):
     dev.free(hx, hy)
 
 
+def test_sigmoid_whole_range(dev):
+    """Every binade of the float range, the subnormal-result tail (-87.3 > x > -104),
+    +-inf, NaN and signed zeros: <= 2 ulp against the float64 result rounded (the
+    result's subnormal spacing counts as its ulp)."""
+    r = np.random.default_rng(77)
+    parts = [np.float32(2.0) ** np.arange(-149, 128, dtype=np.float64).astype(np.float32)]
+    parts.append(r.uniform(-110, -80, 1 << 18).astype(np.float32))
+    parts.append(r.uniform(80, 110, 1 << 12).astype(np.float32))
+    parts.append(np.array([0.0, -0.0, np.inf, -np.inf, np.nan, -87.33655, -103.97, -104.0, 104.0, -1e30, 3e38],
+                          np.float32))
+    x = np.concatenate([parts[0], -parts[0]] + parts[1:]).astype(np.float32)
+    with np.errstate(all="ignore"):
+        want = (1.0 / (1.0 + np.exp(-x.astype(np.float64)))).astype(np.float32)
+    hx, hy = dev.buf(x), dev.empty(x.size)
+    dev.unary("sigmoid", hx, hy, x.size)
+    got = dev.read(hy)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    d = np.abs(got[~nan].view(np.int32).astype(np.int64) - want[~nan].view(np.int32).astype(np.int64))
+    assert d.max() <= 2, f"max ulp {d.max()} at x={x[~nan][d.argmax()]}"
+    assert got[x == np.inf][0] == 1.0 and got[x == -np.inf][0] == 0.0
+    dev.free(hx, hy)
+
+
 def _rel(got, want64):
     want64 = np.asarray(want64, np.float64)
     return np.abs(got.astype(np.float64) - want64) / np.maximum(np.abs(want64), 1e-30)
