@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_con
 // computed and the row costs no registers.  Three passes over shared memory:
 // max; exp written back in place with the float64 sum; probabilities and
 // gradients streamed out.  Every mbarrier wait is bounded (dct_tma.cuh).
-template <int VPL, int WPB>
+template <int VPL, int WPB, bool POW2>
 __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_constant__ RowCtx c, uint32_t buf_bytes,
                                                              uint32_t* err) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -231,38 +231,58 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
     bool lvalid = true;
     float lab = 0.0f;
     if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
-    const uint32_t lidx = !lvalid ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
-    // pass 1: row max
+    const uint32_t lidx = (!lvalid || !c.labels) ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
+    // pass 1: row max, and whether any logit is -inf (exp(-inf - m) needs a guard)
     float m = c.ref_max_init ? -1e30f : -INFINITY;
+    float mn = INFINITY;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
       if (col < K) {
         const float4 v = *reinterpret_cast<const float4*>(row + col);
         m = fmaxf(fmaxf(m, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
+        mn = fminf(fminf(mn, fminf(v.x, v.y)), fminf(v.z, v.w));
       }
     }
     m = warp_max_f(m);
+    const bool ninf = __any_sync(0xffffffffu, mn == -INFINITY);
     // pass 2: e = exp(x - m) in place, float64 normaliser
     double sacc = 0.0;
+    if (!ninf) {
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
-      if (col < K) {
-        float4 v = *reinterpret_cast<const float4*>(row + col);
-        v.x = (v.x == -INFINITY) ? 0.0f : exp_diff(v.x, m);
-        v.y = (v.y == -INFINITY) ? 0.0f : exp_diff(v.y, m);
-        v.z = (v.z == -INFINITY) ? 0.0f : exp_diff(v.z, m);
-        v.w = (v.w == -INFINITY) ? 0.0f : exp_diff(v.w, m);
-        sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
-        *reinterpret_cast<float4*>(row + col) = v;
+      for (int j = 0; j < VPL; ++j) {
+        const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+        if (col < K) {
+          float4 v = *reinterpret_cast<const float4*>(row + col);
+          v.x = exp_diff(v.x, m);
+          v.y = exp_diff(v.y, m);
+          v.z = exp_diff(v.z, m);
+          v.w = exp_diff(v.w, m);
+          sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
+          *reinterpret_cast<float4*>(row + col) = v;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+        if (col < K) {
+          float4 v = *reinterpret_cast<const float4*>(row + col);
+          v.x = (v.x == -INFINITY) ? 0.0f : exp_diff(v.x, m);
+          v.y = (v.y == -INFINITY) ? 0.0f : exp_diff(v.y, m);
+          v.z = (v.z == -INFINITY) ? 0.0f : exp_diff(v.z, m);
+          v.w = (v.w == -INFINITY) ? 0.0f : exp_diff(v.w, m);
+          sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
+          *reinterpret_cast<float4*>(row + col) = v;
+        }
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
     const float invf = (float)(1.0 / sacc);
     __syncwarp();
-    // pass 3: probabilities and gradients
+    // pass 3: probabilities and gradients (p - onehot) / B: p / B everywhere, the
+    // label's one element patched in its float4
     float* prow = c.probs ? c.probs + (uint64_t)r * K : nullptr;
     float* grow = c.dlogits ? c.dlogits + (uint64_t)r * K : nullptr;
 #pragma unroll
@@ -274,10 +294,21 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
                                      __fmul_rn(e.w, invf));
         if (prow) st_stream4(prow + col, p);
         if (grow) {
-          const float4 g = make_float4(grad_of(p.x, (c.labels && col == lidx) ? 1.0f : 0.0f, c),
-                                       grad_of(p.y, (c.labels && col + 1 == lidx) ? 1.0f : 0.0f, c),
-                                       grad_of(p.z, (c.labels && col + 2 == lidx) ? 1.0f : 0.0f, c),
-                                       grad_of(p.w, (c.labels && col + 3 == lidx) ? 1.0f : 0.0f, c));
+          float4 g;
+          if constexpr (POW2) {
+            g = make_float4(__fmul_rn(p.x, c.grad_mul), __fmul_rn(p.y, c.grad_mul), __fmul_rn(p.z, c.grad_mul),
+                            __fmul_rn(p.w, c.grad_mul));
+          } else {
+            g = make_float4(__fdiv_rn(p.x, c.grad_div), __fdiv_rn(p.y, c.grad_div), __fdiv_rn(p.z, c.grad_div),
+                            __fdiv_rn(p.w, c.grad_div));
+          }
+          const uint32_t q = lidx - col;                  // the label falls in this float4
+          if (q < 4u) {
+            if (q == 0) g.x = grad_of(p.x, 1.0f, c);
+            else if (q == 1) g.y = grad_of(p.y, 1.0f, c);
+            else if (q == 2) g.z = grad_of(p.z, 1.0f, c);
+            else g.w = grad_of(p.w, 1.0f, c);
+          }
           st_stream4(grow + col, g);
         }
       }
@@ -439,21 +470,27 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
     const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
     const int blocks_t = tma_blocks(a.rows, K);
     cudaError_t e = cudaSuccess;
-#define DCT_SM_TMA(VPL, WPB)                                                                                  \
+#define DCT_SM_TMA2(VPL, WPB, P2)                                                                             \
   do {                                                                                                        \
     static bool attr_set = false;                                                                             \
     if (!attr_set) {                                                                                          \
-      e = cudaFuncSetAttribute(k_softmax_ce_tma<VPL, WPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+      e = cudaFuncSetAttribute(k_softmax_ce_tma<VPL, WPB, P2>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
                                (int)(128 + 2 * WPB * 8192));                                                   \
       attr_set = (e == cudaSuccess);                                                                          \
     }                                                                                                         \
-    if (e == cudaSuccess) k_softmax_ce_tma<VPL, WPB><<<blocks_t, WPB * 32, smem, st>>>(c, buf_bytes, a.err);  \
+    if (e == cudaSuccess) k_softmax_ce_tma<VPL, WPB, P2><<<blocks_t, WPB * 32, smem, st>>>(c, buf_bytes, a.err); \
+  } while (0)
+#define DCT_SM_TMA(VPL, WPB)                                                                                  \
+  do {                                                                                                        \
+    if (c.grad_div_pow2) DCT_SM_TMA2(VPL, WPB, true);                                                         \
+    else DCT_SM_TMA2(VPL, WPB, false);                                                                        \
   } while (0)
     if (K <= 256) DCT_SM_TMA(2, 8);
     else if (K <= 512) DCT_SM_TMA(4, 8);
     else if (K <= 1024) DCT_SM_TMA(8, 8);
     else DCT_SM_TMA(16, 4);
 #undef DCT_SM_TMA
+#undef DCT_SM_TMA2
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess || !c.want_loss) return e;
