@@ -313,7 +313,7 @@ def run_e2e(L: Lib, c2: C2, steps: int, warmup: int):
 # ---------------------------------------------------------------------------
 # per-op breakdown of the other BASELINE configs
 # ---------------------------------------------------------------------------
-PER_OP_SECTIONS = {"c3": ("c3_sum_axis-1", "c3_sum_axis0", "c3_mean_axis-1", "c3_mean_axis0", "c3_max_axis-1",
+PER_OP_SECTIONS = {"c1": ("c1_dense_step_eager", "c1_dense_step_graph"), "c3": ("c3_sum_axis-1", "c3_sum_axis0", "c3_mean_axis-1", "c3_mean_axis0", "c3_max_axis-1",
                            "c3_max_axis0", "c3_argmax_axis-1", "c3_argmax_axis0"),
                    "c3f": ("c3_fullsum_2^30",), "c4": ("c4_softmax_ce_fused",), "c5a": ("c5a_adam_1.5e9",),
                    "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd")}
@@ -343,6 +343,8 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, wa
         res[name] = {"gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms": round(ms, 4), "bytes": int(nbytes),
                      "launches": launches}
 
+    if section("c1"):
+        _c1(L, rank, measure, res)
     # C3: R[16384,4096] ~ N(0,1) + 0.1% +-1e4 outliers (seed 2)
     R_ROWS, R_COLS = 16384, 4096
     out = L.new(R_ROWS)
@@ -368,6 +370,62 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, wa
         _c5b(L, rank, measure, comm)
     lib.DrainPool()
     return res
+
+
+def _c1(L, rank, measure, res):
+    """C1 (latency, not bandwidth): X[256,784], b[784]; fwd bias_relu, column sums, full sum;
+    bwd relu_grad, bias_grad (+ a grad accumulation), as reference RunShader calls one by one
+    (eager) and as one RunSequence of the same commands (replayed as a CUDA graph)."""
+    C, lib = L.C, L.lib
+    from directcompute_torch_b200._abi import SeqCmd
+    M, N = 256, 784
+    h = {k: L.new(n) for k, n in (("x", M * N), ("b", N), ("y", M * N), ("col", N), ("tot", 1), ("ones", M * N),
+                                  ("dx", M * N), ("db", N), ("acc", N))}
+    L.fill(h["x"], 0 + 1000 * rank, 0, 1, 0.0, 1.0)
+    L.fill(h["b"], 0 + 1000 * rank, 1, 0, -0.1, 0.1)
+    ones = np.ones(M * N, np.float32)
+    L.check(lib.dct_copy_h2d(h["ones"], ones.ctypes.data, 0, M * N), "ones")
+    g = ((M * N + 255) // 256, 1, 1)
+    spec = [("bias_relu", ["x", "b"], ["y"], g, [M, N]), ("bias_grad", ["y"], ["col"], (N, 1, 1), [M, N, N, 1]),
+            ("dct_reduce_all", ["y"], ["tot"], (1, 1, 1), [0, M * N]), ("relu_grad", ["ones", "y"], ["dx"], g, [M * N]),
+            ("bias_grad", ["dx"], ["db"], (N, 1, 1), [M, N, N, 1]),
+            ("grad_accum", ["db"], ["acc"], ((N + 255) // 256, 1, 1), [N])]
+    for name in ("bias_relu", "bias_grad", "relu_grad", "grad_accum"):
+        lib.CompileShader(name.encode(), "")
+    calls, cmds = [], []
+    for name, srv, uav, grp, words in spec:
+        sv = (C.c_void_p * 8)(*[h[k] for k in srv])
+        uv = (C.c_void_p * 4)(*[h[k] for k in uav])
+        th = (C.c_uint * 3)(*grp)
+        cb = np.array(words, np.uint32)
+        calls.append((name.encode(), sv, len(srv), uv, len(uav), th, cb, 4 * len(words)))
+        c = SeqCmd()
+        c.shader = lib.ResolveShader(name.encode())
+        for i, k in enumerate(srv):
+            c.srvs[i] = h[k]
+        for i, k in enumerate(uav):
+            c.uavs[i] = h[k]
+        c.srvCount, c.uavCount = len(srv), len(uav)
+        c.threads[0], c.threads[1], c.threads[2] = grp
+        C.memmove(c.cbData, cb.ctypes.data, 4 * len(words))
+        c.cbSize = 4 * len(words)
+        cmds.append(c)
+    arr = (SeqCmd * len(cmds))(*cmds)
+
+    def eager():
+        for name, sv, ns, uv, nu, th, cb, nb in calls:
+            lib.RunShader(name, sv, ns, uv, nu, th, cb.ctypes.data, nb)
+
+    def graph():
+        lib.RunSequence(C.cast(arr, C.c_void_p), len(cmds))
+    nbytes = 4 * (3 * M * N + 2 * N + 1) + 4 * (3 * M * N + N)      # SURVEY C1 fwd + bwd algorithmic bytes
+    measure("c1_dense_step_eager", nbytes, eager, len(cmds) + 1, it=200)
+    measure("c1_dense_step_graph", nbytes, graph, len(cmds) + 1, it=200)
+    for k in ("c1_dense_step_eager", "c1_dense_step_graph"):
+        if k in res:
+            res[k]["us_per_step"] = round(res[k]["ms"] * 1e3, 2)
+    for v in h.values():
+        lib.ReleaseBuffer(v)
 
 
 def _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS, comm=None):

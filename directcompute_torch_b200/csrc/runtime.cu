@@ -218,8 +218,14 @@ static void release_handle(void* h) {
   if (--b->ref <= 0) release_internal(b);
 }
 
+static bool g_capturing = false;    // RunSequence is capturing the stream into a CUDA graph
+
 static bool ensure_ws(size_t bytes) {
   if (bytes <= g.ws_bytes) return true;
+  if (g_capturing) {                 // an allocation inside a capture would belong to the graph
+    set_error(DCT_ERR_CUDA, "workspace growth during graph capture");
+    return false;
+  }
   size_t want = std::max(bytes, g.ws_bytes * 2);
   want = (want + (1 << 20) - 1) & ~size_t((1 << 20) - 1);
   if (g.ws) cudaFreeAsync(g.ws, g.stream);
@@ -801,9 +807,6 @@ static bool dispatch(Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_
 // ---------------------------------------------------------------------------
 // BatchNorm statistics (shared by the reference name and dct_batchnorm_*)
 // ---------------------------------------------------------------------------
-typedef bool (*ChanAllreduce)(double* chan, uint32_t count);
-static ChanAllreduce g_chan_allreduce = nullptr;      // set when a sharded call is in progress
-
 static bool bn_stats(const Disp& d, const float* x, uint32_t N, uint32_t C, uint32_t S, float* mean, float* var,
                      float* rm, float* rv, bool training, float momentum, uint32_t c_eff) {
   if (!ensure_ws(bn_ws_bytes(N, C))) return false;
@@ -1124,19 +1127,108 @@ DCT_API void* ResolveShader(const char* name) {
   return (s && (s->compiled || s->always)) ? s : nullptr;
 }
 
-DCT_API void RunSequence(DctSeqCmd* cmds, uint32_t count) {
-  LOCK;
-  if (!cmds) return;
+// RunSequence as one CUDA graph launch.  The reference replays the same
+// command list every batch (ComputeGraph, nn_engine.py:2505-2771), so: the first
+// call with a given list runs eagerly (and grows the scratch workspace as
+// needed), the second identical call captures the stream into a graph, later
+// identical calls launch that graph.  "Identical" compares the command bytes
+// and, for every referenced buffer, its device pointer and size, so a handle
+// that was released and reallocated never replays a graph into stale memory.
+// A capture that fails (a command that errs, or would need a larger workspace)
+// is discarded and the list runs eagerly.  DCT_SEQ_GRAPH=0 turns graphs off.
+struct SeqGraph {
+  std::vector<uint8_t> key;
+  bool failed = false;               // this list could not be captured: stay eager
+  cudaGraphExec_t exec = nullptr;
+};
+static SeqGraph g_seq;
+
+static bool seq_key(const DctSeqCmd* cmds, uint32_t count, std::vector<uint8_t>& key) {
+  key.assign(reinterpret_cast<const uint8_t*>(cmds), reinterpret_cast<const uint8_t*>(cmds + count));
+  auto put = [&](const void* p, size_t n) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    key.insert(key.end(), b, b + n);
+  };
+  put(&g.ws, sizeof(g.ws));          // a graph bakes in the scratch workspace too
+  put(&g.ws_bytes, sizeof(g.ws_bytes));
+  for (uint32_t i = 0; i < count; ++i) {
+    const DctSeqCmd& c = cmds[i];
+    if (!c.shader) continue;
+    if (!is_shader_ptr(c.shader)) return false;
+    for (uint32_t v = 0; v < 12; ++v) {
+      void* h = v < 8 ? (v < c.srvCount ? c.srvs[v] : nullptr) : (v - 8 < c.uavCount ? c.uavs[v - 8] : nullptr);
+      if (!h) continue;
+      Buffer* b = buf_of(h);
+      if (!b) return false;
+      put(&b->d, sizeof(b->d));
+      put(&b->count, sizeof(b->count));
+    }
+  }
+  return true;
+}
+
+static bool seq_run(DctSeqCmd* cmds, uint32_t count) {
+  bool ok = true;
   for (uint32_t i = 0; i < count; ++i) {
     DctSeqCmd& c = cmds[i];
     if (!c.shader) continue;
     if (!is_shader_ptr(c.shader)) {
       set_error(DCT_ERR_ARG, "RunSequence: command %u has a foreign shader pointer", i);
+      ok = false;
       continue;
     }
     Shader* s = static_cast<Shader*>(c.shader);
-    dispatch(s, c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs, std::min<uint32_t>(c.uavCount, 4), c.threads,
-             c.cbSize ? c.cbData : nullptr, std::min<uint32_t>(c.cbSize, 64));
+    ok &= dispatch(s, c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs, std::min<uint32_t>(c.uavCount, 4),
+                   c.threads, c.cbSize ? c.cbData : nullptr, std::min<uint32_t>(c.cbSize, 64));
+  }
+  return ok;
+}
+
+static bool seq_capture(DctSeqCmd* cmds, uint32_t count) {
+  if (cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const int code0 = g.err_code;
+  const std::string msg0 = g.err;
+  g_capturing = true;
+  const bool ok = seq_run(cmds, count);
+  g_capturing = false;
+  cudaGraph_t graph = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(g.stream, &graph);
+  cudaGraphExec_t exec = nullptr;
+  bool good = ok && e == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+  if (graph) cudaGraphDestroy(graph);
+  cudaGetLastError();
+  if (!good) {                                       // the eager re-run reports its own errors
+    g.err_code = code0;
+    g.err = msg0;
+    return false;
+  }
+  if (g_seq.exec) cudaGraphExecDestroy(g_seq.exec);
+  g_seq.exec = exec;
+  return true;
+}
+
+DCT_API void RunSequence(DctSeqCmd* cmds, uint32_t count) {
+  LOCK;
+  if (!cmds || !ensure_init()) return;
+  const char* env = getenv("DCT_SEQ_GRAPH");
+  std::vector<uint8_t> key;
+  const bool cacheable = count > 0 && !(env && env[0] == '0') && seq_key(cmds, count, key);
+  if (cacheable && key == g_seq.key && !g_seq.failed) {
+    if (g_seq.exec || seq_capture(cmds, count)) {
+      cuda_ok(cudaGraphLaunch(g_seq.exec, g.stream), "RunSequence(graph launch)");
+      return;
+    }
+    g_seq.failed = true;
+  }
+  seq_run(cmds, count);
+  if (cacheable && key != g_seq.key) {
+    if (g_seq.exec) cudaGraphExecDestroy(g_seq.exec);
+    g_seq.exec = nullptr;
+    g_seq.failed = false;
+    g_seq.key = std::move(key);
   }
 }
 
