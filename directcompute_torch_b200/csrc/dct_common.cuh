@@ -30,6 +30,11 @@ enum : uint32_t {
   DCT_DEVERR_PEER_INVALID = 2u,    // a rank's shard of a sharded op was invalid
 };
 uint32_t* device_error_word();   // defined in runtime.cu
+// Zeroed device counters for "last block folds" reductions (null before
+// InitEngine: callers then use a separate fold launch).  Every kernel that
+// increments one resets it to zero before it exits.
+constexpr uint32_t kReduceCounters = 65536;
+uint32_t* reduce_counters();     // defined in runtime.cu
 
 // Blocks for a grid-stride kernel of `threads`-thread blocks covering `work`
 // independent items: enough to fill every SM `waves` times, never more than

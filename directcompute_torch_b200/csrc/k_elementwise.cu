@@ -127,10 +127,12 @@ __global__ void __launch_bounds__(256) k_unary_chunk(const float* x, float* y, u
     if (i < n4) v[k] = ld_stream4(x + 4 * i);
   }
   if constexpr (OP == EW_SIGMOID) {
-    // the sigmoid's 2^(j/32) table in shared memory: one 8-byte load per element
-    __shared__ float2 tab[32];
-    if (threadIdx.x < 32) tab[threadIdx.x] = kExp2Tab[threadIdx.x];
-    __syncthreads();
+    // the sigmoid's 2^(j/32) table in shared memory, one private copy per warp
+    // (a warp-level sync, no block barrier): one 8-byte load per element
+    __shared__ float2 tabs[8][32];
+    float2* tab = tabs[threadIdx.x >> 5];
+    tab[threadIdx.x & 31] = kExp2Tab[threadIdx.x & 31];
+    __syncwarp();
 #pragma unroll
     for (int k = 0; k < kChunkU; ++k) {
       const uint64_t i = base + 256ull * k;

@@ -277,13 +277,19 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
 // COLUMN kernel: block = 32*VEC adjacent outputs x 8 interleaved row lanes.
 // grid = (column tiles, outer (strided), len chunks)
 // ---------------------------------------------------------------------------
+// With `counters` (one zeroed word per (outer, tile)) and chunks > 1, the block
+// that finishes a tile's last chunk folds that tile's chunk partials in chunk
+// order and emits the result (the order, not the finishing block, fixes the
+// rounding), then re-zeroes the counter: no second launch.  No block waits
+// for another.
 template <int OP, int VEC>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                              uint64_t inner, uint64_t so, uint64_t sl,
                                                              uint32_t chunks, uint64_t chunk_len, RedOut ro,
-                                                             unsigned long long* part) {
+                                                             unsigned long long* part, uint32_t* counters) {
   constexpr int W = 32 * VEC;
   __shared__ unsigned long long sh[kRedWarps][W];
+  __shared__ bool last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t c0 = (uint64_t)blockIdx.x * W + (uint64_t)lane * VEC;
   const uint32_t ch = blockIdx.z;
@@ -340,6 +346,29 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
       if (c < inner) {
         if (chunks == 1) tot.emit(ro, o * inner + c, len);
         else part[(o * chunks + ch) * inner + c] = tot.pack();
+      }
+    }
+    if (chunks > 1 && counters) {
+      uint32_t* cnt = counters + (uint64_t)blockIdx.y * gridDim.x + blockIdx.x;   // o == blockIdx.y here
+      __threadfence();                                  // this block's partials before its count
+      __syncthreads();
+      if (threadIdx.x == 0) last = atomicAdd(cnt, 1u) == chunks - 1;
+      __syncthreads();
+      if (last) {
+        __threadfence();                                // every block's partials are visible
+        if (threadIdx.x < W) {
+          const uint64_t c = (uint64_t)blockIdx.x * W + threadIdx.x;
+          if (c < inner) {
+            Acc<OP> tot;
+            for (uint32_t k = 0; k < chunks; ++k) {
+              Acc<OP> t;
+              t.unpack(__ldcg(&part[(o * chunks + k) * inner + c]));
+              if (k == 0) tot = t; else tot.merge(t);
+            }
+            tot.emit(ro, o * inner + c, len);
+          }
+        }
+        if (threadIdx.x == 0) *cnt = 0u;
       }
     }
     __syncthreads();
@@ -477,8 +506,13 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
     if (p.vec) k_reduce_rows<OP, true><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
     else k_reduce_rows<OP, false><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
   } else if (p.kind == 1) {
-    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
-    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
+    // in-kernel fold when a counter per (outer row, tile) is available
+    uint32_t* cnt = reduce_counters();
+    // one counter per (outer row, tile), each outer row visited once per block
+    if ((uint64_t)p.grid.x * p.grid.y > kReduceCounters || outer > p.grid.y) cnt = nullptr;
+    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, cnt);
+    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, cnt);
+    if (cnt || nparts == 1) return cudaGetLastError();
   } else {
     k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, ro);
   }

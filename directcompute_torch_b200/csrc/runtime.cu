@@ -71,6 +71,7 @@ struct Engine {
   float* host_small = nullptr;    // pinned 64-byte staging for scalar readbacks
   uint32_t* dev_err_host = nullptr;   // mapped error word written by device code
   uint32_t* dev_err_dev = nullptr;
+  uint32_t* counters = nullptr;       // kReduceCounters zeroed words (reduction tile counters)
   char name[128] = {0};
   // error state
   int err_code = 0;
@@ -110,6 +111,7 @@ static void set_error(int code, const char* fmt, ...) {
 }
 
 uint32_t* device_error_word() { return g.dev_err_dev; }
+uint32_t* reduce_counters() { return g.init ? g.counters : nullptr; }
 
 // error recording for entry points that live outside this file
 void note_error(int code, const char* msg) {
@@ -320,6 +322,8 @@ static bool init_engine() {
   *g.dev_err_host = 0;
   if (!cuda_ok(cudaHostGetDevicePointer((void**)&g.dev_err_dev, g.dev_err_host, 0), "InitEngine(error word)"))
     return false;
+  if (!cuda_ok(cudaMalloc(&g.counters, kReduceCounters * sizeof(uint32_t)), "InitEngine(counters)")) return false;
+  if (!cuda_ok(cudaMemset(g.counters, 0, kReduceCounters * sizeof(uint32_t)), "InitEngine(counters)")) return false;
   g.init = true;
   return true;
 }

@@ -67,6 +67,7 @@ def _replay(dev, arr, n, reps, graph):
 
 
 def test_graph_replay_matches_eager(dev):
+    dev.clear_error()
     outs = {}
     for graph in (False, True):
         h, arr, x, b = _c1_sequence(dev)
@@ -90,6 +91,7 @@ def test_graph_replay_matches_eager(dev):
 
 
 def test_graph_not_replayed_on_other_buffers_or_moved_workspace(dev):
+    dev.clear_error()
     lib = dev.lib
     h, arr, x, b = _c1_sequence(dev)
     _replay(dev, arr, len(arr), 3, True)                    # eager, capture, launch
