@@ -225,6 +225,31 @@ struct ColLane {
     }
     return a;
   }
+  // Acc form for the row kernel's lanes: indices first + 128 t + q (q < 4), < end
+  DCT_DEV Acc<OP> finish_rows(const float* row, uint64_t first, uint64_t end) const {
+    Acc<OP> a;
+    a.reset();
+    if (first >= end) return a;
+    if constexpr (kArg) {
+      a.v = v;
+      a.i = i;
+      if (nanf != nanf) {                                 // rare: this lane's first NaN
+        for (uint64_t l = first; l < end; l += 128) {
+          bool found = false;
+          for (int q = 0; q < 4 && l + q < end; ++q) {
+            const float xq = row[l + q];
+            if (xq != xq) { a.v = xq; a.i = (int32_t)(l + q); found = true; break; }
+          }
+          if (found) break;
+        }
+      }
+    } else if constexpr (kExt) {
+      a.v = v;
+    } else {
+      a.s = s;
+    }
+    return a;
+  }
 };
 
 // ---------------------------------------------------------------------------
@@ -247,21 +272,28 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
     Acc<OP> acc;
     acc.reset();
     if (VEC) {
-      uint64_t l = l0 + 4 * (uint64_t)lane;
+      // lane-local streaming state (see ColLane): the lane visits its indices in
+      // increasing order, 4 consecutive per float4
+      const uint64_t first = l0 + 4 * (uint64_t)lane;
+      ColLane<OP> ln;
+      ln.reset((int32_t)first);
+      uint64_t l = first;
       for (; l + 3 * 128 + 3 < l1; l += 4 * 128) {
         float4 v[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[k] = ld_stream4(p + l + 128 * k);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const int64_t b = (int64_t)(l + 128 * k);
-          acc.add(v[k].x, b); acc.add(v[k].y, b + 1); acc.add(v[k].z, b + 2); acc.add(v[k].w, b + 3);
+          const int32_t b = (int32_t)(l + 128 * k);
+          ln.add(v[k].x, b); ln.add(v[k].y, b + 1); ln.add(v[k].z, b + 2); ln.add(v[k].w, b + 3);
         }
       }
       for (; l + 3 < l1; l += 128) {
-        float4 v = ld_stream4(p + l);
-        acc.add(v.x, (int64_t)l); acc.add(v.y, (int64_t)l + 1); acc.add(v.z, (int64_t)l + 2); acc.add(v.w, (int64_t)l + 3);
+        const float4 v = ld_stream4(p + l);
+        const int32_t b = (int32_t)l;
+        ln.add(v.x, b); ln.add(v.y, b + 1); ln.add(v.z, b + 2); ln.add(v.w, b + 3);
       }
+      acc = ln.finish_rows(p, first, l1);
     } else {
       for (uint64_t l = l0 + lane; l < l1; l += 32) acc.add(ld_stream(p + l), (int64_t)l);
     }
