@@ -81,13 +81,18 @@ __global__ void __launch_bounds__(256) k_bn_plane_sums(const float* __restrict__
   }
 }
 
-__global__ void k_bn_fold(const double* __restrict__ ps, uint32_t N, uint32_t C, double* chan) {
-  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;     // (c, j)
+// chan[2c + j] = sum over n of ps[2 (n C + c) + j]: a warp per (c, j); lane l
+// adds n = l, l + 32, ... in order, then a fixed shuffle tree (deterministic,
+// and 32 loads in flight instead of one serial chain of N).
+__global__ void __launch_bounds__(256) k_bn_fold(const double* __restrict__ ps, uint32_t N, uint32_t C, double* chan) {
+  const uint32_t k = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;     // (c, j)
+  const int lane = threadIdx.x & 31;
   if (k >= 2 * C) return;
   const uint32_t c = k >> 1, j = k & 1;
   double acc = 0.0;
-  for (uint32_t n = 0; n < N; ++n) acc += ps[2 * ((uint64_t)n * C + c) + j];
-  chan[k] = acc;
+  for (uint32_t n = lane; n < N; n += 32) acc += ps[2 * ((uint64_t)n * C + c) + j];
+  acc = warp_sum(acc);
+  if (lane == 0) chan[k] = acc;
 }
 
 __global__ void k_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rm,
@@ -270,7 +275,7 @@ cudaError_t launch_bn_plane_sums(const float* x, const float* dy, uint32_t N, ui
 
 cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, double* chan, cudaStream_t st) {
   if (C == 0) return cudaSuccess;
-  k_bn_fold<<<(2 * C + 255) / 256, 256, 0, st>>>(plane_sums, N, C, chan);
+  k_bn_fold<<<(unsigned)((2ull * C * 32 + 255) / 256), 256, 0, st>>>(plane_sums, N, C, chan);
   return cudaGetLastError();
 }
 
