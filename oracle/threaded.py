@@ -21,9 +21,12 @@ def _chunks(n, k):
     return [(i, min(n, i + step)) for i in range(0, n, step)]
 
 
-def c2_sample(threads: int, rows: int = 1024, reps: int = 3, seed: int = 1):
+def c2_sample(threads: int, rows: int = 1024, reps: int = 3, seed: int = 1, min_seconds: float = 0.0,
+              warmup: int = 1):
     """The 11 ops of BASELINE config C2 on a `rows`-row sample (same columns, same
-    distributions); returns (GB/s of algorithmic bytes, seconds per sample pass, text)."""
+    distributions): `warmup` untimed passes, then at least `reps` timed passes and
+    at least `min_seconds` of them.  Returns (GB/s of algorithmic bytes over all
+    timed passes, seconds per pass, text, timed passes)."""
     rng = np.random.default_rng(seed)
     cols = 8192
     A = rng.standard_normal((rows, cols), dtype=F32)
@@ -59,15 +62,17 @@ def c2_sample(threads: int, rows: int = 1024, reps: int = 3, seed: int = 1):
     plan += [(unary, op, 4 * 2 * rows * cols) for op in ("exp", "log_abs1p", "tanh", "sigmoid")]
     total = sum(b for _, _, b in plan)
     with np.errstate(all="ignore"):
-        for fn, op, _ in plan:          # warm-up
-            fn(op)
-        best = float("inf")
-        for _ in range(reps):
-            t0 = time.perf_counter()
+        for _ in range(max(0, warmup)):
             for fn, op, _ in plan:
                 fn(op)
-            best = min(best, time.perf_counter() - t0)
+        passes = 0
+        t0 = time.perf_counter()
+        while passes < reps or time.perf_counter() - t0 < min_seconds:
+            for fn, op, _ in plan:
+                fn(op)
+            passes += 1
+        elapsed = time.perf_counter() - t0
     pool.shutdown()
     desc = (f"C2 sample: A[{rows},8192] (1/{8192 // rows} of the rows), C[{p},1,4096] x D[1,512,4096]; "
-            f"11 ops, best of {reps} passes, {threads} threads")
-    return total / best / 1e9, best, desc
+            f"11 ops; {passes} timed passes in {elapsed:.1f} s (mean), {threads} threads")
+    return total * passes / elapsed / 1e9, elapsed / passes, desc, passes
