@@ -224,13 +224,17 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
   __syncwarp();
   double block_loss = 0.0;
   uint32_t k = 0;
+  // labels are prefetched one row ahead: the global load's latency hides behind a row
+  bool nvalid = true;
+  float nlab = 0.0f;
+  if (c.labels && r0 < c.rows) nlab = label_of(c.labels, c.labels_int32, r0, K, nvalid);
   for (uint32_t r = r0; r < c.rows; r += rstep, ++k) {
     const int st = k & 1;
     float* row = st ? buf1 : buf0;
+    const bool lvalid = nvalid;
+    const float lab = nlab;
+    if (c.labels && r + rstep < c.rows) nlab = label_of(c.labels, c.labels_int32, r + rstep, K, nvalid);
     mbar_wait(&bars[st], (k >> 1) & 1u, err);
-    bool lvalid = true;
-    float lab = 0.0f;
-    if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
     const uint32_t lidx = (!lvalid || !c.labels) ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
     // pass 1: row max, and whether any logit is -inf (exp(-inf - m) needs a guard)
     float m = c.ref_max_init ? -1e30f : -INFINITY;
@@ -246,6 +250,17 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
     }
     m = warp_max_f(m);
     const bool ninf = __any_sync(0xffffffffu, mn == -INFINITY);
+    // the label's logit, from shared memory before pass 2 overwrites the row (a
+    // label >= K reads the flat buffer at r*K + label, as the reference's loss does)
+    float xl = 0.0f;
+    if (c.want_loss && lvalid) {
+      if (lidx < K) {
+        xl = row[lidx];
+      } else {
+        const uint64_t li = (uint64_t)r * K + lidx;
+        xl = li < c.total ? c.logits[li] : 0.0f;
+      }
+    }
     // pass 2: e = exp(x - m) in place, float64 normaliser
     double sacc = 0.0;
     if (!ninf) {
@@ -279,7 +294,7 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
-    const float invf = (float)(1.0 / sacc);
+    const float invf = (float)__drcp_rn(sacc);          // correctly rounded 1/sum, then rounded to float
     __syncwarp();
     // pass 3: probabilities and gradients (p - onehot) / B: p / B everywhere, the
     // label's one element patched in its float4
@@ -314,9 +329,8 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
       }
     }
     if (c.want_loss && lane == 0 && lvalid) {
-      const uint64_t li = (uint64_t)r * K + lidx;
-      const double xl = li < c.total ? (double)c.logits[li] : 0.0;
-      block_loss += -((xl - (double)m) - log(sacc));
+      // float log of the row sum: about 1 ulp of log(sum), far below the loss's rel 1e-5
+      block_loss += -(((double)xl - (double)m) - (double)logf((float)sacc));
     }
     // hand the stage back to the bulk-copy engine for row r + 2*rstep
     fence_proxy_async_smem();
