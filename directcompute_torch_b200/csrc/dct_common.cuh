@@ -8,6 +8,8 @@
 #include <stdint.h>
 #include <math.h>
 
+#include <utility>
+
 #define DCT_DEV __device__ __forceinline__
 
 namespace dct {
@@ -28,6 +30,7 @@ const DevInfo& dev_info();   // defined in runtime.cu
 enum : uint32_t {
   DCT_DEVERR_WAIT_TIMEOUT = 1u,    // a bounded wait in a kernel ran out
   DCT_DEVERR_PEER_INVALID = 2u,    // a rank's shard of a sharded op was invalid
+  DCT_DEVERR_PEER_WAIT = 4u,       // a peer's record did not arrive before the deadline
 };
 uint32_t* device_error_word();   // defined in runtime.cu
 // Zeroed device counters for "last block folds" reductions (null before
@@ -45,6 +48,35 @@ inline unsigned grid_for(uint64_t work, int threads, int waves = 1) {
   uint64_t need = (work + threads - 1) / threads;
   if (need < 1) need = 1;
   return (unsigned)(need < resident ? need : resident);
+}
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch: a kernel launched with launch_pdl may start
+// while the previous kernel on the stream finishes; it must call
+// grid_dep_wait() before reading that kernel's results (a no-op when the
+// kernel was launched the ordinary way)
+// ---------------------------------------------------------------------------
+DCT_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the stream, when launched with launch_pdl, be
+// scheduled before this one ends; it still waits in grid_dep_wait for this
+// grid to complete, so every kernel launched with launch_pdl calls
+// grid_dep_wait before touching what earlier kernels wrote.
+DCT_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

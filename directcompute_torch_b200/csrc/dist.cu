@@ -37,9 +37,11 @@
 #include <chrono>
 #include <condition_variable>
 #include <memory>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "dct_common.cuh"
 #include "kernels.h"
@@ -88,6 +90,15 @@ struct DistState {
   size_t recv_bytes = 0;
   double* fold = nullptr;          // folded sums / counts (float64)
   size_t fold_bytes = 0;
+  // peer-memory exchange: this rank's region holds slots [2][world][slot_bytes]
+  // (by epoch parity, then by writing rank) and flags [2][world] (u64 epochs);
+  // every rank's region is mapped here (CUDA IPC over NVLink)
+  bool peer = false;
+  void* region = nullptr;
+  size_t slot_bytes = 0;
+  std::vector<void*> peer_base;
+  void** peer_dev = nullptr;
+  uint64_t epoch = 0;
 };
 DistState D;
 
@@ -149,6 +160,7 @@ void abort_comm() {
   if (D.comm) D.api.CommAbort(D.comm);
   D.comm = nullptr;
   D.aborted = true;
+  D.peer = false;                // the mappings are released by dct_dist_finalize
   rt_dist_hooks() = DistHooks{};
 }
 
@@ -227,20 +239,217 @@ bool all_gather(const void* send, void* recv, size_t count_u64, const char* wher
 }
 
 // ---------------------------------------------------------------------------
-// record headers and rank-order folds
+// peer-memory exchange
 // ---------------------------------------------------------------------------
-// header of a reduction shard record: [offset, len, len_total, valid]
-__global__ void k_put_header_u64(unsigned long long* h, unsigned long long a, unsigned long long b,
-                                 unsigned long long c, unsigned long long d) {
-  if (threadIdx.x == 0) { h[0] = a; h[1] = b; h[2] = c; h[3] = d; }
+// Each rank stores its record straight into every rank's slot over NVLink
+// (plain stores to a peer's memory mapped with CUDA IPC), then release-stores
+// the exchange's epoch into that rank's flag; each rank waits for all flags
+// of the epoch on its own memory (acquire loads, bounded by a deadline) and
+// folds its local slots.  Slots alternate by epoch parity: a rank can run at
+// most one exchange ahead of a peer (its next fold waits for that peer's next
+// record), so it never overwrites a record the peer has not folded.
+constexpr size_t kSlotBytes = 256 * 1024;
+
+size_t slot_off(int par, int q) { return ((size_t)par * D.world + q) * D.slot_bytes; }
+size_t flag_off(int par, int q) { return 2 * (size_t)D.world * D.slot_bytes + ((size_t)par * D.world + q) * 8; }
+
+__global__ void k_check_axis_shards(const unsigned long long* all, int world, uint64_t stride, uint64_t nout,
+                                    uint32_t* err);
+
+// The host-known part of a record: n u64 words (bit patterns) at offset `off`.
+struct Hdr {
+  uint32_t off = 0, n = 0;
+  unsigned long long v[4] = {0, 0, 0, 0};
+};
+unsigned long long f64_bits(double d) {
+  unsigned long long u;
+  memcpy(&u, &d, sizeof(u));
+  return u;
 }
-// writes the first n (<= 4) of a, b, c, d to h
-__global__ void k_put_f64(double* h, int n, double a, double b, double c, double d) {
-  if (threadIdx.x != 0) return;
-  const double v[4] = {a, b, c, d};
-  for (int i = 0; i < n && i < 4; ++i) h[i] = v[i];
+Hdr make_hdr(uint32_t off, std::initializer_list<unsigned long long> v) {
+  Hdr h;
+  h.off = off;
+  for (unsigned long long x : v) h.v[h.n++] = x;
+  return h;
 }
 
+__global__ void __launch_bounds__(256) k_peer_put(const unsigned long long* __restrict__ rec, Hdr h,
+                                                  void* const* __restrict__ bases, uint64_t slot_off,
+                                                  uint64_t flag_off, unsigned long long epoch) {
+  grid_dep_launch();                                   // the wait kernel may be scheduled now
+  grid_dep_wait();                                     // rec comes from the previous kernel
+  // block p writes this rank's record (device part, then the header words) into
+  // rank p's slot, then p's flag
+  unsigned char* base = static_cast<unsigned char*>(bases[blockIdx.x]);
+  unsigned long long* dst = reinterpret_cast<unsigned long long*>(base + slot_off);
+  const uint64_t n = h.off;
+  const uint64_t n2 = n >> 1;
+  const uint4* s4 = reinterpret_cast<const uint4*>(rec);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (uint64_t i = threadIdx.x; i < n2; i += blockDim.x) d4[i] = s4[i];
+  if ((n & 1) && threadIdx.x == 0) dst[n - 1] = rec[n - 1];
+  if (threadIdx.x < h.n) dst[n + threadIdx.x] = h.v[threadIdx.x];
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long* flag = reinterpret_cast<unsigned long long*>(base + flag_off);
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(epoch) : "memory");
+  }
+}
+
+// header words written into a local record (the NCCL path)
+__global__ void k_put_u64(unsigned long long* rec, Hdr h) {
+  if (threadIdx.x < h.n) rec[h.off + threadIdx.x] = h.v[threadIdx.x];
+}
+
+__global__ void k_peer_wait(const unsigned long long* flags, int world, unsigned long long epoch,
+                            unsigned long long timeout_ns, uint32_t* err, const unsigned long long* slots,
+                            uint64_t stride, int64_t axis_nout) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int q = threadIdx.x;
+  if (q < world) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + q) : "memory");
+      if (v >= epoch) break;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > timeout_ns) {
+        if (err) atomicOr(err, DCT_DEVERR_PEER_WAIT);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  // axis-reduction records: the shards must tile [0, len_total) in rank order
+  if (axis_nout >= 0 && threadIdx.x == 0) {
+    const uint64_t nout = (uint64_t)axis_nout;
+    unsigned long long expect = 0, total = slots[nout + 2];
+    bool ok = true;
+    for (int r = 0; r < world; ++r) {
+      const unsigned long long* hh = slots + (uint64_t)r * stride + nout;
+      ok &= (hh[3] == 1ull) && (hh[0] == expect) && (hh[2] == total);
+      expect += hh[1];
+    }
+    ok &= (expect == total);
+    if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
+  }
+}
+
+// Gather every rank's record: the device part rec[0, h.off) plus the header
+// words h; *all = the records, record q at *all + q * *stride.  axis_nout >= 0
+// also checks axis-reduction shard headers (at word axis_nout of each record).
+bool exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* stride, const char* where,
+              int64_t axis_nout = -1) {
+  cudaStream_t st = rt_stream();
+  const size_t n = (size_t)h.off + h.n;
+  if (D.peer && n * 8 <= D.slot_bytes) {
+    const unsigned long long ep = ++D.epoch;
+    const int par = (int)(ep & 1);
+    unsigned char* base = static_cast<unsigned char*>(D.region);
+    const unsigned long long* slots = reinterpret_cast<const unsigned long long*>(base + slot_off(par, 0));
+    cudaError_t e = launch_pdl(k_peer_put, dim3(D.world), dim3(256), 0, st,
+                               static_cast<const unsigned long long*>(rec), h, (void* const*)D.peer_dev,
+                               (uint64_t)slot_off(par, D.rank), (uint64_t)flag_off(par, D.rank), ep);
+    const double lim = D.timeout_s < 30.0 ? D.timeout_s : 30.0;
+    if (e == cudaSuccess)
+      e = launch_pdl(k_peer_wait, dim3(1), dim3(32 * ((D.world + 31) / 32)), 0, st,
+                     reinterpret_cast<const unsigned long long*>(base + flag_off(par, 0)), D.world, ep,
+                     (unsigned long long)(lim * 1e9), device_error_word(), slots, (uint64_t)(D.slot_bytes / 8),
+                     (int64_t)axis_nout);
+    *all = slots;
+    *stride = D.slot_bytes / 8;
+    return rt_cuda_ok(e, where);
+  }
+  unsigned long long* r64 = static_cast<unsigned long long*>(rec);
+  if (h.n) k_put_u64<<<1, 32, 0, st>>>(r64, h);
+  if (!rt_cuda_ok(cudaGetLastError(), where)) return false;
+  if (!all_gather(rec, D.recv, n, where)) return false;
+  *all = static_cast<const unsigned long long*>(D.recv);
+  *stride = n;
+  if (axis_nout >= 0) {
+    k_check_axis_shards<<<1, 32, 0, st>>>(*all, D.world, n, (uint64_t)axis_nout, device_error_word());
+    if (!rt_cuda_ok(cudaGetLastError(), where)) return false;
+  }
+  return true;
+}
+
+void peer_teardown() {
+  for (int q = 0; q < (int)D.peer_base.size(); ++q)
+    if (q != D.rank && D.peer_base[q]) cudaIpcCloseMemHandle(D.peer_base[q]);
+  D.peer_base.clear();
+  if (D.peer_dev) cudaFree(D.peer_dev);
+  if (D.region) cudaFree(D.region);
+  D.peer_dev = nullptr;
+  D.region = nullptr;
+  D.peer = false;
+  D.epoch = 0;
+  cudaGetLastError();
+}
+
+// Map every rank's exchange region (all ranks or none: the outcome is agreed
+// over the communicator).  DCT_PEER_EXCHANGE=0 keeps NCCL all-gathers.
+bool peer_setup() {
+  const char* env = getenv("DCT_PEER_EXCHANGE");
+  bool ok = !(env && env[0] == '0');
+  D.slot_bytes = kSlotBytes;
+  const size_t bytes = 2 * (size_t)D.world * D.slot_bytes + 2 * (size_t)D.world * 8;
+  cudaIpcMemHandle_t mine{};
+  if (ok) ok = cudaMalloc(&D.region, bytes) == cudaSuccess && cudaMemset(D.region, 0, bytes) == cudaSuccess &&
+               cudaDeviceSynchronize() == cudaSuccess && cudaIpcGetMemHandle(&mine, D.region) == cudaSuccess;
+  cudaGetLastError();
+  // all ranks' handles (64 bytes each) over the communicator
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  unsigned char* dh = nullptr;
+  std::vector<unsigned char> all(hb * D.world);
+  bool xok = cudaMalloc(&dh, hb * (D.world + 1)) == cudaSuccess &&
+             cudaMemcpy(dh, &mine, hb, cudaMemcpyHostToDevice) == cudaSuccess &&
+             settle(D.api.AllGather(dh, dh + hb, hb, ncclUint8, D.comm, rt_stream()), "dct_dist_init(handles)") &&
+             rt_wait_stream("dct_dist_init(handles)") &&
+             cudaMemcpy(all.data(), dh + hb, hb * D.world, cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (dh) cudaFree(dh);
+  cudaGetLastError();
+  if (!xok) { peer_teardown(); return false; }      // the communicator itself failed
+  D.peer_base.assign(D.world, nullptr);
+  if (ok) {
+    D.peer_base[D.rank] = D.region;
+    for (int q = 0; q < D.world && ok; ++q) {
+      if (q == D.rank) continue;
+      cudaIpcMemHandle_t h;
+      memcpy(&h, all.data() + hb * q, hb);
+      ok = cudaIpcOpenMemHandle(&D.peer_base[q], h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    }
+    if (ok) ok = cudaMalloc(&D.peer_dev, sizeof(void*) * D.world) == cudaSuccess &&
+                 cudaMemcpy(D.peer_dev, D.peer_base.data(), sizeof(void*) * D.world, cudaMemcpyHostToDevice) ==
+                     cudaSuccess;
+    cudaGetLastError();
+  }
+  // agree: the peer path only if every rank mapped every region
+  int* flag = nullptr;
+  int agreed = 0;
+  const int mine_ok = ok ? 1 : 0;
+  bool aok = cudaMalloc(&flag, sizeof(int)) == cudaSuccess &&
+             cudaMemcpy(flag, &mine_ok, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+             settle(D.api.AllReduce(flag, flag, 1, ncclInt32, ncclMin, D.comm, rt_stream()), "dct_dist_init(agree)") &&
+             rt_wait_stream("dct_dist_init(agree)") &&
+             cudaMemcpy(&agreed, flag, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (flag) cudaFree(flag);
+  cudaGetLastError();
+  if (!aok || !agreed) {
+    peer_teardown();
+    return false;
+  }
+  D.peer = true;
+  D.epoch = 0;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// record headers and rank-order folds
+// ---------------------------------------------------------------------------
 // Shards of an axis reduction must tile [0, len_total) in rank order and agree
 // on len_total; any invalid or inconsistent header marks the result invalid.
 __global__ void k_check_axis_shards(const unsigned long long* all, int world, uint64_t stride, uint64_t nout,
@@ -259,14 +468,15 @@ __global__ void k_check_axis_shards(const unsigned long long* all, int world, ui
 
 // Full reduction records [value, count, valid, -]: fold in rank order.
 // post: 0 none, 1 mean (divide by the total count).
-__global__ void k_fold_full(const double* all, int world, int op, int post, float* out32, double* out64,
-                            uint32_t* err) {
+__global__ void k_fold_full(const double* all, uint64_t stride, int world, int op, int post, float* out32,
+                            double* out64, uint32_t* err) {
+  grid_dep_wait();
   if (threadIdx.x != 0) return;
   double acc = 0.0, cnt = 0.0;
   bool ok = true, first = true;
   const bool ext = (op == RED_MAX || op == RED_MIN);
   for (int r = 0; r < world; ++r) {
-    const double* rec = all + 4 * r;
+    const double* rec = all + stride * r;
     ok &= (rec[2] == 1.0);
     cnt += rec[1];
     if (ext) {
@@ -290,13 +500,14 @@ __global__ void k_fold_full(const double* all, int world, int op, int post, floa
 }
 
 // Softmax-CE records [sum of row losses, rows, valid, -] -> loss = sum / div
-__global__ void k_fold_loss(const double* all, int world, double div, float* loss, uint32_t* err) {
+__global__ void k_fold_loss(const double* all, uint64_t stride, int world, double div, float* loss, uint32_t* err) {
+  grid_dep_wait();
   if (threadIdx.x != 0) return;
   double acc = 0.0;
   bool ok = true;
   for (int r = 0; r < world; ++r) {
-    ok &= (all[4 * r + 2] == 1.0);
-    acc = r == 0 ? all[0] : acc + all[4 * r];
+    ok &= (all[stride * r + 2] == 1.0);
+    acc = r == 0 ? all[0] : acc + all[stride * r];
   }
   if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
   if (loss) loss[0] = ok ? (float)(acc / div) : NAN;
@@ -304,8 +515,9 @@ __global__ void k_fold_loss(const double* all, int world, double div, float* los
 
 // Channel-sum records [nsum sums][count, valid, nsum, -]: out[j] = sum over
 // ranks in rank order; out[nsum] = total count.
-__global__ void k_fold_sums(const double* all, int world, uint32_t nsum, double* out, uint32_t* err) {
-  const uint64_t stride = (uint64_t)nsum + 4;
+__global__ void k_fold_sums(const double* all, uint64_t stride, int world, uint32_t nsum, double* out,
+                            uint32_t* err) {
+  grid_dep_wait();
   const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j < nsum) {
     double acc = all[j];
@@ -427,12 +639,26 @@ DCT_API int dct_dist_init(const void* id, int len, int nranks, int rank, double 
   hk.async_error = &hook_async_error;
   hk.abort = &hook_abort;
   hk.timeout_s = D.timeout_s;
-  return 0;
+  if (!D.comm) return DCT_ERR_DIST;
+  peer_setup();                                    // falls back to NCCL all-gathers when it cannot map every rank
+  return D.comm ? 0 : DCT_ERR_DIST;
 }
 
 DCT_API int dct_dist_finalize(void) {
   DLOCK;
   int rc = 0;
+  if (D.comm && D.peer) {
+    // every rank unmaps the others' regions before any rank frees its own
+    if (!rt_wait_stream("dct_dist_finalize")) rc = DCT_ERR_DIST;
+    for (int q = 0; q < (int)D.peer_base.size(); ++q)
+      if (q != D.rank && D.peer_base[q]) cudaIpcCloseMemHandle(D.peer_base[q]);
+    for (int q = 0; q < (int)D.peer_base.size(); ++q)
+      if (q != D.rank) D.peer_base[q] = nullptr;
+    if (D.comm && buffers(8, 8 * (size_t)D.world, 8, "dct_dist_finalize") &&
+        all_gather(D.send, D.recv, 1, "dct_dist_finalize(barrier)") && !rt_wait_stream("dct_dist_finalize"))
+      rc = DCT_ERR_DIST;
+    peer_teardown();
+  }
   if (D.comm) {
     if (!rt_wait_stream("dct_dist_finalize")) rc = DCT_ERR_DIST;
     if (D.comm && D.api.CommFinalize) {
@@ -520,17 +746,18 @@ DCT_API int dct_dist_reduce(int op, void* x, uint64_t outer, uint64_t len, uint6
   if (valid && !rt_cuda_ok(launch_reduce3d_packed(op_run, bx->d, outer, len, inner, (int32_t)len_offset, send,
                                                   rt_ws(), st), W))
     valid = false;
-  k_put_header_u64<<<1, 32, 0, st>>>(send + nout, len_offset, len, len_total, valid ? 1ull : 0ull);
-  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
-  if (!all_gather(send, D.recv, stride, W)) return DCT_ERR_DIST;
-  const unsigned long long* all = (const unsigned long long*)D.recv;
-  k_check_axis_shards<<<1, 32, 0, st>>>(all, D.world, stride, nout, device_error_word());
+  // header [offset, len, len_total, valid] after the nout packed partials
+  const unsigned long long* all = nullptr;
+  size_t xs = 0;
+  if (!exchange(send, make_hdr((uint32_t)nout, {len_offset, len, len_total, valid ? 1ull : 0ull}), &all, &xs, W,
+                (int64_t)nout))
+    return DCT_ERR_DIST;
   float* o32 = bo ? bo->d : nullptr;
   int32_t* oi = bi ? reinterpret_cast<int32_t*>(bi->d) : nullptr;
   if (arg && !oi) { oi = reinterpret_cast<int32_t*>(o32); o32 = nullptr; }   // indices into out (dct_reduce rule)
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && valid)
-    e = launch_fold_packed(op_run, all, (uint32_t)D.world, nout, stride, len_total, o32, oi, st);
+    e = launch_fold_packed(op_run, all, (uint32_t)D.world, nout, xs, len_total, o32, oi, st);
   if (!rt_cuda_ok(e, W)) return DCT_ERR_CUDA;
   if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_reduce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
   return 0;
@@ -553,19 +780,24 @@ DCT_API int dct_dist_reduce_all(int op, void* x, uint64_t n, void* out, double* 
   cudaStream_t st = rt_stream();
   double* rec = (double*)D.send;
   const int local_op = op == RED_MEAN ? RED_SUM : op;
-  // record [value, n, valid, 0]; value = float64 sum (mean: the raw sum) or extreme
-  k_put_f64<<<1, 32, 0, st>>>(rec, 4, 0.0, (double)n, 0.0, 0.0);
+  // record [value, n, valid, 0]; value = float64 sum (mean: the raw sum) or
+  // extreme, written by the reduction when one runs and 0 otherwise
+  bool ran = false;
   if (valid && n > 0) {
     if (!rt_ensure_ws(full_reduce_ws_bytes() + 256)) return DCT_ERR_CUDA;
     float* scratch32 = reinterpret_cast<float*>(rec + 4);              // float copy of the local result, unused
     if (!rt_cuda_ok(launch_full_reduce(local_op, bx->d, n, scratch32, rec, rt_ws(), st), W)) valid = false;
+    ran = valid;
   }
-  k_put_f64<<<1, 32, 0, st>>>(rec + 2, 1, valid ? 1.0 : 0.0, 0.0, 0.0, 0.0);
-  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
-  if (!all_gather(rec, D.recv, 4, W)) return DCT_ERR_DIST;
-  k_fold_full<<<1, 32, 0, st>>>((const double*)D.recv, D.world, local_op, op == RED_MEAN ? 1 : 0,
-                                valid ? bo->d : nullptr, D.fold, device_error_word());
-  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  const unsigned long long hn = f64_bits((double)n), hv = f64_bits(valid ? 1.0 : 0.0);
+  const Hdr h = ran ? make_hdr(1, {hn, hv, 0ull}) : make_hdr(0, {0ull, hn, hv, 0ull});
+  const unsigned long long* all = nullptr;
+  size_t xs = 0;
+  if (!exchange(rec, h, &all, &xs, W)) return DCT_ERR_DIST;
+  if (!rt_cuda_ok(launch_pdl(k_fold_full, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
+                             local_op, op == RED_MEAN ? 1 : 0, valid ? bo->d : nullptr, D.fold, device_error_word()),
+                  W))
+    return DCT_ERR_CUDA;
   if (host_out64) {
     double* hs = rt_host_scratch();
     if (!rt_cuda_ok(cudaMemcpyAsync(hs, D.fold, 8, cudaMemcpyDeviceToHost, st), W)) return DCT_ERR_CUDA;
@@ -592,7 +824,9 @@ DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, ui
                (!loss || (bs && bs->count >= 1)) && (!logprobs || (bq && bq->count >= n));
   cudaStream_t st = rt_stream();
   double* rec = (double*)D.send;
-  k_put_f64<<<1, 32, 0, st>>>(rec, 4, 0.0, (double)rows, 0.0, 0.0);            // [loss sum, rows, valid, 0]
+  // record [loss sum, rows, valid, 0]; the loss sum is written by the kernel
+  // when it computes a loss and 0 otherwise
+  bool ran = false;
   if (valid && rows > 0) {
     SoftmaxCEArgs a;
     a.logits = bl->d;
@@ -608,13 +842,17 @@ DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, ui
     a.err = device_error_word();
     if (!rt_ensure_ws(softmax_ce_ws_bytes(rows, K))) return DCT_ERR_CUDA;
     if (!rt_cuda_ok(launch_softmax_ce(a, rt_ws(), st), W)) valid = false;
+    ran = valid && a.loss_partial;
   }
-  k_put_f64<<<1, 32, 0, st>>>(rec + 2, 1, valid ? 1.0 : 0.0, 0.0, 0.0, 0.0);
-  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
-  if (!all_gather(rec, D.recv, 4, W)) return DCT_ERR_DIST;
-  k_fold_loss<<<1, 32, 0, st>>>((const double*)D.recv, D.world, (double)loss_div, bs && valid ? bs->d : nullptr,
-                                device_error_word());
-  if (!rt_cuda_ok(cudaGetLastError(), W)) return DCT_ERR_CUDA;
+  const unsigned long long hr = f64_bits((double)rows), hv = f64_bits(valid ? 1.0 : 0.0);
+  const Hdr h = ran ? make_hdr(1, {hr, hv, 0ull}) : make_hdr(0, {0ull, hr, hv, 0ull});
+  const unsigned long long* all = nullptr;
+  size_t xs = 0;
+  if (!exchange(rec, h, &all, &xs, W)) return DCT_ERR_DIST;
+  if (!rt_cuda_ok(launch_pdl(k_fold_loss, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
+                             (double)loss_div, bs && valid ? bs->d : nullptr, device_error_word()),
+                  W))
+    return DCT_ERR_CUDA;
   if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_softmax_ce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
   return 0;
 }
@@ -636,11 +874,19 @@ bool bn_exchange(const float* x, const float* dy, uint32_t N, uint32_t C, uint32
     if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, rec, st);     // [C][2] sums straight into the record
     if (!rt_cuda_ok(e, W)) valid = false;
   }
-  k_put_f64<<<1, 32, 0, st>>>(rec + nsum, 4, (double)N * (double)S, valid ? 1.0 : 0.0, (double)nsum, 0.0);
-  if (!rt_cuda_ok(cudaGetLastError(), W)) { *rc = DCT_ERR_CUDA; return false; }
-  if (!all_gather(rec, D.recv, stride, W)) { *rc = DCT_ERR_DIST; return false; }
-  k_fold_sums<<<(nsum + 1 + 255) / 256, 256, 0, st>>>((const double*)D.recv, D.world, nsum, D.fold, device_error_word());
-  if (!rt_cuda_ok(cudaGetLastError(), W)) { *rc = DCT_ERR_CUDA; return false; }
+  // header [count, valid, nsum, 0] after the 2C sums (an invalid rank's sums
+  // are never used: its valid word fails the fold on every rank)
+  const Hdr h = make_hdr(nsum, {f64_bits((double)N * (double)S), f64_bits(valid ? 1.0 : 0.0), f64_bits((double)nsum),
+                                0ull});
+  const unsigned long long* all = nullptr;
+  size_t xs = 0;
+  if (!exchange(rec, h, &all, &xs, W)) { *rc = DCT_ERR_DIST; return false; }
+  if (!rt_cuda_ok(launch_pdl(k_fold_sums, dim3((nsum + 1 + 255) / 256), dim3(256), 0, st, (const double*)all,
+                             (uint64_t)xs, D.world, nsum, D.fold, device_error_word()),
+                  W)) {
+    *rc = DCT_ERR_CUDA;
+    return false;
+  }
   return true;
 }
 }  // namespace

@@ -411,6 +411,7 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
                                                      uint32_t chunks, uint64_t inner, uint64_t len, RedOut ro) {
+  grid_dep_wait();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += stride) {
     // k = o*inner + c ; partial index = (o*chunks + ch)*inner + c
@@ -581,9 +582,10 @@ template <int OP>
 cudaError_t run_fold_packed(const unsigned long long* parts, uint32_t nparts, uint64_t nout, uint64_t stride,
                             uint64_t len_total, const RedOut& ro, cudaStream_t st) {
   // parts[p * stride + k]: the chunk-fold layout with outer = 1, inner = stride
-  // (k < nout <= stride, so the fold's outer index is always 0)
-  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(parts, nout, nparts, stride, len_total, ro);
-  return cudaGetLastError();
+  // (k < nout <= stride, so the fold's outer index is always 0); launched as a
+  // programmatic dependent of the kernel that produced the parts
+  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout, 256)), dim3(256), 0, st, parts, nout, nparts, stride,
+                    len_total, ro);
 }
 
 }  // namespace

@@ -135,7 +135,10 @@ static bool check_device_errors() {
   const uint32_t e = *(volatile uint32_t*)g.dev_err_host;
   if (!e) return true;
   *(volatile uint32_t*)g.dev_err_host = 0;
-  if (e & DCT_DEVERR_PEER_INVALID)
+  if (e & DCT_DEVERR_PEER_WAIT)
+    set_error(DCT_ERR_DIST, "sharded op: a peer rank's record did not arrive before the deadline (a rank is "
+              "gone or behind; error bits 0x%x); results are invalid", e);
+  else if (e & DCT_DEVERR_PEER_INVALID)
     set_error(DCT_ERR_DIST, "sharded op: a rank's shard was invalid (bad handle, size or count on that rank; "
               "error bits 0x%x); results are invalid", e);
   else
