@@ -214,6 +214,15 @@ class Lib:
         self.check(self.lib.dct_unary(self.UNARY[op], x, y, n, 0.0), "unary")
         self.launches += 1
 
+    def run(self, name, srvs, uavs, groups, words):
+        """RunShader by reference shader name with the cbuffer `words` (u32)."""
+        C = self.C
+        sv = (C.c_void_p * max(1, len(srvs)))(*srvs)
+        uv = (C.c_void_p * max(1, len(uavs)))(*uavs)
+        th = (C.c_uint * 3)(*groups)
+        cb = (C.c_uint * max(1, len(words)))(*words)
+        self.lib.RunShader(name.encode(), sv, len(srvs), uv, len(uavs), th, C.cast(cb, C.c_void_p), 4 * len(words))
+
     def time(self, fn, iters):
         self.lib.dct_timer_start()
         for _ in range(iters):
@@ -316,7 +325,9 @@ def run_e2e(L: Lib, c2: C2, steps: int, warmup: int):
 PER_OP_SECTIONS = {"c1": ("c1_dense_step_eager", "c1_dense_step_graph"), "c3": ("c3_sum_axis-1", "c3_sum_axis0", "c3_mean_axis-1", "c3_mean_axis0", "c3_max_axis-1",
                            "c3_max_axis0", "c3_argmax_axis-1", "c3_argmax_axis0"),
                    "c3f": ("c3_fullsum_2^30",), "c4": ("c4_softmax_ce_fused",), "c5a": ("c5a_adam_1.5e9",),
-                   "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd")}
+                   "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd"),
+                   "layout": ("f3_upsample2x_fwd", "f3_upsample2x_bwd", "f3_concat", "f3_slice", "f3_maxpool2x2_fwd",
+                              "f3_maxpool2x2_fused_fwd_bwd", "f4_conv_reshape_relu", "f4_conv_grad_reshape_relu")}
 
 
 def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, warmup: int = 3, comm=None):
@@ -368,6 +379,8 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, wa
         _c5a(L, rank, measure)
     if section("c5b"):
         _c5b(L, rank, measure, comm)
+    if section("layout"):
+        _layout(L, rank, measure)
     lib.DrainPool()
     return res
 
@@ -517,6 +530,68 @@ def _c5b(L, rank, measure, comm=None):
         measure("c5b_batchnorm_bwd", 4 * 5 * nx,
                 lambda: comm.batchnorm_backward(x, dy, bm, bv, gam, dg, db, dx, N, Cc, S, 1e-5), 7)
     for h in (x, dy, y, dx, gam, bet, rm, rv, bm, bv, dg, db):
+        lib.ReleaseBuffer(h)
+
+
+def _layout(L, rank, measure):
+    """The layout ops beside the path at UNet-like sizes (every tensor larger than
+    L2 or close to it), dispatched by reference shader name with the reference's
+    cbuffer words: nearest 2x upsample and its gradient, channel concat of two
+    tensors and one slice back, 2x2 max pooling (the shader alone, and
+    MaxPoolForwardFused + MaxPoolBackwardFused as MaxPool2D runs them), and
+    the conv output / gradient reshapes with ReLU.  No reference config sizes
+    these ops; the shapes are synthetic."""
+    C = L.C
+    lib = L.lib
+    for name in ("upsample", "upsample_backward", "concat_insert", "slice", "maxpool_forward", "conv_reshape",
+                 "conv_grad_reshape_relu"):
+        lib.CompileShader(name.encode(), "")
+    B, Ch, H, W = 32, 128, 64, 64
+    n_in, n_up = B * Ch * H * W, B * Ch * 4 * H * W              # 16.8M and 67M floats
+    seed = 5 + 1000 * rank
+    x, y, dx, z, cat = L.new(n_in), L.new(n_up), L.new(n_in), L.new(n_up), L.new(2 * n_up)
+    L.fill(x, seed, 20, 1, 0.0, 1.0)
+    L.fill(z, seed, 21, 1, 0.0, 1.0)
+    up = [B, Ch, H, W, 2 * H, 2 * W, 2, 2]
+    measure("f3_upsample2x_fwd", 4 * (n_in + n_up),
+            lambda: L.run("upsample", [x], [y], ((n_up + 255) // 256, 1, 1), up), 1)
+    measure("f3_upsample2x_bwd", 4 * (n_in + n_up),
+            lambda: L.run("upsample_backward", [y], [dx], ((n_in + 255) // 256, 1, 1), up), 1)
+    S = 4 * H * W
+    grp = ((n_up + 255) // 256, 1, 1)
+
+    def concat():
+        L.run("concat_insert", [y], [cat], grp, [B, Ch, S, 2 * Ch, 0])
+        L.run("concat_insert", [z], [cat], grp, [B, Ch, S, 2 * Ch, Ch])
+    measure("f3_concat", 4 * 4 * n_up, concat, 2)
+    measure("f3_slice", 4 * 2 * n_up, lambda: L.run("slice", [cat], [z], grp, [B, Ch, S, 2 * Ch, Ch]), 1)
+    po, pi = L.new(n_in), L.new(n_in)
+    pool_groups = ((W + 15) // 16, (H + 15) // 16, B * Ch)
+    measure("f3_maxpool2x2_fwd", 4 * (n_up + 2 * n_in),
+            lambda: L.run("maxpool_forward", [y], [po, pi], pool_groups, [B, Ch, 2 * H, 2 * W, 2, 2, H, W]), 1)
+
+    def fused():                                  # MaxPool2D.forward + backward (nn_engine.py:1018-1047)
+        pidx = C.c_void_p()
+        o = lib.MaxPoolForwardFused(y, B, Ch, 2 * H, 2 * W, 2, 2, C.byref(pidx))
+        d = lib.MaxPoolBackwardFused(po, pidx, B, Ch, H, W, n_up)
+        if not (o and d):
+            raise RuntimeError("MaxPool*Fused: " + lib.dct_last_error().decode())
+        lib.ReleaseBuffer(o)
+        lib.ReleaseBuffer(d)
+    measure("f3_maxpool2x2_fused_fwd_bwd", 4 * (n_up + 2 * n_in) + 4 * (2 * n_in + n_up), fused, 3)
+    for h in (x, dx, z, cat, po, pi):
+        lib.ReleaseBuffer(h)
+    OC, Bc, P = 256, 64, 64 * 64
+    nconv = OC * Bc * P                                           # 67M floats
+    mm, bias, co, gr = L.new(nconv), L.new(OC), y, L.new(nconv)
+    L.fill(mm, seed, 22, 1, 0.0, 1.0)
+    L.fill(bias, seed, 23, 1, 0.0, 0.1)
+    cgrp = ((Bc * P + 15) // 16, (OC + 15) // 16, 1)
+    measure("f4_conv_reshape_relu", 4 * (2 * nconv + OC),
+            lambda: L.run("conv_reshape", [mm, bias], [co], cgrp, [Bc, OC, 64, 64, 1]), 1)
+    measure("f4_conv_grad_reshape_relu", 4 * 3 * nconv,
+            lambda: L.run("conv_grad_reshape_relu", [mm, co], [gr], cgrp, [Bc, 0, 0, 0, OC, 0, 0, 64, 64]), 1)
+    for h in (mm, bias, y, gr):
         lib.ReleaseBuffer(h)
 
 

@@ -165,6 +165,35 @@ cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* 
                                   uint32_t N, uint32_t C, uint32_t S, float eps, uint64_t limit,
                                   cudaStream_t st, const double* cnt_dev = nullptr);
 
+// ---- layout ops beside the path (k_layout.cu) ----------------------------------
+// n = elements (or outputs) the dispatch covers, total = the full index space;
+// all index arithmetic is 32-bit (callers refuse index spaces past 2^32).
+cudaError_t launch_upsample(const float* x, float* y, uint32_t n, uint32_t total, uint32_t inH, uint32_t inW,
+                            uint32_t outH, uint32_t outW, uint32_t sH, uint32_t sW, cudaStream_t st);
+cudaError_t launch_upsample_backward(const float* dy, float* dx, uint32_t n, uint32_t total, uint32_t inH,
+                                     uint32_t inW, uint32_t outH, uint32_t outW, uint32_t sH, uint32_t sW,
+                                     cudaStream_t st);
+// rows of L floats: concat writes dst[q*pitch + off + r] = src[q*L + r], slice the reverse
+cudaError_t launch_channel_copy(bool slice, const float* src, float* dst, uint32_t n, uint32_t L, uint32_t pitch,
+                                uint32_t off, cudaStream_t st);
+struct PoolShape {
+  uint32_t bc, inH, inW, p, s, outH, outW;     // bc = batch * channels
+};
+// covered outputs: ow < lw, oh < lh, bc < lb
+cudaError_t launch_maxpool_forward(const float* x, float* out, uint32_t* idx, uint32_t lw, uint32_t lh, uint32_t lb,
+                                   const PoolShape& g, cudaStream_t st);
+cudaError_t launch_maxpool_scatter(const float* dz, const uint32_t* idx, float* d, uint64_t dcount, uint32_t lw,
+                                   uint32_t lh, uint32_t lb, uint32_t outH, uint32_t outW, cudaStream_t st);
+// the whole dInput (bc*inH*inW floats) in one pass, windows not overlapping
+// (s >= p); `flag` is a zeroed device word the call leaves zeroed
+cudaError_t launch_maxpool_backward_gather(const float* dz, const uint32_t* idx, float* d, const PoolShape& g,
+                                           uint32_t* flag, cudaStream_t st);
+// covered: b*P + pixel < lbp, oc < loc
+cudaError_t launch_conv_reshape(const float* mm, const float* bias, float* out, uint32_t B, uint32_t OC, uint32_t P,
+                                uint32_t lbp, uint32_t loc, uint32_t act, cudaStream_t st);
+cudaError_t launch_conv_grad_reshape(const float* dz, const float* fwd, float* out, uint32_t B, uint32_t OC,
+                                     uint32_t P, uint32_t lbp, uint32_t loc, cudaStream_t st);
+
 // ---- synthetic data (k_rng.cu) --------------------------------------------------
 // Philox4x32-10 counter-based fills.  dist 0: uniform [lo, hi); 1: normal(mean=lo, std=hi)
 cudaError_t launch_fill_random(float* y, uint64_t n, uint64_t seed, uint64_t offset, int dist,

@@ -14,8 +14,9 @@
 //                        ResolveShader / RunSequence(WithSGD)
 //   optimizers           SGDBatch / SGDBatchClipped as multi-tensor launches
 //   pool                 WarmPool / GetPoolStats / ResetPoolStats / GetPoolMemory / DrainPool
-//   out of scope         MatMulAlloc / Conv*Fused / MaxPool*Fused: exported stubs
-//                        (return null, record an error)
+//   pooling              MaxPoolForwardFused / MaxPoolBackwardFused
+//   out of scope         MatMulAlloc / Conv*Fused: exported stubs (return null,
+//                        record an error)
 //
 // and extension entry points prefixed dct_ (NumPy-broadcast binary ops, unary
 // ops, axis/full reductions, fused softmax+CE, fused Adam, BatchNorm, device
@@ -185,6 +186,7 @@ static Buffer* create_buffer(const float* host, uint64_t count) {
     b = new Buffer{kBufMagic, 0, count, static_cast<float*>(d), true};
   }
   b->ref = 1;
+  b->has_pool_geom = false;
   g.live.insert(b);
   if (host) {
     cudaPointerAttributes at{};
@@ -532,6 +534,165 @@ static bool h_dice_loss_grad(const Disp& d) {
   LAUNCH(launch_dice_grad(d.srv[0]->d, d.srv[1]->d, d.srv[2]->d, d.uav[0]->d, batch, size, n, g.stream));
 }
 
+// ---- layout ops beside the path ------------------------------------------------------
+// The shaders index with 32-bit `uint`; an index space past 2^32 is refused, as
+// is a buffer smaller than the largest index the dispatch touches.
+static bool idx32(const Disp& d, uint64_t v, const char* what) {
+  if (v <= 0xFFFFFFFFull) return true;
+  set_error(DCT_ERR_ARG, "%s: %s needs %llu elements, past the shader's 32-bit index space", d.name, what,
+            (unsigned long long)v);
+  return false;
+}
+
+static bool h_upsample(const Disp& d) {                       // nn_upsample.hlsl:15-33
+  if (!need(d, 1, 1)) return false;
+  const uint64_t B = d.u[0], C = d.u[1], inH = d.u[2], inW = d.u[3], oH = d.u[4], oW = d.u[5], sH = d.u[6],
+                 sW = d.u[7];
+  const uint64_t total = B * C * oH * oW;
+  if (!idx32(d, total, "the output")) return false;
+  const uint64_t n = lim(total, d.gx);
+  if (n == 0) return true;
+  if (sH == 0 || sW == 0) { set_error(DCT_ERR_ARG, "%s: a scale factor is 0", d.name); return false; }
+  // largest source index over outputs [0, n): the last output, the end of the
+  // row before it and the end of the plane before it (each term is monotone)
+  auto src = [&](uint64_t i) {
+    const uint64_t w = i % oW, r = i / oW, h = r % oH, bc = r / oH;
+    return (bc * inH + h / sH) * inW + w / sW;
+  };
+  const uint64_t last = n - 1, row0 = last - last % oW, plane0 = (last / (oH * oW)) * oH * oW;
+  uint64_t hi = src(last);
+  if (row0 > 0) hi = std::max(hi, src(row0 - 1));
+  if (plane0 > 0) hi = std::max(hi, src(plane0 - 1));
+  if (!idx32(d, hi + 1, "the input")) return false;
+  FITS(d.srv[0], hi + 1, "X"); FITS(d.uav[0], n, "Out");
+  LAUNCH(launch_upsample(d.srv[0]->d, d.uav[0]->d, (uint32_t)n, (uint32_t)total, (uint32_t)inH, (uint32_t)inW,
+                         (uint32_t)oH, (uint32_t)oW, (uint32_t)sH, (uint32_t)sW, g.stream));
+}
+
+static bool h_upsample_backward(const Disp& d) {              // nn_upsample_backward.hlsl:15-45
+  if (!need(d, 1, 1)) return false;
+  const uint64_t B = d.u[0], C = d.u[1], inH = d.u[2], inW = d.u[3], oH = d.u[4], oW = d.u[5], sH = d.u[6],
+                 sW = d.u[7];
+  const uint64_t total = B * C * inH * inW;
+  if (!idx32(d, total, "the input gradient") || !idx32(d, B * C * oH * oW, "the output gradient") ||
+      !idx32(d, inH * sH, "inH * scaleH") || !idx32(d, inW * sW, "inW * scaleW"))
+    return false;
+  const uint64_t n = lim(total, d.gx);
+  if (n == 0) return true;
+  FITS(d.uav[0], n, "DX");
+  if (sH && sW) FITS(d.srv[0], ((n - 1) / (inH * inW) + 1) * oH * oW, "DY");   // reads stay in their plane
+  LAUNCH(launch_upsample_backward(d.srv[0]->d, d.uav[0]->d, (uint32_t)n, (uint32_t)total, (uint32_t)inH,
+                                  (uint32_t)inW, (uint32_t)oH, (uint32_t)oW, (uint32_t)sH, (uint32_t)sW, g.stream));
+}
+
+// nn_concat_insert.hlsl:12-27 (slice = false) and nn_slice.hlsl:12-27 (slice = true)
+static bool channel_copy(const Disp& d, bool slice) {
+  if (!need(d, 1, 1)) return false;
+  const uint64_t B = d.u[0], c_in = d.u[1], S = d.u[2], c_out = d.u[3], c_off = d.u[4];
+  const uint64_t L = c_in * S, total = B * L, pitch = c_out * S, off = c_off * S;
+  if (!idx32(d, total, "the copied block") || !idx32(d, pitch, "c_out * spatial") ||
+      !idx32(d, off, "c_offset * spatial"))
+    return false;
+  const uint64_t n = lim(total, d.gx);
+  if (n == 0) return true;
+  // largest strided index over [0, n): the last element and the end of the row before it
+  const uint64_t q = (n - 1) / L, r = (n - 1) - q * L;
+  uint64_t hi = q * pitch + off + r;
+  if (q > 0) hi = std::max(hi, (q - 1) * pitch + off + L - 1);
+  if (!idx32(d, hi + 1, "the strided tensor")) return false;
+  if (slice) { FITS(d.srv[0], hi + 1, "DY"); FITS(d.uav[0], n, "DX"); }
+  else { FITS(d.srv[0], n, "X"); FITS(d.uav[0], hi + 1, "Out"); }
+  LAUNCH(launch_channel_copy(slice, d.srv[0]->d, d.uav[0]->d, (uint32_t)n, (uint32_t)L, (uint32_t)pitch,
+                             (uint32_t)off, g.stream));
+}
+static bool h_concat_insert(const Disp& d) { return channel_copy(d, false); }
+static bool h_slice(const Disp& d) { return channel_copy(d, true); }
+
+// outputs the 16x16-thread groups reach: ow < lw, oh < lh, bc < lb
+struct PoolCover {
+  uint64_t lw, lh, lb, last;                                  // last = largest output index + 1
+};
+static PoolCover pool_cover(const Disp& d, uint64_t bc, uint64_t oH, uint64_t oW) {
+  PoolCover c;
+  c.lw = std::min<uint64_t>(oW, (uint64_t)d.gx * 16);
+  c.lh = std::min<uint64_t>(oH, (uint64_t)d.gy * 16);
+  c.lb = std::min<uint64_t>(bc, d.gz);
+  c.last = (c.lw && c.lh && c.lb) ? (c.lb - 1) * oH * oW + (c.lh - 1) * oW + c.lw : 0;
+  return c;
+}
+
+static bool h_maxpool_forward(const Disp& d) {                // nn_maxpool_forward.hlsl:16-52
+  if (!need(d, 1, 2)) return false;
+  const uint64_t B = d.u[0], C = d.u[1], inH = d.u[2], inW = d.u[3], p = d.u[4], s = d.u[5], oH = d.u[6],
+                 oW = d.u[7];
+  if (!idx32(d, B * C * oH * oW, "the output") || !idx32(d, B * C * inH * inW, "the input")) return false;
+  const PoolCover c = pool_cover(d, B * C, oH, oW);
+  if (c.last == 0) return true;
+  if (!idx32(d, (c.lh - 1) * s + p, "the window rows") || !idx32(d, (c.lw - 1) * s + p, "the window columns"))
+    return false;
+  FITS(d.uav[0], c.last, "output"); FITS(d.uav[1], c.last, "indices");
+  if (p && inH && inW) {
+    const uint64_t hi = (c.lb - 1) * inH * inW + std::min(inH - 1, (c.lh - 1) * s + p - 1) * inW +
+                        std::min(inW - 1, (c.lw - 1) * s + p - 1);
+    FITS(d.srv[0], hi + 1, "input");
+  }
+  const PoolShape gs{(uint32_t)(B * C), (uint32_t)inH, (uint32_t)inW, (uint32_t)p, (uint32_t)s, (uint32_t)oH,
+                     (uint32_t)oW};
+  LAUNCH(launch_maxpool_forward(d.srv[0]->d, d.uav[0]->d, reinterpret_cast<uint32_t*>(d.uav[1]->d), (uint32_t)c.lw,
+                                (uint32_t)c.lh, (uint32_t)c.lb, gs, g.stream));
+}
+
+static bool h_maxpool_backward(const Disp& d) {               // nn_maxpool_backward.hlsl:12-25
+  if (!need(d, 2, 1)) return false;
+  const uint64_t B = d.u[0], C = d.u[1], oH = d.u[2], oW = d.u[3];
+  if (!idx32(d, B * C * oH * oW, "the output gradient")) return false;
+  const PoolCover c = pool_cover(d, B * C, oH, oW);
+  if (c.last == 0) return true;
+  FITS(d.srv[0], c.last, "dZ"); FITS(d.srv[1], c.last, "indices");
+  LAUNCH(launch_maxpool_scatter(d.srv[0]->d, reinterpret_cast<const uint32_t*>(d.srv[1]->d), d.uav[0]->d,
+                                d.uav[0]->count, (uint32_t)c.lw, (uint32_t)c.lh, (uint32_t)c.lb, (uint32_t)oH,
+                                (uint32_t)oW, g.stream));
+}
+
+// Largest [b][oc][pixel] index over columns bp < lbp of row oc = loc - 1 (the
+// last column and the end of the image before it).
+static uint64_t nchw_hi(uint64_t lbp, uint64_t loc, uint64_t OC, uint64_t P) {
+  auto at = [&](uint64_t bp) { return (bp / P) * OC * P + (loc - 1) * P + bp % P; };
+  uint64_t hi = at(lbp - 1);
+  if (lbp - 1 >= P) hi = std::max(hi, at(((lbp - 1) / P) * P - 1));
+  return hi;
+}
+
+static bool h_conv_reshape(const Disp& d) {                   // nn_conv_reshape.hlsl:13-30
+  if (!need(d, 2, 1)) return false;
+  const uint64_t B = d.u[0], OC = d.u[1], P = (uint64_t)d.u[2] * d.u[3], BP = B * P;
+  if (!idx32(d, OC * BP, "the output")) return false;
+  const uint64_t lbp = std::min<uint64_t>(BP, (uint64_t)d.gx * 16), loc = std::min<uint64_t>(OC, (uint64_t)d.gy * 16);
+  if (lbp == 0 || loc == 0) return true;
+  FITS(d.srv[0], (loc - 1) * BP + lbp, "matmul_res"); FITS(d.srv[1], loc, "bias");
+  FITS(d.uav[0], nchw_hi(lbp, loc, OC, P) + 1, "output");
+  LAUNCH(launch_conv_reshape(d.srv[0]->d, d.srv[1]->d, d.uav[0]->d, (uint32_t)B, (uint32_t)OC, (uint32_t)P,
+                             (uint32_t)lbp, (uint32_t)loc, d.u[4], g.stream));
+}
+
+// nn_conv_grad_reshape.hlsl:16-28 / nn_conv_grad_reshape_relu.hlsl:21-39: the
+// cbuffer's fifth word (`ks`) carries outC, words 8 and 9 outH and outW
+static bool conv_grad_reshape(const Disp& d, bool relu) {
+  if (!need(d, relu ? 2 : 1, 1)) return false;
+  const uint64_t B = d.u[0], OC = d.u[4], P = (uint64_t)d.u[7] * d.u[8], BP = B * P;
+  if (!idx32(d, OC * BP, "the gradient")) return false;
+  const uint64_t lbp = std::min<uint64_t>(BP, (uint64_t)d.gx * 16), loc = std::min<uint64_t>(OC, (uint64_t)d.gy * 16);
+  if (lbp == 0 || loc == 0) return true;
+  const uint64_t hi = nchw_hi(lbp, loc, OC, P) + 1;
+  FITS(d.srv[0], hi, "dZ");
+  if (relu) FITS(d.srv[1], hi, "fwd_output");
+  FITS(d.uav[0], (loc - 1) * BP + lbp, "output");
+  LAUNCH(launch_conv_grad_reshape(d.srv[0]->d, relu ? d.srv[1]->d : nullptr, d.uav[0]->d, (uint32_t)B, (uint32_t)OC,
+                                  (uint32_t)P, (uint32_t)lbp, (uint32_t)loc, g.stream));
+}
+static bool h_conv_grad_reshape(const Disp& d) { return conv_grad_reshape(d, false); }
+static bool h_conv_grad_reshape_relu(const Disp& d) { return conv_grad_reshape(d, true); }
+
 // ---- softmax / CE -------------------------------------------------------------
 static bool run_softmax_ce(const Disp& d, SoftmaxCEArgs a) {
   a.err = g.dev_err_dev;
@@ -766,6 +927,15 @@ static Shader g_shaders[] = {
     {"dice_loss", h_dice_loss, false, false, kShaderMagic},
     {"dice_loss_sums", h_dice_loss_sums, false, false, kShaderMagic},
     {"dice_loss_grad", h_dice_loss_grad, false, false, kShaderMagic},
+    {"upsample", h_upsample, false, false, kShaderMagic},
+    {"upsample_backward", h_upsample_backward, false, false, kShaderMagic},
+    {"concat_insert", h_concat_insert, false, false, kShaderMagic},
+    {"slice", h_slice, false, false, kShaderMagic},
+    {"maxpool_forward", h_maxpool_forward, false, false, kShaderMagic},
+    {"maxpool_backward", h_maxpool_backward, false, false, kShaderMagic},
+    {"conv_reshape", h_conv_reshape, false, false, kShaderMagic},
+    {"conv_grad_reshape", h_conv_grad_reshape, false, false, kShaderMagic},
+    {"conv_grad_reshape_relu", h_conv_grad_reshape_relu, false, false, kShaderMagic},
     {"dct_unary", h_dct_unary, true, false, kShaderMagic},
     {"dct_binary", h_dct_binary, true, false, kShaderMagic},
     {"dct_reduce", h_dct_reduce, true, false, kShaderMagic},
@@ -1045,7 +1215,7 @@ DCT_API float SGDBatchClipped(void** params, void** grads, uint32_t* sizes, uint
   return g.host_small[0];
 }
 
-// -- out-of-scope fused dense / layout ops: exported so the reference binds ----------
+// -- out-of-scope fused dense ops: exported so the reference binds --------------------
 DCT_API void* MatMulAlloc(void*, void*, uint32_t, uint32_t, uint32_t, uint32_t) {
   LOCK;
   set_error(DCT_ERR_UNSUPPORTED, "MatMulAlloc: dense matmul is outside libdct_cuda's scope");
@@ -1067,16 +1237,90 @@ DCT_API void ConvBackwardFused(void*, void*, void*, void*, void*, uint32_t, uint
   if (pDI) *pDI = nullptr;
   set_error(DCT_ERR_UNSUPPORTED, "ConvBackwardFused: convolution is outside libdct_cuda's scope");
 }
-DCT_API void* MaxPoolForwardFused(void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, void** pIdx) {
+
+// -- max pooling (engine.cpp:880-929) ------------------------------------------------
+// Forward: output and index buffers of batch*inC*outH*outW from the pool, the
+// maxpool_forward kernel over every output, *pIndices = the index buffer.  The
+// index buffer remembers the pooling geometry so that the backward pass can
+// build dInput in one gather instead of a clear plus a scatter.
+DCT_API void* MaxPoolForwardFused(void* x, uint32_t batch, uint32_t inC, uint32_t inH, uint32_t inW, uint32_t pool,
+                                  uint32_t stride, void** pIndices) {
   LOCK;
-  if (pIdx) *pIdx = nullptr;
-  set_error(DCT_ERR_UNSUPPORTED, "MaxPoolForwardFused: pooling is outside libdct_cuda's scope");
-  return nullptr;
+  const char* W = "MaxPoolForwardFused";
+  if (!ensure_init()) return nullptr;
+  Buffer* bx = buf_of(x);
+  if (!bx) { set_error(DCT_ERR_HANDLE, "%s: x is not a live buffer", W); return nullptr; }
+  if (pool == 0 || stride == 0 || inH < pool || inW < pool) {
+    set_error(DCT_ERR_ARG, "%s: pool %u / stride %u must be >= 1 and the pool must fit the %ux%u input", W, pool,
+              stride, inH, inW);
+    return nullptr;
+  }
+  const uint64_t bc = (uint64_t)batch * inC, outH = (inH - pool) / stride + 1, outW = (inW - pool) / stride + 1;
+  const uint64_t nin = bc * inH * inW, nout = bc * outH * outW;
+  if (nin > 0xFFFFFFFFull) { set_error(DCT_ERR_ARG, "%s: input past the 32-bit index space", W); return nullptr; }
+  if (bx->count < nin) {
+    set_error(DCT_ERR_SIZE, "%s: x holds %llu floats, the pooling reads %llu", W, (unsigned long long)bx->count,
+              (unsigned long long)nin);
+    return nullptr;
+  }
+  Buffer* out = create_buffer(nullptr, nout);
+  if (!out) return nullptr;
+  Buffer* idx = create_buffer(nullptr, nout);
+  if (!idx) { release_internal(out); return nullptr; }
+  const PoolShape gs{(uint32_t)bc, inH, inW, pool, stride, (uint32_t)outH, (uint32_t)outW};
+  if (!cuda_ok(launch_maxpool_forward(bx->d, out->d, reinterpret_cast<uint32_t*>(idx->d), gs.outW, gs.outH, gs.bc, gs,
+                                      g.stream), W)) {
+    release_internal(out);
+    release_internal(idx);
+    return nullptr;
+  }
+  const uint32_t geom[7] = {gs.bc, gs.inH, gs.inW, gs.p, gs.s, gs.outH, gs.outW};
+  memcpy(idx->pool_geom, geom, sizeof(geom));
+  idx->has_pool_geom = true;
+  if (pIndices) *pIndices = idx;
+  else release_internal(idx);                    // nobody can reach it (the reference leaks it)
+  return out;
 }
-DCT_API void* MaxPoolBackwardFused(void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t) {
+
+// Backward: dInput of x_size floats = zeros plus dZ at each output's index,
+// then the index buffer is released.  With the geometry recorded by the
+// forward pass and windows that do not overlap, one gather kernel writes every
+// element once; otherwise (or for an index buffer from elsewhere) the buffer
+// is cleared and the outputs scattered, as the reference does.
+DCT_API void* MaxPoolBackwardFused(void* grad_output, void* indices, uint32_t batch, uint32_t inC, uint32_t outH,
+                                   uint32_t outW, uint32_t x_size) {
   LOCK;
-  set_error(DCT_ERR_UNSUPPORTED, "MaxPoolBackwardFused: pooling is outside libdct_cuda's scope");
-  return nullptr;
+  const char* W = "MaxPoolBackwardFused";
+  if (!ensure_init()) return nullptr;
+  Buffer* dx = create_buffer(nullptr, x_size);
+  if (!dx) return nullptr;
+  Buffer *bg = buf_of(grad_output), *bi = buf_of(indices);
+  const uint64_t bc = (uint64_t)batch * inC, nout = bc * outH * outW;
+  cudaError_t e = cudaSuccess;
+  if (!bg || !bi) {
+    set_error(DCT_ERR_HANDLE, "%s: grad_output or indices is not a live buffer", W);
+    e = cudaMemsetAsync(dx->d, 0, (size_t)x_size * sizeof(float), g.stream);
+  } else if (nout > 0xFFFFFFFFull || bg->count < nout || bi->count < nout) {
+    set_error(DCT_ERR_SIZE, "%s: grad_output / indices hold fewer than batch*inC*outH*outW = %llu floats", W,
+              (unsigned long long)nout);
+    e = cudaMemsetAsync(dx->d, 0, (size_t)x_size * sizeof(float), g.stream);
+  } else {
+    const uint32_t* gm = bi->pool_geom;
+    const PoolShape gs{gm[0], gm[1], gm[2], gm[3], gm[4], gm[5], gm[6]};
+    const bool gather = bi->has_pool_geom && gs.bc == bc && gs.outH == outH && gs.outW == outW && gs.s >= gs.p &&
+                        (uint64_t)gs.bc * gs.inH * gs.inW == x_size && reduce_counters() != nullptr;
+    const uint32_t* ip = reinterpret_cast<const uint32_t*>(bi->d);
+    if (gather) {
+      e = launch_maxpool_backward_gather(bg->d, ip, dx->d, gs, reduce_counters() + kReduceCounters - 1, g.stream);
+    } else {
+      e = cudaMemsetAsync(dx->d, 0, (size_t)x_size * sizeof(float), g.stream);
+      if (e == cudaSuccess)
+        e = launch_maxpool_scatter(bg->d, ip, dx->d, x_size, outW, outH, (uint32_t)bc, outH, outW, g.stream);
+    }
+  }
+  cuda_ok(e, W);
+  if (bi) release_handle(indices);               // engine.cpp:927: no longer needed after backward
+  return dx;
 }
 
 // -- pool -------------------------------------------------------------------------

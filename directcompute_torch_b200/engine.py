@@ -11,14 +11,15 @@ unchanged, and the parity tests read like the reference's own.
   elementwise Functions              nn_engine.py:1062-1199, 1369-1399
   softmax + CE, dice loss            nn_engine.py:1268-1317
   global average pool                nn_engine.py:1466-1490
+  MaxPool2D, UpSample2D, Concat      nn_engine.py:1018-1047, 1196-1266, 1328-1332
   rms, clip_grad_norm, sgd clipped   nn_engine.py:1335-1367, 1685-1692
   BatchNorm2d                        nn_engine.py:1794-1871, 1904-1916
   SGD, AdamW, Adam                   nn_engine.py:2172-2242
   Metrics, end_batch, pool helpers   nn_engine.py:2322-2475
   ComputeGraph record / replay       nn_engine.py:2490-2771
 
-Dense matmul, convolution, pooling and custom-HLSL entry points are outside
-this library (the C symbols exist and report DCT_ERR_UNSUPPORTED).
+Dense matmul, convolution and custom-HLSL entry points are outside this
+library (the C symbols exist and report DCT_ERR_UNSUPPORTED).
 """
 from __future__ import annotations
 
@@ -50,6 +51,8 @@ SHADERS = (
     "argmax_correct", "accumulate_scalar", "rms", "grad_sq_reduce", "grad_norm_final", "sgd",
     "sgd_clipped", "adam", "batchnorm_mean_var", "batchnorm_forward", "batchnorm_backward_reduce",
     "batchnorm_backward_dx", "dice_loss", "dice_loss_sums", "dice_loss_grad",
+    "upsample", "upsample_backward", "concat_insert", "slice", "maxpool_forward", "maxpool_backward",
+    "conv_reshape", "conv_grad_reshape", "conv_grad_reshape_relu",
 )
 for _s in SHADERS:
     lib.CompileShader(_s.encode(), "")
@@ -447,6 +450,99 @@ class GlobalAvgPool2DFunc(Function):
             _dispatch(b"global_avg_pool_backward", (grad_output.gpu_buf,), (h,), _groups(x.size), 1, 1,
                       u1=n, u2=c, u3=self.S)
             x._accumulate_grad(Tensor.from_gpu(h, x.shape, track=True))
+
+
+# ---------------------------------------------------------------------------
+# layout Functions: max pooling, nearest upsample, channel concat
+# (nn_engine.py:1018-1047, 1196-1266)
+# ---------------------------------------------------------------------------
+class MaxPool2D(Function):
+    """Window max with its flat index kept on the device (MaxPoolForwardFused);
+    the backward call consumes and releases the index buffer."""
+    def __del__(self):
+        h = getattr(self, "indices_handle", None)
+        if h:
+            lib.ReleaseBuffer(h)
+            self.indices_handle = None
+
+    def forward(self, x, pool_size=2, stride=2):
+        self.inputs = (x,)
+        batch, inC, inH, inW = x.shape
+        outH = (inH - pool_size) // stride + 1
+        outW = (inW - pool_size) // stride + 1
+        p_idx = ctypes.c_void_p()
+        h = lib.MaxPoolForwardFused(x.gpu_buf, batch, inC, inH, inW, pool_size, stride, ctypes.byref(p_idx))
+        self.indices_handle = p_idx.value
+        return _out(h, (batch, inC, outH, outW), self, x.requires_grad)
+
+    def backward(self, grad_output):
+        x = self.inputs[0]
+        batch, inC, outH, outW = grad_output.shape
+        d = lib.MaxPoolBackwardFused(grad_output.gpu_buf, self.indices_handle, batch, inC, outH, outW, x.size)
+        self.indices_handle = None                      # released by MaxPoolBackwardFused
+        x._accumulate_grad(Tensor.from_gpu(d, x.shape, track=True))
+
+
+class UpSample2D(Function):
+    """Nearest-neighbour upsample by integer factors."""
+    def forward(self, x, scaleH=2, scaleW=2):
+        self.inputs = (x,)
+        self.scaleH, self.scaleW = scaleH, scaleW
+        batch, C, inH, inW = x.shape
+        outH, outW = inH * scaleH, inW * scaleW
+        n = batch * C * outH * outW
+        h = _new(n)
+        _dispatch(b"upsample", (x.gpu_buf,), (h,), _groups(n), 1, 1,
+                  u1=batch, u2=C, u3=inH, u4=inW, u5=outH, u6=outW, u7=scaleH, u8=scaleW, cbSize=32)
+        return _out(h, (batch, C, outH, outW), self, x.requires_grad)
+
+    def backward(self, grad_output):
+        x = self.inputs[0]
+        if x.requires_grad:
+            batch, C, inH, inW = x.shape
+            h = _new(x.size)
+            _dispatch(b"upsample_backward", (grad_output.gpu_buf,), (h,), _groups(x.size), 1, 1,
+                      u1=batch, u2=C, u3=inH, u4=inW, u5=inH * self.scaleH, u6=inW * self.scaleW,
+                      u7=self.scaleH, u8=self.scaleW, cbSize=32)
+            x._accumulate_grad(Tensor.from_gpu(h, x.shape, track=True))
+
+
+class Concat(Function):
+    """Concatenation along channels (axis 1) of NCHW tensors."""
+    def forward(self, tensors, axis=1):
+        if axis != 1:
+            raise NotImplementedError("Concat currently only supported along channel dimension (axis 1)")
+        self.inputs = tuple(tensors)
+        batch, _, H, W = tensors[0].shape
+        spatial = H * W
+        total_C = sum(t.shape[1] for t in tensors)
+        h = _new(batch * total_C * spatial)
+        self.c_offsets = []
+        c_off = 0
+        for t in tensors:
+            self.c_offsets.append(c_off)
+            c_in = t.shape[1]
+            _dispatch(b"concat_insert", (t.gpu_buf,), (h,), _groups(batch * c_in * spatial), 1, 1,
+                      u1=batch, u2=c_in, u3=spatial, u4=total_C, u5=c_off, cbSize=20)
+            c_off += c_in
+        return _out(h, (batch, total_C, H, W), self, any(t.requires_grad for t in tensors))
+
+    def backward(self, grad_output):
+        batch, total_C, H, W = grad_output.shape
+        spatial = H * W
+        for t, c_off in zip(self.inputs, self.c_offsets):
+            if t.requires_grad:
+                c_in = t.shape[1]
+                n = batch * c_in * spatial
+                h = _new(n)
+                _dispatch(b"slice", (grad_output.gpu_buf,), (h,), _groups(n), 1, 1,
+                          u1=batch, u2=c_in, u3=spatial, u4=total_C, u5=c_off, cbSize=20)
+                t._accumulate_grad(Tensor.from_gpu(h, t.shape, track=True))
+
+
+def maxpool2d(x, pool_size=2, stride=2): return MaxPool2D().forward(x, pool_size, stride)
+def upsample2d(x, scaleH=2, scaleW=2): return UpSample2D().forward(x, scaleH, scaleW)
+def concat(tensors, axis=1): return Concat().forward(tensors, axis)
 
 
 def add_bias(A, B): return AddBias().forward(A, B)

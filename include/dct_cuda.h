@@ -114,8 +114,13 @@ DCT_API void ClearBuffer(void* handle);
  * softmax_ce_grad argmax_correct accumulate_scalar rms grad_sq_reduce
  * grad_norm_final sgd sgd_clipped adam batchnorm_mean_var batchnorm_forward
  * batchnorm_backward_reduce batchnorm_backward_dx dice_loss dice_loss_sums
- * dice_loss_grad, plus the extension names dct_unary dct_binary dct_reduce
- * dct_reduce_all dct_softmax_ce (cbuffer layouts in runtime.cu). */
+ * dice_loss_grad upsample upsample_backward concat_insert slice
+ * maxpool_forward maxpool_backward conv_reshape conv_grad_reshape
+ * conv_grad_reshape_relu, plus the extension names dct_unary dct_binary
+ * dct_reduce dct_reduce_all dct_softmax_ce (cbuffer layouts in runtime.cu).
+ * A buffer smaller than the largest index a dispatch touches is refused
+ * (DCT_ERR_SIZE) rather than overrun; maxpool_backward drops indices past its
+ * UAV, as D3D11 drops out-of-range UAV writes. */
 DCT_API void RunShader(const char* name, void** srvs, uint32_t srvCount, void** uavs, uint32_t uavCount,
                        uint32_t* threads, void* cb, uint32_t cbSize);
 /* engine.cpp:404-406 (alias) */
@@ -146,10 +151,22 @@ DCT_API void ConvBackwardFused(void* go, void* fo, void* x, void* f, void* im2co
                                uint32_t inH, uint32_t inW, uint32_t outC, uint32_t kH, uint32_t kW,
                                uint32_t stride, uint32_t padding, uint32_t actType, uint32_t xg, uint32_t fg,
                                uint32_t bg, void** pDF, void** pDB, void** pDI); /* engine.cpp:802-876 */
+
+/* ---- max pooling ---------------------------------------------------------------- */
+/* engine.cpp:880-902: output and index buffers of batch*inC*outH*outW with
+ * outH = (inH - pool)/stride + 1 (likewise outW); per output the window's first
+ * maximum above -1e30 (strict >, NaN never selected) and its flat input index,
+ * 0xFFFFFFFF when nothing beat -1e30; *pIdx = the index buffer (released if
+ * pIdx is null).  Returns null (DCT_ERR_ARG) for pool or stride 0 or a pool
+ * larger than the input. */
 DCT_API void* MaxPoolForwardFused(void* x, uint32_t batch, uint32_t inC, uint32_t inH, uint32_t inW,
-                                  uint32_t pool, uint32_t stride, void** pIdx); /* engine.cpp:881-903 */
+                                  uint32_t pool, uint32_t stride, void** pIdx);
+/* engine.cpp:905-929: dInput of xSize floats = 0 except dInput[idx[o]] =
+ * go[o] (indices past xSize dropped), then releases idx.  Index buffers from
+ * MaxPoolForwardFused with non-overlapping windows take a one-pass gather;
+ * the result is the same for any index contents. */
 DCT_API void* MaxPoolBackwardFused(void* go, void* idx, uint32_t batch, uint32_t inC, uint32_t outH,
-                                   uint32_t outW, uint32_t xSize); /* engine.cpp:906-931 */
+                                   uint32_t outW, uint32_t xSize);
 
 /* ---- pool -------------------------------------------------------------------- */
 DCT_API void WarmPool(uint32_t* sizes, uint32_t numSizes, uint32_t copies); /* engine.cpp:617-635 */

@@ -75,6 +75,11 @@ def _addr(p):
     return ctypes.cast(p, ctypes.c_void_p).value or 0
 
 
+def _set_out_ptr(p, value) -> None:
+    """Store a handle through a `void**` out-parameter (ctypes.byref / pointer / address)."""
+    ctypes.c_void_p.from_address(_addr(p)).value = int(value) if value else None
+
+
 class _Buf:
     __slots__ = ("data", "count", "ref")
 
@@ -316,11 +321,40 @@ class FakeLib:
     def _ConvBackwardFused(self, *a):
         return None
 
-    def _MaxPoolForwardFused(self, *a):
-        return None
+    def _MaxPoolForwardFused(self, x, batch, inC, inH, inW, pool, stride, p_indices):
+        """engine.cpp:880-902: two buffers of batch*inC*outH*outW, then `maxpool_forward`
+        with the cbuffer {batch, inC, inH, inW, pool, stride, outH, outW} and
+        ((outW+15)/16, (outH+15)/16, batch*inC) groups; *pIndices = the index buffer."""
+        m = 0xFFFFFFFF
+        batch, inC, inH, inW, pool, stride = (int(v) & m for v in (batch, inC, inH, inW, pool, stride))
+        if stride == 0 or pool == 0 or inH < pool or inW < pool:
+            return None                      # the reference divides by zero or wraps to a huge size here
+        outH = (inH - pool) // stride + 1
+        outW = (inW - pool) // stride + 1
+        n = batch * inC * outH * outW
+        out = self._CreateBuffer(None, n)
+        idx = self._CreateBuffer(None, n)
+        if not out or not idx:
+            return None
+        cb = struct.pack("<8I", batch, inC, inH, inW, pool, stride, outH, outW)
+        self._run("maxpool_forward", [x], [out, idx], ((outW + 15) // 16, (outH + 15) // 16, batch * inC), cb)
+        if p_indices:
+            _set_out_ptr(p_indices, idx)
+        return out
 
-    def _MaxPoolBackwardFused(self, *a):
-        return None
+    def _MaxPoolBackwardFused(self, grad_out, indices, batch, inC, outH, outW, x_size):
+        """engine.cpp:905-929: a zeroed buffer of x_size, `maxpool_backward` with
+        {batch, inC, outH, outW} and ((outW+15)/16, (outH+15)/16, batch*inC) groups,
+        then the index buffer is released."""
+        batch, inC, outH, outW, x_size = (int(v) for v in (batch, inC, outH, outW, x_size))
+        d = self._CreateBuffer(None, x_size)
+        if not d:
+            return None
+        self._bufs[d].data[:] = 0
+        cb = struct.pack("<4I", batch, inC, outH, outW)
+        self._run("maxpool_backward", [grad_out, indices], [d], ((outW + 15) // 16, (outH + 15) // 16, batch * inC), cb)
+        self._ReleaseBuffer(indices)
+        return d
 
     # -- pool --------------------------------------------------------------------
     def _WarmPool(self, sizes, n, copies):

@@ -370,6 +370,155 @@ def dice_loss(pred, target, batch, size):
 # dispatcher over the reference's cbuffer layouts
 # ---------------------------------------------------------------------------
 
+# ---------------------------------------------------------------------------
+# layout shaders beside the path: nearest upsample, channel concat / slice,
+# max pooling, and the conv output / gradient reshapes
+# ---------------------------------------------------------------------------
+NO_INDEX = np.uint32(0xFFFFFFFF)
+
+
+def upsample(x, batch, C, inH, inW, outH, outW, sH, sW, limit=None):
+    """nn_upsample.hlsl:15-33: Out[b,c,h,w] = X[b,c,h//sH,w//sW] (nearest, integer scales)
+    for flat output index < min(batch*C*outH*outW, limit)."""
+    total = batch * C * outH * outW
+    n = total if limit is None else min(total, limit)
+    i = np.arange(n, dtype=np.int64)
+    w = i % outW
+    t = i // outW
+    h = t % outH
+    bc = t // outH
+    src = (bc * inH + h // sH) * inW + w // sW
+    return np.asarray(x, F32)[src]
+
+
+def upsample_backward(dy, batch, C, inH, inW, outH, outW, sH, sW, limit=None):
+    """nn_upsample_backward.hlsl:15-45: DX[b,c,h,w] = sum over the sH x sW block of DY
+    (rows outer, columns inner, skipping positions past outH / outW), accumulated in
+    fp32 from 0.0f in that order."""
+    total = batch * C * inH * inW
+    n = total if limit is None else min(total, limit)
+    i = np.arange(n, dtype=np.int64)
+    w = i % inW
+    t = i // inW
+    h = t % inH
+    bc = t // inH
+    dy = np.asarray(dy, F32)
+    acc = np.zeros(n, F32)
+    for sh in range(sH):
+        for sw in range(sW):
+            ho, wo = h * sH + sh, w * sW + sw
+            ok = (ho < outH) & (wo < outW)
+            src = np.where(ok, (bc * outH + ho) * outW + wo, 0)
+            acc = np.where(ok, (acc + dy[src]).astype(F32), acc)
+    return acc
+
+
+def _channel_map(batch, c_in, spatial, c_out, c_off, limit):
+    n = batch * c_in * spatial if limit is None else min(batch * c_in * spatial, limit)
+    i = np.arange(n, dtype=np.int64)
+    s = i % spatial
+    t = i // spatial
+    c = t % c_in
+    b = t // c_in
+    return i, (b * c_out + c + c_off) * spatial + s
+
+
+def concat_insert(out, x, batch, c_in, spatial, c_out, c_off, limit=None):
+    """nn_concat_insert.hlsl:12-27: Out[b, c + c_off, s] = X[b, c, s] (in place on `out`)."""
+    i, dst = _channel_map(batch, c_in, spatial, c_out, c_off, limit)
+    out[dst] = np.asarray(x, F32)[i]
+    return out
+
+
+def slice_channels(dy, batch, c_in, spatial, c_out, c_off, limit=None):
+    """nn_slice.hlsl:12-27: DX[b, c, s] = DY[b, c + c_off, s] for flat index < limit."""
+    _, src = _channel_map(batch, c_in, spatial, c_out, c_off, limit)
+    return np.asarray(dy, F32)[src]
+
+
+def maxpool_forward(x, batch, inC, inH, inW, p, stride, outH, outW, lim_w=None, lim_h=None, lim_bc=None):
+    """nn_maxpool_forward.hlsl:16-52: per output (bc, oh, ow) the window
+    [oh*stride, +p) x [ow*stride, +p), clipped to the input, scanned rows outer /
+    columns inner with a strict `>` from -1e30 (first maximum wins; NaN never
+    selected); the index is the flat input index, 0xFFFFFFFF when nothing beat
+    -1e30.  Returns (out_idx, values, indices) for the threads that run."""
+    lw = outW if lim_w is None else min(outW, lim_w)
+    lh = outH if lim_h is None else min(outH, lim_h)
+    lb = batch * inC if lim_bc is None else min(batch * inC, lim_bc)
+    bc, oh, ow = np.meshgrid(np.arange(lb, dtype=np.int64), np.arange(lh, dtype=np.int64),
+                             np.arange(lw, dtype=np.int64), indexing="ij")
+    x = np.asarray(x, F32)
+    best = np.full(bc.shape, F32(-1e30), F32)
+    idx = np.full(bc.shape, NO_INDEX, np.uint32)
+    base = bc * (inH * inW)
+    for ph in range(p):
+        for pw in range(p):
+            ih, iw = oh * stride + ph, ow * stride + pw
+            ok = (ih < inH) & (iw < inW)
+            src = np.where(ok, base + ih * inW + iw, 0)
+            v = x[src]
+            upd = ok & (v > best)
+            best = np.where(upd, v, best)
+            idx = np.where(upd, src.astype(np.uint32), idx)
+    out_idx = bc * (outH * outW) + oh * outW + ow
+    return out_idx.ravel(), best.ravel(), idx.ravel()
+
+
+def maxpool_backward(dinput, dz, indices_bits, batch, inC, outH, outW, lim_w=None, lim_h=None, lim_bc=None):
+    """nn_maxpool_backward.hlsl:12-25: dInput[idx[o]] = dZ[o] for every output o
+    that runs and whose index is not 0xFFFFFFFF (in place; other elements keep
+    their value).  Indices past the buffer are dropped, as D3D11 drops
+    out-of-range UAV writes.  Two outputs naming one element (overlapping
+    windows) leave either value in the reference; callers of this oracle use
+    windows that do not overlap."""
+    lw = outW if lim_w is None else min(outW, lim_w)
+    lh = outH if lim_h is None else min(outH, lim_h)
+    lb = batch * inC if lim_bc is None else min(batch * inC, lim_bc)
+    bc, oh, ow = np.meshgrid(np.arange(lb, dtype=np.int64), np.arange(lh, dtype=np.int64),
+                             np.arange(lw, dtype=np.int64), indexing="ij")
+    o = (bc * (outH * outW) + oh * outW + ow).ravel()
+    tgt = np.asarray(indices_bits, np.uint32)[o].astype(np.int64)
+    ok = (tgt != int(NO_INDEX)) & (tgt < dinput.size)
+    dinput[tgt[ok]] = np.asarray(dz, F32)[o[ok]]
+    return dinput
+
+
+def conv_reshape(mm, bias, batch, OC, OH, OW, act, lim_bp=None, lim_oc=None):
+    """nn_conv_reshape.hlsl:13-30: z = mm[oc, b*OH*OW + pixel] + bias[oc] (fp32),
+    act 1 -> max(0, z), act 2 -> tanh(z), else z; stored NCHW at
+    [b, oc, pixel].  Returns (dst, values)."""
+    P = OH * OW
+    BP = batch * P
+    lbp = BP if lim_bp is None else min(BP, lim_bp)
+    loc = OC if lim_oc is None else min(OC, lim_oc)
+    oc, bp = np.meshgrid(np.arange(loc, dtype=np.int64), np.arange(lbp, dtype=np.int64), indexing="ij")
+    z = (np.asarray(mm, F32)[oc * BP + bp] + np.asarray(bias, F32)[oc]).astype(F32)
+    if act == 1:
+        a = _relu(z)
+    elif act == 2:
+        a = np.tanh(z.astype(F64)).astype(F32)
+    else:
+        a = z
+    dst = (bp // P) * (OC * P) + oc * P + bp % P
+    return dst.ravel(), a.ravel()
+
+
+def conv_grad_reshape(dz, batch, outC, outH, outW, fwd=None, lim_bp=None, lim_oc=None):
+    """nn_conv_grad_reshape.hlsl:16-28 (and nn_conv_grad_reshape_relu.hlsl:21-39 when
+    `fwd` is given): out[oc, b*P + pixel] = dZ[b, oc, pixel], zeroed where the
+    forward output is <= 0 (NaN keeps the gradient).  Returns (dst, values)."""
+    P = outH * outW
+    BP = batch * P
+    lbp = BP if lim_bp is None else min(BP, lim_bp)
+    loc = outC if lim_oc is None else min(outC, lim_oc)
+    oc, bp = np.meshgrid(np.arange(loc, dtype=np.int64), np.arange(lbp, dtype=np.int64), indexing="ij")
+    src = (bp // P) * (outC * P) + oc * P + bp % P
+    g = np.asarray(dz, F32)[src]
+    if fwd is not None:
+        g = np.where(np.asarray(fwd, F32)[src] <= 0, F32(0.0), g).astype(F32)
+    return (oc * BP + bp).ravel(), g.ravel()
+
+
 def cb_words(cb: bytes, n: int = 16):
     """Decode up to `n` little-endian u32 cbuffer words (missing words read 0)."""
     cb = bytes(cb or b"")
@@ -503,6 +652,30 @@ def run_shader(name: str, srvs, uavs, groups, cb: bytes) -> None:
     elif name == "dice_loss_grad":
         n = _lim(u[0] * u[1], g)
         uavs[0][:n] = dice_loss_grad(srvs[0], srvs[1], srvs[2], u[0], u[1])[:n]
+    elif name == "upsample":
+        uavs[0][: _lim(u[0] * u[1] * u[4] * u[5], g)] = upsample(srvs[0], *u[:8], limit=g[0] * 256)
+    elif name == "upsample_backward":
+        r = upsample_backward(srvs[0], *u[:8], limit=g[0] * 256)
+        uavs[0][: r.size] = r
+    elif name == "concat_insert":
+        concat_insert(uavs[0], srvs[0], *u[:5], limit=g[0] * 256)
+    elif name == "slice":
+        r = slice_channels(srvs[0], *u[:5], limit=g[0] * 256)
+        uavs[0][: r.size] = r
+    elif name == "maxpool_forward":
+        o, v, i = maxpool_forward(srvs[0], *u[:8], lim_w=g[0] * 16, lim_h=g[1] * 16, lim_bc=g[2])
+        uavs[0][o] = v
+        uavs[1].view(np.uint32)[o] = i
+    elif name == "maxpool_backward":
+        maxpool_backward(uavs[0], srvs[0], srvs[1].view(np.uint32), *u[:4],
+                         lim_w=g[0] * 16, lim_h=g[1] * 16, lim_bc=g[2])
+    elif name == "conv_reshape":
+        dst, v = conv_reshape(srvs[0], srvs[1], *u[:5], lim_bp=g[0] * 16, lim_oc=g[1] * 16)
+        uavs[0][dst] = v
+    elif name in ("conv_grad_reshape", "conv_grad_reshape_relu"):
+        fwd = srvs[1] if name == "conv_grad_reshape_relu" else None
+        dst, v = conv_grad_reshape(srvs[0], u[0], u[4], u[7], u[8], fwd=fwd, lim_bp=g[0] * 16, lim_oc=g[1] * 16)
+        uavs[0][dst] = v
     # any other name: silently ignored, like engine.cpp:397-399
 
 
@@ -516,4 +689,6 @@ HOT_PATH_SHADERS = (
     "grad_norm_final", "sgd", "sgd_clipped", "adam", "batchnorm_mean_var",
     "batchnorm_forward", "batchnorm_backward_reduce", "batchnorm_backward_dx",
     "dice_loss", "dice_loss_sums", "dice_loss_grad",
+    "upsample", "upsample_backward", "concat_insert", "slice", "maxpool_forward",
+    "maxpool_backward", "conv_reshape", "conv_grad_reshape", "conv_grad_reshape_relu",
 )

@@ -165,6 +165,44 @@ def workloads(nn, rng):
     g.trace(lambda X: nn.bias_relu(X, w), nn.SGD([w], lr=0.1), xb, yb, [w], clip=1.0)
     g.replay(rng.standard_normal((B, K)).astype(f32), rng.integers(0, K, B).astype(f32))
 
+    # -- layout ops beside the path: upsample -> concat -> maxpool, forward and backward
+    xa = T((2 * rng.standard_normal((2, 3, 6, 8))).astype(f32), requires_grad=True)
+    xc = T(rng.standard_normal((2, 2, 12, 16)).astype(f32), requires_grad=True)
+    cat = nn.concat([nn.upsample2d(xa, 2, 2), xc])                  # [2, 5, 12, 16]
+    pooled = nn.maxpool2d(cat, 2, 2)                                 # [2, 5, 6, 8]
+    nn.softmax_ce(nn.global_avg_pool2d(pooled), T(rng.integers(0, 5, 2).astype(f32))).backward()
+    xs = T(rng.standard_normal((3, 2, 5, 7)).astype(f32), requires_grad=True)
+    up = nn.upsample2d(xs, 3, 2)                                     # uneven scales
+    nn.softmax_ce(nn.global_avg_pool2d(nn.maxpool2d(up, 3, 3)), T(rng.integers(0, 2, 3).astype(f32))).backward()
+    # forward-only pooling: overlapping windows, ragged edges, and values that never
+    # beat the -1e30 start (-inf, NaN, -2e30) -> the 0xFFFFFFFF index
+    xp = rng.standard_normal((2, 3, 9, 11)).astype(f32)
+    xp[0, 0, :3, :3] = -np.inf
+    xp[0, 1, 3:6, 3:6] = np.nan
+    xp[1, 2, :2, :] = f32(-2e30)
+    nn.maxpool2d(T(xp), 3, 2)
+    nn.maxpool2d(T(xp), 2, 3)
+
+    # -- conv output / gradient reshapes, packed as ConvForwardFused and
+    #    ConvBackwardFused pack them (engine.cpp:784-792, :816-835)
+    lib = nn.lib
+    Bc, OC, OH, OW = 2, 5, 3, 4
+    P = OH * OW
+    mm = T((2 * rng.standard_normal((OC, Bc * P))).astype(f32))
+    bias = T(rng.standard_normal(OC).astype(f32))
+    fwd = None
+    for act in (0, 1, 2):
+        out = lib.CreateBuffer(None, Bc * OC * P)
+        nn._dispatch(b"conv_reshape", (mm.gpu_buf, bias.gpu_buf), (out,), (Bc * P + 15) // 16, (OC + 15) // 16, 1,
+                     u1=Bc, u2=OC, u3=OH, u4=OW, u5=act, cbSize=20)
+        if act == 1:
+            fwd = out
+    dz = T(rng.standard_normal((Bc, OC, OH, OW)).astype(f32))
+    for name, srvs in ((b"conv_grad_reshape", (dz.gpu_buf,)), (b"conv_grad_reshape_relu", (dz.gpu_buf, fwd))):
+        out = lib.CreateBuffer(None, OC * Bc * P)
+        nn._dispatch(name, srvs, (out,), (Bc * P + 15) // 16, (OC + 15) // 16, 1,
+                     u1=Bc, u5=OC, u8=OH, u9=OW, cbSize=36)
+
 
 def main(ref_dir: str):
     rec = Recorder()

@@ -10,4 +10,6 @@ HOT_PATH_SHADERS = (
     "grad_norm_final", "sgd", "sgd_clipped", "adam", "batchnorm_mean_var",
     "batchnorm_forward", "batchnorm_backward_reduce", "batchnorm_backward_dx",
     "dice_loss", "dice_loss_sums", "dice_loss_grad",
+    "upsample", "upsample_backward", "concat_insert", "slice", "maxpool_forward",
+    "maxpool_backward", "conv_reshape", "conv_grad_reshape", "conv_grad_reshape_relu",
 )
