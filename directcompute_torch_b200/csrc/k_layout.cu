@@ -10,7 +10,10 @@
 // spaces past 2^32) with FastDiv for the runtime divisors.  Every op has a
 // 128-bit path for the shapes the reference produces (rows that are multiples
 // of 4 floats, full coverage) and a scalar path for ragged shapes and partial
-// group counts; both compute identical values.
+// group counts; both compute identical values.  The 128-bit paths use the
+// chunked schedule of the elementwise kernels: block b owns units
+// [b*256*U, (b+1)*256*U), each thread loads its U units (strided by the block
+// size, so every instruction is coalesced) before it stores any.
 #include "dct_common.cuh"
 #include "kernels.h"
 
@@ -42,45 +45,48 @@ __global__ void __launch_bounds__(kT) k_upsample(const float* __restrict__ x, fl
   }
 }
 
-// Four outputs of one row per step (outW % 4 == 0, every output written).  The
-// input row is read through the read-only cache: each element serves sH*sW outputs.
-__global__ void __launch_bounds__(kT) k_upsample4(const float* __restrict__ x, float* __restrict__ y, uint32_t nq,
-                                                  FastDiv outWq, UpGeom g) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+// Output-major, four outputs of one row per unit (outW % 4 == 0, every output
+// written), chunked.  SW = 1, 2, 4: the unit's inputs are one float4, one
+// float2 or one float of the input row; SW = 0: any scale, four loads.  Input
+// lines are re-read from L2 by the sH output rows they feed.
+template <int SW>
+__global__ void __launch_bounds__(kT) k_upsample_chunk(const float* __restrict__ x, float* __restrict__ y,
+                                                       uint32_t nq, FastDiv outWq, UpGeom g) {
+  constexpr int U = 4;
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  float4 v[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     const uint32_t row = outWq.div(q);
     const uint32_t w0 = (q - row * outWq.d) * 4;
     const uint32_t bc = g.outH.div(row), h = row - bc * g.outH.d;
     const float* src = x + (bc * g.inH + g.sH.div(h)) * g.inW;
-    uint32_t wi = g.sW.div(w0), r = w0 - wi * g.sW.d;
-    float v[4];
+    if constexpr (SW == 1) {
+      v[k] = __ldg(reinterpret_cast<const float4*>(src + w0));
+    } else if constexpr (SW == 2) {
+      const float2 a = __ldg(reinterpret_cast<const float2*>(src + w0 / 2));
+      v[k] = make_float4(a.x, a.x, a.y, a.y);
+    } else if constexpr (SW == 4) {
+      const float a = __ldg(src + w0 / 4);
+      v[k] = make_float4(a, a, a, a);
+    } else {
+      uint32_t wi = g.sW.div(w0), r = w0 - wi * g.sW.d;
+      float t[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      v[k] = __ldg(src + wi);
-      if (++r == g.sW.d) { r = 0; ++wi; }
+      for (int c = 0; c < 4; ++c) {
+        t[c] = __ldg(src + wi);
+        if (++r == g.sW.d) { r = 0; ++wi; }
+      }
+      v[k] = make_float4(t[0], t[1], t[2], t[3]);
     }
-    st_stream4(y + 4 * (size_t)q, make_float4(v[0], v[1], v[2], v[3]));
   }
-}
-
-// Exact scales (outH == inH*sH, outW == inW*SW), inW % 4 == 0, every output:
-// one float4 of an input row becomes SW float4s on each of the sH output rows
-// it feeds, so every load serves sH*SW stores and all accesses are 128-bit.
-template <int SW>
-__global__ void __launch_bounds__(kT) k_upsample_in4(const float* __restrict__ x, float* __restrict__ y, uint32_t nq,
-                                                     FastDiv inWq, uint32_t inW, uint32_t sH) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
-    const uint32_t row = inWq.div(q);                // bc*inH + h: input row
-    const uint32_t j = q - row * inWq.d;
-    const float4 a = ld_stream4(x + 4 * (size_t)q);
-    const float v[4] = {a.x, a.y, a.z, a.w};
-    const size_t outW = (size_t)inW * SW;
-    float* o = y + (size_t)row * sH * outW + (size_t)j * 4 * SW;
-    for (uint32_t r = 0; r < sH; ++r, o += outW) {
 #pragma unroll
-      for (int c = 0; c < SW; ++c)
-        st_stream4(o + 4 * c, make_float4(v[(4 * c) / SW], v[(4 * c + 1) / SW], v[(4 * c + 2) / SW],
-                                          v[(4 * c + 3) / SW]));
-    }
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
+    st_stream4(y + 4 * (size_t)q, v[k]);
   }
 }
 
@@ -114,20 +120,32 @@ __global__ void __launch_bounds__(kT) k_upsample_bwd(const float* __restrict__ d
 }
 
 // The 2x2 case with outH == 2*inH, outW == 2*inW, inW % 4 == 0: four inputs of
-// one row per step from two float4 pairs of DY, summed in the shader's order.
+// one row per unit from two float4 pairs of DY, summed in the shader's order;
+// chunked, two units per thread.
 __global__ void __launch_bounds__(kT) k_upsample_bwd_2x2(const float* __restrict__ dy, float* __restrict__ dx,
                                                          uint32_t nq, FastDiv inWq, uint32_t inW) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+  constexpr int U = 2;
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  float4 a0[U], a1[U], b0[U], b1[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     const uint32_t row = inWq.div(q);                // bc*inH + h
     const uint32_t w0 = (q - row * inWq.d) * 4;
     const float* r0 = dy + (size_t)(2 * row) * (2 * inW) + 2 * w0;
     const float* r1 = r0 + 2 * inW;
-    const float4 a0 = ld_stream4(r0), a1 = ld_stream4(r0 + 4), b0 = ld_stream4(r1), b1 = ld_stream4(r1 + 4);
+    a0[k] = ld_stream4(r0); a1[k] = ld_stream4(r0 + 4); b0[k] = ld_stream4(r1); b1[k] = ld_stream4(r1 + 4);
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     float4 o;
-    o.x = 0.0f; o.x += a0.x; o.x += a0.y; o.x += b0.x; o.x += b0.y;
-    o.y = 0.0f; o.y += a0.z; o.y += a0.w; o.y += b0.z; o.y += b0.w;
-    o.z = 0.0f; o.z += a1.x; o.z += a1.y; o.z += b1.x; o.z += b1.y;
-    o.w = 0.0f; o.w += a1.z; o.w += a1.w; o.w += b1.z; o.w += b1.w;
+    o.x = 0.0f; o.x += a0[k].x; o.x += a0[k].y; o.x += b0[k].x; o.x += b0[k].y;
+    o.y = 0.0f; o.y += a0[k].z; o.y += a0[k].w; o.y += b0[k].z; o.y += b0[k].w;
+    o.z = 0.0f; o.z += a1[k].x; o.z += a1[k].y; o.z += b1[k].x; o.z += b1[k].y;
+    o.w = 0.0f; o.w += a1[k].z; o.w += a1[k].w; o.w += b1[k].z; o.w += b1[k].w;
     st_stream4(dx + 4 * (size_t)q, o);
   }
 }
@@ -147,15 +165,27 @@ __global__ void __launch_bounds__(kT) k_channel_copy(const float* __restrict__ s
     else st_stream(dst + j, ld_stream(src + i));
   }
 }
-// the same with L, pitch, off and n multiples of 4
+// the same with L, pitch, off and n multiples of 4: float4 units, chunked
 template <bool SLICE>
 __global__ void __launch_bounds__(kT) k_channel_copy4(const float* __restrict__ src, float* __restrict__ dst,
                                                       uint32_t nq, FastDiv Lq, uint32_t pitch, uint32_t off) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+  constexpr int U = 4;
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  float4 v[U];
+  size_t at[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     const uint32_t b = Lq.div(q), r = (q - b * Lq.d) * 4;
     const size_t j = (size_t)b * pitch + off + r, i = 4 * (size_t)q;
-    if (SLICE) st_stream4(dst + i, ld_stream4(src + j));
-    else st_stream4(dst + j, ld_stream4(src + i));
+    v[k] = ld_stream4(src + (SLICE ? j : i));
+    at[k] = SLICE ? i : j;
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    if (q0 + k * kT >= nq) break;
+    st_stream4(dst + at[k], v[k]);
   }
 }
 
@@ -193,23 +223,37 @@ __global__ void __launch_bounds__(kT) k_maxpool_fwd(const float* __restrict__ x,
   }
 }
 
-// 2x2 windows, stride 2, every output, inW % 4 == 0: two outputs of one row per
-// step from one float4 of each of the window's two input rows.
+// 2x2 windows, stride 2, every output, inW % 4 == 0: two outputs of one row
+// per unit from one float4 of each of the window's two input rows; chunked.
 __global__ void __launch_bounds__(kT) k_maxpool2x2(const float* __restrict__ x, float* __restrict__ out,
                                                    uint32_t* __restrict__ idx, uint32_t nq, FastDiv outWh,
                                                    FastDiv outH, uint32_t inH, uint32_t inW) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+  constexpr int U = 4;
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  float4 a[U], b[U];
+  uint32_t k0[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     const uint32_t row = outWh.div(q);               // bc*outH + oh
     const uint32_t c2 = q - row * outWh.d;
     const uint32_t bc = outH.div(row), oh = row - bc * outH.d;
-    const uint32_t k0 = (bc * inH + 2 * oh) * inW + 4 * c2, k1 = k0 + inW;
-    const float4 a = ld_stream4(x + k0), b = ld_stream4(x + k1);
+    k0[k] = (bc * inH + 2 * oh) * inW + 4 * c2;
+    a[k] = ld_stream4(x + k0[k]);
+    b[k] = ld_stream4(x + k0[k] + inW);
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
+    const uint32_t e = k0[k], f = e + inW;
     float m0 = kPoolStart, m1 = kPoolStart;
     uint32_t i0 = kNoIndex, i1 = kNoIndex;
-    pool_take(a.x, k0, m0, i0); pool_take(a.y, k0 + 1, m0, i0);
-    pool_take(b.x, k1, m0, i0); pool_take(b.y, k1 + 1, m0, i0);
-    pool_take(a.z, k0 + 2, m1, i1); pool_take(a.w, k0 + 3, m1, i1);
-    pool_take(b.z, k1 + 2, m1, i1); pool_take(b.w, k1 + 3, m1, i1);
+    pool_take(a[k].x, e, m0, i0); pool_take(a[k].y, e + 1, m0, i0);
+    pool_take(b[k].x, f, m0, i0); pool_take(b[k].y, f + 1, m0, i0);
+    pool_take(a[k].z, e + 2, m1, i1); pool_take(a[k].w, e + 3, m1, i1);
+    pool_take(b[k].z, f + 2, m1, i1); pool_take(b[k].w, f + 3, m1, i1);
     const size_t o = 2 * (size_t)q;                  // = row*outW + 2*c2
     *reinterpret_cast<float2*>(out + o) = make_float2(m0, m1);
     *reinterpret_cast<uint2*>(idx + o) = make_uint2(i0, i1);
@@ -270,32 +314,52 @@ __global__ void __launch_bounds__(kT) k_maxpool_gather(const float* __restrict__
 }
 
 // The same for 2x2 windows at stride 2 with inW % 4 == 0: four inputs of one
-// row per step from the (index, dZ) pairs of the two windows above them.
+// row per unit from the (index, dZ) pairs of the two windows above them; chunked.
 __global__ void __launch_bounds__(kT) k_maxpool_gather2x2(const float* __restrict__ dz,
                                                           const uint32_t* __restrict__ idx, float* __restrict__ d,
                                                           uint32_t nq, FastDiv inWq, FastDiv inH, FastDiv inW,
                                                           PoolShape g, uint32_t* flag) {
+  constexpr int U = 4;
   const uint32_t n = g.bc * g.inH * g.inW;
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  uint2 kk[U];
+  float2 zz[U];
+  bool top[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    kk[k] = make_uint2(kNoIndex, kNoIndex);
+    zz[k] = make_float2(0.0f, 0.0f);
+    top[k] = false;
+    if (q >= nq) break;
     const uint32_t row = inWq.div(q), j = q - row * inWq.d;  // input row, float4 column
     const uint32_t bc = inH.div(row), ih = row - bc * inH.d;
-    const uint32_t oh = ih >> 1, e0 = 4 * q;
-    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const uint32_t oh = ih >> 1;
     if (oh < g.outH) {
       const uint32_t o = bc * (g.outH * g.outW) + oh * g.outW + 2 * j;
-      const uint2 k = __ldg(reinterpret_cast<const uint2*>(idx + o));
-      const float2 z = __ldg(reinterpret_cast<const float2*>(dz + o));
-      v.x = k.x == e0 ? z.x : 0.0f;
-      v.y = k.x == e0 + 1 ? z.x : 0.0f;
-      v.z = k.y == e0 + 2 ? z.y : 0.0f;
-      v.w = k.y == e0 + 3 ? z.y : 0.0f;
-      if ((ih & 1) == 0) {                           // the windows' top rows check their indices
-        const uint32_t k1 = e0 + inW.d;              // first element of the second window row
-        const bool ok0 = k.x == kNoIndex || k.x >= n || k.x == e0 || k.x == e0 + 1 || k.x == k1 || k.x == k1 + 1;
-        const bool ok1 = k.y == kNoIndex || k.y >= n || k.y == e0 + 2 || k.y == e0 + 3 || k.y == k1 + 2 ||
-                         k.y == k1 + 3;
-        if (!(ok0 && ok1)) atomicOr(flag, 1u);
-      }
+      kk[k] = __ldg(reinterpret_cast<const uint2*>(idx + o));
+      zz[k] = __ldg(reinterpret_cast<const float2*>(dz + o));
+      top[k] = (ih & 1) == 0;                        // the windows' top rows check their indices
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
+    const uint32_t e0 = 4 * q;
+    const uint2 kx = kk[k];
+    const float2 z = zz[k];
+    float4 v;
+    v.x = kx.x == e0 ? z.x : 0.0f;
+    v.y = kx.x == e0 + 1 ? z.x : 0.0f;
+    v.z = kx.y == e0 + 2 ? z.y : 0.0f;
+    v.w = kx.y == e0 + 3 ? z.y : 0.0f;
+    if (top[k]) {
+      const uint32_t k1 = e0 + inW.d;                // first element of the second window row
+      const bool ok0 = kx.x == kNoIndex || kx.x >= n || kx.x == e0 || kx.x == e0 + 1 || kx.x == k1 || kx.x == k1 + 1;
+      const bool ok1 = kx.y == kNoIndex || kx.y >= n || kx.y == e0 + 2 || kx.y == e0 + 3 || kx.y == k1 + 2 ||
+                       kx.y == k1 + 3;
+      if (!(ok0 && ok1)) atomicOr(flag, 1u);
     }
     st_stream4(d + (size_t)e0, v);
   }
@@ -341,21 +405,34 @@ __global__ void __launch_bounds__(kT) k_conv_reshape(const float* __restrict__ m
     st_stream(out + (b * OC + oc) * P.d + px, conv_act<ACT>(ld_stream(mm + oc * BP + bp) + __ldg(bias + oc)));
   }
 }
-// every output, P % 4 == 0: NCHW float4 per step
+// every output, P % 4 == 0: NCHW float4 units, chunked
 template <int ACT>
 __global__ void __launch_bounds__(kT) k_conv_reshape4(const float* __restrict__ mm, const float* __restrict__ bias,
                                                       float* __restrict__ out, uint32_t nq, FastDiv Pq, FastDiv OC,
                                                       uint32_t P, uint32_t BP) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+  constexpr int U = 4;
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  float4 v[U];
+  float bv[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     const uint32_t row = Pq.div(q), px = (q - row * Pq.d) * 4;
     const uint32_t b = OC.div(row), oc = row - b * OC.d;
-    const float bv = __ldg(bias + oc);
-    float4 v = ld_stream4(mm + (size_t)oc * BP + (size_t)b * P + px);
-    v.x = conv_act<ACT>(v.x + bv);
-    v.y = conv_act<ACT>(v.y + bv);
-    v.z = conv_act<ACT>(v.z + bv);
-    v.w = conv_act<ACT>(v.w + bv);
-    st_stream4(out + 4 * (size_t)q, v);
+    bv[k] = __ldg(bias + oc);
+    v[k] = ld_stream4(mm + (size_t)oc * BP + (size_t)b * P + px);
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
+    float4 w = v[k];
+    w.x = conv_act<ACT>(w.x + bv[k]);
+    w.y = conv_act<ACT>(w.y + bv[k]);
+    w.z = conv_act<ACT>(w.z + bv[k]);
+    w.w = conv_act<ACT>(w.w + bv[k]);
+    st_stream4(out + 4 * (size_t)q, w);
   }
 }
 
@@ -378,19 +455,31 @@ template <bool RELU>
 __global__ void __launch_bounds__(kT) k_conv_grad_reshape4(const float* __restrict__ dz, const float* __restrict__ fwd,
                                                            float* __restrict__ out, uint32_t nq, FastDiv BPq,
                                                            FastDiv Pq, uint32_t OC, uint32_t P) {
-  for (uint32_t q = gtid(); q < nq; q += gstride()) {
+  constexpr int U = 4;
+  const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
+  float4 gv[U], f[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
     const uint32_t oc = BPq.div(q), bq = q - oc * BPq.d;
     const uint32_t b = Pq.div(bq), pq = bq - b * Pq.d;
     const size_t src = ((size_t)b * OC + oc) * P + 4 * (size_t)pq;
-    float4 gv = ld_stream4(dz + src);
+    gv[k] = ld_stream4(dz + src);
+    if (RELU) f[k] = ld_stream4(fwd + src);
+  }
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const uint32_t q = q0 + k * kT;
+    if (q >= nq) break;
+    float4 g = gv[k];
     if (RELU) {
-      const float4 f = ld_stream4(fwd + src);
-      if (f.x <= 0.0f) gv.x = 0.0f;
-      if (f.y <= 0.0f) gv.y = 0.0f;
-      if (f.z <= 0.0f) gv.z = 0.0f;
-      if (f.w <= 0.0f) gv.w = 0.0f;
+      if (f[k].x <= 0.0f) g.x = 0.0f;
+      if (f[k].y <= 0.0f) g.y = 0.0f;
+      if (f[k].z <= 0.0f) g.z = 0.0f;
+      if (f[k].w <= 0.0f) g.w = 0.0f;
     }
-    st_stream4(out + 4 * (size_t)q, gv);
+    st_stream4(out + 4 * (size_t)q, g);
   }
 }
 
@@ -399,23 +488,29 @@ cudaError_t go(K kernel, uint64_t work, cudaStream_t st, A... a) {
   kernel<<<grid_for(work, kT, 2), kT, 0, st>>>(a...);
   return cudaGetLastError();
 }
+// chunked kernels: one block per kT*U units
+template <int U, typename K, typename... A>
+cudaError_t chunked(K kernel, uint32_t units, cudaStream_t st, A... a) {
+  kernel<<<(units + kT * U - 1) / (kT * U), kT, 0, st>>>(a...);
+  return cudaGetLastError();
+}
 
 }  // namespace
 
 cudaError_t launch_upsample(const float* x, float* y, uint32_t n, uint32_t total, uint32_t inH, uint32_t inW,
                             uint32_t outH, uint32_t outW, uint32_t sH, uint32_t sW, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  if (n == total && outH == inH * sH && outW == inW * sW && inW % 4 == 0 && aligned16_h(x) && aligned16_h(y) &&
-      (sW == 1 || sW == 2 || sW == 4)) {
-    const uint32_t nq = total / (sH * sW) / 4;       // input float4s
-    const FastDiv q(inW / 4);
-    if (sW == 1) return go(k_upsample_in4<1>, nq, st, x, y, nq, q, inW, sH);
-    if (sW == 2) return go(k_upsample_in4<2>, nq, st, x, y, nq, q, inW, sH);
-    return go(k_upsample_in4<4>, nq, st, x, y, nq, q, inW, sH);
-  }
   UpGeom g{FastDiv(outW), FastDiv(outH), FastDiv(sH), FastDiv(sW), inH, inW};
-  if (n == total && outW % 4 == 0 && aligned16_h(y))
-    return go(k_upsample4, n / 4, st, x, y, n / 4, FastDiv(outW / 4), g);
+  if (n == total && outW % 4 == 0 && aligned16_h(x) && aligned16_h(y)) {
+    const uint32_t nq = n / 4;
+    const FastDiv q(outW / 4);
+    const unsigned grid = (nq + kT * 4 - 1) / (kT * 4);
+    if (sW == 1 && inW % 4 == 0) k_upsample_chunk<1><<<grid, kT, 0, st>>>(x, y, nq, q, g);
+    else if (sW == 2 && inW % 2 == 0) k_upsample_chunk<2><<<grid, kT, 0, st>>>(x, y, nq, q, g);
+    else if (sW == 4) k_upsample_chunk<4><<<grid, kT, 0, st>>>(x, y, nq, q, g);
+    else k_upsample_chunk<0><<<grid, kT, 0, st>>>(x, y, nq, q, g);
+    return cudaGetLastError();
+  }
   return go(k_upsample, n, st, x, y, n, g);
 }
 
@@ -425,7 +520,7 @@ cudaError_t launch_upsample_backward(const float* dy, float* dx, uint32_t n, uin
   if (n == 0) return cudaSuccess;
   if (n == total && sH == 2 && sW == 2 && outH == 2 * inH && outW == 2 * inW && inW % 4 == 0 && aligned16_h(dy) &&
       aligned16_h(dx))
-    return go(k_upsample_bwd_2x2, n / 4, st, dy, dx, n / 4, FastDiv(inW / 4), inW);
+    return chunked<2>(k_upsample_bwd_2x2, n / 4, st, dy, dx, n / 4, FastDiv(inW / 4), inW);
   UpBackGeom g{FastDiv(inW), FastDiv(inH), outH, outW, sH, sW};
   return go(k_upsample_bwd, n, st, dy, dx, n, g);
 }
@@ -435,8 +530,8 @@ cudaError_t launch_channel_copy(bool slice, const float* src, float* dst, uint32
   if (n == 0) return cudaSuccess;
   const bool v4 = L % 4 == 0 && pitch % 4 == 0 && off % 4 == 0 && n % 4 == 0 && aligned16_h(src) && aligned16_h(dst);
   if (v4)
-    return slice ? go(k_channel_copy4<true>, n / 4, st, src, dst, n / 4, FastDiv(L / 4), pitch, off)
-                 : go(k_channel_copy4<false>, n / 4, st, src, dst, n / 4, FastDiv(L / 4), pitch, off);
+    return slice ? chunked<4>(k_channel_copy4<true>, n / 4, st, src, dst, n / 4, FastDiv(L / 4), pitch, off)
+                 : chunked<4>(k_channel_copy4<false>, n / 4, st, src, dst, n / 4, FastDiv(L / 4), pitch, off);
   return slice ? go(k_channel_copy<true>, n, st, src, dst, n, FastDiv(L), pitch, off)
                : go(k_channel_copy<false>, n, st, src, dst, n, FastDiv(L), pitch, off);
 }
@@ -447,7 +542,8 @@ cudaError_t launch_maxpool_forward(const float* x, float* out, uint32_t* idx, ui
   if (n == 0) return cudaSuccess;
   const bool full = lw == g.outW && lh == g.outH && lb == g.bc;
   if (full && g.p == 2 && g.s == 2 && g.inW % 4 == 0 && 2 * g.outW == g.inW && 2 * g.outH <= g.inH && aligned16_h(x))
-    return go(k_maxpool2x2, n / 2, st, x, out, idx, n / 2, FastDiv(g.outW / 2), FastDiv(g.outH), g.inH, g.inW);
+    return chunked<4>(k_maxpool2x2, n / 2, st, x, out, idx, n / 2, FastDiv(g.outW / 2), FastDiv(g.outH), g.inH,
+                      g.inW);
   return go(k_maxpool_fwd, n, st, x, out, idx, n, FastDiv(lw), FastDiv(lh), g);
 }
 
@@ -466,7 +562,8 @@ cudaError_t launch_maxpool_backward_gather(const float* dz, const uint32_t* idx,
   const FastDiv inW(g.inW);
   cudaError_t e;
   if (g.p == 2 && g.s == 2 && g.inW % 4 == 0 && 2 * g.outW == g.inW && aligned16_h(d))
-    e = go(k_maxpool_gather2x2, n / 4, st, dz, idx, d, n / 4, FastDiv(g.inW / 4), FastDiv(g.inH), inW, g, flag);
+    e = chunked<4>(k_maxpool_gather2x2, n / 4, st, dz, idx, d, n / 4, FastDiv(g.inW / 4), FastDiv(g.inH), inW, g,
+                   flag);
   else
     e = go(k_maxpool_gather, n, st, dz, idx, d, n, inW, FastDiv(g.inH), FastDiv(g.s), g, flag);
   if (e != cudaSuccess || nout == 0) return e;
@@ -482,9 +579,9 @@ cudaError_t launch_conv_reshape(const float* mm, const float* bias, float* out, 
   if (lbp == BP && loc == OC && P % 4 == 0 && aligned16_h(mm) && aligned16_h(out)) {
     const FastDiv Pq(P / 4), fOC(OC);
     const uint32_t nq = n / 4;
-    if (a == 1) return go(k_conv_reshape4<1>, nq, st, mm, bias, out, nq, Pq, fOC, P, BP);
-    if (a == 2) return go(k_conv_reshape4<2>, nq, st, mm, bias, out, nq, Pq, fOC, P, BP);
-    return go(k_conv_reshape4<0>, nq, st, mm, bias, out, nq, Pq, fOC, P, BP);
+    if (a == 1) return chunked<4>(k_conv_reshape4<1>, nq, st, mm, bias, out, nq, Pq, fOC, P, BP);
+    if (a == 2) return chunked<4>(k_conv_reshape4<2>, nq, st, mm, bias, out, nq, Pq, fOC, P, BP);
+    return chunked<4>(k_conv_reshape4<0>, nq, st, mm, bias, out, nq, Pq, fOC, P, BP);
   }
   const FastDiv fl(lbp), fP(P);
   if (a == 1) return go(k_conv_reshape<1>, n, st, mm, bias, out, n, fl, fP, OC, BP);
@@ -498,8 +595,10 @@ cudaError_t launch_conv_grad_reshape(const float* dz, const float* fwd, float* o
   if (n == 0) return cudaSuccess;
   if (lbp == BP && loc == OC && P % 4 == 0 && aligned16_h(dz) && aligned16_h(out) && (!fwd || aligned16_h(fwd))) {
     const uint32_t nq = n / 4;
-    if (fwd) return go(k_conv_grad_reshape4<true>, nq, st, dz, fwd, out, nq, FastDiv(BP / 4), FastDiv(P / 4), OC, P);
-    return go(k_conv_grad_reshape4<false>, nq, st, dz, fwd, out, nq, FastDiv(BP / 4), FastDiv(P / 4), OC, P);
+    if (fwd)
+      return chunked<4>(k_conv_grad_reshape4<true>, nq, st, dz, fwd, out, nq, FastDiv(BP / 4), FastDiv(P / 4), OC, P);
+    return chunked<4>(k_conv_grad_reshape4<false>, nq, st, dz, fwd, out, nq, FastDiv(BP / 4), FastDiv(P / 4), OC,
+                               P);
   }
   if (fwd) return go(k_conv_grad_reshape<true>, n, st, dz, fwd, out, n, FastDiv(lbp), FastDiv(P), OC, BP);
   return go(k_conv_grad_reshape<false>, n, st, dz, fwd, out, n, FastDiv(lbp), FastDiv(P), OC, BP);
