@@ -33,9 +33,9 @@ enum : uint32_t {
   DCT_DEVERR_PEER_WAIT = 4u,       // a peer's record did not arrive before the deadline
 };
 uint32_t* device_error_word();   // defined in runtime.cu
-// Zeroed device counters for "last block folds" reductions (null before
-// InitEngine: callers then use a separate fold launch).  Every kernel that
-// increments one resets it to zero before it exits.
+// Zeroed device words for kernels that raise a flag another kernel of the same
+// stream consumes and clears (null before InitEngine).  Every kernel that
+// sets one leaves it zero when the pair is done.
 constexpr uint32_t kReduceCounters = 65536;
 uint32_t* reduce_counters();     // defined in runtime.cu
 

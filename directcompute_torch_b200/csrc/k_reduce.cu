@@ -179,20 +179,21 @@ struct ColLane {
   static constexpr bool kExt = Acc<OP>::kExt;
   static constexpr bool kMax = Acc<OP>::kMax;
   double s;
-  float v, nanf;
+  float v;
   int32_t i;
   DCT_DEV void reset(int32_t first_row) {
     s = 0.0;
     v = kMax ? -INFINITY : INFINITY;
-    nanf = -INFINITY;
     i = first_row;
   }
   DCT_DEV void add(float x, int32_t row) {
     if constexpr (kArg) {
+      // three instructions: the NaN-propagating extreme is both the running
+      // value (equal to the strict-better one while no NaN was seen) and the
+      // NaN flag (once NaN, no later element is better and finish() rescans)
       const bool u = kMax ? (x > v) : (x < v);
-      v = u ? x : v;
       i = u ? row : i;
-      nanf = fmax_nan(nanf, x);
+      v = kMax ? fmax_nan(v, x) : fmin_nan(v, x);
     } else if constexpr (kExt) {
       v = kMax ? fmax_nan(v, x) : fmin_nan(v, x);
     } else if constexpr (OP == RED_SUMSQ) {
@@ -212,7 +213,7 @@ struct ColLane {
     if constexpr (kArg) {
       a.v = v;
       a.i = i;
-      if (nanf != nanf) {                                 // rare: find this lane's first NaN
+      if (v != v) {                                       // rare: find this lane's first NaN
         for (uint64_t r = first_row; r < end; r += step) {
           const float x = col[r * sl];
           if (x != x) { a.v = x; a.i = (int32_t)r; break; }
@@ -233,7 +234,7 @@ struct ColLane {
     if constexpr (kArg) {
       a.v = v;
       a.i = i;
-      if (nanf != nanf) {                                 // rare: this lane's first NaN
+      if (v != v) {                                       // rare: this lane's first NaN
         for (uint64_t l = first; l < end; l += 128) {
           bool found = false;
           for (int q = 0; q < 4 && l + q < end; ++q) {
@@ -309,19 +310,18 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
 // COLUMN kernel: block = 32*VEC adjacent outputs x 8 interleaved row lanes.
 // grid = (column tiles, outer (strided), len chunks)
 // ---------------------------------------------------------------------------
-// With `counters` (one zeroed word per (outer, tile)) and chunks > 1, the block
-// that finishes a tile's last chunk folds that tile's chunk partials in chunk
-// order and emits the result (the order, not the finishing block, fixes the
-// rounding), then re-zeroes the counter: no second launch.  No block waits
-// for another.
+// With chunks > 1 each block leaves its tile's partial for its chunk; a fold
+// kernel launched with programmatic dependent launch combines them in chunk
+// order.  (A fold by the last block of each tile, found with an atomic counter,
+// was measured slower: its fence and serial fold sit on the kernel's tail.)
 template <int OP, int VEC>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                              uint64_t inner, uint64_t so, uint64_t sl,
                                                              uint32_t chunks, uint64_t chunk_len, RedOut ro,
-                                                             unsigned long long* part, uint32_t* counters) {
+                                                             unsigned long long* part) {
   constexpr int W = 32 * VEC;
   __shared__ unsigned long long sh[kRedWarps][W];
-  __shared__ bool last;
+  grid_dep_launch();                                    // the fold kernel may be scheduled now
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t c0 = (uint64_t)blockIdx.x * W + (uint64_t)lane * VEC;
   const uint32_t ch = blockIdx.z;
@@ -380,49 +380,35 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
         else part[(o * chunks + ch) * inner + c] = tot.pack();
       }
     }
-    if (chunks > 1 && counters) {
-      uint32_t* cnt = counters + (uint64_t)blockIdx.y * gridDim.x + blockIdx.x;   // o == blockIdx.y here
-      __threadfence();                                  // this block's partials before its count
-      __syncthreads();
-      if (threadIdx.x == 0) last = atomicAdd(cnt, 1u) == chunks - 1;
-      __syncthreads();
-      if (last) {
-        __threadfence();                                // every block's partials are visible
-        if (threadIdx.x < W) {
-          const uint64_t c = (uint64_t)blockIdx.x * W + threadIdx.x;
-          if (c < inner) {
-            Acc<OP> tot;
-            for (uint32_t k = 0; k < chunks; ++k) {
-              Acc<OP> t;
-              t.unpack(__ldcg(&part[(o * chunks + k) * inner + c]));
-              if (k == 0) tot = t; else tot.merge(t);
-            }
-            tot.emit(ro, o * inner + c, len);
-          }
-        }
-        if (threadIdx.x == 0) *cnt = 0u;
-      }
-    }
     __syncthreads();
   }
 }
 
-// fold chunk partials: out[k] = combine(part[k*stride_k ... with chunk stride])
+// Fold chunk partials: out[k] = combine over ch of part[(o*chunks + ch)*inner + c]
+// (k = o*inner + c).  One warp per output: lane l folds chunks l, l+32, ... in
+// order, then a fixed shuffle tree merges the lanes, so the result is the same
+// on every run (sums in float64; arg and extreme merges are exact).  A thread
+// per output walking the chunks serially took 3-8 us for 4096 outputs of 27
+// chunks; the warp form keeps every chunk's load in flight at once.
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
                                                      uint32_t chunks, uint64_t inner, uint64_t len, RedOut ro) {
   grid_dep_wait();
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += stride) {
-    // k = o*inner + c ; partial index = (o*chunks + ch)*inner + c
+  const int lane = threadIdx.x & 31;
+  const uint64_t wpb = blockDim.x >> 5;
+  const uint64_t stride = (uint64_t)gridDim.x * wpb;
+  for (uint64_t k = (uint64_t)blockIdx.x * wpb + (threadIdx.x >> 5); k < nout; k += stride) {
     const uint64_t o = k / inner, c = k - o * inner;
-    Acc<OP> tot;
-    for (uint32_t ch = 0; ch < chunks; ++ch) {
+    const unsigned long long* p = part + o * chunks * inner + c;
+    Acc<OP> a;
+    a.reset();
+    for (uint32_t ch = lane; ch < chunks; ch += 32) {
       Acc<OP> t;
-      t.unpack(part[(o * chunks + ch) * inner + c]);
-      if (ch == 0) tot = t; else tot.merge(t);
+      t.unpack(__ldcg(p + (uint64_t)ch * inner));
+      a.merge(t);
     }
-    tot.emit(ro, k, len);
+    a.warp_reduce();
+    if (lane == 0) a.emit(ro, k, len);
   }
 }
 
@@ -539,21 +525,16 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
     if (p.vec) k_reduce_rows<OP, true><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
     else k_reduce_rows<OP, false><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
   } else if (p.kind == 1) {
-    // in-kernel fold when a counter per (outer row, tile) is available
-    uint32_t* cnt = reduce_counters();
-    // one counter per (outer row, tile), each outer row visited once per block
-    if ((uint64_t)p.grid.x * p.grid.y > kReduceCounters || outer > p.grid.y) cnt = nullptr;
-    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, cnt);
-    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, cnt);
-    if (cnt || nparts == 1) return cudaGetLastError();
+    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
+    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
   } else {
     k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, ro);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nparts == 1) return e;
   const uint64_t nout = outer * inner;
-  k_fold_chunks<OP><<<grid_for(nout, 256), 256, 0, st>>>(part, nout, nparts, inner, len, ro);
-  return cudaGetLastError();
+  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout * 32, 256)), dim3(256), 0, st, (const unsigned long long*)part,
+                    nout, nparts, inner, len, ro);
 }
 
 cudaError_t dispatch_reduce(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t so,
@@ -584,7 +565,7 @@ cudaError_t run_fold_packed(const unsigned long long* parts, uint32_t nparts, ui
   // parts[p * stride + k]: the chunk-fold layout with outer = 1, inner = stride
   // (k < nout <= stride, so the fold's outer index is always 0); launched as a
   // programmatic dependent of the kernel that produced the parts
-  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout, 256)), dim3(256), 0, st, parts, nout, nparts, stride,
+  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout * 32, 256)), dim3(256), 0, st, parts, nout, nparts, stride,
                     len_total, ro);
 }
 
@@ -705,7 +686,7 @@ SumPlan plan_sum(int ndim, const int64_t* gshape, const int64_t* tshape) {
 
 // Generic form (two or more reduced groups): one thread per output element and
 // chunk of the reduced index space, walked with an odometer; fp64 sums, folded
-// over chunks in order by k_fold_chunks.
+// over chunks in a fixed order by k_fold_chunks.
 struct SumMap {
   int nk, nr;
   uint64_t kext[kSumMaxDims];

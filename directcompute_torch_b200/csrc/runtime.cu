@@ -72,7 +72,7 @@ struct Engine {
   float* host_small = nullptr;    // pinned 64-byte staging for scalar readbacks
   uint32_t* dev_err_host = nullptr;   // mapped error word written by device code
   uint32_t* dev_err_dev = nullptr;
-  uint32_t* counters = nullptr;       // kReduceCounters zeroed words (reduction tile counters)
+  uint32_t* counters = nullptr;       // kReduceCounters zeroed flag words (maxpool fix-up)
   char name[128] = {0};
   // error state
   int err_code = 0;
