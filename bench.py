@@ -713,11 +713,13 @@ def main():
         e2e_val = ranks.sum(c2.step_bytes * nst) / ranks.max(dt) / 1e9
         e2e = {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
     per_op = {}
+    exchange = None
     if not args.no_per_op:
         comm = None
         if world > 1:
             from directcompute_torch_b200.dist import Communicator
             comm = Communicator.from_process_group(timeout_s=120)
+            exchange = "peer memory (NVLink, CUDA IPC)" if comm.peer_exchange else "NCCL all-gather"
         per_op = per_op_suite(L, ranks.rank, comm=comm)
         if comm is not None:
             comm.close()
@@ -757,6 +759,7 @@ def main():
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
+            "sharded_exchange": exchange,
             "per_op": per_op,
         }
         print(json.dumps(line))

@@ -121,6 +121,7 @@ SIGNATURES = {
     "dct_dist_finalize": ([], C.c_int),
     "dct_dist_rank": ([], C.c_int),
     "dct_dist_world": ([], C.c_int),
+    "dct_dist_peer_active": ([], C.c_int),
     "dct_dist_allreduce": ([VP, U64, C.c_int], C.c_int),
     "dct_dist_broadcast": ([VP, U64, C.c_int], C.c_int),
     "dct_dist_barrier": ([], C.c_int),

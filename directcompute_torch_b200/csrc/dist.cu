@@ -680,6 +680,7 @@ DCT_API int dct_dist_finalize(void) {
 
 DCT_API int dct_dist_rank(void) { DLOCK; return D.comm ? D.rank : -1; }
 DCT_API int dct_dist_world(void) { DLOCK; return D.comm ? D.world : 0; }
+DCT_API int dct_dist_peer_active(void) { DLOCK; return D.comm && D.peer ? 1 : 0; }
 
 DCT_API int dct_dist_allreduce(void* buf, uint64_t count, int op) {
   DLOCK;

@@ -123,6 +123,11 @@ class Communicator:
         return cls(0, 1, cls.new_unique_id(), timeout_s)
 
     # -- plumbing -------------------------------------------------------------
+    @property
+    def peer_exchange(self) -> bool:
+        """True when records travel through mapped peer memory rather than NCCL."""
+        return bool(self.lib.dct_dist_peer_active())
+
     def _check(self, rc: int, what: str) -> None:
         _abi.check(self.lib, rc, what)
 

@@ -300,6 +300,9 @@ DCT_API int dct_dist_init(const void* id, int len, int nranks, int rank, double 
 DCT_API int dct_dist_finalize(void);
 DCT_API int dct_dist_rank(void);    /* -1 without a communicator */
 DCT_API int dct_dist_world(void);   /* 0 without a communicator */
+/* 1 when the sharded ops exchange records through mapped peer memory (NVLink,
+ * CUDA IPC), 0 when they use NCCL all-gathers (or without a communicator) */
+DCT_API int dct_dist_peer_active(void);
 /* in-place fp32 all-reduce of buf[0:count]: op 0 sum, 1 mean, 2 max, 4 min */
 DCT_API int dct_dist_allreduce(void* buf, uint64_t count, int op);
 DCT_API int dct_dist_broadcast(void* buf, uint64_t count, int root);
