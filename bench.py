@@ -319,6 +319,30 @@ def run_e2e(L: Lib, c2: C2, steps: int, warmup: int):
     return dt, h2d, d2h
 
 
+def link_bandwidth(L: Lib, nbytes: int = 1 << 29, reps: int = 3):
+    """Pinned host<->device copy rates (GB/s) on the library's stream: the
+    ceiling for the e2e step's copies."""
+    lib = L.lib
+    n = nbytes // 4
+    h = L.new(n)
+    host = lib.dct_host_alloc(nbytes)
+    if not host:
+        raise RuntimeError("pinned allocation failed")
+    L.check(lib.dct_copy_h2d(h, host, 0, n), "link h2d")
+    lib.dct_synchronize()
+    lib.dct_timer_start()
+    for _ in range(reps):
+        L.check(lib.dct_copy_h2d(h, host, 0, n), "link h2d")
+    h2d = nbytes * reps / (lib.dct_timer_stop_ms() * 1e-3) / 1e9
+    lib.dct_timer_start()
+    for _ in range(reps):
+        L.check(lib.dct_copy_d2h(h, host, 0, n), "link d2h")
+    d2h = nbytes * reps / (lib.dct_timer_stop_ms() * 1e-3) / 1e9
+    lib.dct_host_free(host)
+    lib.ReleaseBuffer(h)
+    return h2d, d2h
+
+
 # ---------------------------------------------------------------------------
 # per-op breakdown of the other BASELINE configs
 # ---------------------------------------------------------------------------
@@ -712,6 +736,13 @@ def main():
         nst = max(1, min(args.steps, 3))
         e2e_val = ranks.sum(c2.step_bytes * nst) / ranks.max(dt) / 1e9
         e2e = {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        # the step's host copies at the measured pinned-copy rates: the floor for e2e
+        lh2d, ld2h = link_bandwidth(L)
+        floor_s = h2d / (lh2d * 1e9) + d2h / (ld2h * 1e9)
+        step_s = ranks.max(dt) / nst
+        e2e["link"] = {"h2d_gbs": round(lh2d, 1), "d2h_gbs": round(ld2h, 1),
+                       "copy_floor_ms_per_step": round(floor_s * 1e3, 2),
+                       "ms_per_step": round(step_s * 1e3, 2), "frac_of_copy_floor": round(floor_s / step_s, 3)}
     per_op = {}
     exchange = None
     if not args.no_per_op:

@@ -62,6 +62,13 @@ DCT_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory")
 // grid to complete, so every kernel launched with launch_pdl calls
 // grid_dep_wait before touching what earlier kernels wrote.
 DCT_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// First statement of every kernel launched with launch_pdl: the next kernel may
+// be scheduled now, and nothing here touches memory before the previous kernel
+// of the stream has completed.  Both are no-ops for an ordinary launch.
+DCT_DEV void pdl_entry() {
+  grid_dep_launch();
+  grid_dep_wait();
+}
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

@@ -118,6 +118,7 @@ inline unsigned chunk_blocks(uint64_t n4) { return (unsigned)((n4 + kChunk4 - 1)
 
 template <int OP>
 __global__ void __launch_bounds__(256) k_unary_chunk(const float* x, float* y, uint64_t n, float al) {
+  pdl_entry();
   const uint64_t n4 = n >> 2;
   const uint64_t base = (uint64_t)blockIdx.x * kChunk4 + threadIdx.x;
   float4 v[kChunkU];
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(256) k_unary_chunk(const float* x, float* y, u
 
 template <int OP>
 __global__ void __launch_bounds__(256) k_unary_scalar(const float* x, float* y, uint64_t n, float al) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     y[i] = unary_op<OP>(x[i], al);
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(256) k_unary_scalar(const float* x, float* y, 
 template <int OP>
 __global__ void __launch_bounds__(256) k_binary_chunk(const float* a, const float* b, float* y, uint64_t n,
                                                       float al, float be) {
+  pdl_entry();
   const uint64_t n4 = n >> 2;
   const uint64_t base = (uint64_t)blockIdx.x * kChunk4 + threadIdx.x;
   float4 va[kChunkU], vb[kChunkU];
@@ -185,6 +188,7 @@ __global__ void __launch_bounds__(256) k_binary_chunk(const float* a, const floa
 template <int OP>
 __global__ void __launch_bounds__(256) k_binary_scalar(const float* a, const float* b, float* y,
                                                        uint64_t n, float al, float be) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     y[i] = binary_op<OP>(a[i], b[i], al, be);
@@ -239,6 +243,7 @@ template <int OP, bool A_BC, bool B_BC>
 __global__ void __launch_bounds__(256) k_bcast_chunk(const float* __restrict__ a, const float* __restrict__ b,
                                                      float* __restrict__ y, uint32_t n4,
                                                      const __grid_constant__ RowMap m) {
+  pdl_entry();
   const uint64_t base = (uint64_t)blockIdx.x * kChunk4 + threadIdx.x;
   float4 o[kChunkU];
 #pragma unroll
@@ -263,6 +268,7 @@ template <int OP, bool SWAP>
 __global__ void __launch_bounds__(256) k_bcast3(const float* __restrict__ a, const float* __restrict__ b,
                                                 float* __restrict__ y, uint32_t R, uint32_t q4, uint32_t rchunk,
                                                 int64_t sap, int64_t sbp, int64_t sbr) {
+  pdl_entry();
   const uint32_t c4 = blockIdx.x * 256 + threadIdx.x;
   if (c4 >= q4) return;
   const uint32_t p = blockIdx.z;
@@ -292,6 +298,7 @@ __global__ void __launch_bounds__(256) k_bcast3(const float* __restrict__ a, con
 template <int OP, bool SWAP, bool RELU>
 __global__ void __launch_bounds__(256) k_rowvec_chunk(const float* A, const float* v, float* y, uint32_t n4,
                                                       FastDiv ncol4) {
+  pdl_entry();
   const uint64_t base = (uint64_t)blockIdx.x * kChunk4 + threadIdx.x;
   float4 x[kChunkU], bv[kChunkU];
 #pragma unroll
@@ -326,6 +333,7 @@ struct ElemMap {
 template <int OP>
 __global__ void __launch_bounds__(256) k_bcast_scalar(const float* a, const float* b, float* y, uint64_t n,
                                                       const __grid_constant__ ElemMap m) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     uint32_t rem = (uint32_t)i;
@@ -345,6 +353,7 @@ __global__ void __launch_bounds__(256) k_bcast_scalar(const float* a, const floa
 template <bool RELU>
 __global__ void __launch_bounds__(256) k_add_bias_scalar(const float* A, const float* B, float* C, uint64_t n,
                                                          uint32_t N, FastDiv dn) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     uint32_t col;
@@ -375,8 +384,8 @@ cudaError_t launch_unary(int op, const float* x, float* y, uint64_t n, float alp
   switch (op) {
 #define X(OPC)                                                                      \
   case OPC:                                                                         \
-    if (vec) k_unary_chunk<OPC><<<blocks, 256, 0, st>>>(x, y, n, alpha);           \
-    else k_unary_scalar<OPC><<<blocks, 256, 0, st>>>(x, y, n, alpha);              \
+    if (vec) launch_pdl(k_unary_chunk<OPC>, dim3(blocks), dim3(256), 0, st, x, y, n, alpha);           \
+    else launch_pdl(k_unary_scalar<OPC>, dim3(blocks), dim3(256), 0, st, x, y, n, alpha);              \
     break;
     DCT_UNARY_CASES(X)
 #undef X
@@ -393,8 +402,8 @@ cudaError_t launch_binary_same(int op, const float* a, const float* b, float* y,
   switch (op) {
 #define X(OPC)                                                                        \
   case OPC:                                                                           \
-    if (vec) k_binary_chunk<OPC><<<blocks, 256, 0, st>>>(a, b, y, n, alpha, beta);   \
-    else k_binary_scalar<OPC><<<blocks, 256, 0, st>>>(a, b, y, n, alpha, beta);      \
+    if (vec) launch_pdl(k_binary_chunk<OPC>, dim3(blocks), dim3(256), 0, st, a, b, y, n, alpha, beta);   \
+    else launch_pdl(k_binary_scalar<OPC>, dim3(blocks), dim3(256), 0, st, a, b, y, n, alpha, beta);      \
     break;
     DCT_BINARY_CASES(X)
 #undef X
@@ -410,14 +419,14 @@ cudaError_t launch_add_bias(const float* A, const float* B, float* C, uint64_t M
   if (N % 4 == 0 && n / 4 < 0xffffffffull && aligned16_h(A) && aligned16_h(B) && aligned16_h(C)) {
     const uint32_t n4 = (uint32_t)(n / 4);
     FastDiv nc((uint32_t)(N / 4));
-    if (relu) k_rowvec_chunk<EW_ADD, false, true><<<chunk_blocks(n4), 256, 0, st>>>(A, B, C, n4, nc);
-    else k_rowvec_chunk<EW_ADD, false, false><<<chunk_blocks(n4), 256, 0, st>>>(A, B, C, n4, nc);
+    if (relu) launch_pdl(k_rowvec_chunk<EW_ADD, false, true>, dim3(chunk_blocks(n4)), dim3(256), 0, st, A, B, C, n4, nc);
+    else launch_pdl(k_rowvec_chunk<EW_ADD, false, false>, dim3(chunk_blocks(n4)), dim3(256), 0, st, A, B, C, n4, nc);
   } else {
     if (N == 0 || N > 0xffffffffull) return cudaErrorInvalidValue;
     const unsigned blocks = grid_for(n, 256);
     FastDiv dn((uint32_t)N);
-    if (relu) k_add_bias_scalar<true><<<blocks, 256, 0, st>>>(A, B, C, n, (uint32_t)N, dn);
-    else k_add_bias_scalar<false><<<blocks, 256, 0, st>>>(A, B, C, n, (uint32_t)N, dn);
+    if (relu) launch_pdl(k_add_bias_scalar<true>, dim3(blocks), dim3(256), 0, st, A, B, C, n, (uint32_t)N, dn);
+    else launch_pdl(k_add_bias_scalar<false>, dim3(blocks), dim3(256), 0, st, A, B, C, n, (uint32_t)N, dn);
   }
   return cudaGetLastError();
 }
@@ -478,7 +487,7 @@ cudaError_t launch_binary_bcast(int op, const float* a, const float* b, float* y
     const FastDiv nc(q4);
     if (b_rowinv && a_full) {
       switch (op) {
-#define X(OPC) case OPC: k_rowvec_chunk<OPC, false, false><<<blocks, 256, 0, st>>>(a, b, y, n4, nc); break;
+#define X(OPC) case OPC: launch_pdl(k_rowvec_chunk<OPC, false, false>, dim3(blocks), dim3(256), 0, st, a, b, y, n4, nc); break;
         DCT_BCAST_CASES(X)
 #undef X
         default: return cudaErrorInvalidValue;
@@ -487,7 +496,7 @@ cudaError_t launch_binary_bcast(int op, const float* a, const float* b, float* y
     }
     if (a_rowinv && b_full) {
       switch (op) {
-#define X(OPC) case OPC: k_rowvec_chunk<OPC, true, false><<<blocks, 256, 0, st>>>(b, a, y, n4, nc); break;
+#define X(OPC) case OPC: launch_pdl(k_rowvec_chunk<OPC, true, false>, dim3(blocks), dim3(256), 0, st, b, a, y, n4, nc); break;
         DCT_BCAST_CASES(X)
 #undef X
         default: return cudaErrorInvalidValue;
@@ -514,8 +523,8 @@ cudaError_t launch_binary_bcast(int op, const float* a, const float* b, float* y
       switch (op) {
 #define X(OPC)                                                                                         \
   case OPC:                                                                                            \
-    if (swap) k_bcast3<OPC, true><<<grid, 256, 0, st>>>(inv, var, y, R, q4, rchunk, sip, svp, svr);     \
-    else k_bcast3<OPC, false><<<grid, 256, 0, st>>>(inv, var, y, R, q4, rchunk, sip, svp, svr);        \
+    if (swap) launch_pdl(k_bcast3<OPC, true>, dim3(grid), dim3(256), 0, st, inv, var, y, R, q4, rchunk, sip, svp, svr);     \
+    else launch_pdl(k_bcast3<OPC, false>, dim3(grid), dim3(256), 0, st, inv, var, y, R, q4, rchunk, sip, svp, svr);        \
     break;
         DCT_BCAST_CASES(X)
 #undef X
@@ -536,9 +545,9 @@ cudaError_t launch_binary_bcast(int op, const float* a, const float* b, float* y
     switch (op) {
 #define X(OPC)                                                                                    \
   case OPC:                                                                                       \
-    if (abc) k_bcast_chunk<OPC, true, false><<<blocks, 256, 0, st>>>(a, b, y, n4, m);              \
-    else if (bbc) k_bcast_chunk<OPC, false, true><<<blocks, 256, 0, st>>>(a, b, y, n4, m);         \
-    else k_bcast_chunk<OPC, false, false><<<blocks, 256, 0, st>>>(a, b, y, n4, m);                 \
+    if (abc) launch_pdl(k_bcast_chunk<OPC, true, false>, dim3(blocks), dim3(256), 0, st, a, b, y, n4, m);              \
+    else if (bbc) launch_pdl(k_bcast_chunk<OPC, false, true>, dim3(blocks), dim3(256), 0, st, a, b, y, n4, m);         \
+    else launch_pdl(k_bcast_chunk<OPC, false, false>, dim3(blocks), dim3(256), 0, st, a, b, y, n4, m);                 \
     break;
       DCT_BCAST_CASES(X)
 #undef X
@@ -557,7 +566,7 @@ cudaError_t launch_binary_bcast(int op, const float* a, const float* b, float* y
   }
   const unsigned blocks = grid_for(n, 256);
   switch (op) {
-#define X(OPC) case OPC: k_bcast_scalar<OPC><<<blocks, 256, 0, st>>>(a, b, y, n, m); break;
+#define X(OPC) case OPC: launch_pdl(k_bcast_scalar<OPC>, dim3(blocks), dim3(256), 0, st, a, b, y, n, m); break;
     DCT_BCAST_CASES(X)
 #undef X
     default: return cudaErrorInvalidValue;
@@ -569,6 +578,7 @@ cudaError_t launch_binary_bcast(int op, const float* a, const float* b, float* y
 // small reference-compat kernels
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_relu_bounded(const float* x, uint64_t n_in, float* y, uint64_t n_out) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_out; i += stride)
     y[i] = i < n_in ? unary_op<EW_RELU>(x[i], 0.f) : 0.0f;
@@ -577,11 +587,12 @@ __global__ void __launch_bounds__(256) k_relu_bounded(const float* x, uint64_t n
 cudaError_t launch_relu_bounded(const float* x, uint64_t n_in, float* y, uint64_t n_out, cudaStream_t st) {
   if (n_out == 0) return cudaSuccess;
   if (n_in >= n_out) return launch_unary(EW_RELU, x, y, n_out, 0.f, st);
-  k_relu_bounded<<<grid_for(n_out, 256), 256, 0, st>>>(x, n_in, y, n_out);
+  launch_pdl(k_relu_bounded, dim3(grid_for(n_out, 256)), dim3(256), 0, st, x, n_in, y, n_out);
   return cudaGetLastError();
 }
 
 __global__ void __launch_bounds__(256) k_gap_bwd(const float* g, float* dx, uint64_t n, uint32_t S, FastDiv ds) {
+  pdl_entry();
   const float fs = (float)S;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -593,12 +604,13 @@ __global__ void __launch_bounds__(256) k_gap_bwd(const float* g, float* dx, uint
 cudaError_t launch_gap_backward(const float* g, float* dx, uint64_t n, uint32_t S, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   if (S == 0) return cudaErrorInvalidValue;
-  k_gap_bwd<<<grid_for(n, 256), 256, 0, st>>>(g, dx, n, S, FastDiv(S));
+  launch_pdl(k_gap_bwd, dim3(grid_for(n, 256)), dim3(256), 0, st, g, dx, n, S, FastDiv(S));
   return cudaGetLastError();
 }
 
 __global__ void __launch_bounds__(256) k_softmax_ce_grad(const float* p, const float* labels, float* grad,
                                                          uint32_t B, uint32_t K, uint32_t rows, uint32_t cols) {
+  pdl_entry();
   const float fb = (float)B;
   for (uint32_t r = blockIdx.y; r < rows; r += gridDim.y) {
     const float lab = labels[r];
@@ -616,19 +628,21 @@ cudaError_t launch_softmax_ce_grad(const float* p, const float* labels, float* g
   unsigned bs = cols >= 256 ? 256 : ((cols + 31) / 32) * 32;
   unsigned gx = (cols + bs - 1) / bs;
   unsigned gy = rows < 65535 ? rows : 65535;
-  k_softmax_ce_grad<<<dim3(gx, gy), bs, 0, st>>>(p, labels, grad, B, K, rows, cols);
+  launch_pdl(k_softmax_ce_grad, dim3(dim3(gx, gy)), dim3(bs), 0, st, p, labels, grad, B, K, rows, cols);
   return cudaGetLastError();
 }
 
-__global__ void k_accumulate_scalar(const float* src, float* dst) { dst[0] = __fadd_rn(dst[0], src[0]); }
+__global__ void k_accumulate_scalar(const float* src, float* dst) {
+  pdl_entry(); dst[0] = __fadd_rn(dst[0], src[0]); }
 
 cudaError_t launch_accumulate_scalar(const float* src, float* dst, cudaStream_t st) {
-  k_accumulate_scalar<<<1, 1, 0, st>>>(src, dst);
+  launch_pdl(k_accumulate_scalar, dim3(1), dim3(1), 0, st, src, dst);
   return cudaGetLastError();
 }
 
 __global__ void __launch_bounds__(256) k_dice_grad(const float* pred, const float* target, const float* sums,
                                                    float* dx, uint32_t batch, uint32_t size, uint64_t n) {
+  pdl_entry();
   const float fb = (float)batch;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -646,7 +660,7 @@ cudaError_t launch_dice_grad(const float* pred, const float* target, const float
                              uint32_t batch, uint32_t size, uint64_t n, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
   if (size == 0 || batch == 0) return cudaErrorInvalidValue;
-  k_dice_grad<<<grid_for(n, 256), 256, 0, st>>>(pred, target, sums, dx, batch, size, n);
+  launch_pdl(k_dice_grad, dim3(grid_for(n, 256)), dim3(256), 0, st, pred, target, sums, dx, batch, size, n);
   return cudaGetLastError();
 }
 

@@ -260,6 +260,7 @@ template <int OP, bool VEC>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __restrict__ x, uint64_t rows, uint64_t len,
                                                              uint64_t so, uint32_t chunks, uint64_t chunk_len,
                                                              RedOut ro, unsigned long long* part) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -319,9 +320,9 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
                                                              uint64_t inner, uint64_t so, uint64_t sl,
                                                              uint32_t chunks, uint64_t chunk_len, RedOut ro,
                                                              unsigned long long* part) {
+  pdl_entry();
   constexpr int W = 32 * VEC;
   __shared__ unsigned long long sh[kRedWarps][W];
-  grid_dep_launch();                                    // the fold kernel may be scheduled now
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t c0 = (uint64_t)blockIdx.x * W + (uint64_t)lane * VEC;
   const uint32_t ch = blockIdx.z;
@@ -393,7 +394,7 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
                                                      uint32_t chunks, uint64_t inner, uint64_t len, RedOut ro) {
-  grid_dep_wait();
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const uint64_t wpb = blockDim.x >> 5;
   const uint64_t stride = (uint64_t)gridDim.x * wpb;
@@ -417,6 +418,7 @@ template <int OP>
 __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                         uint64_t inner, uint64_t so, uint64_t sl, uint64_t si,
                                                         RedOut ro) {
+  pdl_entry();
   const uint64_t nout = outer * inner;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += stride) {
@@ -522,13 +524,13 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
     if (!ws || ws_bytes < need) return cudaErrorInvalidValue;
   }
   if (p.kind == 0) {
-    if (p.vec) k_reduce_rows<OP, true><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
-    else k_reduce_rows<OP, false><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, so, p.chunks, p.chunk_len, ro, part);
+    if (p.vec) launch_pdl(k_reduce_rows<OP, true>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
+    else launch_pdl(k_reduce_rows<OP, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
   } else if (p.kind == 1) {
-    if (p.vec) k_reduce_cols<OP, 4><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
-    else k_reduce_cols<OP, 1><<<p.grid, kRedThreads, 0, st>>>(x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
+    if (p.vec) launch_pdl(k_reduce_cols<OP, 4>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
+    else launch_pdl(k_reduce_cols<OP, 1>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
   } else {
-    k_reduce_generic<OP><<<p.grid, 256, 0, st>>>(x, outer, len, inner, so, sl, si, ro);
+    launch_pdl(k_reduce_generic<OP>, dim3(p.grid), dim3(256), 0, st, x, outer, len, inner, so, sl, si, ro);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nparts == 1) return e;
@@ -554,6 +556,7 @@ cudaError_t dispatch_reduce(int op, const float* x, uint64_t outer, uint64_t len
 // identity partials (a shard with nothing to reduce)
 template <int OP>
 __global__ void k_identity_packed(unsigned long long* packed, uint64_t n) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += stride)
     packed[k] = Acc<OP>::identity_pack();
@@ -623,13 +626,13 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
   if (len == 0) {
     const unsigned b = grid_for(nout, 256);
     switch (op) {
-      case RED_SUM: k_identity_packed<RED_SUM><<<b, 256, 0, st>>>(packed, nout); break;
-      case RED_MEAN: k_identity_packed<RED_MEAN><<<b, 256, 0, st>>>(packed, nout); break;
-      case RED_MAX: k_identity_packed<RED_MAX><<<b, 256, 0, st>>>(packed, nout); break;
-      case RED_ARGMAX: k_identity_packed<RED_ARGMAX><<<b, 256, 0, st>>>(packed, nout); break;
-      case RED_MIN: k_identity_packed<RED_MIN><<<b, 256, 0, st>>>(packed, nout); break;
-      case RED_ARGMIN: k_identity_packed<RED_ARGMIN><<<b, 256, 0, st>>>(packed, nout); break;
-      case RED_SUMSQ: k_identity_packed<RED_SUMSQ><<<b, 256, 0, st>>>(packed, nout); break;
+      case RED_SUM: launch_pdl(k_identity_packed<RED_SUM>, dim3(b), dim3(256), 0, st, packed, nout); break;
+      case RED_MEAN: launch_pdl(k_identity_packed<RED_MEAN>, dim3(b), dim3(256), 0, st, packed, nout); break;
+      case RED_MAX: launch_pdl(k_identity_packed<RED_MAX>, dim3(b), dim3(256), 0, st, packed, nout); break;
+      case RED_ARGMAX: launch_pdl(k_identity_packed<RED_ARGMAX>, dim3(b), dim3(256), 0, st, packed, nout); break;
+      case RED_MIN: launch_pdl(k_identity_packed<RED_MIN>, dim3(b), dim3(256), 0, st, packed, nout); break;
+      case RED_ARGMIN: launch_pdl(k_identity_packed<RED_ARGMIN>, dim3(b), dim3(256), 0, st, packed, nout); break;
+      case RED_SUMSQ: launch_pdl(k_identity_packed<RED_SUMSQ>, dim3(b), dim3(256), 0, st, packed, nout); break;
       default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -698,6 +701,7 @@ struct SumMap {
 __global__ void __launch_bounds__(256) k_sum_generic(const float* __restrict__ g, SumMap m, uint64_t nout,
                                                      uint64_t rtot, uint64_t cl, float* out,
                                                      unsigned long long* part) {
+  pdl_entry();
   const uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= nout) return;
   uint64_t rem = k, base = 0;
@@ -813,7 +817,7 @@ cudaError_t launch_sum_to_shape(const float* g, int ndim, const int64_t* gshape,
     return cudaErrorInvalidValue;
   const dim3 grid((unsigned)((sp.nout + 255) / 256), (unsigned)sp.chunks, 1);
   if (grid.x == 0 || (sp.nout + 255) / 256 > 0x7fffffffull) return cudaErrorInvalidValue;
-  k_sum_generic<<<grid, 256, 0, st>>>(g, m, sp.nout, sp.rtot, sp.cl, out, part);
+  launch_pdl(k_sum_generic, dim3(grid), dim3(256), 0, st, g, m, sp.nout, sp.rtot, sp.cl, out, part);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || sp.chunks == 1) return e;
   return launch_fold_packed(RED_SUM, part, (uint32_t)sp.chunks, sp.nout, sp.nout, sp.rtot, out, nullptr, st);
@@ -832,6 +836,7 @@ size_t full_reduce_ws_bytes() {
 
 template <int OP>
 __global__ void __launch_bounds__(kFullThreads) k_full_pass1(const float* __restrict__ x, uint64_t n, double* part) {
+  pdl_entry();
   __shared__ double sh[32];
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -888,6 +893,7 @@ __global__ void __launch_bounds__(kFullThreads) k_full_pass1(const float* __rest
 
 template <int OP>
 __global__ void k_full_pass2(const double* part, int nparts, uint64_t n, int post, float* out32, double* out64) {
+  pdl_entry();
   __shared__ double sh[32];
   if constexpr (OP == RED_MAX || OP == RED_MIN) {
     if (threadIdx.x == 0) {
@@ -923,14 +929,14 @@ static cudaError_t full_reduce_post(int op, const float* x, uint64_t n, float* o
   int blocks = (int)(need < (uint64_t)maxb ? need : (uint64_t)maxb);
   if (blocks < 1) blocks = 1;
   switch (op) {
-    case RED_SUM: k_full_pass1<RED_SUM><<<blocks, kFullThreads, 0, st>>>(x, n, part);
-      k_full_pass2<RED_SUM><<<1, 1024, 0, st>>>(part, blocks, n, post, out32, out64); break;
-    case RED_SUMSQ: k_full_pass1<RED_SUMSQ><<<blocks, kFullThreads, 0, st>>>(x, n, part);
-      k_full_pass2<RED_SUMSQ><<<1, 1024, 0, st>>>(part, blocks, n, post, out32, out64); break;
-    case RED_MAX: k_full_pass1<RED_MAX><<<blocks, kFullThreads, 0, st>>>(x, n, part);
-      k_full_pass2<RED_MAX><<<1, 32, 0, st>>>(part, blocks, n, 0, out32, out64); break;
-    case RED_MIN: k_full_pass1<RED_MIN><<<blocks, kFullThreads, 0, st>>>(x, n, part);
-      k_full_pass2<RED_MIN><<<1, 32, 0, st>>>(part, blocks, n, 0, out32, out64); break;
+    case RED_SUM: launch_pdl(k_full_pass1<RED_SUM>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2<RED_SUM>, dim3(1), dim3(1024), 0, st, part, blocks, n, post, out32, out64); break;
+    case RED_SUMSQ: launch_pdl(k_full_pass1<RED_SUMSQ>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2<RED_SUMSQ>, dim3(1), dim3(1024), 0, st, part, blocks, n, post, out32, out64); break;
+    case RED_MAX: launch_pdl(k_full_pass1<RED_MAX>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2<RED_MAX>, dim3(1), dim3(32), 0, st, part, blocks, n, 0, out32, out64); break;
+    case RED_MIN: launch_pdl(k_full_pass1<RED_MIN>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2<RED_MIN>, dim3(1), dim3(32), 0, st, part, blocks, n, 0, out32, out64); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
@@ -960,6 +966,7 @@ cudaError_t launch_rms(const float* x, uint64_t n, float* out, void* ws, cudaStr
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_grad_sq(const float* __restrict__ g, uint64_t count, float* part, uint64_t off,
                                                  uint64_t ngroups) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -980,11 +987,12 @@ cudaError_t launch_grad_sq_reduce(const float* g, uint64_t count, float* partial
                                   cudaStream_t st) {
   if (ngroups == 0) return cudaSuccess;
   const uint64_t threads = ngroups * 32;
-  k_grad_sq<<<grid_for(threads, 256), 256, 0, st>>>(g, count, partials, off, ngroups);
+  launch_pdl(k_grad_sq, dim3(grid_for(threads, 256)), dim3(256), 0, st, g, count, partials, off, ngroups);
   return cudaGetLastError();
 }
 
 __global__ void __launch_bounds__(1024) k_grad_norm_final(const float* part, uint64_t n, float max_norm, float* ns) {
+  pdl_entry();
   __shared__ double sh[32];
   double acc = 0.0;
   for (uint64_t k = threadIdx.x; k < n; k += blockDim.x) acc += (double)part[k];
@@ -997,7 +1005,7 @@ __global__ void __launch_bounds__(1024) k_grad_norm_final(const float* part, uin
 }
 
 cudaError_t launch_grad_norm_final(const float* partials, uint64_t n, float max_norm, float* ns, cudaStream_t st) {
-  k_grad_norm_final<<<1, 1024, 0, st>>>(partials, n, max_norm, ns);
+  launch_pdl(k_grad_norm_final, dim3(1), dim3(1024), 0, st, partials, n, max_norm, ns);
   return cudaGetLastError();
 }
 
@@ -1006,6 +1014,7 @@ cudaError_t launch_grad_norm_final(const float* partials, uint64_t n, float max_
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) k_dice_sums(const float* __restrict__ pred, const float* __restrict__ target,
                                                    uint32_t size, float* out, int mode) {
+  pdl_entry();
   __shared__ double sh[32];
   const uint64_t base = (uint64_t)blockIdx.x * size;
   double si = 0.0, sp = 0.0, stt = 0.0;
@@ -1032,7 +1041,7 @@ __global__ void __launch_bounds__(512) k_dice_sums(const float* __restrict__ pre
 cudaError_t launch_dice_sums(const float* pred, const float* target, uint32_t batch, uint32_t size, float* out,
                              int mode, cudaStream_t st) {
   if (batch == 0) return cudaSuccess;
-  k_dice_sums<<<batch, 512, 0, st>>>(pred, target, size, out, mode);
+  launch_pdl(k_dice_sums, dim3(batch), dim3(512), 0, st, pred, target, size, out, mode);
   return cudaGetLastError();
 }
 
