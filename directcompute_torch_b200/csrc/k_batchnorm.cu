@@ -27,6 +27,7 @@ DCT_DEV float rstd_of(float var, float eps) {
 template <bool BWD, bool VEC>
 __global__ void __launch_bounds__(256) k_bn_plane_sums(const float* __restrict__ x, const float* __restrict__ dy,
                                                        uint64_t planes, uint32_t S, double* out) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(256) k_bn_plane_sums(const float* __restrict__
 // adds n = l, l + 32, ... in order, then a fixed shuffle tree (deterministic,
 // and 32 loads in flight instead of one serial chain of N).
 __global__ void __launch_bounds__(256) k_bn_fold(const double* __restrict__ ps, uint32_t N, uint32_t C, double* chan) {
+  pdl_entry();
   const uint32_t k = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;     // (c, j)
   const int lane = threadIdx.x & 31;
   if (k >= 2 * C) return;
@@ -97,6 +99,7 @@ __global__ void __launch_bounds__(256) k_bn_fold(const double* __restrict__ ps, 
 
 __global__ void k_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rm,
                                  float* rv, int training, float momentum, const double* cnt_dev) {
+  pdl_entry();
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   if (cnt_dev) cnt = *cnt_dev;
@@ -114,6 +117,7 @@ __global__ void k_bn_stats_final(const double* chan, uint32_t C, double cnt, flo
 
 __global__ void k_bn_bwd_final(const double* chan, uint32_t C, const float* mean, const float* var, float eps,
                                float* dgamma, float* dbeta) {
+  pdl_entry();
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   const double sdy = chan[2 * c], sdyx = chan[2 * c + 1];
@@ -143,6 +147,7 @@ __global__ void __launch_bounds__(256) k_bn_forward_chunk(const float* __restric
                                                           const float* __restrict__ gamma,
                                                           const float* __restrict__ beta, float* __restrict__ y,
                                                           uint32_t n4, FastDiv s4, FastDiv cdiv, float eps) {
+  pdl_entry();
   const uint64_t base = (uint64_t)blockIdx.x * kBnChunk4 + threadIdx.x;
   float4 v[kBnU];
   uint32_t ch[kBnU];
@@ -173,6 +178,7 @@ __global__ void __launch_bounds__(256) k_bn_dx_chunk(const float* __restrict__ x
                                                      const float* __restrict__ dbeta, float* __restrict__ dx,
                                                      uint32_t n4, FastDiv s4, FastDiv cdiv, float eps, float mf,
                                                      const double* __restrict__ cnt_dev) {
+  pdl_entry();
   if (cnt_dev) mf = (float)*cnt_dev;
   const uint64_t base = (uint64_t)blockIdx.x * kBnChunk4 + threadIdx.x;
   float4 a[kBnU], d[kBnU];
@@ -208,6 +214,7 @@ __global__ void __launch_bounds__(256) k_bn_forward(const float* __restrict__ x,
                                                     const float* __restrict__ beta, float* __restrict__ y,
                                                     uint64_t planes, uint32_t C, uint32_t S, float eps,
                                                     uint64_t limit) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -228,6 +235,7 @@ __global__ void __launch_bounds__(256) k_bn_backward_dx(const float* __restrict_
                                                         const float* __restrict__ dbeta, float* __restrict__ dx,
                                                         uint64_t planes, uint32_t C, uint32_t S, float eps, float mf,
                                                         uint64_t limit, const double* __restrict__ cnt_dev) {
+  pdl_entry();
   if (cnt_dev) mf = (float)*cnt_dev;
   const int lane = threadIdx.x & 31;
   const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -264,25 +272,25 @@ cudaError_t launch_bn_plane_sums(const float* x, const float* dy, uint32_t N, ui
   const bool vec = (S % 4 == 0) && aligned16_h(x) && (!dy || aligned16_h(dy));
   const unsigned blocks = plane_blocks(planes);
   if (dy) {
-    if (vec) k_bn_plane_sums<true, true><<<blocks, 256, 0, st>>>(x, dy, planes, S, plane_sums);
-    else k_bn_plane_sums<true, false><<<blocks, 256, 0, st>>>(x, dy, planes, S, plane_sums);
+    if (vec) launch_pdl(k_bn_plane_sums<true, true>, dim3(blocks), dim3(256), 0, st, x, dy, planes, S, plane_sums);
+    else launch_pdl(k_bn_plane_sums<true, false>, dim3(blocks), dim3(256), 0, st, x, dy, planes, S, plane_sums);
   } else {
-    if (vec) k_bn_plane_sums<false, true><<<blocks, 256, 0, st>>>(x, nullptr, planes, S, plane_sums);
-    else k_bn_plane_sums<false, false><<<blocks, 256, 0, st>>>(x, nullptr, planes, S, plane_sums);
+    if (vec) launch_pdl(k_bn_plane_sums<false, true>, dim3(blocks), dim3(256), 0, st, x, nullptr, planes, S, plane_sums);
+    else launch_pdl(k_bn_plane_sums<false, false>, dim3(blocks), dim3(256), 0, st, x, nullptr, planes, S, plane_sums);
   }
   return cudaGetLastError();
 }
 
 cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, double* chan, cudaStream_t st) {
   if (C == 0) return cudaSuccess;
-  k_bn_fold<<<(unsigned)((2ull * C * 32 + 255) / 256), 256, 0, st>>>(plane_sums, N, C, chan);
+  launch_pdl(k_bn_fold, dim3((unsigned)((2ull * C * 32 + 255) / 256)), dim3(256), 0, st, plane_sums, N, C, chan);
   return cudaGetLastError();
 }
 
 cudaError_t launch_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rmean,
                                   float* rvar, bool training, float momentum, cudaStream_t st, const double* cnt_dev) {
   if (C == 0) return cudaSuccess;
-  k_bn_stats_final<<<(C + 255) / 256, 256, 0, st>>>(chan, C, cnt, mean, var, rmean, rvar, training ? 1 : 0,
+  launch_pdl(k_bn_stats_final, dim3((C + 255) / 256), dim3(256), 0, st, chan, C, cnt, mean, var, rmean, rvar, training ? 1 : 0,
                                                       momentum, cnt_dev);
   return cudaGetLastError();
 }
@@ -290,7 +298,7 @@ cudaError_t launch_bn_stats_final(const double* chan, uint32_t C, double cnt, fl
 cudaError_t launch_bn_bwd_final(const double* chan, uint32_t C, const float* mean, const float* var, float eps,
                                 float* dgamma, float* dbeta, cudaStream_t st) {
   if (C == 0) return cudaSuccess;
-  k_bn_bwd_final<<<(C + 255) / 256, 256, 0, st>>>(chan, C, mean, var, eps, dgamma, dbeta);
+  launch_pdl(k_bn_bwd_final, dim3((C + 255) / 256), dim3(256), 0, st, chan, C, mean, var, eps, dgamma, dbeta);
   return cudaGetLastError();
 }
 
@@ -304,10 +312,10 @@ cudaError_t launch_bn_forward(const float* x, const float* mean, const float* va
   const bool vec = (S % 4 == 0) && (limit % 4 == 0) && limit / 4 < 0xffffffffull && aligned16_h(x) && aligned16_h(y);
   if (vec) {
     const uint32_t n4 = (uint32_t)(limit / 4);
-    k_bn_forward_chunk<<<(unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4), 256, 0, st>>>(
+    launch_pdl(k_bn_forward_chunk, dim3((unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4)), dim3(256), 0, st, 
         x, mean, var, gamma, beta, y, n4, FastDiv(S / 4), FastDiv(C), eps);
   } else {
-    k_bn_forward<<<plane_blocks(planes), 256, 0, st>>>(x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
+    launch_pdl(k_bn_forward, dim3(plane_blocks(planes)), dim3(256), 0, st, x, mean, var, gamma, beta, y, planes, C, S, eps, limit);
   }
   return cudaGetLastError();
 }
@@ -325,10 +333,10 @@ cudaError_t launch_bn_backward_dx(const float* x, const float* dy, const float* 
                    aligned16_h(dy) && aligned16_h(dx);
   if (vec) {
     const uint32_t n4 = (uint32_t)(limit / 4);
-    k_bn_dx_chunk<<<(unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4), 256, 0, st>>>(
+    launch_pdl(k_bn_dx_chunk, dim3((unsigned)((n4 + kBnChunk4 - 1) / kBnChunk4)), dim3(256), 0, st, 
         x, dy, mean, var, gamma, dgamma, dbeta, dx, n4, FastDiv(S / 4), FastDiv(C), eps, mf, cnt_dev);
   } else {
-    k_bn_backward_dx<<<plane_blocks(planes), 256, 0, st>>>(x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C,
+    launch_pdl(k_bn_backward_dx, dim3(plane_blocks(planes)), dim3(256), 0, st, x, dy, mean, var, gamma, dgamma, dbeta, dx, planes, C,
                                                             S, eps, mf, limit, cnt_dev);
   }
   return cudaGetLastError();

@@ -38,6 +38,7 @@ struct UpGeom {
 // Out[i] = X[(bc*inH + h/sH)*inW + w/sW] for i < n  (nn_upsample.hlsl:21-32)
 __global__ void __launch_bounds__(kT) k_upsample(const float* __restrict__ x, float* __restrict__ y, uint32_t n,
                                                  UpGeom g) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     const uint32_t row = g.outW.div(i), w = i - row * g.outW.d;
     const uint32_t bc = g.outH.div(row), h = row - bc * g.outH.d;
@@ -52,6 +53,7 @@ __global__ void __launch_bounds__(kT) k_upsample(const float* __restrict__ x, fl
 template <int SW>
 __global__ void __launch_bounds__(kT) k_upsample_chunk(const float* __restrict__ x, float* __restrict__ y,
                                                        uint32_t nq, FastDiv outWq, UpGeom g) {
+  pdl_entry();
   constexpr int U = 4;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
   float4 v[U];
@@ -100,6 +102,7 @@ struct UpBackGeom {
 // (nn_upsample_backward.hlsl:21-44)
 __global__ void __launch_bounds__(kT) k_upsample_bwd(const float* __restrict__ dy, float* __restrict__ dx,
                                                      uint32_t n, UpBackGeom g) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     const uint32_t row = g.inW.div(i), w = i - row * g.inW.d;
     const uint32_t bc = g.inH.div(row), h = row - bc * g.inH.d;
@@ -124,6 +127,7 @@ __global__ void __launch_bounds__(kT) k_upsample_bwd(const float* __restrict__ d
 // chunked, two units per thread.
 __global__ void __launch_bounds__(kT) k_upsample_bwd_2x2(const float* __restrict__ dy, float* __restrict__ dx,
                                                          uint32_t nq, FastDiv inWq, uint32_t inW) {
+  pdl_entry();
   constexpr int U = 2;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
   float4 a0[U], a1[U], b0[U], b1[U];
@@ -158,6 +162,7 @@ __global__ void __launch_bounds__(kT) k_upsample_bwd_2x2(const float* __restrict
 template <bool SLICE>
 __global__ void __launch_bounds__(kT) k_channel_copy(const float* __restrict__ src, float* __restrict__ dst,
                                                      uint32_t n, FastDiv L, uint32_t pitch, uint32_t off) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     const uint32_t q = L.div(i), r = i - q * L.d;
     const uint32_t j = q * pitch + off + r;
@@ -169,6 +174,7 @@ __global__ void __launch_bounds__(kT) k_channel_copy(const float* __restrict__ s
 template <bool SLICE>
 __global__ void __launch_bounds__(kT) k_channel_copy4(const float* __restrict__ src, float* __restrict__ dst,
                                                       uint32_t nq, FastDiv Lq, uint32_t pitch, uint32_t off) {
+  pdl_entry();
   constexpr int U = 4;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
   float4 v[U];
@@ -200,6 +206,7 @@ DCT_DEV void pool_take(float v, uint32_t k, float& best, uint32_t& bi) {
 __global__ void __launch_bounds__(kT) k_maxpool_fwd(const float* __restrict__ x, float* __restrict__ out,
                                                     uint32_t* __restrict__ idx, uint32_t n, FastDiv lw, FastDiv lh,
                                                     PoolShape g) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     const uint32_t t = lw.div(i), ow = i - t * lw.d;
     const uint32_t bc = lh.div(t), oh = t - bc * lh.d;
@@ -228,6 +235,7 @@ __global__ void __launch_bounds__(kT) k_maxpool_fwd(const float* __restrict__ x,
 __global__ void __launch_bounds__(kT) k_maxpool2x2(const float* __restrict__ x, float* __restrict__ out,
                                                    uint32_t* __restrict__ idx, uint32_t nq, FastDiv outWh,
                                                    FastDiv outH, uint32_t inH, uint32_t inW) {
+  pdl_entry();
   constexpr int U = 4;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
   float4 a[U], b[U];
@@ -267,6 +275,7 @@ __global__ void __launch_bounds__(kT) k_maxpool_scatter(const float* __restrict_
                                                         float* __restrict__ d, uint64_t dcount, uint32_t n,
                                                         FastDiv lw, FastDiv lh, uint32_t outH, uint32_t outW,
                                                         bool full) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     uint32_t o = i;
     if (!full) {
@@ -297,6 +306,7 @@ DCT_DEV bool in_window(uint32_t k, uint32_t bc, uint32_t oh, uint32_t ow, const 
 __global__ void __launch_bounds__(kT) k_maxpool_gather(const float* __restrict__ dz, const uint32_t* __restrict__ idx,
                                                        float* __restrict__ d, uint32_t n, FastDiv inW, FastDiv inH,
                                                        FastDiv s, PoolShape g, uint32_t* flag) {
+  pdl_entry();
   for (uint32_t e = gtid(); e < n; e += gstride()) {
     const uint32_t row = inW.div(e), iw = e - row * inW.d;
     const uint32_t bc = inH.div(row), ih = row - bc * inH.d;
@@ -319,6 +329,7 @@ __global__ void __launch_bounds__(kT) k_maxpool_gather2x2(const float* __restric
                                                           const uint32_t* __restrict__ idx, float* __restrict__ d,
                                                           uint32_t nq, FastDiv inWq, FastDiv inH, FastDiv inW,
                                                           PoolShape g, uint32_t* flag) {
+  pdl_entry();
   constexpr int U = 4;
   const uint32_t n = g.bc * g.inH * g.inW;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
@@ -371,6 +382,7 @@ __global__ void __launch_bounds__(kT) k_maxpool_gather2x2(const float* __restric
 __global__ void __launch_bounds__(1024) k_maxpool_fixup(const float* __restrict__ dz, const uint32_t* __restrict__ idx,
                                                         float* __restrict__ d, uint32_t n, uint32_t nout, FastDiv outW,
                                                         FastDiv outH, FastDiv inW, PoolShape g, uint32_t* flag) {
+  pdl_entry();
   if (*(volatile uint32_t*)flag == 0) return;
   for (uint32_t o = threadIdx.x; o < nout; o += blockDim.x) {
     const uint32_t k = idx[o];
@@ -399,6 +411,7 @@ template <int ACT>
 __global__ void __launch_bounds__(kT) k_conv_reshape(const float* __restrict__ mm, const float* __restrict__ bias,
                                                      float* __restrict__ out, uint32_t n, FastDiv lbp, FastDiv P,
                                                      uint32_t OC, uint32_t BP) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     const uint32_t oc = lbp.div(i), bp = i - oc * lbp.d;
     const uint32_t b = P.div(bp), px = bp - b * P.d;
@@ -410,6 +423,7 @@ template <int ACT>
 __global__ void __launch_bounds__(kT) k_conv_reshape4(const float* __restrict__ mm, const float* __restrict__ bias,
                                                       float* __restrict__ out, uint32_t nq, FastDiv Pq, FastDiv OC,
                                                       uint32_t P, uint32_t BP) {
+  pdl_entry();
   constexpr int U = 4;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
   float4 v[U];
@@ -442,6 +456,7 @@ template <bool RELU>
 __global__ void __launch_bounds__(kT) k_conv_grad_reshape(const float* __restrict__ dz, const float* __restrict__ fwd,
                                                           float* __restrict__ out, uint32_t n, FastDiv lbp, FastDiv P,
                                                           uint32_t OC, uint32_t BP) {
+  pdl_entry();
   for (uint32_t i = gtid(); i < n; i += gstride()) {
     const uint32_t oc = lbp.div(i), bp = i - oc * lbp.d;
     const uint32_t b = P.div(bp), px = bp - b * P.d;
@@ -455,6 +470,7 @@ template <bool RELU>
 __global__ void __launch_bounds__(kT) k_conv_grad_reshape4(const float* __restrict__ dz, const float* __restrict__ fwd,
                                                            float* __restrict__ out, uint32_t nq, FastDiv BPq,
                                                            FastDiv Pq, uint32_t OC, uint32_t P) {
+  pdl_entry();
   constexpr int U = 4;
   const uint32_t q0 = blockIdx.x * (kT * U) + threadIdx.x;
   float4 gv[U], f[U];
@@ -485,14 +501,12 @@ __global__ void __launch_bounds__(kT) k_conv_grad_reshape4(const float* __restri
 
 template <typename K, typename... A>
 cudaError_t go(K kernel, uint64_t work, cudaStream_t st, A... a) {
-  kernel<<<grid_for(work, kT, 2), kT, 0, st>>>(a...);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3(grid_for(work, kT, 2)), dim3(kT), 0, st, a...);
 }
 // chunked kernels: one block per kT*U units
 template <int U, typename K, typename... A>
 cudaError_t chunked(K kernel, uint32_t units, cudaStream_t st, A... a) {
-  kernel<<<(units + kT * U - 1) / (kT * U), kT, 0, st>>>(a...);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3((units + kT * U - 1) / (kT * U)), dim3(kT), 0, st, a...);
 }
 
 }  // namespace
@@ -505,10 +519,10 @@ cudaError_t launch_upsample(const float* x, float* y, uint32_t n, uint32_t total
     const uint32_t nq = n / 4;
     const FastDiv q(outW / 4);
     const unsigned grid = (nq + kT * 4 - 1) / (kT * 4);
-    if (sW == 1 && inW % 4 == 0) k_upsample_chunk<1><<<grid, kT, 0, st>>>(x, y, nq, q, g);
-    else if (sW == 2 && inW % 2 == 0) k_upsample_chunk<2><<<grid, kT, 0, st>>>(x, y, nq, q, g);
-    else if (sW == 4) k_upsample_chunk<4><<<grid, kT, 0, st>>>(x, y, nq, q, g);
-    else k_upsample_chunk<0><<<grid, kT, 0, st>>>(x, y, nq, q, g);
+    if (sW == 1 && inW % 4 == 0) launch_pdl(k_upsample_chunk<1>, dim3(grid), dim3(kT), 0, st, x, y, nq, q, g);
+    else if (sW == 2 && inW % 2 == 0) launch_pdl(k_upsample_chunk<2>, dim3(grid), dim3(kT), 0, st, x, y, nq, q, g);
+    else if (sW == 4) launch_pdl(k_upsample_chunk<4>, dim3(grid), dim3(kT), 0, st, x, y, nq, q, g);
+    else launch_pdl(k_upsample_chunk<0>, dim3(grid), dim3(kT), 0, st, x, y, nq, q, g);
     return cudaGetLastError();
   }
   return go(k_upsample, n, st, x, y, n, g);
@@ -567,7 +581,7 @@ cudaError_t launch_maxpool_backward_gather(const float* dz, const uint32_t* idx,
   else
     e = go(k_maxpool_gather, n, st, dz, idx, d, n, inW, FastDiv(g.inH), FastDiv(g.s), g, flag);
   if (e != cudaSuccess || nout == 0) return e;
-  k_maxpool_fixup<<<1, 1024, 0, st>>>(dz, idx, d, n, nout, FastDiv(g.outW), FastDiv(g.outH), inW, g, flag);
+  launch_pdl(k_maxpool_fixup, dim3(1), dim3(1024), 0, st, dz, idx, d, n, nout, FastDiv(g.outW), FastDiv(g.outH), inW, g, flag);
   return cudaGetLastError();
 }
 

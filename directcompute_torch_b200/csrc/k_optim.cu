@@ -53,6 +53,7 @@ constexpr uint64_t kOptChunk4 = 256ull * kOptU;
 
 __global__ void __launch_bounds__(256) k_adam(float* __restrict__ w, float* __restrict__ m, float* __restrict__ v,
                                               const float* __restrict__ g, uint64_t n, AdamK p) {
+  pdl_entry();
   const uint64_t n4 = n >> 2;
   const uint64_t base = (uint64_t)blockIdx.x * kOptChunk4 + threadIdx.x;
   float4 W[kOptU], M[kOptU], V[kOptU], G[kOptU];
@@ -82,6 +83,7 @@ __global__ void __launch_bounds__(256) k_adam(float* __restrict__ w, float* __re
 }
 
 __global__ void __launch_bounds__(256) k_adam_scalar(float* w, float* m, float* v, const float* g, uint64_t n, AdamK p) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     float W = w[i], M = m[i], V = v[i];
@@ -93,6 +95,7 @@ __global__ void __launch_bounds__(256) k_adam_scalar(float* w, float* m, float* 
 template <bool SCALED>
 __global__ void __launch_bounds__(256) k_sgd(float* w, const float* __restrict__ g, uint64_t n, float lr, float clip,
                                              const float* ns) {
+  pdl_entry();
   const float scale = SCALED ? ns[1] : 1.0f;
   const uint64_t n4 = n >> 2;
   const uint64_t base = (uint64_t)blockIdx.x * kOptChunk4 + threadIdx.x;
@@ -125,6 +128,7 @@ __global__ void __launch_bounds__(256) k_sgd(float* w, const float* __restrict__
 template <bool SCALED>
 __global__ void __launch_bounds__(256) k_sgd_scalar(float* w, const float* g, uint64_t n, float lr, float clip,
                                                     const float* ns) {
+  pdl_entry();
   const float scale = SCALED ? ns[1] : 1.0f;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
@@ -152,6 +156,7 @@ struct MtTable {
 
 template <int OP>
 __global__ void __launch_bounds__(256) k_mt(const __grid_constant__ MtTable tab) {
+  pdl_entry();
   // locate this block's tensor (binary search over the block prefix)
   int lo = 0, hi = tab.count - 1;
   const uint32_t b = blockIdx.x;
@@ -244,7 +249,7 @@ cudaError_t run_mt(const MtTensor* t, int count, MtTable& tab, cudaStream_t st) 
   while (pos < count) {
     const uint32_t blocks = fill_table(tab, t, count, &pos);
     if (tab.count == 0 || blocks == 0) continue;
-    k_mt<OP><<<blocks, 256, 0, st>>>(tab);
+    launch_pdl(k_mt<OP>, dim3(blocks), dim3(256), 0, st, tab);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (OP == MT_SUMSQ) tab.part_base += blocks;
@@ -253,6 +258,7 @@ cudaError_t run_mt(const MtTensor* t, int count, MtTable& tab, cudaStream_t st) 
 }
 
 __global__ void k_norm_scale(const double* part, int n, float max_norm, float* ns) {
+  pdl_entry();
   __shared__ double sh[32];
   double acc = 0.0;
   for (int k = threadIdx.x; k < n; k += blockDim.x) acc += part[k];
@@ -272,9 +278,9 @@ cudaError_t launch_adam(float* w, float* m, float* v, const float* g, uint64_t n
   const AdamK k = to_k(p);
   const uint64_t blocks = ((n >> 2) + kOptChunk4 - 1) / kOptChunk4;
   if (aligned16_h(w) && aligned16_h(m) && aligned16_h(v) && aligned16_h(g) && blocks < (1ull << 31))
-    k_adam<<<(unsigned)(blocks ? blocks : 1), 256, 0, st>>>(w, m, v, g, n, k);
+    launch_pdl(k_adam, dim3((unsigned)(blocks ? blocks : 1)), dim3(256), 0, st, w, m, v, g, n, k);
   else
-    k_adam_scalar<<<grid_for(n, 256), 256, 0, st>>>(w, m, v, g, n, k);
+    launch_pdl(k_adam_scalar, dim3(grid_for(n, 256)), dim3(256), 0, st, w, m, v, g, n, k);
   return cudaGetLastError();
 }
 
@@ -284,9 +290,9 @@ static cudaError_t run_sgd(float* w, const float* g, uint64_t n, float lr, float
   if (n == 0) return cudaSuccess;
   const uint64_t blocks = ((n >> 2) + kOptChunk4 - 1) / kOptChunk4;
   if (aligned16_h(w) && aligned16_h(g) && blocks < (1ull << 31))
-    k_sgd<SCALED><<<(unsigned)(blocks ? blocks : 1), 256, 0, st>>>(w, g, n, lr, clip, ns);
+    launch_pdl(k_sgd<SCALED>, dim3((unsigned)(blocks ? blocks : 1)), dim3(256), 0, st, w, g, n, lr, clip, ns);
   else
-    k_sgd_scalar<SCALED><<<grid_for(n, 256), 256, 0, st>>>(w, g, n, lr, clip, ns);
+    launch_pdl(k_sgd_scalar<SCALED>, dim3(grid_for(n, 256)), dim3(256), 0, st, w, g, n, lr, clip, ns);
   return cudaGetLastError();
 }
 
@@ -332,7 +338,7 @@ uint64_t mt_sumsq_blocks(const MtTensor* t, int count) { return mt_blocks(t, cou
 
 cudaError_t launch_norm_scale_from_parts(const double* partials, int nparts, float max_norm, float* ns,
                                          cudaStream_t st) {
-  k_norm_scale<<<1, 1024, 0, st>>>(partials, nparts, max_norm, ns);
+  launch_pdl(k_norm_scale, dim3(1), dim3(1024), 0, st, partials, nparts, max_norm, ns);
   return cudaGetLastError();
 }
 

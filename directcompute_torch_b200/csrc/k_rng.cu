@@ -30,6 +30,7 @@ DCT_DEV float u24(uint32_t x) { return (float)(x >> 8) * 5.9604644775390625e-08f
 
 __global__ void __launch_bounds__(256) k_fill(float* y, uint64_t n, uint64_t seed, uint64_t offset, int dist,
                                               float lo, float hi) {
+  pdl_entry();
   const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
   const uint64_t groups = (n + 3) / 4;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -68,6 +69,7 @@ __global__ void __launch_bounds__(256) k_fill(float* y, uint64_t n, uint64_t see
 }
 
 __global__ void k_scatter(float* x, const int64_t* idx, const float* vals, uint64_t k) {
+  pdl_entry();
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < k; i += stride) x[idx[i]] = vals[i];
 }
@@ -77,13 +79,13 @@ __global__ void k_scatter(float* x, const int64_t* idx, const float* vals, uint6
 cudaError_t launch_fill_random(float* y, uint64_t n, uint64_t seed, uint64_t offset, int dist, float lo, float hi,
                                cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  k_fill<<<grid_for((n + 3) / 4, 256), 256, 0, st>>>(y, n, seed, offset, dist, lo, hi);
+  launch_pdl(k_fill, dim3(grid_for((n + 3) / 4, 256)), dim3(256), 0, st, y, n, seed, offset, dist, lo, hi);
   return cudaGetLastError();
 }
 
 cudaError_t launch_scatter_values(float* x, const int64_t* idx, const float* vals, uint64_t k, cudaStream_t st) {
   if (k == 0) return cudaSuccess;
-  k_scatter<<<grid_for(k, 256), 256, 0, st>>>(x, idx, vals, k);
+  launch_pdl(k_scatter, dim3(grid_for(k, 256)), dim3(256), 0, st, x, idx, vals, k);
   return cudaGetLastError();
 }
 

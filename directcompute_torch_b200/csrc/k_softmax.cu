@@ -83,6 +83,7 @@ DCT_DEV float grad_of(float p, float oh, const RowCtx& c) {
 // One warp per row, VPL float4 (VEC) or VPL*4 scalars per lane held in registers.
 template <int VPL, bool VEC>
 __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_constant__ RowCtx c) {
+  pdl_entry();
   __shared__ double wsum[kSmWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double block_loss = 0.0;
@@ -195,6 +196,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_con
 template <int VPL, int WPB, bool POW2>
 __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_constant__ RowCtx c, uint32_t buf_bytes,
                                                              uint32_t* err) {
+  pdl_entry();
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double wsum[WPB];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -357,6 +359,7 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
 
 // Rows longer than 2048: one block per row, three streaming passes (L2 keeps the row).
 __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_constant__ RowCtx c) {
+  pdl_entry();
   __shared__ double shd[32];
   __shared__ float shf[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -407,6 +410,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_co
 }
 
 __global__ void k_loss_final(const double* part, int nparts, double div, float* loss, double* raw) {
+  pdl_entry();
   __shared__ double sh[32];
   double acc = 0.0;
   for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
@@ -492,7 +496,7 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
                                (int)(128 + 2 * WPB * 8192));                                                   \
       attr_set = (e == cudaSuccess);                                                                          \
     }                                                                                                         \
-    if (e == cudaSuccess) k_softmax_ce_tma<VPL, WPB, P2><<<blocks_t, WPB * 32, smem, st>>>(c, buf_bytes, a.err); \
+    if (e == cudaSuccess) launch_pdl(k_softmax_ce_tma<VPL, WPB, P2>, dim3(blocks_t), dim3(WPB * 32), smem, st, c, buf_bytes, a.err); \
   } while (0)
 #define DCT_SM_TMA(VPL, WPB)                                                                                  \
   do {                                                                                                        \
@@ -508,31 +512,31 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess || !c.want_loss) return e;
-    k_loss_final<<<1, 1024, 0, st>>>(c.part, blocks_t, a.loss_div, a.loss, a.loss_partial);
+    launch_pdl(k_loss_final, dim3(1), dim3(1024), 0, st, c.part, blocks_t, a.loss_div, a.loss, a.loss_partial);
     return cudaGetLastError();
   }
   const int blocks = softmax_blocks(a.rows, a.K);
   if (K <= 128) {
-    if (vec) k_softmax_ce_warp<1, true><<<blocks, kSmThreads, 0, st>>>(c);
-    else k_softmax_ce_warp<1, false><<<blocks, kSmThreads, 0, st>>>(c);
+    if (vec) launch_pdl(k_softmax_ce_warp<1, true>, dim3(blocks), dim3(kSmThreads), 0, st, c);
+    else launch_pdl(k_softmax_ce_warp<1, false>, dim3(blocks), dim3(kSmThreads), 0, st, c);
   } else if (K <= 256) {
-    if (vec) k_softmax_ce_warp<2, true><<<blocks, kSmThreads, 0, st>>>(c);
-    else k_softmax_ce_warp<2, false><<<blocks, kSmThreads, 0, st>>>(c);
+    if (vec) launch_pdl(k_softmax_ce_warp<2, true>, dim3(blocks), dim3(kSmThreads), 0, st, c);
+    else launch_pdl(k_softmax_ce_warp<2, false>, dim3(blocks), dim3(kSmThreads), 0, st, c);
   } else if (K <= 512) {
-    if (vec) k_softmax_ce_warp<4, true><<<blocks, kSmThreads, 0, st>>>(c);
-    else k_softmax_ce_warp<4, false><<<blocks, kSmThreads, 0, st>>>(c);
+    if (vec) launch_pdl(k_softmax_ce_warp<4, true>, dim3(blocks), dim3(kSmThreads), 0, st, c);
+    else launch_pdl(k_softmax_ce_warp<4, false>, dim3(blocks), dim3(kSmThreads), 0, st, c);
   } else if (K <= 1024) {
-    if (vec) k_softmax_ce_warp<8, true><<<blocks, kSmThreads, 0, st>>>(c);
-    else k_softmax_ce_warp<8, false><<<blocks, kSmThreads, 0, st>>>(c);
+    if (vec) launch_pdl(k_softmax_ce_warp<8, true>, dim3(blocks), dim3(kSmThreads), 0, st, c);
+    else launch_pdl(k_softmax_ce_warp<8, false>, dim3(blocks), dim3(kSmThreads), 0, st, c);
   } else if (K <= 2048) {
-    if (vec) k_softmax_ce_warp<16, true><<<blocks, kSmThreads, 0, st>>>(c);
-    else k_softmax_ce_warp<16, false><<<blocks, kSmThreads, 0, st>>>(c);
+    if (vec) launch_pdl(k_softmax_ce_warp<16, true>, dim3(blocks), dim3(kSmThreads), 0, st, c);
+    else launch_pdl(k_softmax_ce_warp<16, false>, dim3(blocks), dim3(kSmThreads), 0, st, c);
   } else {
-    k_softmax_ce_block<<<blocks, kSmThreads, 0, st>>>(c);
+    launch_pdl(k_softmax_ce_block, dim3(blocks), dim3(kSmThreads), 0, st, c);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !c.want_loss) return e;
-  k_loss_final<<<1, 1024, 0, st>>>(c.part, blocks, a.loss_div, a.loss, a.loss_partial);
+  launch_pdl(k_loss_final, dim3(1), dim3(1024), 0, st, c.part, blocks, a.loss_div, a.loss, a.loss_partial);
   return cudaGetLastError();
 }
 
@@ -544,6 +548,7 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
 __global__ void __launch_bounds__(256) k_argmax_correct(const float* __restrict__ logits,
                                                         const float* __restrict__ labels, uint32_t rows, uint32_t K,
                                                         uint32_t* counter) {
+  pdl_entry();
   __shared__ uint32_t sc[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t hits = 0;
@@ -583,7 +588,7 @@ cudaError_t launch_argmax_correct(const float* logits, const float* labels, uint
   uint32_t blocks = (rows + 7) / 8;
   const uint32_t cap = (uint32_t)d.sm_count * 8;
   if (blocks > cap) blocks = cap;
-  k_argmax_correct<<<blocks, 256, 0, st>>>(logits, labels, rows, K, counter);
+  launch_pdl(k_argmax_correct, dim3(blocks), dim3(256), 0, st, logits, labels, rows, K, counter);
   return cudaGetLastError();
 }
 
