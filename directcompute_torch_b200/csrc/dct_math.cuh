@@ -49,14 +49,14 @@ static __device__ __align__(256) const float2 kExp2Tab[32] = {
 };
 
 // sigmoid to within 1.5 ulp of the exact value over the whole float range (the
-// ops' bar is 2 ulp), about 31 instructions and no branch.  `tab` is kExp2Tab
+// ops' bar is 2 ulp), about 30 instructions and no branch.  `tab` is kExp2Tab
 // or a copy of it (in shared memory for the streaming kernel).
 //  * e = exp(-|x|) by Tang's table-driven method (ACM TOMS 15(2), 1989):
 //    |x| is clamped to 104 (e^-104 rounds to 0; NaN stays NaN); k =
 //    rint(-|x| * 32/ln2) by the 1.5*2^23 rounding trick; r = -|x| - k*ln2/32 with
 //    ln2/32 split in two parts (the first has 12 significant bits, so k * part1
-//    is exact for |k| < 2^13); exp(r) - 1 = r + r^2 (1/2 + r/6 + r^2/24) on
-//    |r| <= ln2/64 (truncation below 2^-40); e = 2^(k>>5) * (T_hi + (T_hi p +
+//    is exact for |k| < 2^13); exp(r) - 1 = r + r^2 (1/2 + r/6) on |r| <= ln2/64
+//    (the omitted r^4/24 is below 2^-30.7, under 0.01 ulp); e = 2^(k>>5) * (T_hi + (T_hi p +
 //    T_lo)), with the power of two applied as 2^(m+64) (exact: the product stays
 //    normal) and then 2^-64 (one rounding, into the subnormals for |x| > 87.3).
 //  * sigmoid = n / (1 + e), n = 1 for x >= 0 and e for x < 0: the denominator
@@ -71,7 +71,7 @@ DCT_DEV float sigmoid_tab(float x, const float2* tab) {
   const int k = __float_as_int(kb) - __float_as_int(kMagic);     // in [-4802, 0] (NaN: any int)
   float r = __fmaf_rn(-kf, 0x1.62ep-6f, -a);           // exact
   r = __fmaf_rn(-kf, 0x1.0bfbe8p-20f, r);
-  const float w = __fmaf_rn(__fmaf_rn(r, 0x1.555556p-5f, 0x1.555556p-3f), r, 0.5f);   // 1/2 + r/6 + r^2/24
+  const float w = __fmaf_rn(r, 0x1.555556p-3f, 0.5f);  // 1/2 + r/6
   const float p = __fmaf_rn(w, __fmul_rn(r, r), r);    // exp(r) - 1
   const float2 t2 = tab[k & 31];
   const float ef = __fadd_rn(t2.x, __fmaf_rn(t2.x, p, t2.y));

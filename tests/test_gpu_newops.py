@@ -84,13 +84,16 @@ def test_unary_2ulp(dev, op, n):
 
 
 def test_sigmoid_whole_range(dev):
-    """Every binade of the float range, the subnormal-result tail (-87.3 > x > -104),
-    +-inf, NaN and signed zeros: <= 2 ulp against the float64 result rounded (the
-    result's subnormal spacing counts as its ulp)."""
+    """Every binade of the float range, 5M dense samples in [-20, 20], the
+    subnormal-result tail (-87.3 > x > -104), +-inf, NaN and signed zeros: <= 2 ulp
+    against the float64 result rounded (the result's subnormal spacing counts as its
+    ulp)."""
     r = np.random.default_rng(77)
     parts = [np.float32(2.0) ** np.arange(-149, 128, dtype=np.float64).astype(np.float32)]
     parts.append(r.uniform(-110, -80, 1 << 18).astype(np.float32))
     parts.append(r.uniform(80, 110, 1 << 12).astype(np.float32))
+    parts.append(r.uniform(-20, 20, 1 << 22).astype(np.float32))        # dense where sigmoid is not 0 / 1
+    parts.append((3 * r.standard_normal(1 << 20)).astype(np.float32))
     parts.append(np.array([0.0, -0.0, np.inf, -np.inf, np.nan, -87.33655, -103.97, -104.0, 104.0, -1e30, 3e38],
                           np.float32))
     x = np.concatenate([parts[0], -parts[0]] + parts[1:]).astype(np.float32)
