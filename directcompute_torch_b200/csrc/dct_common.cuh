@@ -36,8 +36,8 @@ uint32_t* device_error_word();   // defined in runtime.cu
 // Zeroed device words for kernels that raise a flag another kernel of the same
 // stream consumes and clears (null before InitEngine).  Every kernel that
 // sets one leaves it zero when the pair is done.
-constexpr uint32_t kReduceCounters = 65536;
-uint32_t* reduce_counters();     // defined in runtime.cu
+constexpr uint32_t kDeviceFlags = 64;
+uint32_t* device_flags();        // defined in runtime.cu
 
 // Blocks for a grid-stride kernel of `threads`-thread blocks covering `work`
 // independent items: enough to fill every SM `waves` times, never more than

@@ -72,7 +72,7 @@ struct Engine {
   float* host_small = nullptr;    // pinned 64-byte staging for scalar readbacks
   uint32_t* dev_err_host = nullptr;   // mapped error word written by device code
   uint32_t* dev_err_dev = nullptr;
-  uint32_t* counters = nullptr;       // kReduceCounters zeroed flag words (maxpool fix-up)
+  uint32_t* flags = nullptr;          // kDeviceFlags zeroed device words (the maxpool fix-up flag)
   char name[128] = {0};
   // error state
   int err_code = 0;
@@ -112,7 +112,7 @@ static void set_error(int code, const char* fmt, ...) {
 }
 
 uint32_t* device_error_word() { return g.dev_err_dev; }
-uint32_t* reduce_counters() { return g.init ? g.counters : nullptr; }
+uint32_t* device_flags() { return g.init ? g.flags : nullptr; }
 
 // error recording for entry points that live outside this file
 void note_error(int code, const char* msg) {
@@ -327,8 +327,8 @@ static bool init_engine() {
   *g.dev_err_host = 0;
   if (!cuda_ok(cudaHostGetDevicePointer((void**)&g.dev_err_dev, g.dev_err_host, 0), "InitEngine(error word)"))
     return false;
-  if (!cuda_ok(cudaMalloc(&g.counters, kReduceCounters * sizeof(uint32_t)), "InitEngine(counters)")) return false;
-  if (!cuda_ok(cudaMemset(g.counters, 0, kReduceCounters * sizeof(uint32_t)), "InitEngine(counters)")) return false;
+  if (!cuda_ok(cudaMalloc(&g.flags, kDeviceFlags * sizeof(uint32_t)), "InitEngine(flags)")) return false;
+  if (!cuda_ok(cudaMemset(g.flags, 0, kDeviceFlags * sizeof(uint32_t)), "InitEngine(flags)")) return false;
   g.init = true;
   return true;
 }
@@ -1308,10 +1308,10 @@ DCT_API void* MaxPoolBackwardFused(void* grad_output, void* indices, uint32_t ba
     const uint32_t* gm = bi->pool_geom;
     const PoolShape gs{gm[0], gm[1], gm[2], gm[3], gm[4], gm[5], gm[6]};
     const bool gather = bi->has_pool_geom && gs.bc == bc && gs.outH == outH && gs.outW == outW && gs.s >= gs.p &&
-                        (uint64_t)gs.bc * gs.inH * gs.inW == x_size && reduce_counters() != nullptr;
+                        (uint64_t)gs.bc * gs.inH * gs.inW == x_size && device_flags() != nullptr;
     const uint32_t* ip = reinterpret_cast<const uint32_t*>(bi->d);
     if (gather) {
-      e = launch_maxpool_backward_gather(bg->d, ip, dx->d, gs, reduce_counters() + kReduceCounters - 1, g.stream);
+      e = launch_maxpool_backward_gather(bg->d, ip, dx->d, gs, device_flags(), g.stream);
     } else {
       e = cudaMemsetAsync(dx->d, 0, (size_t)x_size * sizeof(float), g.stream);
       if (e == cudaSuccess)
