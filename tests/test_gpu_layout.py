@@ -319,3 +319,97 @@ def test_layout_shaders_refuse_small_buffers(dev):
     assert dev.error()[0] != 0
     dev.clear_error()
     dev.free(hx, hy)
+
+
+def test_layout_refuses_index_space_past_32_bits(dev):
+    """The shaders index with 32-bit uint; a dispatch whose index space passes 2^32 is
+    refused (DCT_ERR_ARG) and writes nothing."""
+    hx, hy = dev.buf(np.arange(64, dtype=np.float32)), dev.empty(64, fill=4.0)
+    dev.run("upsample", [hx], [hy], (1, 1, 1), [65536, 65536, 1, 1, 1, 1, 1, 1])
+    assert dev.error()[0] == 4                                      # DCT_ERR_ARG
+    dev.clear_error()
+    dev.run("conv_grad_reshape", [hx], [hy], (1, 1, 1), [65536, 0, 0, 0, 65536, 0, 0, 1, 1])
+    assert dev.error()[0] == 4
+    dev.clear_error()
+    assert np.all(dev.read(hy) == 4.0)
+    dev.free(hx, hy)
+
+
+def test_maxpool_fused_backward_bad_inputs(dev):
+    """A dead index handle or a short gradient buffer: a zeroed dInput and an error,
+    never an overrun."""
+    B, C, H, W = 1, 2, 8, 8
+    hx = dev.buf(np.random.default_rng(3).standard_normal(B * C * H * W).astype(np.float32))
+    out, hidx = _fused_forward(dev, hx, B, C, H, W, 2, 2)
+    small = dev.buf(np.ones(5, np.float32))                          # needs 2*4*4 = 32
+    dx = dev.lib.MaxPoolBackwardFused(small, hidx, B, C, 4, 4, B * C * H * W)
+    assert dx and dev.error()[0] == 3                                # DCT_ERR_SIZE
+    assert np.all(dev.read(dx) == 0.0)
+    dev.clear_error()
+    dx2 = dev.lib.MaxPoolBackwardFused(out, hidx, B, C, 4, 4, B * C * H * W)   # hidx was released above
+    assert dx2 and dev.error()[0] == 2                               # DCT_ERR_HANDLE
+    assert np.all(dev.read(dx2) == 0.0)
+    dev.clear_error()
+    dev.free(hx, out, small, dx, dx2)
+
+
+def test_layout_sequence_graph_replay_matches_eager(dev):
+    """upsample -> concat_insert -> maxpool_forward -> slice as one RunSequence list:
+    replayed as a CUDA graph (captured on the second call) it gives the eager bits."""
+    import os
+    from directcompute_torch_b200._abi import SeqCmd
+    lib = dev.lib
+    for n in ("upsample", "concat_insert", "maxpool_forward", "slice"):
+        lib.CompileShader(n.encode(), "")
+
+    def cmd(name, srvs, uavs, groups, words):
+        c = SeqCmd()
+        c.shader = lib.ResolveShader(name.encode())
+        assert c.shader, name
+        for i, h in enumerate(srvs):
+            c.srvs[i] = h
+        for i, h in enumerate(uavs):
+            c.uavs[i] = h
+        c.srvCount, c.uavCount = len(srvs), len(uavs)
+        c.threads[0], c.threads[1], c.threads[2] = groups
+        cb = np.array(words, np.uint32).tobytes()
+        ctypes.memmove(c.cbData, cb, len(cb))
+        c.cbSize = len(cb)
+        return c
+
+    rng = np.random.default_rng(12)
+    B, C, H, W = 2, 3, 8, 16
+    x = rng.standard_normal(B * C * H * W).astype(np.float32)
+    z = rng.standard_normal(B * C * 4 * H * W).astype(np.float32)
+    outs = {}
+    for graph in (False, True):
+        h = {"x": dev.buf(x), "z": dev.buf(z), "u": dev.empty(B * C * 4 * H * W), "cat": dev.empty(2 * B * C * 4 * H * W),
+             "po": dev.empty(2 * B * C * H * W), "pi": dev.empty(2 * B * C * H * W), "sl": dev.empty(B * C * 4 * H * W)}
+        S_ = 4 * H * W
+        cmds = [
+            cmd("upsample", [h["x"]], [h["u"]], ((B * C * S_ + 255) // 256, 1, 1), [B, C, H, W, 2 * H, 2 * W, 2, 2]),
+            cmd("concat_insert", [h["u"]], [h["cat"]], ((B * C * S_ + 255) // 256, 1, 1), [B, C, S_, 2 * C, 0]),
+            cmd("concat_insert", [h["z"]], [h["cat"]], ((B * C * S_ + 255) // 256, 1, 1), [B, C, S_, 2 * C, C]),
+            cmd("maxpool_forward", [h["cat"]], [h["po"], h["pi"]], ((W + 15) // 16, (H + 15) // 16, 2 * B * C),
+                [B, 2 * C, 2 * H, 2 * W, 2, 2, H, W]),
+            cmd("slice", [h["cat"]], [h["sl"]], ((B * C * S_ + 255) // 256, 1, 1), [B, C, S_, 2 * C, C]),
+        ]
+        arr = (SeqCmd * len(cmds))(*cmds)
+        os.environ["DCT_SEQ_GRAPH"] = "1" if graph else "0"
+        try:
+            for _ in range(4):
+                lib.RunSequence(ctypes.cast(arr, ctypes.c_void_p), len(cmds))
+            dev.sync()
+        finally:
+            os.environ.pop("DCT_SEQ_GRAPH", None)
+        outs[graph] = {k: dev.read(v) for k, v in h.items()}
+        dev.free(*h.values())
+    for k in outs[False]:
+        assert np.array_equal(outs[True][k].view(np.uint32), outs[False][k].view(np.uint32)), k
+    u = S.upsample(x, B, C, H, W, 2 * H, 2 * W, 2, 2)
+    assert np.array_equal(outs[True]["sl"], z)
+    cat = np.empty(2 * B * C * 4 * H * W, np.float32)
+    S.concat_insert(cat, u, B, C, 4 * H * W, 2 * C, 0)
+    S.concat_insert(cat, z, B, C, 4 * H * W, 2 * C, C)
+    _, v, i = S.maxpool_forward(cat, B, 2 * C, 2 * H, 2 * W, 2, 2, H, W)
+    assert np.array_equal(outs[True]["po"], v) and np.array_equal(outs[True]["pi"].view(np.uint32), i)
