@@ -435,14 +435,21 @@ int softmax_blocks(uint32_t rows, uint32_t K) {
 
 }  // namespace
 
-// blocks of the TMA-staged kernel: up to 3 per SM (shared memory bound), one
+// Shared-memory stage of one row (16-byte multiple, the bulk copy's rule) and
+// warps per block of the TMA-staged kernel.  For rows up to 1024 floats, 7
+// warps per block let 4 blocks (28 warps) fit an SM's 228 KB with two stages
+// per warp; 8 warps fit only 3 blocks (24 warps).
+static uint32_t tma_stage_bytes(uint32_t K) { return ((K * 4u) + 15u) & ~15u; }
+static int tma_warps(uint32_t K) { return tma_stage_bytes(K) <= 4096 ? 7 : 4; }
+
+// blocks of the TMA-staged kernel: up to 4 per SM (shared memory bound), one
 // row per warp per step
 int tma_blocks(uint32_t rows, uint32_t K) {
-  const uint32_t buf_bytes = ((K * 4u) + 127u) & ~127u;
-  const int wpb = buf_bytes <= 4096 ? 8 : 4;
+  const uint32_t buf_bytes = tma_stage_bytes(K);
+  const int wpb = tma_warps(K);
   const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
   const DevInfo& di = dev_info();
-  const int per_sm = std::min<int>(3, std::max<int>(1, (int)((228u * 1024u) / (smem + 1024))));
+  const int per_sm = std::min<int>(4, std::max<int>(1, (int)((228u * 1024u) / (smem + 1024))));
   const uint64_t need = ((uint64_t)rows + wpb - 1) / wpb;
   const uint64_t cap = (uint64_t)di.sm_count * per_sm;
   return (int)std::max<uint64_t>(1, std::min(need, cap));
@@ -483,8 +490,8 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
                    (!a.dlogits || aligned16_h(a.dlogits));
   const uint32_t K = a.K;
   if (vec && !a.logprobs && K <= 2048 && K >= 128) {
-    const uint32_t buf_bytes = ((K * 4u) + 127u) & ~127u;
-    const int wpb = buf_bytes <= 4096 ? 8 : 4;
+    const uint32_t buf_bytes = tma_stage_bytes(K);
+    const int wpb = tma_warps(K);
     const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
     const int blocks_t = tma_blocks(a.rows, K);
     cudaError_t e = cudaSuccess;
@@ -503,9 +510,9 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
     if (c.grad_div_pow2) DCT_SM_TMA2(VPL, WPB, true);                                                         \
     else DCT_SM_TMA2(VPL, WPB, false);                                                                        \
   } while (0)
-    if (K <= 256) DCT_SM_TMA(2, 8);
-    else if (K <= 512) DCT_SM_TMA(4, 8);
-    else if (K <= 1024) DCT_SM_TMA(8, 8);
+    if (K <= 256) DCT_SM_TMA(2, 7);
+    else if (K <= 512) DCT_SM_TMA(4, 7);
+    else if (K <= 1024) DCT_SM_TMA(8, 7);
     else DCT_SM_TMA(16, 4);
 #undef DCT_SM_TMA
 #undef DCT_SM_TMA2
