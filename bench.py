@@ -456,8 +456,11 @@ def _c1(L, rank, measure, res):
     def graph():
         lib.RunSequence(C.cast(arr, C.c_void_p), len(cmds))
     nbytes = 4 * (3 * M * N + 2 * N + 1) + 4 * (3 * M * N + N)      # SURVEY C1 fwd + bwd algorithmic bytes
-    measure("c1_dense_step_eager", nbytes, eager, len(cmds) + 1, it=200)
-    measure("c1_dense_step_graph", nbytes, graph, len(cmds) + 1, it=200)
+    # kernels per step: bias_relu, relu_grad and grad_accum one each; each column sum
+    # (bias_grad) and the full sum two (partials, then their fold)
+    launches = 9
+    measure("c1_dense_step_eager", nbytes, eager, launches, it=200)
+    measure("c1_dense_step_graph", nbytes, graph, launches, it=200)
     for k in ("c1_dense_step_eager", "c1_dense_step_graph"):
         if k in res:
             res[k]["us_per_step"] = round(res[k]["ms"] * 1e3, 2)
