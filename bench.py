@@ -644,8 +644,8 @@ def c2_config(world: int) -> dict:
             "step_bytes": step_bytes}
 
 
-def reference_arm(args, ranks: Ranks):
-    if ranks.rank != 0:
+def reference_arm(args, rank: int):
+    if rank != 0:
         return 0
     threads = os.cpu_count() or 1
     # one step = one pass of the bounded C2 sample (1/8 of the rows); W + K passes
@@ -674,11 +674,11 @@ def main():
     ap.add_argument("--only", default=None, help="profiling mode: run one C2 op (e.g. c2_rowbcast_add) "
                     "--warmup + --steps times and print its timing only")
     args = ap.parse_args()
-    ranks = Ranks(args.gpus)
     if args.impl == "reference":
-        rc = reference_arm(args, ranks)
-        ranks.close()
-        return rc
+        # the CPU arm needs no GPU and no process group: rank 0 alone runs it,
+        # the other ranks of a torchrun launch exit 0 at once
+        return reference_arm(args, int(os.environ.get("RANK", "0")))
+    ranks = Ranks(args.gpus)
     os.environ.setdefault("DCT_DEVICE", str(ranks.local))
     L = Lib()
     if args.only and not args.only.startswith("c2_"):
