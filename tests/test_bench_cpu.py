@@ -1,0 +1,51 @@
+"""bench.py's reference arm on CPU: the JSON line the driver reads (no GPU needed).
+
+`bench.py --impl reference` times the reference's CPU arithmetic for the C2
+workload (the NumPy restatement, as the reference's own CPU path is NumPy).
+Launched alone or by torchrun, rank 0 prints exactly one line with the
+contract's keys and every rank exits 0.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+KEYS = {"metric", "impl", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+        "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"}
+
+
+def _lines(out: str):
+    return [json.loads(s) for s in out.splitlines() if s.startswith("{")]
+
+
+def _check(line, n_gpus):
+    assert KEYS <= set(line), KEYS - set(line)
+    assert line["impl"] == "reference" and line["n_gpus"] == n_gpus and line["value"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert "workload" in line["config"]
+
+
+def test_reference_arm_single_process():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = _lines(r.stdout)
+    assert len(lines) == 1
+    _check(lines[0], 1)
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    pytest.importorskip("torch")
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29637", "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--steps", "1", "--warmup", "0"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = _lines(r.stdout)
+    assert len(lines) == 1
+    _check(lines[0], 2)
