@@ -273,13 +273,21 @@ Hdr make_hdr(uint32_t off, std::initializer_list<unsigned long long> v) {
   return h;
 }
 
-__global__ void __launch_bounds__(256) k_peer_put(const unsigned long long* __restrict__ rec, Hdr h,
-                                                  void* const* __restrict__ bases, uint64_t slot_off,
-                                                  uint64_t flag_off, unsigned long long epoch) {
-  grid_dep_launch();                                   // the wait kernel may be scheduled now
-  grid_dep_wait();                                     // rec comes from the previous kernel
-  // block p writes this rank's record (device part, then the header words) into
-  // rank p's slot, then p's flag
+// The whole gather over peer memory, one kernel.  Block q < world writes this
+// rank's record into rank q's slot (the device part rec[0, h.off), then the
+// header words), fences at system scope and stores the epoch into rank q's
+// flag for this rank (release).  Block 0 then waits, bounded by %globaltimer,
+// for every rank's flag here, and for axis records checks that the shards
+// tile the axis.  The kernel's blocks (world <= 256) are all resident before a
+// dependent kernel can be scheduled, and block 0 waits only on other GPUs.
+__global__ void __launch_bounds__(256) k_peer_put_wait(const unsigned long long* __restrict__ rec, Hdr h,
+                                                       void* const* __restrict__ bases, uint64_t slot_off,
+                                                       uint64_t flag_off, unsigned long long epoch,
+                                                       const unsigned long long* flags, int world,
+                                                       unsigned long long timeout_ns, uint32_t* err,
+                                                       const unsigned long long* slots, uint64_t stride,
+                                                       int64_t axis_nout) {
+  pdl_entry();                                         // rec comes from the previous kernel
   unsigned char* base = static_cast<unsigned char*>(bases[blockIdx.x]);
   unsigned long long* dst = reinterpret_cast<unsigned long long*>(base + slot_off);
   const uint64_t n = h.off;
@@ -295,20 +303,8 @@ __global__ void __launch_bounds__(256) k_peer_put(const unsigned long long* __re
     unsigned long long* flag = reinterpret_cast<unsigned long long*>(base + flag_off);
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(epoch) : "memory");
   }
-}
-
-// header words written into a local record (the NCCL path)
-__global__ void k_put_u64(unsigned long long* rec, Hdr h) {
-  if (threadIdx.x < h.n) rec[h.off + threadIdx.x] = h.v[threadIdx.x];
-}
-
-__global__ void k_peer_wait(const unsigned long long* flags, int world, unsigned long long epoch,
-                            unsigned long long timeout_ns, uint32_t* err, const unsigned long long* slots,
-                            uint64_t stride, int64_t axis_nout) {
-  grid_dep_launch();
-  grid_dep_wait();
-  const int q = threadIdx.x;
-  if (q < world) {
+  if (blockIdx.x != 0) return;
+  for (int q = threadIdx.x; q < world; q += blockDim.x) {
     unsigned long long t0, t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     for (;;) {
@@ -339,6 +335,11 @@ __global__ void k_peer_wait(const unsigned long long* flags, int world, unsigned
   }
 }
 
+// header words written into a local record (the NCCL path)
+__global__ void k_put_u64(unsigned long long* rec, Hdr h) {
+  if (threadIdx.x < h.n) rec[h.off + threadIdx.x] = h.v[threadIdx.x];
+}
+
 // Gather every rank's record: the device part rec[0, h.off) plus the header
 // words h; *all = the records, record q at *all + q * *stride.  axis_nout >= 0
 // also checks axis-reduction shard headers (at word axis_nout of each record).
@@ -351,15 +352,13 @@ bool exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* s
     const int par = (int)(ep & 1);
     unsigned char* base = static_cast<unsigned char*>(D.region);
     const unsigned long long* slots = reinterpret_cast<const unsigned long long*>(base + slot_off(par, 0));
-    cudaError_t e = launch_pdl(k_peer_put, dim3(D.world), dim3(256), 0, st,
-                               static_cast<const unsigned long long*>(rec), h, (void* const*)D.peer_dev,
-                               (uint64_t)slot_off(par, D.rank), (uint64_t)flag_off(par, D.rank), ep);
     const double lim = D.timeout_s < 30.0 ? D.timeout_s : 30.0;
-    if (e == cudaSuccess)
-      e = launch_pdl(k_peer_wait, dim3(1), dim3(32 * ((D.world + 31) / 32)), 0, st,
-                     reinterpret_cast<const unsigned long long*>(base + flag_off(par, 0)), D.world, ep,
-                     (unsigned long long)(lim * 1e9), device_error_word(), slots, (uint64_t)(D.slot_bytes / 8),
-                     (int64_t)axis_nout);
+    const cudaError_t e = launch_pdl(
+        k_peer_put_wait, dim3(D.world), dim3(256), 0, st, static_cast<const unsigned long long*>(rec), h,
+        (void* const*)D.peer_dev, (uint64_t)slot_off(par, D.rank), (uint64_t)flag_off(par, D.rank), ep,
+        reinterpret_cast<const unsigned long long*>(base + flag_off(par, 0)), D.world,
+        (unsigned long long)(lim * 1e9), device_error_word(), slots, (uint64_t)(D.slot_bytes / 8),
+        (int64_t)axis_nout);
     *all = slots;
     *stride = D.slot_bytes / 8;
     return rt_cuda_ok(e, where);
@@ -743,6 +742,10 @@ DCT_API int dct_dist_reduce(int op, void* x, uint64_t outer, uint64_t len, uint6
                (!bo || bo->count >= nout) && (!bi || bi->count >= nout) && len_offset + len <= len_total;
   unsigned long long* send = (unsigned long long*)D.send;
   cudaStream_t st = rt_stream();
+  // The packed partials are staged in the local record and cross NVLink in the
+  // put kernel's 16-byte stores.  (Storing them into every peer's slot from
+  // the emitting kernel itself was slower: 8-byte scattered remote stores and
+  // a system-scope fence in every thread of the grid.)
   if (valid && !rt_ensure_ws(reduce3d_ws_bytes(op_run, outer, len, inner))) return DCT_ERR_CUDA;
   if (valid && !rt_cuda_ok(launch_reduce3d_packed(op_run, bx->d, outer, len, inner, (int32_t)len_offset, send,
                                                   rt_ws(), st), W))
