@@ -311,7 +311,7 @@ static bool init_engine() {
   g.info.max_threads_per_sm = p.maxThreadsPerMultiProcessor;
   g.info.smem_optin = p.sharedMemPerBlockOptin;
   g.info.total_mem = p.totalGlobalMem;
-  snprintf(g.name, sizeof(g.name), "%s", p.name);
+  snprintf(g.name, sizeof(g.name), "%.127s", p.name);   // GPUInfo::description holds 128 bytes
   if (!cuda_ok(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), "InitEngine(stream)")) return false;
   cudaEventCreate(&g.ev0);
   cudaEventCreate(&g.ev1);

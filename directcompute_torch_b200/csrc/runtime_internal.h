@@ -16,8 +16,8 @@ struct Buffer {
   bool owned;              // false: wraps caller memory (dct_wrap_device_ptr)
   // an index buffer made by MaxPoolForwardFused: its pooling geometry (bc, inH,
   // inW, pool, stride, outH, outW); cleared whenever the buffer is handed out
-  bool has_pool_geom;
-  uint32_t pool_geom[7];
+  bool has_pool_geom = false;
+  uint32_t pool_geom[7] = {};
 };
 
 std::recursive_mutex& rt_mutex();
