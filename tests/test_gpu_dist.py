@@ -275,9 +275,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worldn_worker(rank, world, port, q):
+def _worldn_worker(rank, world, port, q, transport="peer"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), DCT_DEVICE=str(rank),
-                      NCCL_NVLS_ENABLE="0")
+                      NCCL_NVLS_ENABLE="0", DCT_PEER_EXCHANGE="0" if transport == "nccl" else "1")
     try:
         import torch  # noqa: F401  (loads PyTorch's NCCL first)
         import torch.distributed as td
@@ -378,9 +378,11 @@ def _worldn_worker(rank, world, port, q):
         q.put((rank, False, traceback.format_exc()))
 
 
-def test_worldn_sharded_ops_match_unsharded_oracle():
-    """Every visible GPU (2 to 8) as one rank: the sharded ops over the peer-memory
-    exchange match the oracle on the unsharded tensors."""
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_worldn_sharded_ops_match_unsharded_oracle(transport):
+    """Every visible GPU (2 to 8) as one rank: the sharded ops, over the peer-memory
+    exchange and over the NCCL all-gather fallback, match the oracle on the unsharded
+    tensors."""
     import torch
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
@@ -388,7 +390,7 @@ def test_worldn_sharded_ops_match_unsharded_oracle():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worldn_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worldn_worker, args=(r, world, port, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -405,6 +407,7 @@ def test_worldn_sharded_ops_match_unsharded_oracle():
         ok, e = res[r]
         assert ok, e
         print(f"rank {r}: {e}")
+        assert e["peer_exchange"] == (transport == "peer"), (r, transport)
         for k in ("max", "argmax", "min", "argmin", "full_max", "dlogits", "bn_y", "bn_dx", "allreduce"):
             assert e[k] == 0, (r, k, e[k])
         for k in ("sum", "mean", "full_sum", "loss", "bn_mean", "bn_var", "bn_running", "bn_dgamma", "bn_dbeta"):
