@@ -114,3 +114,40 @@ def test_graph_not_replayed_on_other_buffers_or_moved_workspace(dev):
     assert np.array_equal(y3.view(np.uint32), y_ref.view(np.uint32))
     assert dev.error()[0] == 0, dev.error()
     dev.free(x2, big, hb, *h.values())
+
+
+def test_run_sequence_with_sgd_equals_sequence_then_sgdbatch(dev):
+    """RunSequenceWithSGD (engine.cpp:958-977): the command list, then one SGD step over
+    the (param, grad) pairs, equals RunSequence followed by SGDBatch bit for bit."""
+    dev.clear_error()
+    lib = dev.lib
+    r = np.random.default_rng(61)
+    w0 = r.standard_normal(784).astype(np.float32)
+    outs = []
+    for fused in (False, True):
+        h, arr, x, b = _c1_sequence(dev)
+        hw = dev.buf(w0)
+        P = (ctypes.c_void_p * 1)(hw)
+        G = (ctypes.c_void_p * 1)(h["db"])
+        Sz = (ctypes.c_uint * 1)(784)
+        os.environ["DCT_SEQ_GRAPH"] = "1"
+        try:
+            for _ in range(3):
+                if fused:
+                    lib.RunSequenceWithSGD(ctypes.cast(arr, ctypes.c_void_p), len(arr), P, G, Sz, 1, 0.05, 1.0)
+                else:
+                    lib.RunSequence(ctypes.cast(arr, ctypes.c_void_p), len(arr))
+                    lib.SGDBatch(P, G, Sz, 1, 0.05, 1.0)
+            dev.sync()
+        finally:
+            os.environ.pop("DCT_SEQ_GRAPH", None)
+        outs.append((dev.read(hw), dev.read(h["acc"]), dev.read(h["db"])))
+        assert dev.error()[0] == 0, dev.error()
+        dev.free(hw, *h.values())
+    assert np.array_equal(outs[0][0].view(np.uint32), outs[1][0].view(np.uint32))
+    assert np.array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
+    w = w0.copy()                                                  # db is the same on every replay
+    for _ in range(3):
+        w = S.sgd(w, outs[1][2], 784, 0.05, 1.0)
+    assert np.array_equal(outs[1][0].view(np.uint32), w.view(np.uint32))
+    assert not np.array_equal(outs[1][0], w0)
