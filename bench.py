@@ -114,7 +114,7 @@ class Ranks:
 
 
 # ---------------------------------------------------------------------------
-# clocks sampled during the timed region (NVML, every 2 ms, read-only)
+# clocks sampled during the timed region (NVML, every 2 ms or as fast as it answers; read-only)
 # ---------------------------------------------------------------------------
 class Clocks:
     """Samples SM clock, power and clock-event reasons of our GPU while timing."""
@@ -148,12 +148,16 @@ class Clocks:
             N, h = self.N, self.h
             get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 N.nvmlDeviceGetCurrentClocksThrottleReasons
+            k, watts = 0, None
             while not self._stop.is_set():
                 try:
-                    self.rows.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM),
-                                      N.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
+                    if k % 8 == 0:                  # the power query is the slow one: every 8th sample
+                        watts = N.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.rows.append((N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM), watts, int(get_reasons(h)),
+                                      time.monotonic()))
                 except Exception:
                     pass
+                k += 1
                 self._stop.wait(self.period)
         self._t = threading.Thread(target=loop, daemon=True)
         self._t.start()
@@ -168,11 +172,15 @@ class Clocks:
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
                     "source": "nvml", "note": getattr(self, "err", "timed region shorter than one sample")}
-        reasons = sorted({name for _, _, r in self.rows for bit, name in self.REASONS.items() if r & bit})
+        reasons = sorted({name for _, _, r, _ in self.rows for bit, name in self.REASONS.items() if r & bit})
         sm = [r[0] for r in self.rows]
+        watts = [r[1] for r in self.rows if r[1] is not None]
+        span = self.rows[-1][3] - self.rows[0][3]
+        period = span / (len(self.rows) - 1) * 1e3 if len(self.rows) > 1 else None
         return {"sm_mhz": float(np.median(sm)), "sm_min_mhz": float(min(sm)), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.rows), "power_w_max": round(max(r[1] for r in self.rows), 1),
-                "source": "nvml, 2 ms"}
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w_max": round(max(watts), 1) if watts else None,
+                "source": "nvml", "period_ms": round(period, 2) if period else None}
 
 
 # ---------------------------------------------------------------------------
