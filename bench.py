@@ -355,7 +355,8 @@ def link_bandwidth(L: Lib, nbytes: int = 1 << 29, reps: int = 3):
 # ---------------------------------------------------------------------------
 PER_OP_SECTIONS = {"c1": ("c1_dense_step_eager", "c1_dense_step_graph"), "c3": ("c3_sum_axis-1", "c3_sum_axis0", "c3_mean_axis-1", "c3_mean_axis0", "c3_max_axis-1",
                            "c3_max_axis0", "c3_argmax_axis-1", "c3_argmax_axis0"),
-                   "c3f": ("c3_fullsum_2^30",), "c4": ("c4_softmax_ce_fused",), "c5a": ("c5a_adam_1.5e9",),
+                   "c3f": ("c3_fullsum_2^30", "c3_fullsum_2^28_small"), "c4": ("c4_softmax_ce_fused",),
+                   "c5a": ("c5a_adam_1.5e9", "c5a_adam_1.5e8_small"),
                    "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd"),
                    "layout": ("f3_upsample2x_fwd", "f3_upsample2x_bwd", "f3_concat", "f3_slice", "f3_maxpool2x2_fwd",
                               "f3_maxpool2x2_fused_fwd_bwd", "f4_conv_reshape_relu", "f4_conv_grad_reshape_relu")}
@@ -394,20 +395,24 @@ def per_op_suite(L: Lib, rank: int, iters: int = 10, only: str | None = None, wa
     if section("c3"):
         _c3(L, rank, out, oidx, measure, R_ROWS, R_COLS, comm)
     if section("c3f"):
-        V = L.new(1 << 30)
+        # the 2^28 case (1 GB, still 8x L2) is run only when named: it is the small
+        # case for profiler captures of the same kernels
+        small = only == "c3_fullsum_2^28_small"
+        nv = 1 << (28 if small else 30)
+        V = L.new(nv)
         L.fill(V, 2 + 1000 * rank, 7, 0, -1.0, 1.0)
         if comm is None:
-            fs = lambda: L.check(lib.dct_reduce_all(0, V, 1 << 30, out, None), "fullsum")  # noqa: E731
+            fs = lambda: L.check(lib.dct_reduce_all(0, V, nv, out, None), "fullsum")  # noqa: E731
         else:
-            fs = lambda: comm.reduce_all("sum", V, 1 << 30, out)  # noqa: E731
-        measure("c3_fullsum_2^30", 4 << 30, fs, 2 if comm is None else 5, it=5)
+            fs = lambda: comm.reduce_all("sum", V, nv, out)  # noqa: E731
+        measure("c3_fullsum_2^28_small" if small else "c3_fullsum_2^30", 4 * nv, fs, 2 if comm is None else 5, it=5)
         lib.ReleaseBuffer(V)
     lib.ReleaseBuffer(out)
     lib.ReleaseBuffer(oidx)
     if section("c4"):
         _c4(L, rank, measure, comm)
     if section("c5a"):
-        _c5a(L, rank, measure)
+        _c5a(L, rank, measure, small=only == "c5a_adam_1.5e8_small")
     if section("c5b"):
         _c5b(L, rank, measure, comm)
     if section("layout"):
@@ -519,10 +524,11 @@ def _c4(L, rank, measure, comm=None):
         lib.ReleaseBuffer(h)
 
 
-def _c5a(L, rank, measure):
-    """C5a: Adam on 1.5e9 fp32 (seed 4), zero m/v."""
+def _c5a(L, rank, measure, small=False):
+    """C5a: Adam on 1.5e9 fp32 (seed 4), zero m/v.  `small` (1.5e8, 2.4 GB held, run
+    only when named) is the case for profiler captures of the same kernel."""
     lib = L.lib
-    n = 1_500_000_000
+    n = 150_000_000 if small else 1_500_000_000
     W, Gr, M, Vv = L.new(n), L.new(n), L.new(n), L.new(n)
     L.fill(W, 4 + 1000 * rank, 0, 1, 0.0, 0.02)
     L.fill(Gr, 4 + 1000 * rank, 1, 1, 0.0, 1e-3)
@@ -534,7 +540,7 @@ def _c5a(L, rank, measure):
         t[0] += 1
         step = 1e-3 * (1 - 0.999 ** t[0]) ** 0.5 / (1 - 0.9 ** t[0])
         L.check(lib.dct_adam(W, M, Vv, Gr, n, step, 0.9, 0.999, 1e-8, 0.0, 1.0), "adam")
-    measure("c5a_adam_1.5e9", 28 * n, adam, 1, it=10)
+    measure("c5a_adam_1.5e8_small" if small else "c5a_adam_1.5e9", 28 * n, adam, 1, it=10)
     for h in (W, Gr, M, Vv):
         lib.ReleaseBuffer(h)
 
@@ -678,8 +684,9 @@ def main():
     ap.add_argument("--no-per-op", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--only", default=None, help="profiling mode: run one C2 op (e.g. c2_rowbcast_add) "
-                    "--warmup + --steps times and print its timing only")
+    ap.add_argument("--only", default=None, help="profiling mode: run one op (a C2 op such as c2_rowbcast_add, "
+                    "or a per_op name; c3_fullsum_2^28_small and c5a_adam_1.5e8_small are smaller cases of "
+                    "the same kernels for profiler captures) --warmup + --steps times and print its timing only")
     args = ap.parse_args()
     if args.impl == "reference":
         # the CPU arm needs no GPU and no process group: rank 0 alone runs it,
