@@ -945,9 +945,12 @@ static cudaError_t full_reduce_post(int op, const float* x, uint64_t n, float* o
 cudaError_t launch_full_reduce(int op, const float* x, uint64_t n, float* out32, double* out64, void* ws,
                                cudaStream_t st) {
   if (n == 0) {
-    if (op == RED_SUM || op == RED_SUMSQ) {
-      cudaError_t e = cudaMemsetAsync(out32, 0, sizeof(float), st);
-      if (e == cudaSuccess && out64) e = cudaMemsetAsync(out64, 0, sizeof(double), st);
+    // the sum of nothing is 0 and its mean NaN (all-ones bytes are a NaN in
+    // both widths); max / min have no identity
+    if (op == RED_SUM || op == RED_SUMSQ || op == RED_MEAN) {
+      const int byte = op == RED_MEAN ? 0xFF : 0;
+      cudaError_t e = cudaMemsetAsync(out32, byte, sizeof(float), st);
+      if (e == cudaSuccess && out64) e = cudaMemsetAsync(out64, byte, sizeof(double), st);
       return e;
     }
     return cudaErrorInvalidValue;

@@ -461,7 +461,12 @@ size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K) {
 
 cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st) {
   if (a.rows == 0) {
-    if (a.loss) { cudaError_t e = cudaMemsetAsync(a.loss, 0, sizeof(float), st); if (e) return e; }
+    // the loss is the empty sum over its divisor: 0, or NaN (0 / 0) when the
+    // divisor is the empty batch itself, as nn_loss.hlsl:41 computes it
+    if (a.loss) {
+      cudaError_t e = cudaMemsetAsync(a.loss, a.loss_div != 0.0 ? 0 : 0xFF, sizeof(float), st);
+      if (e) return e;
+    }
     if (a.loss_partial) return cudaMemsetAsync(a.loss_partial, 0, sizeof(double), st);
     return cudaSuccess;
   }

@@ -847,6 +847,15 @@ static bool h_dct_reduce(const Disp& d) {
   int32_t* idx = nullptr;
   if (d.nuav > 1 && d.uav[1]) { FITS(d.uav[1], outer * inner, "idx"); idx = reinterpret_cast<int32_t*>(d.uav[1]->d); }
   float* out = d.uav[0]->d;
+  if (len == 0 && outer * inner > 0) {
+    // NumPy: the sum over an empty axis is 0 and the mean NaN; the extremes and
+    // their indices have no identity (NumPy raises)
+    if (op == RED_SUM || op == RED_MEAN)
+      return cuda_ok(cudaMemsetAsync(out, op == RED_SUM ? 0 : 0xFF, outer * inner * sizeof(float), g.stream),
+                     "dct_reduce(empty axis)");
+    set_error(DCT_ERR_ARG, "dct_reduce: op %d over a zero-length axis has no identity", op);
+    return false;
+  }
   int op_run = op;
   if (op == RED_ARGMAX || op == RED_ARGMIN) {
     // the index is the product; values are not requested
@@ -867,6 +876,10 @@ static bool h_dct_reduce_all(const Disp& d) {
   if (!need(d, 1, 1)) return false;
   const uint64_t n = d.u[1];
   FITS(d.srv[0], n, "x"); FITS(d.uav[0], 1, "out");
+  if (n == 0 && (d.u[0] == RED_MAX || d.u[0] == RED_MIN)) {
+    set_error(DCT_ERR_ARG, "dct_reduce_all: max/min of an empty vector has no identity");
+    return false;
+  }
   if (!ensure_ws(full_reduce_ws_bytes())) return false;
   LAUNCH(launch_full_reduce((int)d.u[0], d.srv[0]->d, n, d.uav[0]->d, nullptr, g.ws, g.stream));
 }
@@ -1768,6 +1781,10 @@ DCT_API int dct_reduce_all(int op, void* x, uint64_t n, void* out, double* host_
   Buffer* bo = buf_of(out);
   if (!bx || !bo) return DCT_ERR_HANDLE;
   if (bx->count < n) return DCT_ERR_SIZE;
+  if (n == 0 && (op == RED_MAX || op == RED_MIN)) {
+    set_error(DCT_ERR_ARG, "dct_reduce_all: max/min of an empty vector has no identity");
+    return DCT_ERR_ARG;
+  }
   if (!ensure_ws(full_reduce_ws_bytes() + 256)) return DCT_ERR_CUDA;
   double* d64 = (double*)((char*)g.ws + full_reduce_ws_bytes());
   if (!cuda_ok(launch_full_reduce(op, bx->d, n, bo->d, d64, g.ws, g.stream), "dct_reduce_all")) return DCT_ERR_CUDA;

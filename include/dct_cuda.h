@@ -237,14 +237,20 @@ DCT_API int dct_broadcast_to(void* x, const int64_t* x_shape, int x_ndim, const 
                              void* out);
 /* reduce x viewed as [outer, len, inner] over len: 0 sum 1 mean 2 max 3 argmax 4 min
  * 5 argmin 6 sum of squares; float64 accumulation; arg ops write int32 to out_idx
- * (or to out when out_idx is null); max/min also write indices when out_idx is set */
+ * (or to out when out_idx is null); max/min also write indices when out_idx is set.
+ * Empty operands follow NumPy: with len 0, sum writes 0 and mean NaN, and the
+ * extremes and arg ops return DCT_ERR_ARG and write nothing; with outer or inner 0
+ * there is nothing to write. */
 DCT_API int dct_reduce(int op, void* x, uint64_t outer, uint64_t len, uint64_t inner, void* out, void* out_idx);
 /* full reduction of n elements (sum, mean, max, min, sumsq) into out[0]; the
- * float64 value is returned in *host_out64 when non-null (waits) */
+ * float64 value is returned in *host_out64 when non-null (waits).  n = 0 gives 0
+ * for the sums and NaN for the mean; max and min return DCT_ERR_ARG. */
 DCT_API int dct_reduce_all(int op, void* x, uint64_t n, void* out, double* host_out64);
 /* fused row softmax + cross-entropy forward and backward in one pass:
  * probs, dlogits = (p - onehot)/grad_div, loss[0] = sum(ce)/loss_div, logprobs;
- * any output may be null; labels are float (reference layout) or int32 */
+ * any output may be null; labels are float (reference layout) or int32.  A
+ * divisor of 0 means `rows`; with rows = 0 the loss is 0 / loss_div (NaN for an
+ * empty batch, as nn_loss.hlsl:41 computes it). */
 DCT_API int dct_softmax_ce(void* logits, void* labels, int labels_int32, uint32_t rows, uint32_t K, void* probs,
                            void* dlogits, void* loss, void* logprobs, float loss_div, float grad_div);
 /* nn_adam.hlsl semantics; step_size carries lr and the bias correction */

@@ -172,3 +172,20 @@ def test_ulp_diff_known_answers():
     tiny = np.array([1e-45], F32)                                   # the smallest subnormal
     assert O.ulp_diff(tiny, -tiny).tolist() == [2]
     assert O.ulp_diff(np.array([np.inf], F32), np.array([np.finfo(F32).max], F32)).tolist() == [1]
+
+
+def test_empty_operands():
+    """Empty operands: NumPy's sum 0 / mean NaN / extremes raise, and the reference
+    loss over an empty batch is 0/0 = NaN (nn_loss.hlsl:41) in the shader oracle."""
+    import warnings
+    from oracle import shaders as S
+    e = np.zeros((3, 0, 4), F32)
+    assert np.array_equal(O.reduce("sum", e, 1), np.zeros((3, 4), F32))
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", RuntimeWarning)
+        assert np.isnan(O.reduce("mean", e, 1)).all()
+        assert np.isnan(S.ce_loss_f64(np.zeros(4, F32), np.zeros(1, F32), 0, 4))
+    for op in ("max", "argmax", "min", "argmin"):
+        with pytest.raises(ValueError):
+            O.reduce(op, e, 1)
+    assert O.binary("add", np.zeros((0, 4), F32), np.ones((1, 4), F32)).shape == (0, 4)
