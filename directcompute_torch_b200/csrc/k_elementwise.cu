@@ -34,7 +34,7 @@ DCT_DEV float unary_op(float x, float alpha) {
   } else if constexpr (OP == EW_LEAKY_RELU) {
     return x > 0.0f ? x : __fmul_rn(x, alpha);
   } else if constexpr (OP == EW_SIGMOID) {
-    return sigmoid_acc(x);                            // <= 1 ulp, branch-free (dct_math.cuh)
+    return sigmoid_acc(x);                            // <= 1.5 ulp, branch-free (dct_math.cuh)
   } else if constexpr (OP == EW_EXP) {
     return expf(x);
   } else if constexpr (OP == EW_LOG_ABS1P) {
