@@ -49,3 +49,42 @@ def test_reference_arm_under_torchrun_prints_once():
     lines = _lines(r.stdout)
     assert len(lines) == 1
     _check(lines[0], 2)
+
+
+def test_clock_record_with_a_fake_nvml(monkeypatch):
+    """bench.Clocks samples NVML during the timed region: median / minimum SM clock,
+    the active clock-event reasons by name, the sample count and the measured period."""
+    import time
+    import types
+    state = {"k": 0}
+    N = types.ModuleType("pynvml")
+    N.NVML_CLOCK_SM = 1
+    N.nvmlInit = lambda: None
+    N.nvmlDeviceGetHandleByPciBusId = lambda bus: 0
+    N.nvmlDeviceGetMaxClockInfo = lambda h, c: 1965
+
+    def clock(h, c):
+        state["k"] += 1
+        return 1965 if state["k"] % 3 else 1732
+    N.nvmlDeviceGetClockInfo = clock
+    N.nvmlDeviceGetPowerUsage = lambda h: 650000                   # mW
+    N.nvmlDeviceGetCurrentClocksEventReasons = lambda h: 0x4 | 0x40  # power cap + HW thermal
+    monkeypatch.setitem(sys.modules, "pynvml", N)
+    sys.path.insert(0, ROOT)
+    try:
+        import bench
+    finally:
+        sys.path.remove(ROOT)
+    with bench.Clocks("0000:00:00.0", period_s=0.002) as clk:
+        time.sleep(0.1)
+    rec = clk.summary()
+    assert rec["samples"] >= 10 and rec["sm_max_mhz"] == 1965
+    assert rec["sm_mhz"] == 1965.0 and rec["sm_min_mhz"] == 1732.0
+    assert rec["reasons"] == ["hw_thermal_slowdown", "sw_power_cap"]
+    assert rec["power_w_max"] == 650.0 and 1.5 < rec["period_ms"] < 20
+    # no NVML at all: the record says so instead of inventing clocks
+    monkeypatch.setitem(sys.modules, "pynvml", types.ModuleType("pynvml"))
+    with bench.Clocks("0000:00:00.0") as clk:
+        pass
+    rec = clk.summary()
+    assert rec["samples"] == 0 and rec["reasons"] == ["unsampled"] and rec["sm_mhz"] is None
