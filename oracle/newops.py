@@ -177,6 +177,20 @@ def softmax_ce_f64(logits: np.ndarray, labels: np.ndarray, loss_divisor=None):
     return p.astype(F32), F32(loss), logp.astype(F32)
 
 
+def softmax_ce_rows_f64(logits: np.ndarray, labels: np.ndarray):
+    """Row-wise form of `softmax_ce_f64` for chunked checks of large batches.
+
+    Returns (probs fp32, per-row cross-entropy float64, logprobs fp32); the mean
+    loss of a batch is the float64 sum of the row losses over the global divisor.
+    """
+    X = np.asarray(logits, dtype=F32).astype(F64)
+    B = X.shape[0]
+    lab = np.asarray(labels).astype(np.int64)
+    z = X - X.max(axis=1, keepdims=True)
+    logp = z - np.log(np.exp(z).sum(axis=1, keepdims=True))
+    return np.exp(logp).astype(F32), -logp[np.arange(B), lab], logp.astype(F32)
+
+
 def softmax_ce_dlogits(p_dev: np.ndarray, labels: np.ndarray, divisor: int) -> np.ndarray:
     """dlogits = (p - onehot) / divisor in fp32 from the device's own probs (bit-exact target)."""
     p = np.asarray(p_dev, dtype=F32)

@@ -214,13 +214,16 @@ def batchnorm_forward(x, mean, var, gamma, beta, N, C, S, eps):
     return (xhat * gamma[c] + beta[c]).astype(F32)
 
 
-def batchnorm_backward_dx(x, dy, mean, var, gamma, dgamma, dbeta, N, C, S, eps):
-    """nn_batchnorm_backward_dx.hlsl:20-38 -- dx = (g*rstd) * (dy - (db + xhat*dg) / m)."""
+def batchnorm_backward_dx(x, dy, mean, var, gamma, dgamma, dbeta, N, C, S, eps, count=None):
+    """nn_batchnorm_backward_dx.hlsl:20-38 -- dx = (g*rstd) * (dy - (db + xhat*dg) / m).
+
+    m is the batch's N*S; `count` overrides it when x holds only some samples of
+    the batch (a chunked check, or one rank's shard)."""
     n = N * C * S
     c = (np.arange(n, dtype=np.int64) // S) % C
     rstd = (F32(1.0) / np.sqrt(var[:C] + F32(eps))).astype(F32)
     xhat = ((x[:n] - mean[c]) * rstd[c]).astype(F32)
-    m = F32(N * S)
+    m = F32(N * S if count is None else count)
     inner = ((dbeta[c] + xhat * dgamma[c]) / m).astype(F32)
     return ((gamma[c] * rstd[c]) * (dy[:n] - inner)).astype(F32)
 
