@@ -89,9 +89,8 @@ def uniform(seed: int, offset: int, start: int, count: int, a: float, b: float) 
 def normal_f64(seed: int, offset: int, start: int, count: int, mean: float, std: float) -> np.ndarray:
     """Elements [start, start + count) of a normal fill, evaluated in float64 from the same uniforms."""
     g0 = start // 4
-    w = words(seed, offset, 4 * g0, start + count - 4 * g0).astype(np.uint64)
-    pad = (-w.size) % 4
-    w = np.concatenate([w, np.zeros(pad, np.uint64)]).reshape(-1, 2, 2)   # [block][pair][(a, b)]
+    g1 = (start + count + 3) // 4                  # whole blocks: a pair's second word may lie past the end
+    w = words(seed, offset, 4 * g0, 4 * (g1 - g0)).astype(np.uint64).reshape(-1, 2, 2)   # [block][pair][(a, b)]
     u1 = ((w[:, :, 0] >> np.uint64(8)) + np.uint64(1)).astype(np.float64) * TWO_M24
     u2 = (w[:, :, 1] >> np.uint64(8)).astype(np.float64) * TWO_M24
     r = np.sqrt(-2.0 * np.log(u1))

@@ -39,6 +39,9 @@ def test_normal_moments_and_slices():
     z = rng.normal_f64(4, 0, 0, 1 << 18, 0.0, 1.0)
     assert abs(z.mean()) < 0.01 and abs(z.std() - 1.0) < 0.01
     assert np.array_equal(rng.normal_f64(4, 0, 5, 11, 0.0, 1.0), z[5:16])
+    # a slice ending inside a block still pairs its last element with the block's next word
+    assert np.array_equal(rng.normal_f64(4, 0, 0, 7, 0.0, 1.0), z[:7])
+    assert np.array_equal(rng.normal_f64(4, 0, 6, 1, 0.0, 1.0), z[6:7])
     y = rng.normal_f64(4, 10, 0, 1 << 16, 0.5, 2.0)
     assert abs(y.mean() - 0.5) < 0.05 and abs(y.std() - 2.0) < 0.05
     assert np.all(rng.normal_error_bound(y, 0.5, 2.0) > 0)
