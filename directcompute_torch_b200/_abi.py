@@ -112,6 +112,7 @@ SIGNATURES = {
     "dct_batchnorm_forward_train_noalloc": ([VP] * 8 + [U32, U32, U32, F32, F32, VP], C.c_int),
     "dct_sum_to_shape": ([VP, C.POINTER(C.c_int64), C.c_int, C.POINTER(C.c_int64), C.c_int, VP], C.c_int),
     "dct_broadcast_to": ([VP, C.POINTER(C.c_int64), C.c_int, C.POINTER(C.c_int64), C.c_int, VP], C.c_int),
+    "dct_bias_relu_backward": ([VP, VP, VP, VP, U32, U32], C.c_int),
     # sharding over NCCL
     "dct_dist_available": ([], C.c_int),
     "dct_dist_nccl_version": ([], C.c_int),

@@ -315,11 +315,26 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
 // kernel launched with programmatic dependent launch combines them in chunk
 // order.  (A fold by the last block of each tile, found with an atomic counter,
 // was measured slower: its fence and serial fold sit on the kernel's tail.)
-template <int OP, int VEC>
+//
+// GATE fuses the backward of bias + ReLU (nn_engine.py:1091-1106) into the
+// column sum: the reduced value is relu_grad(x, y) = y > 0 ? x : 0
+// (nn_relu_grad.hlsl:6-9), stored to dx as it streams by, and the column sums
+// of it are bias_grad (nn_bias_grad.hlsl:8-29) -- one read of the gradient and
+// of the forward output instead of two passes.  y and dx share x's layout.  The
+// per-lane order of the adds is the ungated kernel's, so for the same plan the
+// sums are bit-identical to relu_grad followed by bias_grad.
+struct ColGate {
+  const float* y = nullptr;
+  float* dx = nullptr;
+};
+
+DCT_DEV float relu_gate(float g, float y) { return y > 0.0f ? g : 0.0f; }
+
+template <int OP, int VEC, bool GATE = false>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                              uint64_t inner, uint64_t so, uint64_t sl,
                                                              uint32_t chunks, uint64_t chunk_len, RedOut ro,
-                                                             unsigned long long* part) {
+                                                             unsigned long long* part, ColGate gate) {
   pdl_entry();
   constexpr int W = 32 * VEC;
   __shared__ unsigned long long sh[kRedWarps][W];
@@ -331,10 +346,12 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
   for (uint64_t o = blockIdx.y; o < outer; o += gridDim.y) {
     Acc<OP> acc[VEC];
     const float* base = x + o * so;
+    const float* ybase = GATE ? gate.y + o * so : nullptr;
+    float* dbase = GATE ? gate.dx + o * so : nullptr;
     if (VEC == 4 && c0 + 3 < inner) {
       // 8 rows (8 x 512 B per warp) in flight per batch: the loop is bound by
-      // memory latency, not by the per-element work
-      constexpr int U = 8;
+      // memory latency, not by the per-element work (4 rows of two operands gated)
+      constexpr int U = GATE ? 4 : 8;
       const uint64_t first = l0 + warp;
       ColLane<OP> ln[4];
 #pragma unroll
@@ -344,6 +361,17 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
         float4 v[U];
 #pragma unroll
         for (int k = 0; k < U; ++k) v[k] = ld_stream4(base + (l + k * kRedWarps) * sl + c0);
+        if constexpr (GATE) {
+          float4 yv[U];
+#pragma unroll
+          for (int k = 0; k < U; ++k) yv[k] = ld_stream4(ybase + (l + k * kRedWarps) * sl + c0);
+#pragma unroll
+          for (int k = 0; k < U; ++k) {
+            v[k] = make_float4(relu_gate(v[k].x, yv[k].x), relu_gate(v[k].y, yv[k].y), relu_gate(v[k].z, yv[k].z),
+                               relu_gate(v[k].w, yv[k].w));
+            st_stream4(dbase + (l + k * kRedWarps) * sl + c0, v[k]);
+          }
+        }
 #pragma unroll
         for (int k = 0; k < U; ++k) {
           const int32_t li = (int32_t)(l + k * kRedWarps);
@@ -351,7 +379,12 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
         }
       }
       for (; l < l1; l += kRedWarps) {
-        const float4 v = ld_stream4(base + l * sl + c0);
+        float4 v = ld_stream4(base + l * sl + c0);
+        if constexpr (GATE) {
+          const float4 yv = ld_stream4(ybase + l * sl + c0);
+          v = make_float4(relu_gate(v.x, yv.x), relu_gate(v.y, yv.y), relu_gate(v.z, yv.z), relu_gate(v.w, yv.w));
+          st_stream4(dbase + l * sl + c0, v);
+        }
         const int32_t li = (int32_t)l;
         ln[0].add(v.x, li); ln[1].add(v.y, li); ln[2].add(v.z, li); ln[3].add(v.w, li);
       }
@@ -362,7 +395,14 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
         if (c0 + j >= inner) break;
-        for (uint64_t l = l0 + warp; l < l1; l += kRedWarps) acc[j].add(ld_stream(base + l * sl + c0 + j), (int64_t)l);
+        for (uint64_t l = l0 + warp; l < l1; l += kRedWarps) {
+          float v = ld_stream(base + l * sl + c0 + j);
+          if constexpr (GATE) {
+            v = relu_gate(v, ld_stream(ybase + l * sl + c0 + j));
+            st_stream(dbase + l * sl + c0 + j, v);
+          }
+          acc[j].add(v, (int64_t)l);
+        }
       }
     }
 #pragma unroll
@@ -497,24 +537,30 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
   return p;
 }
 
+// resident blocks per SM of the (ungated) column kernel, VEC 1 or 4; -1 if unknown
+template <int OP>
+int cols_occupancy(bool vec) {
+  static int cols_occ[2] = {0, 0};                        // per instantiation: VEC 1 / 4
+  const int vi = vec ? 1 : 0;
+  if (cols_occ[vi] == 0) {
+    int b = 0;
+    const cudaError_t e =
+        vi ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 4, false>, kRedThreads, 0)
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 1, false>, kRedThreads, 0);
+    cols_occ[vi] = (e == cudaSuccess && b > 0) ? b : -1;
+    cudaGetLastError();
+  }
+  return cols_occ[vi];
+}
+
 template <int OP>
 cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
                        uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (outer == 0 || inner == 0) return cudaSuccess;
   if (len == 0) return cudaErrorInvalidValue;
-  static int cols_occ[2] = {0, 0};                        // per instantiation: VEC 1 / 4
-  for (int vi = 0; vi < 2; ++vi) {
-    if (cols_occ[vi] == 0) {
-      int b = 0;
-      const cudaError_t e = vi ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 4>, kRedThreads, 0)
-                               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 1>, kRedThreads, 0);
-      cols_occ[vi] = (e == cudaSuccess && b > 0) ? b : -1;
-      cudaGetLastError();
-    }
-  }
   Plan p = make_plan(outer, len, inner, so, sl, si, x);
   if (p.kind == 1) {
-    const int occ = cols_occ[p.vec ? 1 : 0];
+    const int occ = cols_occupancy<OP>(p.vec);
     if (occ > 0) p = make_plan(outer, len, inner, so, sl, si, x, occ);
   }
   unsigned long long* part = (unsigned long long*)ws;
@@ -527,8 +573,8 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
     if (p.vec) launch_pdl(k_reduce_rows<OP, true>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
     else launch_pdl(k_reduce_rows<OP, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
   } else if (p.kind == 1) {
-    if (p.vec) launch_pdl(k_reduce_cols<OP, 4>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
-    else launch_pdl(k_reduce_cols<OP, 1>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part);
+    if (p.vec) launch_pdl(k_reduce_cols<OP, 4, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColGate{});
+    else launch_pdl(k_reduce_cols<OP, 1, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColGate{});
   } else {
     launch_pdl(k_reduce_generic<OP>, dim3(p.grid), dim3(256), 0, st, x, outer, len, inner, so, sl, si, ro);
   }
@@ -598,6 +644,44 @@ cudaError_t launch_reduce_strided(int op, const float* x, uint64_t outer, uint64
   ro.out = out;
   ro.idx = out_idx;
   return dispatch_reduce(op, x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+}
+
+size_t relu_grad_colsum_ws_bytes(uint64_t rows, uint64_t cols) {
+  return reduce_strided_ws_bytes(1, rows, cols, 0, cols, 1);
+}
+
+cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, float* db, uint64_t rows,
+                                    uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (cols == 0) return cudaSuccess;
+  if (rows == 0) return cudaMemsetAsync(db, 0, cols * sizeof(float), st);
+  // bias_grad's column plan over [rows, cols]: the same chunks, so the same sums
+  Plan p = make_plan(1, rows, cols, 0, cols, 1, g);
+  const int occ = cols_occupancy<RED_SUM>(p.vec);
+  if (occ > 0) p = make_plan(1, rows, cols, 0, cols, 1, g, occ);
+  // 128-bit loads need all three operands aligned; the chunking stays the plan's
+  const bool vec = p.vec && aligned16_h(y) && aligned16_h(dx);
+  unsigned long long* part = (unsigned long long*)ws;
+  if (p.chunks > 1) {
+    const size_t need = (size_t)cols * p.chunks * sizeof(unsigned long long);
+    if (!ws || ws_bytes < need) return cudaErrorInvalidValue;
+  }
+  RedOut ro;
+  ro.out = db;
+  ColGate gate;
+  gate.y = y;
+  gate.dx = dx;
+  if (vec) {
+    launch_pdl(k_reduce_cols<RED_SUM, 4, true>, dim3(p.grid), dim3(kRedThreads), 0, st, g, (uint64_t)1, rows, cols,
+               (uint64_t)0, cols, p.chunks, p.chunk_len, ro, part, gate);
+  } else {
+    const dim3 grid((unsigned)((cols + 31) / 32), 1, p.grid.z);       // scalar tiles are 32 columns wide
+    launch_pdl(k_reduce_cols<RED_SUM, 1, true>, grid, dim3(kRedThreads), 0, st, g, (uint64_t)1, rows, cols,
+               (uint64_t)0, cols, p.chunks, p.chunk_len, ro, part, gate);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || p.chunks == 1) return e;
+  return launch_pdl(k_fold_chunks<RED_SUM>, dim3(grid_for(cols * 32, 256)), dim3(256), 0, st,
+                    (const unsigned long long*)part, cols, p.chunks, cols, rows, ro);
 }
 
 size_t reduce3d_ws_bytes(int op, uint64_t outer, uint64_t len, uint64_t inner) {

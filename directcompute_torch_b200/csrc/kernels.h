@@ -75,6 +75,12 @@ cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t
 size_t sum_to_shape_ws_bytes(int ndim, const int64_t* gshape, const int64_t* tshape);
 cudaError_t launch_sum_to_shape(const float* g, int ndim, const int64_t* gshape, const int64_t* tshape,
                                 float* out, void* ws, size_t ws_bytes, cudaStream_t st);
+// Backward of bias + ReLU over [rows, cols] in one pass: dx = y > 0 ? g : 0 and
+// db[c] = sum_r dx[r, c] (float64, rounded once), bit-identical to relu_grad
+// followed by bias_grad.  dx may alias g.  `ws` holds relu_grad_colsum_ws_bytes.
+size_t relu_grad_colsum_ws_bytes(uint64_t rows, uint64_t cols);
+cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, float* db, uint64_t rows,
+                                    uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st);
 // General strided form: out[o*inner + i] = reduce_l x[o*so + l*sl + i*si].
 size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
                                uint64_t si);

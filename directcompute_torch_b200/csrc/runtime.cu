@@ -969,10 +969,8 @@ static bool is_shader_ptr(const void* p) {
   return s >= g_shaders && s < g_shaders + kNumShaders && s->magic == kShaderMagic;
 }
 
-static bool dispatch(Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav, const uint32_t* groups,
-                     const void* cb, uint32_t cbsize) {
-  if (!ensure_init()) return false;
-  Disp d;
+static bool make_disp(Disp& d, Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav,
+                      const uint32_t* groups, const void* cb, uint32_t cbsize) {
   memset(&d, 0, sizeof(d));
   d.name = s->name;
   if (nsrv > 16 || nuav > 16) { set_error(DCT_ERR_ARG, "%s: too many views", s->name); return false; }
@@ -991,7 +989,38 @@ static bool dispatch(Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_
   d.gz = groups ? groups[2] : 1;
   d.cbsize = cbsize;
   if (cb && cbsize) memcpy(d.u, cb, std::min<uint32_t>(cbsize, sizeof(d.u)));
+  return true;
+}
+
+static bool dispatch(Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_t nuav, const uint32_t* groups,
+                     const void* cb, uint32_t cbsize) {
+  if (!ensure_init()) return false;
+  Disp d;
+  if (!make_disp(d, s, srvs, nsrv, uavs, nuav, groups, cb, cbsize)) return false;
   return s->fn(d);
+}
+
+// relu_grad (grad, y -> dx) directly followed by bias_grad over that dx with
+// row strides (the backward of bias + ReLU, nn_engine.py:1091-1106): one pass
+// over grad and y writes dx and the column sums (launch_relu_grad_colsum),
+// with the same results as the two dispatches.  Returns false, launching
+// nothing, when the pair does not have that form.
+static bool try_fused_relu_bias_grad(const Disp& a, const Disp& b, bool& ok) {
+  if (strcmp(a.name, "relu_grad") != 0 || strcmp(b.name, "bias_grad") != 0) return false;
+  if (a.nsrv < 2 || a.nuav < 1 || b.nsrv < 1 || b.nuav < 1) return false;
+  if (!a.srv[0] || !a.srv[1] || !a.uav[0] || !b.srv[0] || !b.uav[0]) return false;
+  if (b.srv[0] != a.uav[0]) return false;                         // bias_grad reads the dx just written
+  const uint64_t n = lim(a.u[0], a.gx);
+  const uint64_t B = b.u[0], K = std::min<uint64_t>(b.u[1], b.gx);
+  if (K == 0 || B == 0 || b.u[3] != 1 || b.u[2] != K || B * K != n) return false;
+  Buffer *bg = a.srv[0], *by = a.srv[1], *bdx = a.uav[0], *bdb = b.uav[0];
+  if (bdb == bg || bdb == by || bdb == bdx) return false;
+  if (bg->count < n || by->count < n || bdx->count < n || bdb->count < K) return false;
+  const size_t ws = relu_grad_colsum_ws_bytes(B, K);
+  if (ws && !ensure_ws(ws)) { ok = false; return true; }
+  ok = cuda_ok(launch_relu_grad_colsum(bg->d, by->d, bdx->d, bdb->d, B, K, g.ws, g.ws_bytes, g.stream),
+               "relu_grad + bias_grad");
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -1442,6 +1471,25 @@ static bool seq_run(DctSeqCmd* cmds, uint32_t count) {
       continue;
     }
     Shader* s = static_cast<Shader*>(c.shader);
+    if (i + 1 < count && cmds[i + 1].shader && is_shader_ptr(cmds[i + 1].shader) && ensure_init()) {
+      DctSeqCmd& c2 = cmds[i + 1];
+      Disp a, b;
+      bool fused_ok = true;
+      const int code0 = g.err_code;                  // a pair that does not fuse leaves no error behind
+      const std::string msg0 = g.err;
+      if (make_disp(a, s, c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs, std::min<uint32_t>(c.uavCount, 4),
+                    c.threads, c.cbSize ? c.cbData : nullptr, std::min<uint32_t>(c.cbSize, 64)) &&
+          make_disp(b, static_cast<Shader*>(c2.shader), c2.srvs, std::min<uint32_t>(c2.srvCount, 8), c2.uavs,
+                    std::min<uint32_t>(c2.uavCount, 4), c2.threads, c2.cbSize ? c2.cbData : nullptr,
+                    std::min<uint32_t>(c2.cbSize, 64)) &&
+          try_fused_relu_bias_grad(a, b, fused_ok)) {
+        ok &= fused_ok;
+        ++i;
+        continue;
+      }
+      g.err_code = code0;
+      g.err = msg0;
+    }
     ok &= dispatch(s, c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs, std::min<uint32_t>(c.uavCount, 4),
                    c.threads, c.cbSize ? c.cbData : nullptr, std::min<uint32_t>(c.cbSize, 64));
   }
@@ -1743,6 +1791,30 @@ DCT_API int dct_sum_to_shape(void* grad, const int64_t* g_shape, int g_ndim, con
   if (ws && !ensure_ws(ws)) return DCT_ERR_CUDA;
   return cuda_ok(launch_sum_to_shape(bg->d, g_ndim, g_shape, t, bo->d, g.ws, g.ws_bytes, g.stream),
                  "dct_sum_to_shape") ? 0 : DCT_ERR_CUDA;
+}
+
+DCT_API int dct_bias_relu_backward(void* grad, void* out, void* dx, void* db, uint32_t rows, uint32_t cols) {
+  LOCK;
+  if (!ensure_init()) return DCT_ERR_NO_DEVICE;
+  Buffer *bg = buf_of(grad), *by = buf_of(out), *bdx = buf_of(dx), *bdb = buf_of(db);
+  if (!bg || !by || !bdx || !bdb) {
+    set_error(DCT_ERR_HANDLE, "dct_bias_relu_backward: not a live buffer");
+    return DCT_ERR_HANDLE;
+  }
+  const uint64_t n = (uint64_t)rows * cols;
+  if (bg->count < n || by->count < n || bdx->count < n || bdb->count < cols) {
+    set_error(DCT_ERR_SIZE, "dct_bias_relu_backward: a buffer holds fewer than %llu (or %u) floats",
+              (unsigned long long)n, cols);
+    return DCT_ERR_SIZE;
+  }
+  if (bdb == bg || bdb == by || bdb == bdx) {
+    set_error(DCT_ERR_ARG, "dct_bias_relu_backward: db must not alias grad, out or dx");
+    return DCT_ERR_ARG;
+  }
+  const size_t ws = relu_grad_colsum_ws_bytes(rows, cols);
+  if (ws && !ensure_ws(ws)) return DCT_ERR_CUDA;
+  return cuda_ok(launch_relu_grad_colsum(bg->d, by->d, bdx->d, bdb->d, rows, cols, g.ws, g.ws_bytes, g.stream),
+                 "dct_bias_relu_backward") ? 0 : DCT_ERR_CUDA;
 }
 
 DCT_API int dct_broadcast_to(void* x, const int64_t* x_shape, int x_ndim, const int64_t* out_shape, int out_ndim,

@@ -232,6 +232,13 @@ DCT_API int dct_binary(int op, void* a, const int64_t* a_shape, int a_ndim, void
  * accumulation rounded once (the reverse of NumPy broadcasting) */
 DCT_API int dct_sum_to_shape(void* g, const int64_t* g_shape, int g_ndim, const int64_t* t_shape, int t_ndim,
                              void* out);
+/* backward of bias + ReLU over [rows, cols] in one pass (replaces the relu_grad
+ * then bias_grad dispatches of BiasReLUFunc.backward, nn_engine.py:1091-1106;
+ * nn_relu_grad.hlsl:6-9, nn_bias_grad.hlsl:8-29): dx = out > 0 ? grad : 0 and
+ * db[c] = sum over rows of dx[r, c] (float64, rounded once).  Results equal the
+ * two dispatches bit for bit.  dx may be grad itself.  RunSequence fuses a
+ * relu_grad command followed by a bias_grad over its output the same way. */
+DCT_API int dct_bias_relu_backward(void* grad, void* out, void* dx, void* db, uint32_t rows, uint32_t cols);
 /* out (out_shape) = x (x_shape) broadcast NumPy-style (the reverse of dct_sum_to_shape) */
 DCT_API int dct_broadcast_to(void* x, const int64_t* x_shape, int x_ndim, const int64_t* out_shape, int out_ndim,
                              void* out);
