@@ -76,3 +76,159 @@ def c2_sample(threads: int, rows: int = 1024, reps: int = 3, seed: int = 1, min_
     desc = (f"C2 sample: A[{rows},8192] (1/{8192 // rows} of the rows), C[{p},1,4096] x D[1,512,4096]; "
             f"11 ops; {passes} timed passes in {elapsed:.1f} s (mean), {threads} threads")
     return total * passes / elapsed / 1e9, elapsed / passes, desc, passes
+
+
+def _timed(fn, reps: int, min_seconds: float, warmup: int = 1):
+    """`warmup` untimed calls, then at least `reps` timed calls and at least `min_seconds`."""
+    for _ in range(max(0, warmup)):
+        fn()
+    n = 0
+    t0 = time.perf_counter()
+    while n < reps or time.perf_counter() - t0 < min_seconds:
+        fn()
+        n += 1
+    return (time.perf_counter() - t0) / n, n
+
+
+def c3_sample(threads: int, rows: int = 2048, cols: int = 4096, seed: int = 2, reps: int = 2,
+              min_seconds: float = 2.0):
+    """Config C3's eight axis reductions (sum / mean / max / argmax along axis -1 and
+    axis 0) on a `rows`-row sample of R with the same outliers, each thread taking a
+    block of rows (axis 0: per-block float64 column partials combined in block order).
+    Returns (GB/s of algorithmic bytes, seconds per pass, text)."""
+    rng = np.random.default_rng(seed)
+    R = rng.standard_normal((rows, cols), dtype=F32)
+    k = R.size // 1000
+    idx = rng.choice(R.size, k, replace=False)
+    R.flat[idx] = np.where(rng.integers(0, 2, k) == 1, 1e4, -1e4).astype(F32)
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+    rch = _chunks(rows, threads)
+
+    def axis_last():
+        def part(s):
+            blk = R[s[0]:s[1]]
+            sm = np.sum(blk, axis=1, dtype=np.float64)
+            return sm.astype(F32), (sm / cols).astype(F32), blk.max(axis=1), blk.argmax(axis=1)
+        list(pool.map(part, rch))
+
+    def axis_first():
+        def part(s):
+            blk = R[s[0]:s[1]]
+            return np.sum(blk, axis=0, dtype=np.float64), blk.max(axis=0), blk.argmax(axis=0) + s[0]
+        parts = list(pool.map(part, rch))
+        sm = sum(p[0] for p in parts)
+        (sm / rows).astype(F32)
+        mx = np.stack([p[1] for p in parts])
+        win = mx.argmax(axis=0)                       # first block holding the maximum: first index
+        np.stack([p[2] for p in parts])[win, np.arange(cols)]
+
+    def step():
+        axis_last()
+        axis_first()
+    secs, n = _timed(step, reps, min_seconds)
+    pool.shutdown()
+    nbytes = 4 * (4 * (rows * cols + rows) + 4 * (rows * cols + cols))
+    desc = f"C3 sample: R[{rows},{cols}] (1/{16384 // rows} of the rows), 8 axis reductions; {n} passes, {threads} threads"
+    return nbytes / secs / 1e9, secs, desc
+
+
+def c4_sample(threads: int, rows: int = 8192, K: int = 1000, seed: int = 3, reps: int = 2, min_seconds: float = 2.0):
+    """Config C4's fused softmax + cross-entropy forward and backward (probs, mean loss,
+    dlogits) on a `rows`-row sample, float64 per row as the oracle computes it."""
+    rng = np.random.default_rng(seed)
+    X = (F32(3.0) * rng.standard_normal((rows, K), dtype=F32)).astype(F32)
+    lab = rng.integers(0, K, rows).astype(np.int32)
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+    rch = _chunks(rows, threads)
+
+    def step():
+        def part(s):
+            p, row_loss, _ = O.softmax_ce_rows_f64(X[s[0]:s[1]], lab[s[0]:s[1]])
+            O.softmax_ce_dlogits(p, lab[s[0]:s[1]], rows)
+            return float(row_loss.sum())
+        sum(pool.map(part, rch)) / rows
+    secs, n = _timed(step, reps, min_seconds)
+    pool.shutdown()
+    nbytes = 4 * (3 * rows * K + rows) + 4
+    desc = f"C4 sample: logits[{rows},{K}] (1/{65536 // rows} of the rows), fused softmax+CE fwd+bwd; {n} passes, {threads} threads"
+    return nbytes / secs / 1e9, secs, desc
+
+
+def c5a_sample(threads: int, n: int = 30_000_000, seed: int = 4, reps: int = 2, min_seconds: float = 2.0):
+    """Config C5a's Adam step (nn_adam.hlsl:18-34 restated) on an `n`-element subsample,
+    each thread updating contiguous slices."""
+    from . import shaders as S
+    rng = np.random.default_rng(seed)
+    w = (F32(0.02) * rng.standard_normal(n, dtype=F32)).astype(F32)
+    g = (F32(1e-3) * rng.standard_normal(n, dtype=F32)).astype(F32)
+    m = np.zeros(n, F32)
+    v = np.zeros(n, F32)
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+    ch = _chunks(n, max(threads, n // (1 << 22)))
+    t = [0]
+
+    def step():
+        t[0] += 1
+        sz = S.adam_step_size(1e-3, 0.9, 0.999, t[0])
+
+        def part(s):
+            sl = slice(s[0], s[1])
+            w[sl], m[sl], v[sl] = S.adam(w[sl], m[sl], v[sl], g[sl], s[1] - s[0], sz, 0.9, 0.999, 1e-8, 0.0, 1.0)
+        list(pool.map(part, ch))
+    secs, k = _timed(step, reps, min_seconds)
+    pool.shutdown()
+    desc = f"C5a sample: Adam on {n:.2e} elements (1/{1_500_000_000 // n} of 1.5e9); {k} steps, {threads} threads"
+    return 28 * n / secs / 1e9, secs, desc
+
+
+def c5b_sample(threads: int, N: int = 16, C: int = 256, S_: int = 56 * 56, seed: int = 4, reps: int = 1,
+               min_seconds: float = 2.0):
+    """Config C5b's BatchNorm training forward (statistics, then the apply) and backward
+    (dgamma / dbeta, then dx) on an N-sample slice of the batch, each thread taking a
+    block of samples (float64 channel partials combined in block order)."""
+    from . import shaders as S
+    rng = np.random.default_rng(seed)
+    x = (F32(0.5) + F32(2.0) * rng.standard_normal(N * C * S_, dtype=F32)).astype(F32)
+    dy = rng.standard_normal(N * C * S_, dtype=F32)
+    gamma, beta = np.ones(C, F32), np.zeros(C, F32)
+    pool = cf.ThreadPoolExecutor(max_workers=threads)
+    nch = _chunks(N, threads)
+    plane = C * S_
+    eps = F32(1e-5)
+
+    def step():
+        def stats(s):
+            X = x[s[0] * plane:s[1] * plane].reshape(-1, C, S_)
+            return np.sum(X, axis=(0, 2), dtype=np.float64), np.sum(np.square(X, dtype=np.float64), axis=(0, 2))
+        parts = list(pool.map(stats, nch))
+        cnt = N * S_
+        mean = sum(p[0] for p in parts) / cnt
+        var = np.maximum(0.0, sum(p[1] for p in parts) / cnt - mean * mean)
+        m32, v32 = mean.astype(F32), var.astype(F32)
+
+        def fwd(s):
+            sl = slice(s[0] * plane, s[1] * plane)
+            return S.batchnorm_forward(x[sl], m32, v32, gamma, beta, s[1] - s[0], C, S_, eps)
+        list(pool.map(fwd, nch))
+
+        def red(s):
+            sl = slice(s[0] * plane, s[1] * plane)
+            X = x[sl].reshape(-1, C, S_)
+            D = dy[sl].reshape(-1, C, S_)
+            return (np.sum(D * (X - m32[None, :, None]), axis=(0, 2), dtype=np.float64),
+                    np.sum(D, axis=(0, 2), dtype=np.float64))
+        parts = list(pool.map(red, nch))
+        rstd = (F32(1.0) / np.sqrt(v32 + eps)).astype(F32)
+        dg = (sum(p[0] for p in parts) * rstd).astype(F32)
+        db = sum(p[1] for p in parts).astype(F32)
+
+        def bwd(s):
+            sl = slice(s[0] * plane, s[1] * plane)
+            return S.batchnorm_backward_dx(x[sl], dy[sl], m32, v32, gamma, dg, db, s[1] - s[0], C, S_, eps,
+                                           count=cnt)
+        list(pool.map(bwd, nch))
+    secs, n = _timed(step, reps, min_seconds)
+    pool.shutdown()
+    nbytes = 4 * 3 * N * plane + 4 * 5 * N * plane
+    desc = f"C5b sample: x[{N},{C},56,56] (1/{256 // N} of the batch), BN train fwd+bwd; {n} passes, {threads} threads"
+    return nbytes / secs / 1e9, secs, desc
