@@ -5,18 +5,19 @@ The product is `libdct_cuda.so` (built in-tree from `csrc/` by `build.py`), a
 C-ABI drop-in for the reference's ctypes-loaded `engine.dll`.  This package
 holds the loader and the Python host side:
 
-* `engine`  -- the reference's Python API for the hot path (Tensor + tape
-  autograd, add_bias / bias_relu / relu / ... / softmax_ce / batchnorm2d, SGD /
-  Adam(W), Metrics, pool helpers), bound to libdct_cuda.so with the
-  reference's ctypes signatures;
+* `tensor`  -- `DeviceTensor`, a device tensor over one library buffer with
+  reverse-mode autograd (the reference Tensor's attribute protocol);
 * `ops`     -- the NumPy-semantics ops the reference has no GPU kernel for
   (broadcast binary ops with broadcast gradients, exp/log/tanh, axis and full
-  reductions, fused softmax-CE, fused Adam / BatchNorm);
+  reductions, fused softmax-CE, bias + ReLU with the fused backward,
+  BatchNorm2d); `ops.bind(nn_engine)` builds them on the reference's own
+  Tensor instead;
 * `dist`    -- leading-dimension sharding across the GPUs of one node (one
   process per GPU, NCCL for the reduced-axis exchanges).
 
-There is no CPU fallback: every entry point runs on the CUDA library, and
-importing `engine` raises if the library or a CUDA device is missing.
+The reference's own Python tier (`nn_engine.py`) is not part of this package:
+it loads `libdct_cuda.so` unmodified in place of `engine.dll`.  There is no CPU
+fallback: every entry point runs on the CUDA library.
 """
 from __future__ import annotations
 

@@ -3,8 +3,7 @@
 The reference's tensor math beyond its fixed shaders lives on its NumPy side
 (its checks in nn_verify.py:224-491 and verify_dice_loss.py:17-40, and
 `clip_grad_norm` at nn_engine.py:1335-1355), so NumPy's float32 semantics
-define these ops.  They run on the library's dct_* entry points over the
-engine's `Tensor` (a device fp32 buffer on the reference's tape autograd):
+define these ops.  They run on the library's dct_* entry points:
 
 * broadcast binary ops `add sub mul div maximum minimum` with NumPy's
   right-aligned broadcasting, bit-exact against NumPy float32;
@@ -18,27 +17,55 @@ engine's `Tensor` (a device fp32 buffer on the reference's tape autograd):
   (float64 accumulation; first index on ties; NaN is the maximum); `sum` and
   `mean` are differentiable;
 * `softmax_cross_entropy`: the fused row softmax + mean cross-entropy; its
-  forward pass also writes dlogits, so the backward is one scaled copy.
+  forward pass also writes dlogits, so the backward is one scaled copy;
+* `bias_relu` (the reference's bias_relu shader, nn_bias_relu.hlsl:8-12) whose
+  backward is one fused pass (dct_bias_relu_backward), and `batch_norm2d`
+  (training statistics, running-stat update, fused backward).
 
-There is no CPU fallback: importing this module needs libdct_cuda.so and a
-CUDA device (through `engine`).
+The graph is built on a tensor type with the reference Tensor's protocol
+(`gpu_buf`, `shape`, `requires_grad`, `grad`, `_ctx`, `_accumulate_grad`,
+`from_gpu`, `sync`).  By default that is `directcompute_torch_b200.tensor.
+DeviceTensor`; `bind(nn_engine)` makes the ops build on the reference's own
+`nn_engine.Tensor` instead (its module loaded over this library as
+`engine.dll`), so one tape holds both the reference's Functions and these ops.
+
+There is no CPU fallback: the ops need libdct_cuda.so and a CUDA device.
 """
 from __future__ import annotations
 
 import builtins
 import ctypes
+import struct
 
 import numpy as np
 
-from . import engine as E
+from . import load_library
 from ._abi import BINARY, REDUCE, UNARY, check
+from .tensor import DeviceTensor, Node
 
 __all__ = ["add", "sub", "mul", "div", "maximum", "minimum", "exp", "log_abs1p", "tanh", "sigmoid", "neg",
            "abs", "sum", "mean", "max", "min", "argmax", "argmin", "sum_to_shape", "broadcast_to",
-           "softmax_cross_entropy", "tensor", "to_numpy"]
+           "softmax_cross_entropy", "bias_relu", "batch_norm2d", "tensor", "to_numpy", "bind"]
 
-lib = E.lib
-Tensor = E.Tensor
+lib = load_library()
+Tensor = DeviceTensor
+
+
+def bind(module=None):
+    """Build the ops' graphs on `module.Tensor` (e.g. the reference's `nn_engine`,
+    loaded over this library); `bind()` returns to DeviceTensor.  Returns the
+    tensor type now in use."""
+    global Tensor
+    if module is None:
+        Tensor = DeviceTensor
+        return Tensor
+    t = getattr(module, "Tensor", None)
+    need = ("from_gpu", "sync", "_accumulate_grad", "backward")
+    if t is None or not all(hasattr(t, a) for a in need):
+        raise TypeError(f"bind: {module!r} has no Tensor type with {', '.join(need)}")
+    Tensor = t
+    _scalars.clear()
+    return Tensor
 
 
 def _shape_arr(shape):
@@ -60,13 +87,13 @@ def _buf(n):
     return h
 
 
+_scalars = {}
+
+
 def _wrap(h, shape, ctx=None, requires_grad=False):
     t = Tensor.from_gpu(h, tuple(shape), requires_grad=requires_grad)
     t._ctx = ctx
     return t
-
-
-_scalars = {}
 
 
 def _scalar(v: float):
@@ -147,7 +174,7 @@ def broadcast_to(x: Tensor, shape) -> Tensor:
 # ---------------------------------------------------------------------------
 # broadcast binary ops
 # ---------------------------------------------------------------------------
-class BinaryFunc(E.Function):
+class BinaryFunc(Node):
     def __init__(self, op):
         super().__init__()
         self.op = op
@@ -231,7 +258,7 @@ def minimum(a, b): return BinaryFunc("minimum").forward(_as_tensor(a), _as_tenso
 # ---------------------------------------------------------------------------
 # unary ops
 # ---------------------------------------------------------------------------
-class UnaryFunc(E.Function):
+class UnaryFunc(Node):
     # op -> (backward kernel, what it takes besides g: "y" the output or "x" the input)
     GRADS = {"exp": ("exp_grad", "y"), "tanh": ("tanh_grad", "y"), "sigmoid": ("sigmoid_grad", "y"),
              "log_abs1p": ("log_abs1p_grad", "x"), "neg": (None, None), "abs": (None, "x")}
@@ -290,7 +317,7 @@ def _view3(shape, axis):
     return outer, int(shape[ax]), inner, tuple(shape[:ax]) + tuple(shape[ax + 1:])
 
 
-class ReduceFunc(E.Function):
+class ReduceFunc(Node):
     def __init__(self, op, axis, keepdims):
         super().__init__()
         self.op, self.axis, self.keepdims = op, axis, keepdims
@@ -363,7 +390,7 @@ def argmin(x, axis=None):
 # ---------------------------------------------------------------------------
 # fused softmax + cross-entropy
 # ---------------------------------------------------------------------------
-class SoftmaxCrossEntropyFunc(E.Function):
+class SoftmaxCrossEntropyFunc(Node):
     """Mean cross-entropy of row softmax; one kernel writes probs, the loss and dlogits."""
 
     def forward(self, logits: Tensor, labels: Tensor, want_probs=False):
@@ -394,3 +421,114 @@ def softmax_cross_entropy(logits: Tensor, labels: Tensor, return_probs=False):
     f = SoftmaxCrossEntropyFunc()
     loss = f.forward(logits, labels, want_probs=return_probs)
     return (loss, f.probs) if return_probs else loss
+
+
+# ---------------------------------------------------------------------------
+# bias + ReLU with the fused backward, BatchNorm2d
+# ---------------------------------------------------------------------------
+def _run_shader(name: str, srvs, uavs, groups, words):
+    """One reference dispatch by shader name with its cbuffer words; raises on a library error."""
+    lib.CompileShader(name.encode(), "")
+    lib.dct_clear_error()
+    sv = (ctypes.c_void_p * builtins.max(1, len(srvs)))(*srvs)
+    uv = (ctypes.c_void_p * builtins.max(1, len(uavs)))(*uavs)
+    th = (ctypes.c_uint * 3)(*groups)
+    cb = (ctypes.c_uint * builtins.max(1, len(words)))(*words)
+    lib.RunShader(name.encode(), sv, len(srvs), uv, len(uavs), th, ctypes.cast(cb, ctypes.c_void_p), 4 * len(words))
+    check(lib, lib.dct_error_code(), name)
+
+
+def _f2u(v: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", float(v)))[0]
+
+
+class BiasReLUFunc(Node):
+    """y = max(0, x + b) over rows (nn_bias_relu.hlsl:8-12); the backward writes dx and db in
+    one pass over the upstream gradient and y (dct_bias_relu_backward)."""
+
+    def forward(self, x, b):
+        self.inputs = (x, b)
+        M, N = x.size // b.size, b.size
+        if M * N != x.size or x.shape[-1] != N:
+            raise ValueError(f"bias_relu: bias of {b.size} does not match the rows of {x.shape}")
+        h = _buf(x.size)
+        _run_shader("bias_relu", [x.gpu_buf, b.gpu_buf], [h], ((x.size + 255) // 256, 1, 1), [M, N])
+        self.M, self.N = M, N
+        self.out = _wrap(h, x.shape, self, x.requires_grad or b.requires_grad)
+        return self.out
+
+    def backward(self, g):
+        x, b = self.inputs
+        dx, db = _buf(x.size), _buf(b.size)
+        check(lib, lib.dct_bias_relu_backward(g.gpu_buf, self.out.gpu_buf, dx, db, self.M, self.N),
+              "dct_bias_relu_backward")
+        if x.requires_grad:
+            x._accumulate_grad(_wrap(dx, x.shape))
+        else:
+            _release(dx)
+        if b.requires_grad:
+            b._accumulate_grad(_wrap(db, b.shape))
+        else:
+            _release(db)
+
+
+def bias_relu(x, b):
+    """max(0, x + b) with b broadcast over the rows of x."""
+    return BiasReLUFunc().forward(x, b)
+
+
+class BatchNorm2dFunc(Node):
+    """Training-mode BatchNorm over NCHW: batch statistics in float64, the running
+    statistics updated with momentum and the unbiased variance, then the apply
+    (nn_batchnorm_mean_var.hlsl, nn_batchnorm_forward.hlsl); the backward gives
+    dx, dgamma and dbeta (nn_batchnorm_backward_reduce.hlsl,
+    nn_batchnorm_backward_dx.hlsl) from two passes over x and dy."""
+
+    def forward(self, x, gamma, beta, running_mean, running_var, momentum=0.1, eps=1e-5):
+        if len(x.shape) != 4:
+            raise ValueError("batch_norm2d: x must be NCHW")
+        N, C, H, W = x.shape
+        self.inputs = (x, gamma, beta)
+        self.dims = (N, C, H * W)
+        self.eps = float(eps)
+        self.mean, self.var = _buf(C), _buf(C)
+        h = _buf(x.size)
+        check(lib, lib.dct_batchnorm_forward_train(x.gpu_buf, gamma.gpu_buf, beta.gpu_buf, running_mean.gpu_buf,
+                                                   running_var.gpu_buf, self.mean, self.var, h, N, C, H * W,
+                                                   float(eps), float(momentum)), "dct_batchnorm_forward_train")
+        return _wrap(h, x.shape, self, x.requires_grad or gamma.requires_grad or beta.requires_grad)
+
+    def backward(self, g):
+        x, gamma, beta = self.inputs
+        N, C, S = self.dims
+        dx, dg, db = _buf(x.size), _buf(C), _buf(C)
+        check(lib, lib.dct_batchnorm_backward(x.gpu_buf, g.gpu_buf, self.mean, self.var, gamma.gpu_buf, dg, db, dx,
+                                              N, C, S, self.eps), "dct_batchnorm_backward")
+        for t, h in ((x, dx), (gamma, dg), (beta, db)):
+            if t.requires_grad:
+                t._accumulate_grad(_wrap(h, t.shape))
+            else:
+                _release(h)
+
+    def __del__(self):
+        for k in ("mean", "var"):
+            h = getattr(self, k, None)
+            if h:
+                try:
+                    lib.ReleaseBuffer(h)
+                except Exception:
+                    pass
+                setattr(self, k, None)
+
+
+def batch_norm2d(x, gamma, beta, running_mean, running_var, training=True, momentum=0.1, eps=1e-5):
+    """BatchNorm over NCHW.  Training: batch statistics (the running ones updated in
+    place), differentiable in x, gamma and beta.  Evaluation: the running statistics,
+    no gradient (the reference's eval path, nn_engine.py:1794-1868)."""
+    if training:
+        return BatchNorm2dFunc().forward(x, gamma, beta, running_mean, running_var, momentum, eps)
+    N, C, H, W = x.shape
+    h = _buf(x.size)
+    _run_shader("batchnorm_forward", [x.gpu_buf, running_mean.gpu_buf, running_var.gpu_buf, gamma.gpu_buf,
+                                      beta.gpu_buf], [h], ((x.size + 255) // 256, 1, 1), [N, C, H * W, _f2u(eps)])
+    return _wrap(h, x.shape)

@@ -203,3 +203,82 @@ def test_chain_rule_through_broadcast(dev, ops):
     dz = 2 * z64 / z64.size
     np.testing.assert_allclose(ops.to_numpy(W.grad), (dz * x).sum(axis=0), rtol=1e-5, atol=1e-7)
     np.testing.assert_allclose(ops.to_numpy(Bt.grad), [dz.sum()], rtol=1e-5, atol=1e-7)
+
+
+# ---------------------------------------------------------------------------
+# bias + ReLU and BatchNorm2d ops against PyTorch (float32 on the CPU)
+# ---------------------------------------------------------------------------
+def test_dense_head_bias_relu_softmax_ce_vs_torch(dev, ops):
+    """softmax-CE(bias_relu(x, b)): the loss and both gradients, the backward of
+    bias_relu in one fused pass (dct_bias_relu_backward)."""
+    torch = pytest.importorskip("torch")
+    r = np.random.default_rng(23)
+    B, K = 64, 10
+    x = (2 * r.standard_normal((B, K))).astype(np.float32)
+    b = (0.1 * r.standard_normal(K)).astype(np.float32)
+    lab = r.integers(0, K, B)
+    X, Bt = ops.tensor(x, requires_grad=True), ops.tensor(b, requires_grad=True)
+    h = ops.bias_relu(X, Bt)
+    np.testing.assert_array_equal(ops.to_numpy(h), np.maximum(x + b, 0).astype(np.float32))
+    loss = ops.softmax_cross_entropy(h, ops.tensor(lab.astype(np.float32)))
+    loss.backward()
+    xt = torch.tensor(x, requires_grad=True)
+    bt = torch.tensor(b, requires_grad=True)
+    lt = torch.nn.functional.cross_entropy(torch.relu(xt + bt), torch.tensor(lab))
+    lt.backward()
+    assert abs(float(ops.to_numpy(loss)[0]) - float(lt.detach())) <= 1e-5 * abs(float(lt.detach()))
+    np.testing.assert_allclose(ops.to_numpy(X.grad), xt.grad.numpy(), rtol=1e-5, atol=1e-8)
+    np.testing.assert_allclose(ops.to_numpy(Bt.grad), bt.grad.numpy(), rtol=1e-5, atol=1e-8)
+
+
+def test_batch_norm2d_train_and_eval_vs_torch(dev, ops):
+    torch = pytest.importorskip("torch")
+    r = np.random.default_rng(24)
+    x = (0.5 + 2 * r.standard_normal((8, 4, 6, 6))).astype(np.float32)
+    g = r.standard_normal((8, 4, 6, 6)).astype(np.float32)
+    gamma, beta = r.random(4, dtype=np.float32) + 0.5, r.standard_normal(4).astype(np.float32)
+    X = ops.tensor(x, requires_grad=True)
+    G, Be = ops.tensor(gamma, requires_grad=True), ops.tensor(beta, requires_grad=True)
+    rm, rv = ops.tensor(np.zeros(4, np.float32)), ops.tensor(np.ones(4, np.float32))
+    y = ops.batch_norm2d(X, G, Be, rm, rv, training=True)
+    y.backward(ops.tensor(g))
+    bn = torch.nn.BatchNorm2d(4, eps=1e-5, momentum=0.1)
+    with torch.no_grad():
+        bn.weight.copy_(torch.tensor(gamma))
+        bn.bias.copy_(torch.tensor(beta))
+    xt = torch.tensor(x, requires_grad=True)
+    yt = bn(xt)
+    yt.backward(torch.tensor(g))
+    np.testing.assert_allclose(ops.to_numpy(y), yt.detach().numpy(), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(ops.to_numpy(X.grad), xt.grad.numpy(), rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(ops.to_numpy(G.grad), bn.weight.grad.numpy(), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(ops.to_numpy(Be.grad), bn.bias.grad.numpy(), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(ops.to_numpy(rm), bn.running_mean.numpy(), rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(ops.to_numpy(rv), bn.running_var.numpy(), rtol=1e-5, atol=1e-7)
+    bn.eval()
+    ye = ops.batch_norm2d(ops.tensor(x), G, Be, rm, rv, training=False)
+    np.testing.assert_allclose(ops.to_numpy(ye), bn(torch.tensor(x)).detach().numpy(), rtol=1e-5, atol=1e-5)
+
+
+def test_ops_build_on_a_bound_tensor_type(dev, ops):
+    """bind(module) puts the ops' graph on another tensor type with the reference
+    Tensor's protocol (here a subclass standing in for nn_engine.Tensor)."""
+    from directcompute_torch_b200.tensor import DeviceTensor
+
+    class Other(DeviceTensor):
+        __slots__ = ()
+
+    class Mod:
+        Tensor = Other
+    try:
+        assert ops.bind(Mod) is Other
+        a = ops.tensor(np.arange(6, dtype=np.float32).reshape(2, 3), requires_grad=True)
+        assert type(a) is Other
+        y = ops.sum(ops.mul(a, a))
+        y.backward()
+        assert type(a.grad) is Other or isinstance(a.grad, DeviceTensor)
+        np.testing.assert_allclose(ops.to_numpy(a.grad), 2 * np.arange(6, dtype=np.float32).reshape(2, 3))
+        with pytest.raises(TypeError):
+            ops.bind(object())
+    finally:
+        ops.bind()
