@@ -352,7 +352,9 @@ bool exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* s
     const int par = (int)(ep & 1);
     unsigned char* base = static_cast<unsigned char*>(D.region);
     const unsigned long long* slots = reinterpret_cast<const unsigned long long*>(base + slot_off(par, 0));
-    const double lim = D.timeout_s < 30.0 ? D.timeout_s : 30.0;
+    // the device gives up at 0.8 of the host's deadline, so its error (a peer's
+    // record did not arrive) reaches the host before the host's own deadline
+    const double lim = 0.8 * (D.timeout_s < 30.0 ? D.timeout_s : 30.0);
     const cudaError_t e = launch_pdl(
         k_peer_put_wait, dim3(D.world), dim3(256), 0, st, static_cast<const unsigned long long*>(rec), h,
         (void* const*)D.peer_dev, (uint64_t)slot_off(par, D.rank), (uint64_t)flag_off(par, D.rank), ep,
@@ -657,6 +659,20 @@ DCT_API int dct_dist_finalize(void) {
         all_gather(D.send, D.recv, 1, "dct_dist_finalize(barrier)") && !rt_wait_stream("dct_dist_finalize"))
       rc = DCT_ERR_DIST;
     peer_teardown();
+  } else if (D.aborted && !D.peer_base.empty()) {
+    // After an abort no barrier is possible, and other ranks may still hold this
+    // rank's region mapped: close this rank's mappings of theirs and keep its
+    // own region allocated until the process exits (a later dct_dist_init makes
+    // a new one).
+    if (!rt_wait_stream("dct_dist_finalize")) rc = DCT_ERR_DIST;
+    for (int q = 0; q < (int)D.peer_base.size(); ++q)
+      if (q != D.rank && D.peer_base[q]) cudaIpcCloseMemHandle(D.peer_base[q]);
+    D.peer_base.clear();
+    if (D.peer_dev) cudaFree(D.peer_dev);
+    D.peer_dev = nullptr;
+    D.region = nullptr;
+    D.epoch = 0;
+    cudaGetLastError();
   }
   if (D.comm) {
     if (!rt_wait_stream("dct_dist_finalize")) rc = DCT_ERR_DIST;

@@ -236,7 +236,16 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
     const bool lvalid = nvalid;
     const float lab = nlab;
     if (c.labels && r + rstep < c.rows) nlab = label_of(c.labels, c.labels_int32, r + rstep, K, nvalid);
-    mbar_wait(&bars[st], (k >> 1) & 1u, err);
+    const bool landed = mbar_wait(&bars[st], (k >> 1) & 1u, err);
+    if (__any_sync(0xffffffffu, !landed)) {
+      // the row never landed (the error bit is set): issue no more copies, write
+      // nothing for this row, and wait (bounded again) for the copies still in
+      // flight into this warp's stages before leaving, so none lands in shared
+      // memory after the block exits
+      mbar_wait(&bars[st], (k >> 1) & 1u, err);
+      if (r + rstep < c.rows) mbar_wait(&bars[st ^ 1], ((k + 1) >> 1) & 1u, err);
+      break;
+    }
     const uint32_t lidx = (!lvalid || !c.labels) ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
     // pass 1: row max, and whether any logit is -inf (exp(-inf - m) needs a guard)
     float m = c.ref_max_init ? -1e30f : -INFINITY;

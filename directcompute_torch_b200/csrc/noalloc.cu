@@ -98,7 +98,9 @@ extern "C" DCT_API int dct_batchnorm_forward_train_noalloc(const float* x, const
     note_error(DCT_ERR_SIZE, msg);
     return DCT_ERR_SIZE;
   }
-  if (planes == 0 || S == 0) return DCT_OK;
+  // an empty batch (N or S zero) runs the same launches as dct_batchnorm_forward_train:
+  // statistics over no elements (0 / 0) and their running update
+  if (C == 0) return DCT_OK;
   double* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch);
   if (rc != DCT_OK) return rc;

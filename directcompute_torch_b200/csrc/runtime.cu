@@ -129,6 +129,8 @@ static bool cuda_ok(cudaError_t e, const char* where) {
 
 static bool ensure_init();
 
+static DistHooks g_hooks;           // the sharding layer's wait hooks (set while a communicator is active)
+
 // Device code reports bounded-wait timeouts through a mapped host word; surface
 // them after every wait on the stream.
 static bool check_device_errors() {
@@ -136,9 +138,12 @@ static bool check_device_errors() {
   const uint32_t e = *(volatile uint32_t*)g.dev_err_host;
   if (!e) return true;
   *(volatile uint32_t*)g.dev_err_host = 0;
-  if (e & DCT_DEVERR_PEER_WAIT)
+  if (e & DCT_DEVERR_PEER_WAIT) {
+    // the ranks' exchange epochs no longer agree: the communicator cannot be used again
     set_error(DCT_ERR_DIST, "sharded op: a peer rank's record did not arrive before the deadline (a rank is "
-              "gone or behind; error bits 0x%x); results are invalid", e);
+              "gone or behind; error bits 0x%x); results are invalid; communicator aborted", e);
+    if (g_hooks.abort) g_hooks.abort();
+  }
   else if (e & DCT_DEVERR_PEER_INVALID)
     set_error(DCT_ERR_DIST, "sharded op: a rank's shard was invalid (bad handle, size or count on that rank; "
               "error bits 0x%x); results are invalid", e);
@@ -246,7 +251,6 @@ static bool ensure_ws(size_t bytes) {
 // ---------------------------------------------------------------------------
 // internal API for the other translation units (runtime_internal.h)
 // ---------------------------------------------------------------------------
-static DistHooks g_hooks;
 DistHooks& rt_dist_hooks() { return g_hooks; }
 std::recursive_mutex& rt_mutex() { return g_mu; }
 Buffer* rt_buf(void* h) { return buf_of(h); }

@@ -412,3 +412,87 @@ def test_worldn_sharded_ops_match_unsharded_oracle(transport):
             assert e[k] == 0, (r, k, e[k])
         for k in ("sum", "mean", "full_sum", "loss", "bn_mean", "bn_var", "bn_running", "bn_dgamma", "bn_dbeta"):
             assert e[k] <= 1e-5, (r, k, e[k])
+
+
+# ---------------------------------------------------------------------------
+# a live rank that skips one exchange (two GPUs): the bounded device wait
+# ---------------------------------------------------------------------------
+def _skip_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), DCT_DEVICE=str(rank),
+                      NCCL_NVLS_ENABLE="0", DCT_PEER_EXCHANGE="1")
+    try:
+        import torch  # noqa: F401  (loads PyTorch's NCCL first)
+        import torch.distributed as td
+        td.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+        from tests.devhelp import Dev
+        from directcompute_torch_b200.dist import Communicator
+        dev = Dev()
+        comm = Communicator.from_process_group(timeout_s=3)
+        out = {"peer": comm.peer_exchange}
+        v = np.ones(4096, np.float32)
+        hv, ho = dev.buf(v), dev.empty(1)
+        out["warm"] = comm.reduce_all("sum", hv, v.size, ho, want_host=True)     # every rank takes part
+        td.barrier()
+        if rank == 0:                         # rank 1 stays alive but skips this exchange
+            t0 = time.monotonic()
+            try:
+                comm.reduce_all("sum", hv, v.size, ho, want_host=True)
+                out["missed"] = None
+            except RuntimeError as e:
+                out["missed"] = str(e)
+            out["secs"] = time.monotonic() - t0
+        td.barrier()
+        # teardown without any kernel of ours in flight: the rank whose communicator
+        # was aborted closes its mappings first, then the other finalizes (its closing
+        # barrier over NCCL ends at the 3 s limit, since rank 0's communicator is gone)
+        for turn in range(world):
+            if rank == turn:
+                try:
+                    comm.close()
+                    out["close"] = "ok"
+                except RuntimeError as e:
+                    out["close"] = str(e)
+            td.barrier()
+        out["after"] = dev.reduce_all("sum", hv, v.size, ho)                      # the context still works
+        dev.free(hv, ho)
+        td.destroy_process_group()
+        q.put((rank, True, out))
+    except BaseException:
+        q.put((rank, False, traceback.format_exc()))
+
+
+def test_worldn_peer_wait_times_out_when_a_rank_skips_an_exchange():
+    """Two GPUs over the peer-memory exchange, timeout 3 s: rank 1 stays alive but
+    skips one dct_dist_reduce_all.  Rank 0's exchange kernel gives up at its bounded
+    %globaltimer wait and returns DCT_ERR_DIST naming the missing record, within the
+    limit; both ranks then close their communicators and keep a usable context."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_skip_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, ok, payload = q.get(timeout=300)
+            res[r] = (ok, payload)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        ok, e = res[r]
+        assert ok, e
+        print(f"rank {r}: {e}")
+        assert e["warm"] == 2 * 4096.0 and e["after"] == 4096.0, e
+        if not e["peer"]:
+            pytest.skip("the peer-memory exchange is not available between these GPUs")
+    e0 = res[0][1]
+    assert e0["missed"] is not None and "DIST" in e0["missed"] and "did not arrive" in e0["missed"], e0
+    assert 1.0 < e0["secs"] < 15.0, e0
