@@ -14,7 +14,9 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-REFERENCE_DIR = os.environ.get("DCT_REFERENCE_DIR", "/root/reference")
+# the reference checkout: DCT_REFERENCE_DIR, else a `reference` directory beside
+# this repository; the tests that need it skip when neither holds nn_engine.py
+REFERENCE_DIR = os.environ.get("DCT_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
 
 
 def pytest_configure(config):

@@ -220,4 +220,6 @@ def main(ref_dir: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DCT_REFERENCE_DIR", "/root/reference"))
+    _repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    main(sys.argv[1] if len(sys.argv) > 1 else
+         (os.environ.get("DCT_REFERENCE_DIR") or os.path.join(os.path.dirname(_repo), "reference")))

@@ -304,8 +304,14 @@ def _worldn_worker(rank, world, port, q, transport="peer"):
             got = dev.read(ho, np.int32 if op.startswith("arg") else np.float32)
             want = O.reduce(op, x, axis=0)
             if op in ("sum", "mean"):
+                # a true relative bound on the float64-accumulated result, plus the float64
+                # accumulation's own noise (1e-12 of sum|x|) where the column nearly cancels
+                x64 = x.astype(np.float64)
+                want = x64.sum(axis=0) / (1 if op == "sum" else R)
+                mag = np.abs(x64).sum(axis=0) / (1 if op == "sum" else R)
                 fin = np.isfinite(want)
-                errs[op] = float(np.max(np.abs(got[fin] - want[fin]) / np.maximum(np.abs(want[fin]), 1.0)))
+                err = np.abs(got[fin] - want[fin])
+                errs[op] = float(np.max(np.maximum(err - 1e-12 * mag[fin], 0.0) / np.abs(want[fin])))
             else:
                 errs[op] = int(np.sum(~((got == want) | (np.isnan(got.astype(np.float32)) & np.isnan(
                     want.astype(np.float32))))))
