@@ -187,12 +187,23 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_warp(const __grid_con
   }
 }
 
-// TMA-staged variant (K % 4 == 0, row <= 8 KB, no log-probs): each warp owns
-// a two-stage ring of row buffers in shared memory filled by 1-D bulk copies
-// completing on per-stage mbarriers, so row r+2 streams in while row r is
-// computed and the row costs no registers.  Three passes over shared memory:
-// max; exp written back in place with the float64 sum; probabilities and
-// gradients streamed out.  Every mbarrier wait is bounded (dct_tma.cuh).
+// TMA-staged variant (K % 4 == 0, row <= 8 KB, no log-probs).  Block b owns the
+// WPB * kTmaRows consecutive rows starting at b * WPB * kTmaRows; warp w takes
+// rows base + i * WPB + w, i < kTmaRows, so at every step a block's warps cover
+// WPB adjacent rows and the grid sweeps the logits in address order (blocks are
+// not persistent: the hardware scheduler starts them in index order, as in the
+// chunked elementwise schedule).  Each warp owns a two-stage ring of row buffers
+// in shared memory filled by 1-D bulk copies (the TMA engine) completing on
+// mbarriers: both of its rows are requested up front, so the second streams in
+// while the first is computed.  A landed row is read into registers (VPL float4
+// per lane) and its stage handed back at once; max, exp with the float64 sum,
+// then probabilities and gradients come from registers.  Every mbarrier wait is
+// bounded (dct_tma.cuh); a wait that runs out stops the warp's copies and output.
+// (The persistent grid-stride form of this kernel reached 0.84 of the copy peak
+// on logits[65536, 1000]; this schedule 0.99, at the level of a trivial-compute
+// probe of the same one-read, two-write row pattern.)
+constexpr int kTmaRows = 2;
+
 template <int VPL, int WPB, bool POW2>
 __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_constant__ RowCtx c, uint32_t buf_bytes,
                                                              uint32_t* err) {
@@ -205,18 +216,17 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
   float* const buf1 = reinterpret_cast<float*>(smem + 128 + (size_t)(2 * warp + 1) * buf_bytes);
   const uint32_t K = c.K;
   const uint32_t rb = K * 4u;
+  const uint32_t base = blockIdx.x * (uint32_t)(WPB * kTmaRows) + warp;
   if (lane == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     mbar_fence_init();
   }
   __syncwarp();
-  const uint32_t r0 = blockIdx.x * WPB + warp;
-  const uint32_t rstep = gridDim.x * WPB;
   if (lane == 0) {
 #pragma unroll
-    for (int s2 = 0; s2 < 2; ++s2) {
-      const uint32_t r = r0 + s2 * rstep;
+    for (int s2 = 0; s2 < 2 && s2 < kTmaRows; ++s2) {
+      const uint32_t r = base + s2 * WPB;
       if (r < c.rows) {
         mbar_arrive_expect_tx(&bars[s2], rb);
         bulk_load(s2 ? buf1 : buf0, c.logits + (uint64_t)r * K, rb, &bars[s2]);
@@ -225,44 +235,35 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
   }
   __syncwarp();
   double block_loss = 0.0;
-  uint32_t k = 0;
-  // labels are prefetched one row ahead: the global load's latency hides behind a row
-  bool nvalid = true;
-  float nlab = 0.0f;
-  if (c.labels && r0 < c.rows) nlab = label_of(c.labels, c.labels_int32, r0, K, nvalid);
-  for (uint32_t r = r0; r < c.rows; r += rstep, ++k) {
-    const int st = k & 1;
+#pragma unroll 1
+  for (int i = 0; i < kTmaRows; ++i) {
+    const uint32_t r = base + i * WPB;
+    if (r >= c.rows) break;
+    const int st = i & 1;
     float* row = st ? buf1 : buf0;
-    const bool lvalid = nvalid;
-    const float lab = nlab;
-    if (c.labels && r + rstep < c.rows) nlab = label_of(c.labels, c.labels_int32, r + rstep, K, nvalid);
-    const bool landed = mbar_wait(&bars[st], (k >> 1) & 1u, err);
+    bool lvalid = true;
+    float lab = 0.0f;
+    if (c.labels) lab = label_of(c.labels, c.labels_int32, r, K, lvalid);
+    const bool landed = mbar_wait(&bars[st], (uint32_t)(i >> 1) & 1u, err);
     if (__any_sync(0xffffffffu, !landed)) {
       // the row never landed (the error bit is set): issue no more copies, write
       // nothing for this row, and wait (bounded again) for the copies still in
       // flight into this warp's stages before leaving, so none lands in shared
       // memory after the block exits
-      mbar_wait(&bars[st], (k >> 1) & 1u, err);
-      if (r + rstep < c.rows) mbar_wait(&bars[st ^ 1], ((k + 1) >> 1) & 1u, err);
+      mbar_wait(&bars[st], (uint32_t)(i >> 1) & 1u, err);
+      if (i + 1 < kTmaRows && r + WPB < c.rows) mbar_wait(&bars[st ^ 1], (uint32_t)((i + 1) >> 1) & 1u, err);
       break;
     }
     const uint32_t lidx = (!lvalid || !c.labels) ? 0xffffffffu : (c.labels_int32 ? (uint32_t)lab : hlsl_f2u(lab));
-    // pass 1: row max, and whether any logit is -inf (exp(-inf - m) needs a guard)
-    float m = c.ref_max_init ? -1e30f : -INFINITY;
-    float mn = INFINITY;
+    float4 x[VPL];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
-      if (col < K) {
-        const float4 v = *reinterpret_cast<const float4*>(row + col);
-        m = fmaxf(fmaxf(m, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
-        mn = fminf(fminf(mn, fminf(v.x, v.y)), fminf(v.z, v.w));
-      }
+      x[j] = col < K ? *reinterpret_cast<const float4*>(row + col)
+                     : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
     }
-    m = warp_max_f(m);
-    const bool ninf = __any_sync(0xffffffffu, mn == -INFINITY);
-    // the label's logit, from shared memory before pass 2 overwrites the row (a
-    // label >= K reads the flat buffer at r*K + label, as the reference's loss does)
+    // the label's logit (a label >= K reads the flat buffer at r*K + label, as the
+    // reference's loss does)
     float xl = 0.0f;
     if (c.want_loss && lvalid) {
       if (lidx < K) {
@@ -272,50 +273,61 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
         xl = li < c.total ? c.logits[li] : 0.0f;
       }
     }
-    // pass 2: e = exp(x - m) in place, float64 normaliser
-    double sacc = 0.0;
-    if (!ninf) {
+    // hand the stage back to the bulk-copy engine for this warp's row i + 2
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && i + 2 < kTmaRows) {
+      const uint32_t nr = r + 2 * WPB;
+      if (nr < c.rows) {
+        mbar_arrive_expect_tx(&bars[st], rb);
+        bulk_load(row, c.logits + (uint64_t)nr * K, rb, &bars[st]);
+      }
+    }
+    // row max, and whether any logit is -inf (exp(-inf - m) needs a guard)
+    float m = c.ref_max_init ? -1e30f : -INFINITY;
+    float mn = INFINITY;
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
-        if (col < K) {
-          float4 v = *reinterpret_cast<const float4*>(row + col);
+    for (int j = 0; j < VPL; ++j) {
+      m = fmaxf(fmaxf(m, fmaxf(x[j].x, x[j].y)), fmaxf(x[j].z, x[j].w));
+      const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+      if (col < K) mn = fminf(fminf(mn, fminf(x[j].x, x[j].y)), fminf(x[j].z, x[j].w));
+    }
+    m = warp_max_f(m);
+    const bool ninf = __any_sync(0xffffffffu, mn == -INFINITY);
+    // e = exp(x - m), float64 normaliser (padding slots are -inf and give 0)
+    double sacc = 0.0;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
+      if (col < K) {
+        float4 v = x[j];
+        if (!ninf) {
           v.x = exp_diff(v.x, m);
           v.y = exp_diff(v.y, m);
           v.z = exp_diff(v.z, m);
           v.w = exp_diff(v.w, m);
-          sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
-          *reinterpret_cast<float4*>(row + col) = v;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
-        if (col < K) {
-          float4 v = *reinterpret_cast<const float4*>(row + col);
+        } else {
           v.x = (v.x == -INFINITY) ? 0.0f : exp_diff(v.x, m);
           v.y = (v.y == -INFINITY) ? 0.0f : exp_diff(v.y, m);
           v.z = (v.z == -INFINITY) ? 0.0f : exp_diff(v.z, m);
           v.w = (v.w == -INFINITY) ? 0.0f : exp_diff(v.w, m);
-          sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
-          *reinterpret_cast<float4*>(row + col) = v;
         }
+        sacc += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
+        x[j] = v;
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
     const float invf = (float)__drcp_rn(sacc);          // correctly rounded 1/sum, then rounded to float
-    __syncwarp();
-    // pass 3: probabilities and gradients (p - onehot) / B: p / B everywhere, the
-    // label's one element patched in its float4
+    // probabilities and gradients (p - onehot) / B: p / B everywhere, the label's
+    // one element patched in its float4
     float* prow = c.probs ? c.probs + (uint64_t)r * K : nullptr;
     float* grow = c.dlogits ? c.dlogits + (uint64_t)r * K : nullptr;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const uint32_t col = (uint32_t)(lane + 32 * j) * 4;
       if (col < K) {
-        const float4 e = *reinterpret_cast<const float4*>(row + col);
+        const float4 e = x[j];
         const float4 p = make_float4(__fmul_rn(e.x, invf), __fmul_rn(e.y, invf), __fmul_rn(e.z, invf),
                                      __fmul_rn(e.w, invf));
         if (prow) st_stream4(prow + col, p);
@@ -343,17 +355,6 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
       // float log of the row sum: about 1 ulp of log(sum), far below the loss's rel 1e-5
       block_loss += -(((double)xl - (double)m) - (double)logf((float)sacc));
     }
-    // hand the stage back to the bulk-copy engine for row r + 2*rstep
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      const uint32_t nr = r + 2 * rstep;
-      if (nr < c.rows) {
-        mbar_arrive_expect_tx(&bars[st], rb);
-        bulk_load(row, c.logits + (uint64_t)nr * K, rb, &bars[st]);
-      }
-    }
-    __syncwarp();
   }
   if (c.want_loss) {
     if (lane == 0) wsum[warp] = block_loss;
@@ -451,17 +452,10 @@ int softmax_blocks(uint32_t rows, uint32_t K) {
 static uint32_t tma_stage_bytes(uint32_t K) { return ((K * 4u) + 15u) & ~15u; }
 static int tma_warps(uint32_t K) { return tma_stage_bytes(K) <= 4096 ? 7 : 4; }
 
-// blocks of the TMA-staged kernel: up to 4 per SM (shared memory bound), one
-// row per warp per step
+// blocks of the TMA-staged kernel: one per WPB * kTmaRows consecutive rows
 int tma_blocks(uint32_t rows, uint32_t K) {
-  const uint32_t buf_bytes = tma_stage_bytes(K);
-  const int wpb = tma_warps(K);
-  const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
-  const DevInfo& di = dev_info();
-  const int per_sm = std::min<int>(4, std::max<int>(1, (int)((228u * 1024u) / (smem + 1024))));
-  const uint64_t need = ((uint64_t)rows + wpb - 1) / wpb;
-  const uint64_t cap = (uint64_t)di.sm_count * per_sm;
-  return (int)std::max<uint64_t>(1, std::min(need, cap));
+  const uint64_t per = (uint64_t)tma_warps(K) * kTmaRows;
+  return (int)std::max<uint64_t>(1, ((uint64_t)rows + per - 1) / per);
 }
 
 size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K) {
