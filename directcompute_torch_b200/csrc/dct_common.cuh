@@ -38,9 +38,6 @@ uint32_t* device_error_word();   // defined in runtime.cu
 // sets one leaves it zero when the pair is done.
 constexpr uint32_t kDeviceFlags = 64;
 uint32_t* device_flags();        // defined in runtime.cu
-// word 0: the max-pool gather's fix-up flag; word 1: the softmax-CE kernel's
-// count of finished blocks (its last block folds the loss partials)
-constexpr uint32_t kFlagSoftmaxFold = 1;
 
 // Blocks for a grid-stride kernel of `threads`-thread blocks covering `work`
 // independent items: enough to fill every SM `waves` times, never more than

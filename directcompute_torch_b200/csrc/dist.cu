@@ -860,7 +860,6 @@ DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, ui
     a.loss_partial = bt ? rec : nullptr;
     a.grad_div = grad_div;
     a.err = device_error_word();
-    a.fold_counter = device_flags() ? device_flags() + kFlagSoftmaxFold : nullptr;
     if (!rt_ensure_ws(softmax_ce_ws_bytes(rows, K))) return DCT_ERR_CUDA;
     if (!rt_cuda_ok(launch_softmax_ce(a, rt_ws(), st), W)) valid = false;
     ran = valid && a.loss_partial;

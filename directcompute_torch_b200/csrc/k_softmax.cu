@@ -68,12 +68,6 @@ struct RowCtx {
   float* dlogits;
   float* logprobs;
   double* part;            // per-block fp64 loss partials
-  // the TMA kernel folds the partials itself in its last block when `counter`
-  // (a zeroed device word, zeroed again by that block) is given
-  uint32_t* counter;
-  float* loss;             // loss = sum / loss_div
-  double* loss_raw;        // the raw float64 sum (sharded combine)
-  double loss_div;
   float grad_div;
   bool grad_div_pow2;
   float grad_mul;
@@ -363,34 +357,12 @@ __global__ void __launch_bounds__(WPB * 32) k_softmax_ce_tma(const __grid_consta
     }
   }
   if (c.want_loss) {
-    __shared__ bool last;
     if (lane == 0) wsum[warp] = block_loss;
     __syncthreads();
     if (threadIdx.x == 0) {
       double t = 0.0;
       for (int w = 0; w < WPB; ++w) t += wsum[w];
       c.part[blockIdx.x] = t;
-      last = false;
-      if (c.counter) {
-        __threadfence();                                  // this block's partial before its count
-        last = atomicAdd(c.counter, 1u) == gridDim.x - 1;
-      }
-    }
-    __syncthreads();
-    if (last) {
-      // the last block folds every partial in a fixed order (thread k takes
-      // partials k, k + blockDim, ...; then a fixed shuffle tree), so the loss is
-      // the same whichever block finishes last; then it re-zeroes the counter
-      __threadfence();
-      double acc = 0.0;
-      for (uint32_t k = threadIdx.x; k < gridDim.x; k += blockDim.x) acc += __ldcg(c.part + k);
-      __shared__ double sh[32];
-      const double t = block_sum(acc, sh);
-      if (threadIdx.x == 0) {
-        if (c.loss_raw) c.loss_raw[0] = t;
-        if (c.loss) c.loss[0] = (float)(t / c.loss_div);
-        *c.counter = 0u;
-      }
     }
   }
 }
@@ -515,10 +487,6 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
   c.want_loss = (a.loss != nullptr || a.loss_partial != nullptr) && a.labels != nullptr;
   c.part = (double*)ws;
   if (c.want_loss && !ws) return cudaErrorInvalidValue;
-  c.counter = nullptr;
-  c.loss = a.loss;
-  c.loss_raw = a.loss_partial;
-  c.loss_div = a.loss_div;
   c.grad_div = a.grad_div;
   int ex = 0;
   const float fr = frexpf(a.grad_div, &ex);
@@ -534,7 +502,6 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
     const int wpb = tma_warps(K);
     const size_t smem = 128 + (size_t)2 * wpb * buf_bytes;
     const int blocks_t = tma_blocks(a.rows, K);
-    c.counter = a.fold_counter;               // the kernel folds the loss itself when it has a counter
     cudaError_t e = cudaSuccess;
 #define DCT_SM_TMA2(VPL, WPB, P2)                                                                             \
   do {                                                                                                        \
@@ -559,7 +526,7 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
 #undef DCT_SM_TMA2
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();
-    if (e != cudaSuccess || !c.want_loss || c.counter) return e;
+    if (e != cudaSuccess || !c.want_loss) return e;
     launch_pdl(k_loss_final, dim3(1), dim3(1024), 0, st, c.part, blocks_t, a.loss_div, a.loss, a.loss_partial);
     return cudaGetLastError();
   }

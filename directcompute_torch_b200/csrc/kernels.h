@@ -119,9 +119,6 @@ struct SoftmaxCEArgs {
   float grad_div = 1.0f;
   bool ref_max_init = false;       // true: max starts at -1e30 (nn_softmax.hlsl:8)
   uint32_t* err = nullptr;         // device-visible error word (bounded waits)
-  // a zeroed device word the row kernel may use to fold the loss in its last
-  // block (left zeroed); null: a separate fold launch
-  uint32_t* fold_counter = nullptr;
 };
 size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K);
 cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st);

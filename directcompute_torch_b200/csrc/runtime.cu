@@ -700,7 +700,6 @@ static bool h_conv_grad_reshape_relu(const Disp& d) { return conv_grad_reshape(d
 // ---- softmax / CE -------------------------------------------------------------
 static bool run_softmax_ce(const Disp& d, SoftmaxCEArgs a) {
   a.err = g.dev_err_dev;
-  a.fold_counter = g.flags ? g.flags + kFlagSoftmaxFold : nullptr;
   const size_t ws = softmax_ce_ws_bytes(a.rows, a.K);
   if (!ensure_ws(ws)) return false;
   LAUNCH(launch_softmax_ce(a, g.ws, g.stream));
