@@ -177,6 +177,12 @@ class Clocks:
                 self.h = N.nvmlDeviceGetHandleByIndex(0)
             self.N = N
             self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            # one untimed round of the queries the sampler makes: the first calls are slow
+            # and would otherwise eat a short timed region
+            N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+            N.nvmlDeviceGetPowerUsage(self.h)
+            (getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or
+             N.nvmlDeviceGetCurrentClocksThrottleReasons)(self.h)
         except Exception as e:                      # no NVML: record why
             self.err = repr(e)
             return self
