@@ -34,6 +34,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <chrono>
 #include <condition_variable>
 #include <memory>
@@ -44,6 +45,7 @@
 #include <vector>
 
 #include "dct_common.cuh"
+#include "dct_peer.cuh"
 #include "kernels.h"
 #include "runtime_internal.h"
 #include "../../include/dct_cuda.h"
@@ -256,11 +258,6 @@ size_t flag_off(int par, int q) { return 2 * (size_t)D.world * D.slot_bytes + ((
 __global__ void k_check_axis_shards(const unsigned long long* all, int world, uint64_t stride, uint64_t nout,
                                     uint32_t* err);
 
-// The host-known part of a record: n u64 words (bit patterns) at offset `off`.
-struct Hdr {
-  uint32_t off = 0, n = 0;
-  unsigned long long v[4] = {0, 0, 0, 0};
-};
 unsigned long long f64_bits(double d) {
   unsigned long long u;
   memcpy(&u, &d, sizeof(u));
@@ -273,78 +270,22 @@ Hdr make_hdr(uint32_t off, std::initializer_list<unsigned long long> v) {
   return h;
 }
 
-// The whole gather over peer memory, one kernel.  Block q < world writes this
-// rank's record into rank q's slot (the device part rec[0, h.off), then the
-// header words), fences at system scope and stores the epoch into rank q's
-// flag for this rank (release).  Block 0 then waits, bounded by %globaltimer,
-// for every rank's flag here, and for axis records checks that the shards
-// tile the axis.  The kernel's blocks (world <= 256) are all resident before a
-// dependent kernel can be scheduled, and block 0 waits only on other GPUs.
-__global__ void __launch_bounds__(256) k_peer_put_wait(const unsigned long long* __restrict__ rec, Hdr h,
-                                                       void* const* __restrict__ bases, uint64_t slot_off,
-                                                       uint64_t flag_off, unsigned long long epoch,
-                                                       const unsigned long long* flags, int world,
-                                                       unsigned long long timeout_ns, uint32_t* err,
-                                                       const unsigned long long* slots, uint64_t stride,
-                                                       int64_t axis_nout) {
-  pdl_entry();                                         // rec comes from the previous kernel
-  unsigned char* base = static_cast<unsigned char*>(bases[blockIdx.x]);
-  unsigned long long* dst = reinterpret_cast<unsigned long long*>(base + slot_off);
-  const uint64_t n = h.off;
-  const uint64_t n2 = n >> 1;
-  const uint4* s4 = reinterpret_cast<const uint4*>(rec);
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
-  for (uint64_t i = threadIdx.x; i < n2; i += blockDim.x) d4[i] = s4[i];
-  if ((n & 1) && threadIdx.x == 0) dst[n - 1] = rec[n - 1];
-  if (threadIdx.x < h.n) dst[n + threadIdx.x] = h.v[threadIdx.x];
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long* flag = reinterpret_cast<unsigned long long*>(base + flag_off);
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(epoch) : "memory");
-  }
-  if (blockIdx.x != 0) return;
-  for (int q = threadIdx.x; q < world; q += blockDim.x) {
-    unsigned long long t0, t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-      unsigned long long v;
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + q) : "memory");
-      if (v >= epoch) break;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (t - t0 > timeout_ns) {
-        if (err) atomicOr(err, DCT_DEVERR_PEER_WAIT);
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  __syncthreads();
-  // axis-reduction records: the shards must tile [0, len_total) in rank order
-  if (axis_nout >= 0 && threadIdx.x == 0) {
-    const uint64_t nout = (uint64_t)axis_nout;
-    unsigned long long expect = 0, total = slots[nout + 2];
-    bool ok = true;
-    for (int r = 0; r < world; ++r) {
-      const unsigned long long* hh = slots + (uint64_t)r * stride + nout;
-      ok &= (hh[3] == 1ull) && (hh[0] == expect) && (hh[2] == total);
-      expect += hh[1];
-    }
-    ok &= (expect == total);
-    if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
-  }
-}
-
 // header words written into a local record (the NCCL path)
 __global__ void k_put_u64(unsigned long long* rec, Hdr h) {
   if (threadIdx.x < h.n) rec[h.off + threadIdx.x] = h.v[threadIdx.x];
 }
 
 // Gather every rank's record: the device part rec[0, h.off) plus the header
-// words h; *all = the records, record q at *all + q * *stride.  axis_nout >= 0
-// also checks axis-reduction shard headers (at word axis_nout of each record).
-bool exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* stride, const char* where,
-              int64_t axis_nout = -1) {
+// words h.  Over peer memory nothing is launched here: *px describes the put
+// and the wait, which the caller's fold kernel runs itself (dct_peer.cuh), and
+// the function returns XCH_PEER.  Over NCCL the all-gather runs now, *all =
+// the records (record q at *all + q * *stride), and it returns XCH_NCCL; the
+// caller folds with a separate kernel.  axis_nout >= 0 also checks
+// axis-reduction shard headers (at word axis_nout of each record).  XCH_FAIL:
+// the error is recorded.
+enum Xch { XCH_FAIL = 0, XCH_NCCL = 1, XCH_PEER = 2 };
+Xch exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* stride, PeerXfer* px,
+             const char* where, int64_t axis_nout = -1) {
   cudaStream_t st = rt_stream();
   const size_t n = (size_t)h.off + h.n;
   if (D.peer && n * 8 <= D.slot_bytes) {
@@ -355,27 +296,45 @@ bool exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* s
     // the device gives up at 0.8 of the host's deadline, so its error (a peer's
     // record did not arrive) reaches the host before the host's own deadline
     const double lim = 0.8 * (D.timeout_s < 30.0 ? D.timeout_s : 30.0);
-    const cudaError_t e = launch_pdl(
-        k_peer_put_wait, dim3(D.world), dim3(256), 0, st, static_cast<const unsigned long long*>(rec), h,
-        (void* const*)D.peer_dev, (uint64_t)slot_off(par, D.rank), (uint64_t)flag_off(par, D.rank), ep,
-        reinterpret_cast<const unsigned long long*>(base + flag_off(par, 0)), D.world,
-        (unsigned long long)(lim * 1e9), device_error_word(), slots, (uint64_t)(D.slot_bytes / 8),
-        (int64_t)axis_nout);
+    px->rec = static_cast<const unsigned long long*>(rec);
+    px->h = h;
+    px->bases = (void* const*)D.peer_dev;
+    px->slot_off = (uint64_t)slot_off(par, D.rank);
+    px->flag_off = (uint64_t)flag_off(par, D.rank);
+    px->epoch = ep;
+    px->flags = reinterpret_cast<const unsigned long long*>(base + flag_off(par, 0));
+    px->world = D.world;
+    px->timeout_ns = (unsigned long long)(lim * 1e9);
+    px->err = device_error_word();
+    px->slots = slots;
+    px->stride = (uint64_t)(D.slot_bytes / 8);
+    px->axis_nout = axis_nout;
     *all = slots;
     *stride = D.slot_bytes / 8;
-    return rt_cuda_ok(e, where);
+    return XCH_PEER;
   }
   unsigned long long* r64 = static_cast<unsigned long long*>(rec);
   if (h.n) k_put_u64<<<1, 32, 0, st>>>(r64, h);
-  if (!rt_cuda_ok(cudaGetLastError(), where)) return false;
-  if (!all_gather(rec, D.recv, n, where)) return false;
+  if (!rt_cuda_ok(cudaGetLastError(), where)) return XCH_FAIL;
+  if (!all_gather(rec, D.recv, n, where)) return XCH_FAIL;
   *all = static_cast<const unsigned long long*>(D.recv);
   *stride = n;
   if (axis_nout >= 0) {
     k_check_axis_shards<<<1, 32, 0, st>>>(*all, D.world, n, (uint64_t)axis_nout, device_error_word());
-    if (!rt_cuda_ok(cudaGetLastError(), where)) return false;
+    if (!rt_cuda_ok(cudaGetLastError(), where)) return XCH_FAIL;
   }
-  return true;
+  return XCH_NCCL;
+}
+
+// blocks of a put-wait-fold kernel: every rank's put block, enough to fold
+// `work` items 256 at a time, never more than one per SM (all resident at once,
+// since every block waits for every rank's record, its own rank's included)
+unsigned fold_blocks(uint64_t work) {
+  uint64_t b = (work + 255) / 256;
+  const uint64_t cap = (uint64_t)std::max(D.world, dev_info().sm_count);
+  if (b > cap) b = cap;
+  if (b < (uint64_t)D.world) b = (uint64_t)D.world;
+  return (unsigned)b;
 }
 
 void peer_teardown() {
@@ -468,11 +427,9 @@ __global__ void k_check_axis_shards(const unsigned long long* all, int world, ui
 }
 
 // Full reduction records [value, count, valid, -]: fold in rank order.
-// post: 0 none, 1 mean (divide by the total count).
-__global__ void k_fold_full(const double* all, uint64_t stride, int world, int op, int post, float* out32,
-                            double* out64, uint32_t* err) {
-  grid_dep_wait();
-  if (threadIdx.x != 0) return;
+// post: 0 none, 1 mean (divide by the total count).  One thread.
+DCT_DEV void fold_full(const double* all, uint64_t stride, int world, int op, int post, float* out32,
+                       double* out64, uint32_t* err) {
   double acc = 0.0, cnt = 0.0;
   bool ok = true, first = true;
   const bool ext = (op == RED_MAX || op == RED_MIN);
@@ -500,10 +457,8 @@ __global__ void k_fold_full(const double* all, uint64_t stride, int world, int o
   if (out64) out64[0] = acc;
 }
 
-// Softmax-CE records [sum of row losses, rows, valid, -] -> loss = sum / div
-__global__ void k_fold_loss(const double* all, uint64_t stride, int world, double div, float* loss, uint32_t* err) {
-  grid_dep_wait();
-  if (threadIdx.x != 0) return;
+// Softmax-CE records [sum of row losses, rows, valid, -] -> loss = sum / div.  One thread.
+DCT_DEV void fold_loss(const double* all, uint64_t stride, int world, double div, float* loss, uint32_t* err) {
   double acc = 0.0;
   bool ok = true;
   for (int r = 0; r < world; ++r) {
@@ -515,11 +470,9 @@ __global__ void k_fold_loss(const double* all, uint64_t stride, int world, doubl
 }
 
 // Channel-sum records [nsum sums][count, valid, nsum, -]: out[j] = sum over
-// ranks in rank order; out[nsum] = total count.
-__global__ void k_fold_sums(const double* all, uint64_t stride, int world, uint32_t nsum, double* out,
-                            uint32_t* err) {
-  grid_dep_wait();
-  const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+// ranks in rank order; out[nsum] = total count.  Item j of nsum + 1.
+DCT_DEV void fold_sums(const double* all, uint64_t stride, int world, uint32_t nsum, double* out, uint32_t* err,
+                       uint32_t j) {
   if (j < nsum) {
     double acc = all[j];
     for (int r = 1; r < world; ++r) acc += all[(uint64_t)r * stride + j];
@@ -535,6 +488,45 @@ __global__ void k_fold_sums(const double* all, uint64_t stride, int world, uint3
     out[nsum] = cnt;
     if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
   }
+}
+
+// the folds after an NCCL all-gather
+__global__ void k_fold_full(const double* all, uint64_t stride, int world, int op, int post, float* out32,
+                            double* out64, uint32_t* err) {
+  grid_dep_wait();
+  if (threadIdx.x == 0) fold_full(all, stride, world, op, post, out32, out64, err);
+}
+__global__ void k_fold_loss(const double* all, uint64_t stride, int world, double div, float* loss, uint32_t* err) {
+  grid_dep_wait();
+  if (threadIdx.x == 0) fold_loss(all, stride, world, div, loss, err);
+}
+__global__ void k_fold_sums(const double* all, uint64_t stride, int world, uint32_t nsum, double* out,
+                            uint32_t* err) {
+  grid_dep_wait();
+  fold_sums(all, stride, world, nsum, out, err, blockIdx.x * blockDim.x + threadIdx.x);
+}
+
+// the same folds over peer memory: put, wait and fold in one launch (dct_peer.cuh)
+__global__ void __launch_bounds__(256) k_peer_fold_full(const __grid_constant__ PeerXfer p, int op, int post,
+                                                        float* out32, double* out64) {
+  pdl_entry();                                         // the record comes from the previous kernel
+  peer_put_wait(p);
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    fold_full(reinterpret_cast<const double*>(p.slots), p.stride, p.world, op, post, out32, out64, p.err);
+}
+__global__ void __launch_bounds__(256) k_peer_fold_loss(const __grid_constant__ PeerXfer p, double div,
+                                                        float* loss) {
+  pdl_entry();
+  peer_put_wait(p);
+  if (blockIdx.x == 0 && threadIdx.x == 0)
+    fold_loss(reinterpret_cast<const double*>(p.slots), p.stride, p.world, div, loss, p.err);
+}
+__global__ void __launch_bounds__(256) k_peer_fold_sums(const __grid_constant__ PeerXfer p, uint32_t nsum,
+                                                        double* out) {
+  pdl_entry();
+  peer_put_wait(p);
+  for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j <= nsum; j += gridDim.x * blockDim.x)
+    fold_sums(reinterpret_cast<const double*>(p.slots), p.stride, p.world, nsum, out, p.err, j);
 }
 
 Buffer* live(void* h) { return h ? rt_buf(h) : nullptr; }
@@ -769,14 +761,18 @@ DCT_API int dct_dist_reduce(int op, void* x, uint64_t outer, uint64_t len, uint6
   // header [offset, len, len_total, valid] after the nout packed partials
   const unsigned long long* all = nullptr;
   size_t xs = 0;
-  if (!exchange(send, make_hdr((uint32_t)nout, {len_offset, len, len_total, valid ? 1ull : 0ull}), &all, &xs, W,
-                (int64_t)nout))
-    return DCT_ERR_DIST;
+  PeerXfer px;
+  const Xch how = exchange(send, make_hdr((uint32_t)nout, {len_offset, len, len_total, valid ? 1ull : 0ull}), &all,
+                           &xs, &px, W, (int64_t)nout);
+  if (how == XCH_FAIL) return DCT_ERR_DIST;
   float* o32 = bo ? bo->d : nullptr;
   int32_t* oi = bi ? reinterpret_cast<int32_t*>(bi->d) : nullptr;
   if (arg && !oi) { oi = reinterpret_cast<int32_t*>(o32); o32 = nullptr; }   // indices into out (dct_reduce rule)
+  if (!valid) { o32 = nullptr; oi = nullptr; }                                // still puts and waits: no outputs
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess && valid)
+  if (e == cudaSuccess && how == XCH_PEER)
+    e = launch_peer_fold_axis(op_run, px, fold_blocks(nout), nout, len_total, o32, oi, st);
+  else if (e == cudaSuccess && valid)
     e = launch_fold_packed(op_run, all, (uint32_t)D.world, nout, xs, len_total, o32, oi, st);
   if (!rt_cuda_ok(e, W)) return DCT_ERR_CUDA;
   if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_reduce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
@@ -813,11 +809,16 @@ DCT_API int dct_dist_reduce_all(int op, void* x, uint64_t n, void* out, double* 
   const Hdr h = ran ? make_hdr(1, {hn, hv, 0ull}) : make_hdr(0, {0ull, hn, hv, 0ull});
   const unsigned long long* all = nullptr;
   size_t xs = 0;
-  if (!exchange(rec, h, &all, &xs, W)) return DCT_ERR_DIST;
-  if (!rt_cuda_ok(launch_pdl(k_fold_full, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
-                             local_op, op == RED_MEAN ? 1 : 0, valid ? bo->d : nullptr, D.fold, device_error_word()),
-                  W))
-    return DCT_ERR_CUDA;
+  PeerXfer px;
+  const Xch how = exchange(rec, h, &all, &xs, &px, W);
+  if (how == XCH_FAIL) return DCT_ERR_DIST;
+  const cudaError_t fe =
+      how == XCH_PEER
+          ? launch_pdl(k_peer_fold_full, dim3(fold_blocks(1)), dim3(256), 0, st, px, local_op, op == RED_MEAN ? 1 : 0,
+                       valid ? bo->d : nullptr, D.fold)
+          : launch_pdl(k_fold_full, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world, local_op,
+                       op == RED_MEAN ? 1 : 0, valid ? bo->d : nullptr, D.fold, device_error_word());
+  if (!rt_cuda_ok(fe, W)) return DCT_ERR_CUDA;
   if (host_out64) {
     double* hs = rt_host_scratch();
     if (!rt_cuda_ok(cudaMemcpyAsync(hs, D.fold, 8, cudaMemcpyDeviceToHost, st), W)) return DCT_ERR_CUDA;
@@ -868,11 +869,16 @@ DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, ui
   const Hdr h = ran ? make_hdr(1, {hr, hv, 0ull}) : make_hdr(0, {0ull, hr, hv, 0ull});
   const unsigned long long* all = nullptr;
   size_t xs = 0;
-  if (!exchange(rec, h, &all, &xs, W)) return DCT_ERR_DIST;
-  if (!rt_cuda_ok(launch_pdl(k_fold_loss, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
-                             (double)loss_div, bs && valid ? bs->d : nullptr, device_error_word()),
-                  W))
-    return DCT_ERR_CUDA;
+  PeerXfer px;
+  const Xch how = exchange(rec, h, &all, &xs, &px, W);
+  if (how == XCH_FAIL) return DCT_ERR_DIST;
+  const cudaError_t fe =
+      how == XCH_PEER
+          ? launch_pdl(k_peer_fold_loss, dim3(fold_blocks(1)), dim3(256), 0, st, px, (double)loss_div,
+                       bs && valid ? bs->d : nullptr)
+          : launch_pdl(k_fold_loss, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
+                       (double)loss_div, bs && valid ? bs->d : nullptr, device_error_word());
+  if (!rt_cuda_ok(fe, W)) return DCT_ERR_CUDA;
   if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_softmax_ce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
   return 0;
 }
@@ -900,10 +906,15 @@ bool bn_exchange(const float* x, const float* dy, uint32_t N, uint32_t C, uint32
                                 0ull});
   const unsigned long long* all = nullptr;
   size_t xs = 0;
-  if (!exchange(rec, h, &all, &xs, W)) { *rc = DCT_ERR_DIST; return false; }
-  if (!rt_cuda_ok(launch_pdl(k_fold_sums, dim3((nsum + 1 + 255) / 256), dim3(256), 0, st, (const double*)all,
-                             (uint64_t)xs, D.world, nsum, D.fold, device_error_word()),
-                  W)) {
+  PeerXfer px;
+  const Xch how = exchange(rec, h, &all, &xs, &px, W);
+  if (how == XCH_FAIL) { *rc = DCT_ERR_DIST; return false; }
+  const cudaError_t fe =
+      how == XCH_PEER
+          ? launch_pdl(k_peer_fold_sums, dim3(fold_blocks((uint64_t)nsum + 1)), dim3(256), 0, st, px, nsum, D.fold)
+          : launch_pdl(k_fold_sums, dim3((nsum + 1 + 255) / 256), dim3(256), 0, st, (const double*)all,
+                       (uint64_t)xs, D.world, nsum, D.fold, device_error_word());
+  if (!rt_cuda_ok(fe, W)) {
     *rc = DCT_ERR_CUDA;
     return false;
   }

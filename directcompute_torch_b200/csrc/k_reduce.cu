@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "dct_common.cuh"
+#include "dct_peer.cuh"
 #include "kernels.h"
 
 namespace dct {
@@ -724,6 +725,49 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
   const size_t need = reduce3d_ws_bytes(op, outer, len, inner);
   if (inner == 1) return dispatch_reduce(op, x, outer, len, 1, len, 1, 1, ro, ws, need, st);
   return dispatch_reduce(op, x, outer, len, inner, len * inner, inner, 1, ro, ws, need, st);
+}
+
+namespace {
+// The rank fold of a sharded axis reduction, in the same launch as the exchange
+// over peer memory (dct_peer.cuh): after the put and the wait, thread k folds
+// output k over the ranks' packed partials in rank order (ties to the lower
+// index; mean divides by len_total).
+template <int OP>
+__global__ void __launch_bounds__(256) k_peer_fold_axis(const __grid_constant__ PeerXfer p, uint64_t nout,
+                                                        uint64_t len_total, RedOut ro) {
+  pdl_entry();                                         // the record comes from the previous kernel
+  peer_put_wait(p);
+  if (!ro.out && !ro.idx) return;                      // an invalid rank only takes part in the exchange
+  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += step) {
+    Acc<OP> a;
+    a.reset();
+    for (int r = 0; r < p.world; ++r) {
+      Acc<OP> t;
+      t.unpack(p.slots[(uint64_t)r * p.stride + k]);
+      a.merge(t);
+    }
+    a.emit(ro, k, len_total);
+  }
+}
+}  // namespace
+
+cudaError_t launch_peer_fold_axis(int op, const PeerXfer& p, unsigned blocks, uint64_t nout, uint64_t len_total,
+                                  float* out, int32_t* out_idx, cudaStream_t st) {
+  RedOut ro;
+  ro.out = out;
+  ro.idx = out_idx;
+  switch (op) {
+    case RED_SUM: launch_pdl(k_peer_fold_axis<RED_SUM>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    case RED_MEAN: launch_pdl(k_peer_fold_axis<RED_MEAN>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    case RED_MAX: launch_pdl(k_peer_fold_axis<RED_MAX>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    case RED_ARGMAX: launch_pdl(k_peer_fold_axis<RED_ARGMAX>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    case RED_MIN: launch_pdl(k_peer_fold_axis<RED_MIN>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    case RED_ARGMIN: launch_pdl(k_peer_fold_axis<RED_ARGMIN>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    case RED_SUMSQ: launch_pdl(k_peer_fold_axis<RED_SUMSQ>, dim3(blocks), dim3(256), 0, st, p, nout, len_total, ro); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
 }
 
 cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,

@@ -69,6 +69,11 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
                                    int32_t idx_off, unsigned long long* packed, void* ws, cudaStream_t st);
 cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,
                                uint64_t stride, uint64_t len_total, float* out, int32_t* out_idx, cudaStream_t st);
+// The same rank fold fused with the exchange over peer memory (dct_peer.cuh):
+// put this rank's record, wait for every rank's, fold; `blocks` >= world.
+struct PeerXfer;
+cudaError_t launch_peer_fold_axis(int op, const PeerXfer& p, unsigned blocks, uint64_t nout, uint64_t len_total,
+                                  float* out, int32_t* out_idx, cudaStream_t st);
 // Broadcast gradient: out (shape t) = g (shape gshape, ndim <= 8) summed over
 // every dim where t has extent 1 and g does not (t right-aligned and padded
 // with 1s to ndim).  float64 accumulation, rounded once.
