@@ -105,3 +105,21 @@ def test_unmodified_reference_binds_libdct(so, reference_dir):
     r = subprocess.run(["python", "-c", code], capture_output=True, text=True, timeout=300,
                        env={**os.environ, "CUDA_VISIBLE_DEVICES": ""})
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+def test_ops_bind_refuses_a_module_without_a_tensor_type():
+    """ops.bind takes any module whose Tensor has the reference Tensor's protocol; others are refused."""
+    from directcompute_torch_b200 import ops
+    from directcompute_torch_b200.tensor import DeviceTensor
+    try:
+        with pytest.raises(TypeError):
+            ops.bind(object())
+
+        class M:
+            class Tensor:
+                pass
+        with pytest.raises(TypeError):
+            ops.bind(M)
+        assert ops.bind() is DeviceTensor
+    finally:
+        ops.bind()

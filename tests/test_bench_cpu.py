@@ -88,3 +88,27 @@ def test_clock_record_with_a_fake_nvml(monkeypatch):
         pass
     rec = clk.summary()
     assert rec["samples"] == 0 and rec["reasons"] == ["unsampled"] and rec["sm_mhz"] is None
+
+
+def test_compact_maps_and_parity_bookkeeping():
+    """The short op keys the line ends with are unique, and a failed check is recorded
+    (with its message) without stopping the others."""
+    sys.path.insert(0, ROOT)
+    import bench
+    names = [n for sec in bench.PER_OP_SECTIONS.values() for n in sec if "small" not in n]
+    names += [f"c2_rowbcast_{o}" for o in bench.C2_BINARY] + [f"c2_outer_{o}" for o in bench.C2_OUTER]
+    names += [f"c2_unary_{o}" for o in bench.C2_UNARY]
+    keys = [bench.short(n) for n in names]
+    assert len(set(keys)) == len(keys), keys
+    p = bench.Parity(True)
+    p.run("a", lambda: None)
+
+    def bad():
+        raise AssertionError("off by one ulp")
+    p.run("b", bad)
+    p.run("c", lambda: None)
+    assert p.finish(bench._OneRank()) == {"a": True, "b": False, "c": True}
+    assert "off by one" in p.msg["b"]
+    q = bench.Parity(False)
+    q.run("a", bad)
+    assert q.finish(bench._OneRank()) == {}
