@@ -912,8 +912,7 @@ class Suite:
         MaxPoolForwardFused + MaxPoolBackwardFused as MaxPool2D runs them), and
         the conv output / gradient reshapes with ReLU.  No reference config sizes
         these ops; the shapes are synthetic.  Checks cover the first and last
-        sample of each output (sample 0 of the conv reshapes; the fused max-pool
-        pair releases its outputs, and its kernels are checked by the tests)."""
+        sample of each output (sample 0 of the conv reshapes)."""
         L, C, lib = self.L, self.C, self.lib
         for name in ("upsample", "upsample_backward", "concat_insert", "slice", "maxpool_forward", "conv_reshape",
                      "conv_grad_reshape_relu"):
@@ -970,16 +969,28 @@ class Suite:
                     assert np.array_equal(got, ix.astype(np.int64) + b * pup), f"maxpool indices sample {b}"
             self.check("f3_maxpool2x2_fwd", chk)
 
+        kept = []                                     # the last call's outputs, kept for the check
+
         def fused():                                  # MaxPool2D.forward + backward (nn_engine.py:1018-1047)
             pidx = C.c_void_p()
             o = lib.MaxPoolForwardFused(y, B, Ch, 2 * H, 2 * W, 2, 2, C.byref(pidx))
-            d = lib.MaxPoolBackwardFused(po, pidx, B, Ch, H, W, n_up)
+            d = lib.MaxPoolBackwardFused(po, pidx, B, Ch, H, W, n_up)     # releases the index buffer
             if not (o and d):
                 raise RuntimeError("MaxPool*Fused: " + lib.dct_last_error().decode())
-            lib.ReleaseBuffer(o)
-            lib.ReleaseBuffer(d)
-        self.measure("f3_maxpool2x2_fused_fwd_bwd", 4 * (n_up + 2 * n_in) + 4 * (2 * n_in + n_up), fused, 3)
-        for h in (x, dx, z, cat, po, pi):
+            for h in kept:
+                lib.ReleaseBuffer(h)
+            kept[:] = [o, d]
+        if self.measure("f3_maxpool2x2_fused_fwd_bwd", 4 * (n_up + 2 * n_in) + 4 * (2 * n_in + n_up), fused, 3):
+            def chk():
+                S = _oracle_shaders()
+                o, d = kept
+                for b in ends:
+                    _, v, ix = S.maxpool_forward(L.read(y, b * pup, pup), 1, Ch, 2 * H, 2 * W, 2, 2, H, W)
+                    _assert_bits(L.read(o, b * pin, pin), v, f"MaxPoolForwardFused sample {b}")
+                    want = S.maxpool_backward(np.zeros(pup, np.float32), L.read(po, b * pin, pin), ix, 1, Ch, H, W)
+                    _assert_bits(L.read(d, b * pup, pup), want, f"MaxPoolBackwardFused sample {b}")
+            self.check("f3_maxpool2x2_fused_fwd_bwd", chk)
+        for h in kept + [x, dx, z, cat, po, pi]:
             lib.ReleaseBuffer(h)
         OC, Bc, P = 256, 64, 64 * 64
         nconv = OC * Bc * P                                           # 67M floats
