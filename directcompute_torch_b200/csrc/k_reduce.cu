@@ -427,30 +427,47 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 }
 
 // Fold chunk partials: out[k] = combine over ch of part[(o*chunks + ch)*inner + c]
-// (k = o*inner + c).  One warp per output: lane l folds chunks l, l+32, ... in
-// order, then a fixed shuffle tree merges the lanes, so the result is the same
-// on every run (sums in float64; arg and extreme merges are exact).  A thread
-// per output walking the chunks serially took 3-8 us for 4096 outputs of 27
-// chunks; the warp form keeps every chunk's load in flight at once.
+// (k = o*inner + c).  A block takes 32 adjacent outputs, one per lane; warp w
+// folds chunks w, w+8, ... of its lane's output in order (each warp load reads
+// one chunk's 32 adjacent partials: 256 contiguous bytes), then warp 0 merges
+// the 8 warp partials in warp order, so the result is the same on every run
+// (sums in float64; arg and extreme merges are exact).  The earlier form, a
+// warp per output with lane l folding chunks l, l+32, ..., read one 8-byte
+// word per 32-byte sector.
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* __restrict__ part, uint64_t nout,
                                                      uint32_t chunks, uint64_t inner, uint64_t len, RedOut ro) {
   pdl_entry();
-  const int lane = threadIdx.x & 31;
-  const uint64_t wpb = blockDim.x >> 5;
-  const uint64_t stride = (uint64_t)gridDim.x * wpb;
-  for (uint64_t k = (uint64_t)blockIdx.x * wpb + (threadIdx.x >> 5); k < nout; k += stride) {
-    const uint64_t o = k / inner, c = k - o * inner;
-    const unsigned long long* p = part + o * chunks * inner + c;
+  __shared__ unsigned long long sh[kRedWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (uint64_t k0 = (uint64_t)blockIdx.x * 32; k0 < nout; k0 += (uint64_t)gridDim.x * 32) {
+    const uint64_t k = k0 + lane;
     Acc<OP> a;
     a.reset();
-    for (uint32_t ch = lane; ch < chunks; ch += 32) {
-      Acc<OP> t;
-      t.unpack(__ldcg(p + (uint64_t)ch * inner));
-      a.merge(t);
+    if (k < nout) {
+      const uint64_t o = k / inner, c = k - o * inner;
+      const unsigned long long* p = part + o * chunks * inner + c;
+#pragma unroll 4
+      for (uint32_t ch = warp; ch < chunks; ch += kRedWarps) {
+        Acc<OP> t;
+        t.unpack(__ldcg(p + (uint64_t)ch * inner));
+        a.merge(t);
+      }
     }
-    a.warp_reduce();
-    if (lane == 0) a.emit(ro, k, len);
+    sh[warp][lane] = a.pack();
+    __syncthreads();
+    if (warp == 0 && k < nout) {
+      Acc<OP> tot;
+      tot.unpack(sh[0][lane]);
+#pragma unroll
+      for (int w = 1; w < kRedWarps; ++w) {
+        Acc<OP> t;
+        t.unpack(sh[w][lane]);
+        tot.merge(t);
+      }
+      tot.emit(ro, k, len);
+    }
+    __syncthreads();
   }
 }
 
@@ -582,7 +599,7 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nparts == 1) return e;
   const uint64_t nout = outer * inner;
-  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout * 32, 256)), dim3(256), 0, st, (const unsigned long long*)part,
+  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout, 32)), dim3(256), 0, st, (const unsigned long long*)part,
                     nout, nparts, inner, len, ro);
 }
 
@@ -615,7 +632,7 @@ cudaError_t run_fold_packed(const unsigned long long* parts, uint32_t nparts, ui
   // parts[p * stride + k]: the chunk-fold layout with outer = 1, inner = stride
   // (k < nout <= stride, so the fold's outer index is always 0); launched as a
   // programmatic dependent of the kernel that produced the parts
-  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout * 32, 256)), dim3(256), 0, st, parts, nout, nparts, stride,
+  return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout, 32)), dim3(256), 0, st, parts, nout, nparts, stride,
                     len_total, ro);
 }
 
@@ -681,7 +698,7 @@ cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, f
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.chunks == 1) return e;
-  return launch_pdl(k_fold_chunks<RED_SUM>, dim3(grid_for(cols * 32, 256)), dim3(256), 0, st,
+  return launch_pdl(k_fold_chunks<RED_SUM>, dim3(grid_for(cols, 32)), dim3(256), 0, st,
                     (const unsigned long long*)part, cols, p.chunks, cols, rows, ro);
 }
 
