@@ -2,13 +2,24 @@
 // kernels that fold the exchanged records (dist.cu: full sums, the softmax-CE
 // loss, BatchNorm channel sums; k_reduce.cu: axis reductions).
 //
-// Each rank stores its record straight into every rank's slot (plain 16-byte
-// stores to a peer's memory mapped with CUDA IPC), fences at system scope and
-// release-stores the exchange's epoch into that rank's flag for it.  Every block
-// of the folding kernel then waits, bounded by %globaltimer, until every rank's
-// flag here holds the epoch, acquires each flag in every thread, and folds its
-// share of the local slots -- put, wait and fold in one launch.  No load ever
-// reads another GPU's memory.
+// A record is a run of 64-bit words.  Each word crosses NVLink as two 64-bit
+// lines, its low and its high 32 bits each paired with the exchange's 32-bit
+// tag, in one 16-byte store of two single-copy-atomic 64-bit elements.  Every
+// block of the folding kernel first stores a slice of this rank's record into
+// every peer's slot; the folding threads then read the peers' lines they need
+// from their own GPU's memory, spinning (bounded by %globaltimer) until both
+// lines of a word carry this exchange's tag.  A line proves its own arrival,
+// so there are no fences and no flags: put, wait and fold are one launch, and
+// no load ever reads another GPU's memory.  This rank's own words come straight
+// from its record.
+//
+// Slots alternate by exchange parity.  Block 0 of every fold reads one line of
+// every peer (peer_sync), so a rank's fold of exchange e + 1 ends only after
+// every peer has stored its e + 1 lines, which each peer does only after its
+// own fold of e has ended (stream order).  A rank therefore stores e + 2 into a
+// peer's parity slot only after that peer has read the e lines there.  Tags
+// run 1, 2, ..., 2^32 - 1, 1, ... in zeroed slots: a line left from exchange
+// e - 2 or never written never carries the tag of e.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -25,74 +36,104 @@ struct Hdr {
 
 struct PeerXfer {
   const unsigned long long* rec;     // this rank's record, words [0, h.off)
-  Hdr h;                             // and its header words
+  Hdr h;                             // and its header words [h.off, h.off + h.n)
   void* const* bases;                // every rank's exchange region (mapped here)
-  uint64_t slot_off, flag_off;       // this rank's slot / flag in every region
-  unsigned long long epoch;
-  const unsigned long long* flags;   // this rank's flags of this parity, one per rank
-  int world;
+  uint64_t slot_off;                 // byte offset of this rank's slot (this parity) in every region
+  uint32_t tag;                      // this exchange's tag, never 0
+  int rank, world;
   unsigned long long timeout_ns;
   uint32_t* err;
-  const unsigned long long* slots;   // this rank's slots of this parity: rank r's record at r * stride
-  uint64_t stride;
+  const unsigned long long* slots;   // this rank's slots of this parity: rank r's lines at r * stride
+  uint64_t stride;                   // lines per rank slot
   int64_t axis_nout;                 // >= 0: axis records; block 0 checks that the shards tile the axis
 };
 
-// Block q < world stores the record into rank q's slot and raises rank q's flag;
-// then every block waits for all flags (bounded: past the deadline the error
-// word gets DCT_DEVERR_PEER_WAIT and the block goes on) and every thread
-// acquires them.  Ends with the block synchronised.
-DCT_DEV void peer_put_wait(const PeerXfer& p) {
-  if ((int)blockIdx.x < p.world) {
-    unsigned char* base = static_cast<unsigned char*>(p.bases[blockIdx.x]);
-    unsigned long long* dst = reinterpret_cast<unsigned long long*>(base + p.slot_off);
-    const uint64_t n = p.h.off;
-    const uint64_t n2 = n >> 1;
-    const uint4* s4 = reinterpret_cast<const uint4*>(p.rec);
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-    for (uint64_t i = threadIdx.x; i < n2; i += blockDim.x) d4[i] = s4[i];
-    if ((n & 1) && threadIdx.x == 0) dst[n - 1] = p.rec[n - 1];
-    if (threadIdx.x < p.h.n) dst[n + threadIdx.x] = p.h.v[threadIdx.x];
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned long long* flag = reinterpret_cast<unsigned long long*>(base + p.flag_off);
-      asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(p.epoch) : "memory");
+DCT_DEV uint64_t peer_words(const PeerXfer& p) { return (uint64_t)p.h.off + p.h.n; }
+
+DCT_DEV unsigned long long peer_word(const PeerXfer& p, uint64_t i) {
+  return i < p.h.off ? p.rec[i] : p.h.v[i - p.h.off];
+}
+
+// Every block stores its slice of this rank's record (record words then header
+// words) into every peer's slot.
+DCT_DEV void peer_put(const PeerXfer& p) {
+  const uint64_t nw = peer_words(p);
+  const uint64_t per = (nw + gridDim.x - 1) / gridDim.x;
+  const uint64_t w0 = (uint64_t)blockIdx.x * per, w1 = min(nw, w0 + per);
+  const unsigned long long tag = (unsigned long long)p.tag << 32;
+  for (uint64_t i = w0 + threadIdx.x; i < w1; i += blockDim.x) {
+    const unsigned long long w = peer_word(p, i);
+    const unsigned long long lo = (w & 0xffffffffull) | tag, hi = (w >> 32) | tag;
+    for (int q = 0; q < p.world; ++q) {
+      if (q == p.rank) continue;
+      unsigned long long* dst =
+          reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(p.bases[q]) + p.slot_off) + 2 * i;
+      asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(lo), "l"(hi) : "memory");
     }
   }
-  for (int q = threadIdx.x; q < p.world; q += blockDim.x) {
-    unsigned long long t0, t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (;;) {
-      unsigned long long v;
-      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p.flags + q) : "memory");
-      if (v >= p.epoch) break;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (t - t0 > p.timeout_ns) {
-        if (p.err) atomicOr(p.err, DCT_DEVERR_PEER_WAIT);
-        break;
-      }
-      __nanosleep(64);
+}
+
+// Word i of rank r's record: this rank's from its record, a peer's once both of
+// its lines carry this exchange's tag.  `gave_up` is the calling thread's:
+// after one wait runs out (the error word gets DCT_DEVERR_PEER_WAIT) the thread
+// waits no more and reads whatever is there.
+DCT_DEV unsigned long long peer_get(const PeerXfer& p, int r, uint64_t i, bool& gave_up) {
+  if (r == p.rank) return peer_word(p, i);
+  const unsigned long long* src = p.slots + (uint64_t)r * p.stride + 2 * i;
+  unsigned long long lo, hi, t0 = 0;
+  bool started = false;
+  for (;;) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "l"(src) : "memory");
+    if (((uint32_t)(lo >> 32) == p.tag && (uint32_t)(hi >> 32) == p.tag) || gave_up) break;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (!started) {
+      t0 = t;
+      started = true;
+    } else if (t - t0 > p.timeout_ns) {
+      if (p.err) atomicOr(p.err, DCT_DEVERR_PEER_WAIT);
+      gave_up = true;
+      break;
     }
   }
-  __syncthreads();
-  for (int q = 0; q < p.world; ++q) {               // every thread's own acquire of every record
-    [[maybe_unused]] unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p.flags + q) : "memory");
+  return (lo & 0xffffffffull) | (hi << 32);
+}
+
+DCT_DEV double peer_get_f64(const PeerXfer& p, int r, uint64_t i, bool& gave_up) {
+  return __longlong_as_double((long long)peer_get(p, r, i, gave_up));
+}
+
+// Block 0: thread q waits for peer q's last word (the ordering the slot reuse
+// relies on, whatever the fold itself reads).
+DCT_DEV void peer_sync(const PeerXfer& p, bool& gave_up) {
+  if (blockIdx.x != 0) return;
+  for (int q = threadIdx.x; q < p.world; q += blockDim.x)
+    if (q != p.rank) (void)peer_get(p, q, peer_words(p) - 1, gave_up);
+}
+
+// Block 0, thread 0 of an axis reduction: the shards' headers [offset, len,
+// len_total, valid] must tile [0, len_total) in rank order.
+DCT_DEV void peer_check_axis(const PeerXfer& p, bool& gave_up) {
+  if (p.axis_nout < 0 || blockIdx.x != 0 || threadIdx.x != 0) return;
+  const uint64_t nout = (uint64_t)p.axis_nout;
+  unsigned long long expect = 0;
+  const unsigned long long total = peer_get(p, 0, nout + 2, gave_up);
+  bool ok = true;
+  for (int r = 0; r < p.world; ++r) {
+    const unsigned long long off = peer_get(p, r, nout, gave_up), len = peer_get(p, r, nout + 1, gave_up);
+    ok &= (peer_get(p, r, nout + 3, gave_up) == 1ull) && (off == expect) && (peer_get(p, r, nout + 2, gave_up) == total);
+    expect += len;
   }
-  // axis-reduction records: the shards must tile [0, len_total) in rank order
-  if (p.axis_nout >= 0 && blockIdx.x == 0 && threadIdx.x == 0) {
-    const uint64_t nout = (uint64_t)p.axis_nout;
-    unsigned long long expect = 0, total = p.slots[nout + 2];
-    bool ok = true;
-    for (int r = 0; r < p.world; ++r) {
-      const unsigned long long* hh = p.slots + (uint64_t)r * p.stride + nout;
-      ok &= (hh[3] == 1ull) && (hh[0] == expect) && (hh[2] == total);
-      expect += hh[1];
-    }
-    ok &= (expect == total);
-    if (!ok && p.err) atomicOr(p.err, DCT_DEVERR_PEER_INVALID);
-  }
+  ok &= (expect == total);
+  if (!ok && p.err) atomicOr(p.err, DCT_DEVERR_PEER_INVALID);
+}
+
+// The start of every fold kernel over peer memory: put, then the ordering wait
+// and (axis records) the shard check.
+DCT_DEV void peer_begin(const PeerXfer& p, bool& gave_up) {
+  peer_put(p);
+  peer_sync(p, gave_up);
+  peer_check_axis(p, gave_up);
 }
 
 }  // namespace dct

@@ -93,8 +93,8 @@ struct DistState {
   double* fold = nullptr;          // folded sums / counts (float64)
   size_t fold_bytes = 0;
   // peer-memory exchange: this rank's region holds slots [2][world][slot_bytes]
-  // (by epoch parity, then by writing rank) and flags [2][world] (u64 epochs);
-  // every rank's region is mapped here (CUDA IPC over NVLink)
+  // (by exchange parity, then by writing rank) of tagged 64-bit lines, two per
+  // record word; every rank's region is mapped here (CUDA IPC over NVLink)
   bool peer = false;
   void* region = nullptr;
   size_t slot_bytes = 0;
@@ -243,17 +243,14 @@ bool all_gather(const void* send, void* recv, size_t count_u64, const char* wher
 // ---------------------------------------------------------------------------
 // peer-memory exchange
 // ---------------------------------------------------------------------------
-// Each rank stores its record straight into every rank's slot over NVLink
-// (plain stores to a peer's memory mapped with CUDA IPC), then release-stores
-// the exchange's epoch into that rank's flag; each rank waits for all flags
-// of the epoch on its own memory (acquire loads, bounded by a deadline) and
-// folds its local slots.  Slots alternate by epoch parity: a rank can run at
-// most one exchange ahead of a peer (its next fold waits for that peer's next
-// record), so it never overwrites a record the peer has not folded.
-constexpr size_t kSlotBytes = 256 * 1024;
+// Each rank stores its record straight into every peer's slot over NVLink
+// (stores to a peer's memory mapped with CUDA IPC) as tagged lines, and each
+// rank folds the lines in its own memory once they carry the exchange's tag
+// (dct_peer.cuh).  A slot holds 32K record words (16 bytes of lines per
+// word); larger records go over NCCL.
+constexpr size_t kSlotBytes = 512 * 1024;
 
 size_t slot_off(int par, int q) { return ((size_t)par * D.world + q) * D.slot_bytes; }
-size_t flag_off(int par, int q) { return 2 * (size_t)D.world * D.slot_bytes + ((size_t)par * D.world + q) * 8; }
 
 __global__ void k_check_axis_shards(const unsigned long long* all, int world, uint64_t stride, uint64_t nout,
                                     uint32_t* err);
@@ -288,7 +285,7 @@ Xch exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* st
              const char* where, int64_t axis_nout = -1) {
   cudaStream_t st = rt_stream();
   const size_t n = (size_t)h.off + h.n;
-  if (D.peer && n * 8 <= D.slot_bytes) {
+  if (D.peer && n * 16 <= D.slot_bytes) {
     const unsigned long long ep = ++D.epoch;
     const int par = (int)(ep & 1);
     unsigned char* base = static_cast<unsigned char*>(D.region);
@@ -300,17 +297,16 @@ Xch exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* st
     px->h = h;
     px->bases = (void* const*)D.peer_dev;
     px->slot_off = (uint64_t)slot_off(par, D.rank);
-    px->flag_off = (uint64_t)flag_off(par, D.rank);
-    px->epoch = ep;
-    px->flags = reinterpret_cast<const unsigned long long*>(base + flag_off(par, 0));
+    px->tag = (uint32_t)((ep - 1) % 0xffffffffull) + 1u;
+    px->rank = D.rank;
     px->world = D.world;
     px->timeout_ns = (unsigned long long)(lim * 1e9);
     px->err = device_error_word();
     px->slots = slots;
     px->stride = (uint64_t)(D.slot_bytes / 8);
     px->axis_nout = axis_nout;
-    *all = slots;
-    *stride = D.slot_bytes / 8;
+    *all = nullptr;
+    *stride = 0;
     return XCH_PEER;
   }
   unsigned long long* r64 = static_cast<unsigned long long*>(rec);
@@ -356,7 +352,7 @@ bool peer_setup() {
   const char* env = getenv("DCT_PEER_EXCHANGE");
   bool ok = !(env && env[0] == '0');
   D.slot_bytes = kSlotBytes;
-  const size_t bytes = 2 * (size_t)D.world * D.slot_bytes + 2 * (size_t)D.world * 8;
+  const size_t bytes = 2 * (size_t)D.world * D.slot_bytes;
   cudaIpcMemHandle_t mine{};
   if (ok) ok = cudaMalloc(&D.region, bytes) == cudaSuccess && cudaMemset(D.region, 0, bytes) == cudaSuccess &&
                cudaDeviceSynchronize() == cudaSuccess && cudaIpcGetMemHandle(&mine, D.region) == cudaSuccess;
@@ -426,24 +422,39 @@ __global__ void k_check_axis_shards(const unsigned long long* all, int world, ui
   if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
 }
 
+// Record readers for the folds: word i of rank r as a double.  LocalRecs
+// reads the records an NCCL all-gather left in local memory; PeerRecs reads
+// them over the peer exchange (dct_peer.cuh), this rank's from its record.
+struct LocalRecs {
+  const double* all;
+  uint64_t stride;
+  DCT_DEV double operator()(int r, uint64_t i) const { return all[(uint64_t)r * stride + i]; }
+};
+struct PeerRecs {
+  const PeerXfer& p;
+  bool& gave_up;
+  DCT_DEV double operator()(int r, uint64_t i) const { return peer_get_f64(p, r, i, gave_up); }
+};
+
 // Full reduction records [value, count, valid, -]: fold in rank order.
 // post: 0 none, 1 mean (divide by the total count).  One thread.
-DCT_DEV void fold_full(const double* all, uint64_t stride, int world, int op, int post, float* out32,
-                       double* out64, uint32_t* err) {
+template <class G>
+DCT_DEV void fold_full(const G& get, int world, int op, int post, float* out32, double* out64, uint32_t* err) {
   double acc = 0.0, cnt = 0.0;
   bool ok = true, first = true;
   const bool ext = (op == RED_MAX || op == RED_MIN);
   for (int r = 0; r < world; ++r) {
-    const double* rec = all + stride * r;
-    ok &= (rec[2] == 1.0);
-    cnt += rec[1];
+    const double n = get(r, 1);
+    ok &= (get(r, 2) == 1.0);
+    cnt += n;
     if (ext) {
-      if (rec[1] == 0.0) continue;                       // empty shard: no candidate
-      const double v = rec[0];
+      if (n == 0.0) continue;                            // empty shard: no candidate
+      const double v = get(r, 0);
       if (first || isnan(v) || (!isnan(acc) && (op == RED_MAX ? v > acc : v < acc))) acc = v;
       first = false;
     } else {
-      acc = first ? rec[0] : acc + rec[0];
+      const double v = get(r, 0);
+      acc = first ? v : acc + v;
       first = false;
     }
   }
@@ -458,12 +469,14 @@ DCT_DEV void fold_full(const double* all, uint64_t stride, int world, int op, in
 }
 
 // Softmax-CE records [sum of row losses, rows, valid, -] -> loss = sum / div.  One thread.
-DCT_DEV void fold_loss(const double* all, uint64_t stride, int world, double div, float* loss, uint32_t* err) {
+template <class G>
+DCT_DEV void fold_loss(const G& get, int world, double div, float* loss, uint32_t* err) {
   double acc = 0.0;
   bool ok = true;
   for (int r = 0; r < world; ++r) {
-    ok &= (all[stride * r + 2] == 1.0);
-    acc = r == 0 ? all[0] : acc + all[stride * r];
+    ok &= (get(r, 2) == 1.0);
+    const double v = get(r, 0);
+    acc = r == 0 ? v : acc + v;
   }
   if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
   if (loss) loss[0] = ok ? (float)(acc / div) : NAN;
@@ -471,19 +484,18 @@ DCT_DEV void fold_loss(const double* all, uint64_t stride, int world, double div
 
 // Channel-sum records [nsum sums][count, valid, nsum, -]: out[j] = sum over
 // ranks in rank order; out[nsum] = total count.  Item j of nsum + 1.
-DCT_DEV void fold_sums(const double* all, uint64_t stride, int world, uint32_t nsum, double* out, uint32_t* err,
-                       uint32_t j) {
+template <class G>
+DCT_DEV void fold_sums(const G& get, int world, uint32_t nsum, double* out, uint32_t* err, uint32_t j) {
   if (j < nsum) {
-    double acc = all[j];
-    for (int r = 1; r < world; ++r) acc += all[(uint64_t)r * stride + j];
+    double acc = get(0, j);
+    for (int r = 1; r < world; ++r) acc += get(r, j);
     out[j] = acc;
   } else if (j == nsum) {
     double cnt = 0.0;
     bool ok = true;
     for (int r = 0; r < world; ++r) {
-      const double* h = all + (uint64_t)r * stride + nsum;
-      cnt += h[0];
-      ok &= (h[1] == 1.0) && (h[2] == (double)nsum);
+      cnt += get(r, nsum);
+      ok &= (get(r, nsum + 1) == 1.0) && (get(r, nsum + 2) == (double)nsum);
     }
     out[nsum] = cnt;
     if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
@@ -494,39 +506,40 @@ DCT_DEV void fold_sums(const double* all, uint64_t stride, int world, uint32_t n
 __global__ void k_fold_full(const double* all, uint64_t stride, int world, int op, int post, float* out32,
                             double* out64, uint32_t* err) {
   grid_dep_wait();
-  if (threadIdx.x == 0) fold_full(all, stride, world, op, post, out32, out64, err);
+  if (threadIdx.x == 0) fold_full(LocalRecs{all, stride}, world, op, post, out32, out64, err);
 }
 __global__ void k_fold_loss(const double* all, uint64_t stride, int world, double div, float* loss, uint32_t* err) {
   grid_dep_wait();
-  if (threadIdx.x == 0) fold_loss(all, stride, world, div, loss, err);
+  if (threadIdx.x == 0) fold_loss(LocalRecs{all, stride}, world, div, loss, err);
 }
 __global__ void k_fold_sums(const double* all, uint64_t stride, int world, uint32_t nsum, double* out,
                             uint32_t* err) {
   grid_dep_wait();
-  fold_sums(all, stride, world, nsum, out, err, blockIdx.x * blockDim.x + threadIdx.x);
+  fold_sums(LocalRecs{all, stride}, world, nsum, out, err, blockIdx.x * blockDim.x + threadIdx.x);
 }
 
 // the same folds over peer memory: put, wait and fold in one launch (dct_peer.cuh)
 __global__ void __launch_bounds__(256) k_peer_fold_full(const __grid_constant__ PeerXfer p, int op, int post,
                                                         float* out32, double* out64) {
   pdl_entry();                                         // the record comes from the previous kernel
-  peer_put_wait(p);
-  if (blockIdx.x == 0 && threadIdx.x == 0)
-    fold_full(reinterpret_cast<const double*>(p.slots), p.stride, p.world, op, post, out32, out64, p.err);
+  bool gave_up = false;
+  peer_begin(p, gave_up);
+  if (blockIdx.x == 0 && threadIdx.x == 0) fold_full(PeerRecs{p, gave_up}, p.world, op, post, out32, out64, p.err);
 }
 __global__ void __launch_bounds__(256) k_peer_fold_loss(const __grid_constant__ PeerXfer p, double div,
                                                         float* loss) {
   pdl_entry();
-  peer_put_wait(p);
-  if (blockIdx.x == 0 && threadIdx.x == 0)
-    fold_loss(reinterpret_cast<const double*>(p.slots), p.stride, p.world, div, loss, p.err);
+  bool gave_up = false;
+  peer_begin(p, gave_up);
+  if (blockIdx.x == 0 && threadIdx.x == 0) fold_loss(PeerRecs{p, gave_up}, p.world, div, loss, p.err);
 }
 __global__ void __launch_bounds__(256) k_peer_fold_sums(const __grid_constant__ PeerXfer p, uint32_t nsum,
                                                         double* out) {
   pdl_entry();
-  peer_put_wait(p);
+  bool gave_up = false;
+  peer_begin(p, gave_up);
   for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j <= nsum; j += gridDim.x * blockDim.x)
-    fold_sums(reinterpret_cast<const double*>(p.slots), p.stride, p.world, nsum, out, p.err, j);
+    fold_sums(PeerRecs{p, gave_up}, p.world, nsum, out, p.err, j);
 }
 
 Buffer* live(void* h) { return h ? rt_buf(h) : nullptr; }

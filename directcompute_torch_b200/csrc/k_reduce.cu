@@ -746,14 +746,15 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
 
 namespace {
 // The rank fold of a sharded axis reduction, in the same launch as the exchange
-// over peer memory (dct_peer.cuh): after the put and the wait, thread k folds
-// output k over the ranks' packed partials in rank order (ties to the lower
+// over peer memory (dct_peer.cuh): after the put, thread k folds output k over
+// the ranks' packed partials in rank order as each arrives (ties to the lower
 // index; mean divides by len_total).
 template <int OP>
 __global__ void __launch_bounds__(256) k_peer_fold_axis(const __grid_constant__ PeerXfer p, uint64_t nout,
                                                         uint64_t len_total, RedOut ro) {
   pdl_entry();                                         // the record comes from the previous kernel
-  peer_put_wait(p);
+  bool gave_up = false;
+  peer_begin(p, gave_up);
   if (!ro.out && !ro.idx) return;                      // an invalid rank only takes part in the exchange
   const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += step) {
@@ -761,7 +762,7 @@ __global__ void __launch_bounds__(256) k_peer_fold_axis(const __grid_constant__ 
     a.reset();
     for (int r = 0; r < p.world; ++r) {
       Acc<OP> t;
-      t.unpack(p.slots[(uint64_t)r * p.stride + k]);
+      t.unpack(peer_get(p, r, k, gave_up));
       a.merge(t);
     }
     a.emit(ro, k, len_total);
