@@ -28,6 +28,10 @@
 
 namespace dct {
 
+// The peer exchange serves at most this many ranks (the axis check stages
+// every rank's header in shared memory); larger worlds use NCCL.
+constexpr int kPeerMaxWorld = 64;
+
 // The host-known part of a record: n u64 words (bit patterns) at offset `off`.
 struct Hdr {
   uint32_t off = 0, n = 0;
@@ -54,23 +58,30 @@ DCT_DEV unsigned long long peer_word(const PeerXfer& p, uint64_t i) {
   return i < p.h.off ? p.rec[i] : p.h.v[i - p.h.off];
 }
 
+// Word i of this rank's record, value w, into every peer's slot.
+DCT_DEV void peer_put_word(const PeerXfer& p, uint64_t i, unsigned long long w) {
+  const unsigned long long tag = (unsigned long long)p.tag << 32;
+  const unsigned long long lo = (w & 0xffffffffull) | tag, hi = (w >> 32) | tag;
+  for (int q = 0; q < p.world; ++q) {
+    if (q == p.rank) continue;
+    unsigned long long* dst =
+        reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(p.bases[q]) + p.slot_off) + 2 * i;
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(lo), "l"(hi) : "memory");
+  }
+}
+
 // Every block stores its slice of this rank's record (record words then header
 // words) into every peer's slot.
 DCT_DEV void peer_put(const PeerXfer& p) {
   const uint64_t nw = peer_words(p);
   const uint64_t per = (nw + gridDim.x - 1) / gridDim.x;
   const uint64_t w0 = (uint64_t)blockIdx.x * per, w1 = min(nw, w0 + per);
-  const unsigned long long tag = (unsigned long long)p.tag << 32;
-  for (uint64_t i = w0 + threadIdx.x; i < w1; i += blockDim.x) {
-    const unsigned long long w = peer_word(p, i);
-    const unsigned long long lo = (w & 0xffffffffull) | tag, hi = (w >> 32) | tag;
-    for (int q = 0; q < p.world; ++q) {
-      if (q == p.rank) continue;
-      unsigned long long* dst =
-          reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(p.bases[q]) + p.slot_off) + 2 * i;
-      asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(lo), "l"(hi) : "memory");
-    }
-  }
+  for (uint64_t i = w0 + threadIdx.x; i < w1; i += blockDim.x) peer_put_word(p, i, peer_word(p, i));
+}
+
+// Block 0 stores the header words (a kernel that puts its record words itself).
+DCT_DEV void peer_put_header(const PeerXfer& p) {
+  if (blockIdx.x == 0 && threadIdx.x < p.h.n) peer_put_word(p, p.h.off + threadIdx.x, p.h.v[threadIdx.x]);
 }
 
 // Word i of rank r's record: this rank's from its record, a peer's once both of
@@ -111,18 +122,22 @@ DCT_DEV void peer_sync(const PeerXfer& p, bool& gave_up) {
     if (q != p.rank) (void)peer_get(p, q, peer_words(p) - 1, gave_up);
 }
 
-// Block 0, thread 0 of an axis reduction: the shards' headers [offset, len,
-// len_total, valid] must tile [0, len_total) in rank order.
+// Block 0 of an axis reduction (every thread of the block calls it): the
+// shards' headers [offset, len, len_total, valid] must tile [0, len_total) in
+// rank order.  The block fetches every rank's four header words at once.
 DCT_DEV void peer_check_axis(const PeerXfer& p, bool& gave_up) {
-  if (p.axis_nout < 0 || blockIdx.x != 0 || threadIdx.x != 0) return;
+  if (p.axis_nout < 0 || blockIdx.x != 0) return;
+  __shared__ unsigned long long hv[kPeerMaxWorld][4];
   const uint64_t nout = (uint64_t)p.axis_nout;
+  for (int t = threadIdx.x; t < 4 * p.world; t += blockDim.x) hv[t >> 2][t & 3] = peer_get(p, t >> 2, nout + (t & 3), gave_up);
+  __syncthreads();
+  if (threadIdx.x != 0) return;
   unsigned long long expect = 0;
-  const unsigned long long total = peer_get(p, 0, nout + 2, gave_up);
+  const unsigned long long total = hv[0][2];
   bool ok = true;
   for (int r = 0; r < p.world; ++r) {
-    const unsigned long long off = peer_get(p, r, nout, gave_up), len = peer_get(p, r, nout + 1, gave_up);
-    ok &= (peer_get(p, r, nout + 3, gave_up) == 1ull) && (off == expect) && (peer_get(p, r, nout + 2, gave_up) == total);
-    expect += len;
+    ok &= (hv[r][3] == 1ull) && (hv[r][0] == expect) && (hv[r][2] == total);
+    expect += hv[r][1];
   }
   ok &= (expect == total);
   if (!ok && p.err) atomicOr(p.err, DCT_DEVERR_PEER_INVALID);

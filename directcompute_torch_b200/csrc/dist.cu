@@ -45,7 +45,7 @@
 #include <vector>
 
 #include "dct_common.cuh"
-#include "dct_peer.cuh"
+#include "dct_fold.cuh"
 #include "kernels.h"
 #include "runtime_internal.h"
 #include "../../include/dct_cuda.h"
@@ -281,11 +281,13 @@ __global__ void k_put_u64(unsigned long long* rec, Hdr h) {
 // axis-reduction shard headers (at word axis_nout of each record).  XCH_FAIL:
 // the error is recorded.
 enum Xch { XCH_FAIL = 0, XCH_NCCL = 1, XCH_PEER = 2 };
+// whether a record of `words` words goes over peer memory
+bool peer_fits(size_t words) { return D.peer && words * 16 <= D.slot_bytes; }
 Xch exchange(void* rec, const Hdr& h, const unsigned long long** all, size_t* stride, PeerXfer* px,
              const char* where, int64_t axis_nout = -1) {
   cudaStream_t st = rt_stream();
   const size_t n = (size_t)h.off + h.n;
-  if (D.peer && n * 16 <= D.slot_bytes) {
+  if (peer_fits(n)) {
     const unsigned long long ep = ++D.epoch;
     const int par = (int)(ep & 1);
     unsigned char* base = static_cast<unsigned char*>(D.region);
@@ -350,7 +352,7 @@ void peer_teardown() {
 // over the communicator).  DCT_PEER_EXCHANGE=0 keeps NCCL all-gathers.
 bool peer_setup() {
   const char* env = getenv("DCT_PEER_EXCHANGE");
-  bool ok = !(env && env[0] == '0');
+  bool ok = !(env && env[0] == '0') && D.world <= kPeerMaxWorld;
   D.slot_bytes = kSlotBytes;
   const size_t bytes = 2 * (size_t)D.world * D.slot_bytes;
   cudaIpcMemHandle_t mine{};
@@ -420,86 +422,6 @@ __global__ void k_check_axis_shards(const unsigned long long* all, int world, ui
   }
   ok &= (expect == total);
   if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
-}
-
-// Record readers for the folds: word i of rank r as a double.  LocalRecs
-// reads the records an NCCL all-gather left in local memory; PeerRecs reads
-// them over the peer exchange (dct_peer.cuh), this rank's from its record.
-struct LocalRecs {
-  const double* all;
-  uint64_t stride;
-  DCT_DEV double operator()(int r, uint64_t i) const { return all[(uint64_t)r * stride + i]; }
-};
-struct PeerRecs {
-  const PeerXfer& p;
-  bool& gave_up;
-  DCT_DEV double operator()(int r, uint64_t i) const { return peer_get_f64(p, r, i, gave_up); }
-};
-
-// Full reduction records [value, count, valid, -]: fold in rank order.
-// post: 0 none, 1 mean (divide by the total count).  One thread.
-template <class G>
-DCT_DEV void fold_full(const G& get, int world, int op, int post, float* out32, double* out64, uint32_t* err) {
-  double acc = 0.0, cnt = 0.0;
-  bool ok = true, first = true;
-  const bool ext = (op == RED_MAX || op == RED_MIN);
-  for (int r = 0; r < world; ++r) {
-    const double n = get(r, 1);
-    ok &= (get(r, 2) == 1.0);
-    cnt += n;
-    if (ext) {
-      if (n == 0.0) continue;                            // empty shard: no candidate
-      const double v = get(r, 0);
-      if (first || isnan(v) || (!isnan(acc) && (op == RED_MAX ? v > acc : v < acc))) acc = v;
-      first = false;
-    } else {
-      const double v = get(r, 0);
-      acc = first ? v : acc + v;
-      first = false;
-    }
-  }
-  if (ext && first) ok = false;                          // max / min of nothing
-  if (post == 1) acc = acc / cnt;
-  if (!ok) {
-    acc = (double)NAN;
-    if (err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
-  }
-  if (out32) out32[0] = (float)acc;
-  if (out64) out64[0] = acc;
-}
-
-// Softmax-CE records [sum of row losses, rows, valid, -] -> loss = sum / div.  One thread.
-template <class G>
-DCT_DEV void fold_loss(const G& get, int world, double div, float* loss, uint32_t* err) {
-  double acc = 0.0;
-  bool ok = true;
-  for (int r = 0; r < world; ++r) {
-    ok &= (get(r, 2) == 1.0);
-    const double v = get(r, 0);
-    acc = r == 0 ? v : acc + v;
-  }
-  if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
-  if (loss) loss[0] = ok ? (float)(acc / div) : NAN;
-}
-
-// Channel-sum records [nsum sums][count, valid, nsum, -]: out[j] = sum over
-// ranks in rank order; out[nsum] = total count.  Item j of nsum + 1.
-template <class G>
-DCT_DEV void fold_sums(const G& get, int world, uint32_t nsum, double* out, uint32_t* err, uint32_t j) {
-  if (j < nsum) {
-    double acc = get(0, j);
-    for (int r = 1; r < world; ++r) acc += get(r, j);
-    out[j] = acc;
-  } else if (j == nsum) {
-    double cnt = 0.0;
-    bool ok = true;
-    for (int r = 0; r < world; ++r) {
-      cnt += get(r, nsum);
-      ok &= (get(r, nsum + 1) == 1.0) && (get(r, nsum + 2) == (double)nsum);
-    }
-    out[nsum] = cnt;
-    if (!ok && err) atomicOr(err, DCT_DEVERR_PEER_INVALID);
-  }
 }
 
 // the folds after an NCCL all-gather
@@ -763,31 +685,46 @@ DCT_API int dct_dist_reduce(int op, void* x, uint64_t outer, uint64_t len, uint6
                (!bo || bo->count >= nout) && (!bi || bi->count >= nout) && len_offset + len <= len_total;
   unsigned long long* send = (unsigned long long*)D.send;
   cudaStream_t st = rt_stream();
-  // The packed partials are staged in the local record and cross NVLink in the
-  // put kernel's 16-byte stores.  (Storing them into every peer's slot from
-  // the emitting kernel itself was slower: 8-byte scattered remote stores and
-  // a system-scope fence in every thread of the grid.)
-  if (valid && !rt_ensure_ws(reduce3d_ws_bytes(op_run, outer, len, inner))) return DCT_ERR_CUDA;
-  if (valid && !rt_cuda_ok(launch_reduce3d_packed(op_run, bx->d, outer, len, inner, (int32_t)len_offset, send,
-                                                  rt_ws(), st), W))
-    valid = false;
-  // header [offset, len, len_total, valid] after the nout packed partials
-  const unsigned long long* all = nullptr;
-  size_t xs = 0;
-  PeerXfer px;
-  const Xch how = exchange(send, make_hdr((uint32_t)nout, {len_offset, len, len_total, valid ? 1ull : 0ull}), &all,
-                           &xs, &px, W, (int64_t)nout);
-  if (how == XCH_FAIL) return DCT_ERR_DIST;
   float* o32 = bo ? bo->d : nullptr;
   int32_t* oi = bi ? reinterpret_cast<int32_t*>(bi->d) : nullptr;
   if (arg && !oi) { oi = reinterpret_cast<int32_t*>(o32); o32 = nullptr; }   // indices into out (dct_reduce rule)
-  if (!valid) { o32 = nullptr; oi = nullptr; }                                // still puts and waits: no outputs
-  cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess && how == XCH_PEER)
-    e = launch_peer_fold_axis(op_run, px, fold_blocks(nout), nout, len_total, o32, oi, st);
-  else if (e == cudaSuccess && valid)
-    e = launch_fold_packed(op_run, all, (uint32_t)D.world, nout, xs, len_total, o32, oi, st);
-  if (!rt_cuda_ok(e, W)) return DCT_ERR_CUDA;
+  // header [offset, len, len_total, valid] after the nout packed partials
+  auto hdr = [&](bool ok) { return make_hdr((uint32_t)nout, {len_offset, len, len_total, ok ? 1ull : 0ull}); };
+  const unsigned long long* all = nullptr;
+  size_t xs = 0;
+  PeerXfer px;
+  if (peer_fits(nout + 4)) {
+    // Over peer memory the local reduction's last stage (the chunk fold) puts
+    // this rank's partials, waits for the peers' and folds them, one launch
+    // fewer than staging the record.  (Storing the partials into the peers
+    // from the column kernel itself was slower: 8-byte scattered remote stores
+    // from every thread of its grid.)
+    if (valid && !rt_ensure_ws(reduce3d_ws_bytes(op_run, outer, len, inner))) return DCT_ERR_CUDA;
+    if (exchange(send, hdr(valid), &all, &xs, &px, W, (int64_t)nout) != XCH_PEER) return DCT_ERR_DIST;
+    cudaError_t e = cudaErrorInvalidValue;
+    if (valid) {
+      e = launch_reduce3d_xchg(op_run, bx->d, outer, len, inner, (int32_t)len_offset, px, len_total, o32, oi, rt_ws(),
+                               fold_blocks(nout), st);
+      if (e != cudaSuccess) cudaGetLastError();
+    }
+    if (e != cudaSuccess) {                          // still puts and waits: an invalid header, no outputs
+      valid = false;
+      px.h = hdr(false);
+      e = launch_peer_fold_axis(op_run, px, fold_blocks(nout), nout, len_total, nullptr, nullptr, st);
+    }
+    if (!rt_cuda_ok(e, W)) return DCT_ERR_CUDA;
+  } else {
+    // the packed partials are staged in the local record and all-gathered
+    if (valid && !rt_ensure_ws(reduce3d_ws_bytes(op_run, outer, len, inner))) return DCT_ERR_CUDA;
+    if (valid && !rt_cuda_ok(launch_reduce3d_packed(op_run, bx->d, outer, len, inner, (int32_t)len_offset, send,
+                                                    rt_ws(), st), W))
+      valid = false;
+    const Xch how = exchange(send, hdr(valid), &all, &xs, &px, W, (int64_t)nout);
+    if (how == XCH_FAIL) return DCT_ERR_DIST;
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess && valid) e = launch_fold_packed(op_run, all, (uint32_t)D.world, nout, xs, len_total, o32, oi, st);
+    if (!rt_cuda_ok(e, W)) return DCT_ERR_CUDA;
+  }
   if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_reduce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
   return 0;
 }
@@ -810,27 +747,42 @@ DCT_API int dct_dist_reduce_all(int op, void* x, uint64_t n, void* out, double* 
   double* rec = (double*)D.send;
   const int local_op = op == RED_MEAN ? RED_SUM : op;
   // record [value, n, valid, 0]; value = float64 sum (mean: the raw sum) or
-  // extreme, written by the reduction when one runs and 0 otherwise
-  bool ran = false;
-  if (valid && n > 0) {
-    if (!rt_ensure_ws(full_reduce_ws_bytes() + 256)) return DCT_ERR_CUDA;
-    float* scratch32 = reinterpret_cast<float*>(rec + 4);              // float copy of the local result, unused
-    if (!rt_cuda_ok(launch_full_reduce(local_op, bx->d, n, scratch32, rec, rt_ws(), st), W)) valid = false;
-    ran = valid;
-  }
-  const unsigned long long hn = f64_bits((double)n), hv = f64_bits(valid ? 1.0 : 0.0);
-  const Hdr h = ran ? make_hdr(1, {hn, hv, 0ull}) : make_hdr(0, {0ull, hn, hv, 0ull});
+  // extreme, computed by the reduction when one runs and 0 otherwise
+  const int post = op == RED_MEAN ? 1 : 0;
+  const unsigned long long hn = f64_bits((double)n);
+  auto hdr = [&](bool ran, bool ok) {
+    const unsigned long long hv = f64_bits(ok ? 1.0 : 0.0);
+    return ran ? make_hdr(1, {hn, hv, 0ull}) : make_hdr(0, {0ull, hn, hv, 0ull});
+  };
   const unsigned long long* all = nullptr;
   size_t xs = 0;
   PeerXfer px;
-  const Xch how = exchange(rec, h, &all, &xs, &px, W);
-  if (how == XCH_FAIL) return DCT_ERR_DIST;
-  const cudaError_t fe =
-      how == XCH_PEER
-          ? launch_pdl(k_peer_fold_full, dim3(fold_blocks(1)), dim3(256), 0, st, px, local_op, op == RED_MEAN ? 1 : 0,
-                       valid ? bo->d : nullptr, D.fold)
-          : launch_pdl(k_fold_full, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world, local_op,
-                       op == RED_MEAN ? 1 : 0, valid ? bo->d : nullptr, D.fold, device_error_word());
+  if (valid && n > 0 && !rt_ensure_ws(full_reduce_ws_bytes() + 256)) return DCT_ERR_CUDA;
+  cudaError_t fe = cudaSuccess;
+  if (peer_fits(4)) {
+    // over peer memory pass 2 of the reduction puts, waits and folds itself
+    bool fused = false;
+    if (valid && n > 0) {
+      if (exchange(rec, hdr(true, true), &all, &xs, &px, W) != XCH_PEER) return DCT_ERR_DIST;
+      fused = launch_full_reduce_xchg(local_op, bx->d, n, px, post, bo->d, D.fold, rt_ws(), st) == cudaSuccess;
+      if (!fused) { cudaGetLastError(); valid = false; px.h = hdr(false, false); }
+    } else if (exchange(rec, hdr(false, valid), &all, &xs, &px, W) != XCH_PEER) {
+      return DCT_ERR_DIST;
+    }
+    if (!fused)
+      fe = launch_pdl(k_peer_fold_full, dim3(fold_blocks(1)), dim3(256), 0, st, px, local_op, post,
+                      valid ? bo->d : nullptr, D.fold);
+  } else {
+    bool ran = false;
+    if (valid && n > 0) {
+      float* scratch32 = reinterpret_cast<float*>(rec + 4);              // float copy of the local result, unused
+      if (!rt_cuda_ok(launch_full_reduce(local_op, bx->d, n, scratch32, rec, rt_ws(), st), W)) valid = false;
+      ran = valid;
+    }
+    if (exchange(rec, hdr(ran, valid), &all, &xs, &px, W) == XCH_FAIL) return DCT_ERR_DIST;
+    fe = launch_pdl(k_fold_full, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world, local_op, post,
+                    valid ? bo->d : nullptr, D.fold, device_error_word());
+  }
   if (!rt_cuda_ok(fe, W)) return DCT_ERR_CUDA;
   if (host_out64) {
     double* hs = rt_host_scratch();
@@ -858,9 +810,21 @@ DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, ui
                (!loss || (bs && bs->count >= 1)) && (!logprobs || (bq && bq->count >= n));
   cudaStream_t st = rt_stream();
   double* rec = (double*)D.send;
-  // record [loss sum, rows, valid, 0]; the loss sum is written by the kernel
+  // record [loss sum, rows, valid, 0]; the loss sum is computed by the kernel
   // when it computes a loss and 0 otherwise
-  bool ran = false;
+  const unsigned long long hr = f64_bits((double)rows);
+  auto hdr = [&](bool ran, bool ok) {
+    const unsigned long long hv = f64_bits(ok ? 1.0 : 0.0);
+    return ran ? make_hdr(1, {hr, hv, 0ull}) : make_hdr(0, {0ull, hr, hv, 0ull});
+  };
+  const unsigned long long* all = nullptr;
+  size_t xs = 0;
+  PeerXfer px;
+  if (valid && rows > 0 && !rt_ensure_ws(softmax_ce_ws_bytes(rows, K))) return DCT_ERR_CUDA;
+  // over peer memory the loss fold puts, waits and folds itself
+  const bool fuse = peer_fits(4) && valid && rows > 0 && bt;
+  if (fuse && exchange(rec, hdr(true, true), &all, &xs, &px, W) != XCH_PEER) return DCT_ERR_DIST;
+  bool ran = false, fused = false;
   if (valid && rows > 0) {
     SoftmaxCEArgs a;
     a.logits = bl->d;
@@ -871,26 +835,34 @@ DCT_API int dct_dist_softmax_ce(void* logits, void* labels, int labels_int32, ui
     a.probs = bp ? bp->d : nullptr;
     a.dlogits = bd ? bd->d : nullptr;
     a.logprobs = bq ? bq->d : nullptr;
-    a.loss_partial = bt ? rec : nullptr;
     a.grad_div = grad_div;
     a.err = device_error_word();
-    if (!rt_ensure_ws(softmax_ce_ws_bytes(rows, K))) return DCT_ERR_CUDA;
+    if (fuse) {
+      a.xchg = &px;
+      a.loss = bs ? bs->d : nullptr;
+      a.loss_div = (double)loss_div;
+    } else {
+      a.loss_partial = bt ? rec : nullptr;
+    }
     if (!rt_cuda_ok(launch_softmax_ce(a, rt_ws(), st), W)) valid = false;
     ran = valid && a.loss_partial;
+    fused = valid && fuse;
   }
-  const unsigned long long hr = f64_bits((double)rows), hv = f64_bits(valid ? 1.0 : 0.0);
-  const Hdr h = ran ? make_hdr(1, {hr, hv, 0ull}) : make_hdr(0, {0ull, hr, hv, 0ull});
-  const unsigned long long* all = nullptr;
-  size_t xs = 0;
-  PeerXfer px;
-  const Xch how = exchange(rec, h, &all, &xs, &px, W);
-  if (how == XCH_FAIL) return DCT_ERR_DIST;
-  const cudaError_t fe =
-      how == XCH_PEER
-          ? launch_pdl(k_peer_fold_loss, dim3(fold_blocks(1)), dim3(256), 0, st, px, (double)loss_div,
-                       bs && valid ? bs->d : nullptr)
-          : launch_pdl(k_fold_loss, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
-                       (double)loss_div, bs && valid ? bs->d : nullptr, device_error_word());
+  cudaError_t fe = cudaSuccess;
+  if (fuse) {
+    if (!fused) {                                   // still puts and waits: an invalid header, no loss
+      px.h = hdr(false, false);
+      fe = launch_pdl(k_peer_fold_loss, dim3(fold_blocks(1)), dim3(256), 0, st, px, (double)loss_div, nullptr);
+    }
+  } else {
+    const Xch how = exchange(rec, hdr(ran, valid), &all, &xs, &px, W);
+    if (how == XCH_FAIL) return DCT_ERR_DIST;
+    fe = how == XCH_PEER
+             ? launch_pdl(k_peer_fold_loss, dim3(fold_blocks(1)), dim3(256), 0, st, px, (double)loss_div,
+                          bs && valid ? bs->d : nullptr)
+             : launch_pdl(k_fold_loss, dim3(1), dim3(32), 0, st, (const double*)all, (uint64_t)xs, D.world,
+                          (double)loss_div, bs && valid ? bs->d : nullptr, device_error_word());
+  }
   if (!rt_cuda_ok(fe, W)) return DCT_ERR_CUDA;
   if (!valid) { note_error(DCT_ERR_ARG, "dct_dist_softmax_ce: invalid handles or sizes on this rank"); return DCT_ERR_ARG; }
   return 0;
@@ -906,27 +878,41 @@ bool bn_exchange(const float* x, const float* dy, uint32_t N, uint32_t C, uint32
   if (!buffers(stride * 8, stride * 8 * (size_t)D.world, ((size_t)nsum + 1) * 8, W)) { *rc = DCT_ERR_CUDA; return false; }
   cudaStream_t st = rt_stream();
   double* rec = (double*)D.send;
-  if (valid) {
-    if (!rt_ensure_ws(bn_ws_bytes(N, C))) { *rc = DCT_ERR_CUDA; return false; }
-    double* ps = (double*)rt_ws();
-    cudaError_t e = launch_bn_plane_sums(x, dy, N, C, S, ps, st);
-    if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, rec, st);     // [C][2] sums straight into the record
-    if (!rt_cuda_ok(e, W)) valid = false;
-  }
+  if (valid && !rt_ensure_ws(bn_ws_bytes(N, C))) { *rc = DCT_ERR_CUDA; return false; }
   // header [count, valid, nsum, 0] after the 2C sums (an invalid rank's sums
   // are never used: its valid word fails the fold on every rank)
-  const Hdr h = make_hdr(nsum, {f64_bits((double)N * (double)S), f64_bits(valid ? 1.0 : 0.0), f64_bits((double)nsum),
-                                0ull});
+  auto hdr = [&](bool ok) {
+    return make_hdr(nsum, {f64_bits((double)N * (double)S), f64_bits(ok ? 1.0 : 0.0), f64_bits((double)nsum), 0ull});
+  };
   const unsigned long long* all = nullptr;
   size_t xs = 0;
   PeerXfer px;
-  const Xch how = exchange(rec, h, &all, &xs, &px, W);
-  if (how == XCH_FAIL) { *rc = DCT_ERR_DIST; return false; }
-  const cudaError_t fe =
-      how == XCH_PEER
-          ? launch_pdl(k_peer_fold_sums, dim3(fold_blocks((uint64_t)nsum + 1)), dim3(256), 0, st, px, nsum, D.fold)
-          : launch_pdl(k_fold_sums, dim3((nsum + 1 + 255) / 256), dim3(256), 0, st, (const double*)all,
-                       (uint64_t)xs, D.world, nsum, D.fold, device_error_word());
+  cudaError_t fe = cudaSuccess;
+  if (peer_fits(stride)) {
+    // over peer memory the channel fold puts, waits and folds itself
+    if (exchange(rec, hdr(valid), &all, &xs, &px, W) != XCH_PEER) { *rc = DCT_ERR_DIST; return false; }
+    bool fused = false;
+    if (valid) {
+      double* ps = (double*)rt_ws();
+      cudaError_t e = launch_bn_plane_sums(x, dy, N, C, S, ps, st);
+      if (e == cudaSuccess) e = launch_bn_fold_xchg(ps, N, C, px, D.fold, st);
+      fused = e == cudaSuccess;
+      if (!fused) { cudaGetLastError(); px.h = hdr(false); }
+    }
+    if (!fused)                                     // still puts and waits: an invalid header
+      fe = launch_pdl(k_peer_fold_sums, dim3(fold_blocks((uint64_t)nsum + 1)), dim3(256), 0, st, px, nsum, D.fold);
+  } else {
+    if (valid) {
+      double* ps = (double*)rt_ws();
+      cudaError_t e = launch_bn_plane_sums(x, dy, N, C, S, ps, st);
+      if (e == cudaSuccess) e = launch_bn_fold(ps, N, C, rec, st);     // [C][2] sums straight into the record
+      if (!rt_cuda_ok(e, W)) valid = false;
+    }
+    const Xch how = exchange(rec, hdr(valid), &all, &xs, &px, W);
+    if (how == XCH_FAIL) { *rc = DCT_ERR_DIST; return false; }
+    fe = launch_pdl(k_fold_sums, dim3((nsum + 1 + 255) / 256), dim3(256), 0, st, (const double*)all, (uint64_t)xs,
+                    D.world, nsum, D.fold, device_error_word());
+  }
   if (!rt_cuda_ok(fe, W)) {
     *rc = DCT_ERR_CUDA;
     return false;

@@ -13,6 +13,7 @@
 // dgamma / dbeta.  The apply kernels stream the flat array in 16 KB chunks per
 // block and find each float4's channel with two fast divisions.
 #include "dct_common.cuh"
+#include "dct_fold.cuh"
 #include "kernels.h"
 
 namespace dct {
@@ -95,6 +96,39 @@ __global__ void __launch_bounds__(256) k_bn_fold(const double* __restrict__ ps, 
   for (uint32_t n = lane; n < N; n += 32) acc += ps[2 * ((uint64_t)n * C + c) + j];
   acc = warp_sum(acc);
   if (lane == 0) chan[k] = acc;
+}
+
+// The same fold for a sharded batch, in the same launch as the exchange over
+// peer memory: lane 0 of the warp for sum k stores this rank's sum (record word
+// k) into every peer's slot, then adds every rank's in rank order into out[k];
+// block 0 also stores the header [count, valid, 2C, -] and writes out[2C], the
+// global count (fold_sums).  The launch keeps every block resident, since each
+// waits for the peers' puts.
+__global__ void __launch_bounds__(256) k_bn_fold_xchg(const double* __restrict__ ps, uint32_t N, uint32_t C,
+                                                      double* out, const __grid_constant__ PeerXfer p) {
+  pdl_entry();
+  bool gave_up = false;
+  peer_put_header(p);
+  const uint32_t nsum = 2 * C;
+  const int lane = threadIdx.x & 31;
+  const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+  for (uint32_t k = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; k < nsum; k += warps) {
+    const uint32_t c = k >> 1, j = k & 1;
+    double acc = 0.0;
+    for (uint32_t n = lane; n < N; n += 32) acc += ps[2 * ((uint64_t)n * C + c) + j];
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      peer_put_word(p, k, (unsigned long long)__double_as_longlong(acc));
+      double tot = 0.0;
+      for (int r = 0; r < p.world; ++r) {
+        const double v = r == p.rank ? acc : peer_get_f64(p, r, k, gave_up);
+        tot = r == 0 ? v : tot + v;
+      }
+      out[k] = tot;
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) fold_sums(PeerRecs{p, gave_up}, p.world, nsum, out, p.err, nsum);
+  peer_sync(p, gave_up);
 }
 
 __global__ void k_bn_stats_final(const double* chan, uint32_t C, double cnt, float* mean, float* var, float* rm,
@@ -284,6 +318,21 @@ cudaError_t launch_bn_plane_sums(const float* x, const float* dy, uint32_t N, ui
 cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, double* chan, cudaStream_t st) {
   if (C == 0) return cudaSuccess;
   launch_pdl(k_bn_fold, dim3((unsigned)((2ull * C * 32 + 255) / 256)), dim3(256), 0, st, plane_sums, N, C, chan);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bn_fold_xchg(const double* plane_sums, uint32_t N, uint32_t C, const PeerXfer& p, double* out,
+                                cudaStream_t st) {
+  if (C == 0) return cudaErrorInvalidValue;
+  static int occ = 0;
+  if (occ == 0) {
+    int b = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_bn_fold_xchg, 256, 0);
+    occ = (e == cudaSuccess && b > 0) ? b : 1;
+    cudaGetLastError();
+  }
+  const uint64_t need = (2ull * C * 32 + 255) / 256, cap = (uint64_t)dev_info().sm_count * (uint64_t)occ;
+  launch_pdl(k_bn_fold_xchg, dim3((unsigned)(need < cap ? need : cap)), dim3(256), 0, st, plane_sums, N, C, out, p);
   return cudaGetLastError();
 }
 

@@ -24,7 +24,7 @@
 #include <algorithm>
 
 #include "dct_common.cuh"
-#include "dct_peer.cuh"
+#include "dct_fold.cuh"
 #include "kernels.h"
 
 namespace dct {
@@ -471,6 +471,66 @@ __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* _
   }
 }
 
+// The last stage of a sharded axis reduction whose plan has more than one
+// chunk, in the same launch as the exchange over peer memory (dct_peer.cuh):
+// lane l of warp 0 folds column k's chunk partials as k_fold_chunks does,
+// stores this rank's packed partial (global index) into every peer's slot,
+// then merges every rank's partial for k in rank order as each arrives (ties
+// to the lower index; mean divides by len_total) and emits.  The launch keeps
+// every block resident, since each waits for the peers' puts.
+template <int OP>
+__global__ void __launch_bounds__(256) k_fold_chunks_xchg(const unsigned long long* __restrict__ part, uint64_t nout,
+                                                          uint32_t chunks, uint64_t inner, uint64_t len_total,
+                                                          int32_t idx_off, RedOut fin,
+                                                          const __grid_constant__ PeerXfer p) {
+  pdl_entry();
+  bool gave_up = false;
+  peer_put_header(p);
+  __shared__ unsigned long long sh[kRedWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (uint64_t k0 = (uint64_t)blockIdx.x * 32; k0 < nout; k0 += (uint64_t)gridDim.x * 32) {
+    const uint64_t k = k0 + lane;
+    Acc<OP> a;
+    a.reset();
+    if (k < nout) {
+      const uint64_t o = k / inner, c = k - o * inner;
+      const unsigned long long* q = part + o * chunks * inner + c;
+#pragma unroll 4
+      for (uint32_t ch = warp; ch < chunks; ch += kRedWarps) {
+        Acc<OP> t;
+        t.unpack(__ldcg(q + (uint64_t)ch * inner));
+        a.merge(t);
+      }
+    }
+    sh[warp][lane] = a.pack();
+    __syncthreads();
+    if (warp == 0 && k < nout) {
+      Acc<OP> tot;
+      tot.unpack(sh[0][lane]);
+#pragma unroll
+      for (int w = 1; w < kRedWarps; ++w) {
+        Acc<OP> t;
+        t.unpack(sh[w][lane]);
+        tot.merge(t);
+      }
+      if constexpr (Acc<OP>::kArg) { if (tot.i >= 0) tot.i += idx_off; }
+      const unsigned long long mine = tot.pack();
+      peer_put_word(p, k, mine);
+      Acc<OP> g;
+      g.reset();
+      for (int r = 0; r < p.world; ++r) {
+        Acc<OP> t;
+        t.unpack(r == p.rank ? mine : peer_get(p, r, k, gave_up));
+        g.merge(t);
+      }
+      if (fin.out || fin.idx) g.emit(fin, k, len_total);
+    }
+    __syncthreads();
+  }
+  peer_sync(p, gave_up);
+  peer_check_axis(p, gave_up);
+}
+
 // generic strided: one thread per output
 template <int OP>
 __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict__ x, uint64_t outer, uint64_t len,
@@ -571,9 +631,34 @@ int cols_occupancy(bool vec) {
   return cols_occ[vi];
 }
 
+// Blocks of k_fold_chunks_xchg that are resident at once (every block waits
+// for the peers' puts): at most the SMs times its occupancy.
+template <int OP>
+unsigned xchg_fold_blocks(uint64_t nout) {
+  static int occ = 0;
+  if (occ == 0) {
+    int b = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_fold_chunks_xchg<OP>, 256, 0);
+    occ = (e == cudaSuccess && b > 0) ? b : 1;
+    cudaGetLastError();
+  }
+  const uint64_t cap = (uint64_t)dev_info().sm_count * (uint64_t)occ;
+  const uint64_t need = (nout + 31) / 32;
+  return (unsigned)(need < cap ? need : cap);
+}
+
+// The exchange a sharded axis reduction's last stage runs (null: none).
+struct XchgFold {
+  const PeerXfer* p = nullptr;
+  uint64_t len_total = 0;
+  RedOut fin;                 // the final outputs
+  bool* done = nullptr;       // set when the last stage exchanged and folded
+};
+
 template <int OP>
 cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
-                       uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st) {
+                       uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st,
+                       const XchgFold& xf = XchgFold{}) {
   if (outer == 0 || inner == 0) return cudaSuccess;
   if (len == 0) return cudaErrorInvalidValue;
   Plan p = make_plan(outer, len, inner, so, sl, si, x);
@@ -599,20 +684,26 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || nparts == 1) return e;
   const uint64_t nout = outer * inner;
+  if (xf.p) {
+    if (xf.done) *xf.done = true;
+    return launch_pdl(k_fold_chunks_xchg<OP>, dim3(xchg_fold_blocks<OP>(nout)), dim3(256), 0, st,
+                      (const unsigned long long*)part, nout, nparts, inner, xf.len_total, ro.idx_off, xf.fin, *xf.p);
+  }
   return launch_pdl(k_fold_chunks<OP>, dim3(grid_for(nout, 32)), dim3(256), 0, st, (const unsigned long long*)part,
                     nout, nparts, inner, len, ro);
 }
 
 cudaError_t dispatch_reduce(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner, uint64_t so,
-                            uint64_t sl, uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st) {
+                            uint64_t sl, uint64_t si, const RedOut& ro, void* ws, size_t ws_bytes, cudaStream_t st,
+                            const XchgFold& xf = XchgFold{}) {
   switch (op) {
-    case RED_SUM: return run_reduce<RED_SUM>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
-    case RED_MEAN: return run_reduce<RED_MEAN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
-    case RED_MAX: return run_reduce<RED_MAX>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
-    case RED_ARGMAX: return run_reduce<RED_ARGMAX>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
-    case RED_MIN: return run_reduce<RED_MIN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
-    case RED_ARGMIN: return run_reduce<RED_ARGMIN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
-    case RED_SUMSQ: return run_reduce<RED_SUMSQ>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st);
+    case RED_SUM: return run_reduce<RED_SUM>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
+    case RED_MEAN: return run_reduce<RED_MEAN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
+    case RED_MAX: return run_reduce<RED_MAX>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
+    case RED_ARGMAX: return run_reduce<RED_ARGMAX>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
+    case RED_MIN: return run_reduce<RED_MIN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
+    case RED_ARGMIN: return run_reduce<RED_ARGMIN>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
+    case RED_SUMSQ: return run_reduce<RED_SUMSQ>(x, outer, len, inner, so, sl, si, ro, ws, ws_bytes, st, xf);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -786,6 +877,34 @@ cudaError_t launch_peer_fold_axis(int op, const PeerXfer& p, unsigned blocks, ui
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_reduce3d_xchg(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
+                                 int32_t idx_off, const PeerXfer& p, uint64_t len_total, float* out,
+                                 int32_t* out_idx, void* ws, unsigned fold_blocks, cudaStream_t st) {
+  const uint64_t nout = outer * inner;
+  if (nout == 0) return cudaSuccess;
+  unsigned long long* rec = const_cast<unsigned long long*>(p.rec);
+  bool done = false;
+  cudaError_t e;
+  if (len == 0) {
+    e = launch_reduce3d_packed(op, x, outer, len, inner, idx_off, rec, ws, st);     // identity partials
+  } else {
+    RedOut ro;
+    ro.packed = rec;                    // a single-chunk plan emits the record here
+    ro.idx_off = idx_off;
+    XchgFold xf;
+    xf.p = &p;
+    xf.len_total = len_total;
+    xf.fin.out = out;
+    xf.fin.idx = out_idx;
+    xf.done = &done;
+    const size_t need = reduce3d_ws_bytes(op, outer, len, inner);
+    e = inner == 1 ? dispatch_reduce(op, x, outer, len, 1, len, 1, 1, ro, ws, need, st, xf)
+                   : dispatch_reduce(op, x, outer, len, inner, len * inner, inner, 1, ro, ws, need, st, xf);
+  }
+  if (e != cudaSuccess || done) return e;
+  return launch_peer_fold_axis(op, p, fold_blocks, nout, len_total, out, out_idx, st);
 }
 
 cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,
@@ -1037,32 +1156,57 @@ __global__ void __launch_bounds__(kFullThreads) k_full_pass1(const float* __rest
   }
 }
 
+// The block's fold of the pass-1 partials; the result is thread 0's.
 template <int OP>
-__global__ void k_full_pass2(const double* part, int nparts, uint64_t n, int post, float* out32, double* out64) {
-  pdl_entry();
-  __shared__ double sh[32];
+DCT_DEV double full_pass2_value(const double* part, int nparts, double* sh) {
   if constexpr (OP == RED_MAX || OP == RED_MIN) {
+    double t = 0.0;
     if (threadIdx.x == 0) {
-      double t = part[0];
+      t = part[0];
       for (int k = 1; k < nparts; ++k) {
         double ov = part[k];
         if (isnan(ov) || (!isnan(t) && ((OP == RED_MAX) ? ov > t : ov < t))) t = ov;
       }
-      out32[0] = (float)t;
-      if (out64) out64[0] = t;
     }
+    return t;
   } else {
     // fixed assignment: thread t sums parts t, t+B, ... in order, then block tree
     double acc = 0.0;
     for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
-    double t = block_sum(acc, sh);
-    if (threadIdx.x == 0) {
-      if (post == 1) t = t / (double)n;                 // mean
-      else if (post == 2) t = sqrt(t / (double)n);      // rms
-      out32[0] = (float)t;
-      if (out64) out64[0] = t;
-    }
+    return block_sum(acc, sh);
   }
+}
+
+template <int OP>
+__global__ void k_full_pass2(const double* part, int nparts, uint64_t n, int post, float* out32, double* out64) {
+  pdl_entry();
+  __shared__ double sh[32];
+  double t = full_pass2_value<OP>(part, nparts, sh);
+  if (threadIdx.x == 0) {
+    if (post == 1) t = t / (double)n;                 // mean
+    else if (post == 2) t = sqrt(t / (double)n);      // rms
+    out32[0] = (float)t;
+    if (out64) out64[0] = t;
+  }
+}
+
+// Pass 2 of a sharded full reduction, in the same launch as the exchange over
+// peer memory: thread 0 stores this rank's value (record word 0) into every
+// peer's slot, block 0 the header [count, valid, -], and thread 0 folds every
+// rank's record in rank order (fold_full; post 1 divides by the global count).
+template <int OP>
+__global__ void k_full_pass2_xchg(const double* part, int nparts, int post, float* out32, double* out64,
+                                  const __grid_constant__ PeerXfer p) {
+  pdl_entry();
+  __shared__ double sh[32];
+  bool gave_up = false;
+  peer_put_header(p);
+  const double t = full_pass2_value<OP>(part, nparts, sh);
+  if (threadIdx.x == 0) {
+    peer_put_word(p, 0, (unsigned long long)__double_as_longlong(t));
+    fold_full(PeerRecsOwn0{p, gave_up, t}, p.world, OP, post, out32, out64, p.err);
+  }
+  peer_sync(p, gave_up);
 }
 
 static cudaError_t full_reduce_post(int op, const float* x, uint64_t n, float* out32, double* out64, void* ws,
@@ -1083,6 +1227,29 @@ static cudaError_t full_reduce_post(int op, const float* x, uint64_t n, float* o
       launch_pdl(k_full_pass2<RED_MAX>, dim3(1), dim3(32), 0, st, part, blocks, n, 0, out32, out64); break;
     case RED_MIN: launch_pdl(k_full_pass1<RED_MIN>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
       launch_pdl(k_full_pass2<RED_MIN>, dim3(1), dim3(32), 0, st, part, blocks, n, 0, out32, out64); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_full_reduce_xchg(int op, const float* x, uint64_t n, const PeerXfer& p, int post, float* out32,
+                                    double* out64, void* ws, cudaStream_t st) {
+  if (!ws || n == 0) return cudaErrorInvalidValue;
+  double* part = (double*)ws;
+  const DevInfo& d = dev_info();
+  const int maxb = d.sm_count * (d.max_threads_per_sm / kFullThreads);
+  uint64_t need = (n + 4 * (uint64_t)kFullThreads - 1) / (4 * (uint64_t)kFullThreads);
+  int blocks = (int)(need < (uint64_t)maxb ? need : (uint64_t)maxb);
+  if (blocks < 1) blocks = 1;
+  switch (op) {
+    case RED_SUM: launch_pdl(k_full_pass1<RED_SUM>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2_xchg<RED_SUM>, dim3(1), dim3(1024), 0, st, part, blocks, post, out32, out64, p); break;
+    case RED_SUMSQ: launch_pdl(k_full_pass1<RED_SUMSQ>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2_xchg<RED_SUMSQ>, dim3(1), dim3(1024), 0, st, part, blocks, post, out32, out64, p); break;
+    case RED_MAX: launch_pdl(k_full_pass1<RED_MAX>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2_xchg<RED_MAX>, dim3(1), dim3(32), 0, st, part, blocks, post, out32, out64, p); break;
+    case RED_MIN: launch_pdl(k_full_pass1<RED_MIN>, dim3(blocks), dim3(kFullThreads), 0, st, x, n, part);
+      launch_pdl(k_full_pass2_xchg<RED_MIN>, dim3(1), dim3(32), 0, st, part, blocks, post, out32, out64, p); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -19,6 +19,7 @@
 #include <algorithm>
 
 #include "dct_common.cuh"
+#include "dct_fold.cuh"
 #include "dct_tma.cuh"
 #include "kernels.h"
 
@@ -431,6 +432,26 @@ __global__ void k_loss_final(const double* part, int nparts, double div, float* 
   }
 }
 
+// The same fold for a sharded batch, in the same launch as the exchange over
+// peer memory: thread 0 stores this rank's loss sum (record word 0) into every
+// peer's slot, block 0 the header [rows, valid, -], and thread 0 folds every
+// rank's record in rank order into loss = sum / div (fold_loss).
+__global__ void k_loss_final_xchg(const double* part, int nparts, double div, float* loss,
+                                  const __grid_constant__ PeerXfer p) {
+  pdl_entry();
+  __shared__ double sh[32];
+  bool gave_up = false;
+  peer_put_header(p);
+  double acc = 0.0;
+  for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
+  const double t = block_sum(acc, sh);
+  if (threadIdx.x == 0) {
+    peer_put_word(p, 0, (unsigned long long)__double_as_longlong(t));
+    fold_loss(PeerRecsOwn0{p, gave_up, t}, p.world, div, loss, p.err);
+  }
+  peer_sync(p, gave_up);
+}
+
 int softmax_blocks(uint32_t rows, uint32_t K) {
   const DevInfo& d = dev_info();
   if (K > 2048) {
@@ -451,6 +472,14 @@ int softmax_blocks(uint32_t rows, uint32_t K) {
 // per warp; 8 warps fit only 3 blocks (24 warps).
 static uint32_t tma_stage_bytes(uint32_t K) { return ((K * 4u) + 15u) & ~15u; }
 static int tma_warps(uint32_t K) { return tma_stage_bytes(K) <= 4096 ? 7 : 4; }
+
+// The block-order fold of the per-block loss partials: loss / loss_partial,
+// or, for a sharded batch over peer memory, the exchange and the rank fold.
+static cudaError_t launch_loss_fold(const RowCtx& c, int nparts, const SoftmaxCEArgs& a, cudaStream_t st) {
+  if (a.xchg) launch_pdl(k_loss_final_xchg, dim3(1), dim3(1024), 0, st, c.part, nparts, a.loss_div, a.loss, *a.xchg);
+  else launch_pdl(k_loss_final, dim3(1), dim3(1024), 0, st, c.part, nparts, a.loss_div, a.loss, a.loss_partial);
+  return cudaGetLastError();
+}
 
 // blocks of the TMA-staged kernel: one per WPB * kTmaRows consecutive rows
 int tma_blocks(uint32_t rows, uint32_t K) {
@@ -484,7 +513,7 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
   c.probs = a.probs;
   c.dlogits = a.dlogits;
   c.logprobs = a.logprobs;
-  c.want_loss = (a.loss != nullptr || a.loss_partial != nullptr) && a.labels != nullptr;
+  c.want_loss = (a.loss != nullptr || a.loss_partial != nullptr || a.xchg != nullptr) && a.labels != nullptr;
   c.part = (double*)ws;
   if (c.want_loss && !ws) return cudaErrorInvalidValue;
   c.grad_div = a.grad_div;
@@ -527,8 +556,7 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess || !c.want_loss) return e;
-    launch_pdl(k_loss_final, dim3(1), dim3(1024), 0, st, c.part, blocks_t, a.loss_div, a.loss, a.loss_partial);
-    return cudaGetLastError();
+    return launch_loss_fold(c, blocks_t, a, st);
   }
   const int blocks = softmax_blocks(a.rows, a.K);
   if (K <= 128) {
@@ -551,8 +579,7 @@ cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st)
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !c.want_loss) return e;
-  launch_pdl(k_loss_final, dim3(1), dim3(1024), 0, st, c.part, blocks, a.loss_div, a.loss, a.loss_partial);
-  return cudaGetLastError();
+  return launch_loss_fold(c, blocks, a, st);
 }
 
 // ---------------------------------------------------------------------------

@@ -70,10 +70,17 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
 cudaError_t launch_fold_packed(int op, const unsigned long long* parts, uint32_t nparts, uint64_t nout,
                                uint64_t stride, uint64_t len_total, float* out, int32_t* out_idx, cudaStream_t st);
 // The same rank fold fused with the exchange over peer memory (dct_peer.cuh):
-// put this rank's record, wait for every rank's, fold; `blocks` >= world.
+// put this rank's record (p.rec), wait for every rank's, fold.
 struct PeerXfer;
 cudaError_t launch_peer_fold_axis(int op, const PeerXfer& p, unsigned blocks, uint64_t nout, uint64_t len_total,
                                   float* out, int32_t* out_idx, cudaStream_t st);
+// A whole sharded axis reduction over peer memory: the local reduction whose
+// last stage (the chunk fold) also puts this rank's partials, waits for the
+// peers' and folds them in rank order; a single-chunk plan instead emits the
+// record into p.rec and launches launch_peer_fold_axis with `fold_blocks`.
+cudaError_t launch_reduce3d_xchg(int op, const float* x, uint64_t outer, uint64_t len, uint64_t inner,
+                                 int32_t idx_off, const PeerXfer& p, uint64_t len_total, float* out,
+                                 int32_t* out_idx, void* ws, unsigned fold_blocks, cudaStream_t st);
 // Broadcast gradient: out (shape t) = g (shape gshape, ndim <= 8) summed over
 // every dim where t has extent 1 and g does not (t right-aligned and padded
 // with 1s to ndim).  float64 accumulation, rounded once.
@@ -97,6 +104,11 @@ cudaError_t launch_reduce_strided(int op, const float* x, uint64_t outer, uint64
 size_t full_reduce_ws_bytes();
 cudaError_t launch_full_reduce(int op, const float* x, uint64_t n, float* out32, double* out64,
                                void* ws, cudaStream_t st);
+// The same over this rank's n > 0 elements of a sharded vector, pass 2 also
+// exchanging the records [value, count, valid, -] over peer memory and folding
+// them in rank order (post 1: divide by the global count) into out32 / out64.
+cudaError_t launch_full_reduce_xchg(int op, const float* x, uint64_t n, const PeerXfer& p, int post, float* out32,
+                                    double* out64, void* ws, cudaStream_t st);
 // Per-group sum of squares: part[off + g] = sum_{i in group g} x[i]^2, groups of 256.
 cudaError_t launch_grad_sq_reduce(const float* g, uint64_t count, float* partials, uint64_t off,
                                   uint64_t ngroups, cudaStream_t st);
@@ -124,6 +136,9 @@ struct SoftmaxCEArgs {
   float grad_div = 1.0f;
   bool ref_max_init = false;       // true: max starts at -1e30 (nn_softmax.hlsl:8)
   uint32_t* err = nullptr;         // device-visible error word (bounded waits)
+  // sharded: the loss fold also exchanges the records [loss sum, rows, valid, -]
+  // over peer memory and writes loss = (sum over ranks) / loss_div
+  const PeerXfer* xchg = nullptr;
 };
 size_t softmax_ce_ws_bytes(uint32_t rows, uint32_t K);
 cudaError_t launch_softmax_ce(const SoftmaxCEArgs& a, void* ws, cudaStream_t st);
@@ -159,6 +174,11 @@ cudaError_t launch_bn_plane_sums(const float* x, const float* dy, uint32_t N, ui
 // Fold plane partials over n into per-channel fp64 sums: chan[c*2+k].
 cudaError_t launch_bn_fold(const double* plane_sums, uint32_t N, uint32_t C, double* chan,
                            cudaStream_t st);
+// The same for a sharded batch, also exchanging the records [2C sums][count,
+// valid, 2C, -] over peer memory: out[0, 2C) = the sums over ranks in rank
+// order, out[2C] = the global count.
+cudaError_t launch_bn_fold_xchg(const double* plane_sums, uint32_t N, uint32_t C, const PeerXfer& p, double* out,
+                                cudaStream_t st);
 // Finalize the forward statistics from per-channel (sum, sumsq) over cnt elements.
 // cnt_dev (optional): element count per channel read on the device instead of
 // `cnt` (a count combined across ranks)
