@@ -24,8 +24,10 @@ The reference drives one D3D11 device and has no multi-GPU path
 Every exchange gathers one small record per rank and folds them on the device
 in rank order, so all ranks get identical results, and at world size 1 the
 sharded ops are bit-identical to the single-GPU entry points.  The records
-travel through NVLink peer memory (one put/wait kernel; CUDA IPC mappings set
-up at init) when every rank could map every other, else by an NCCL all-gather.
+travel through NVLink peer memory when every rank could map every other (CUDA
+IPC mappings set up at init; the op's last kernel stores its record words into
+the peers as tagged lines, waits for theirs and folds), else by an NCCL
+all-gather.
 
     import torch.distributed as td
     td.init_process_group("nccl")                 # or "gloo"
