@@ -579,7 +579,8 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
     }
     uint64_t cl = (len + chunks - 1) / chunks;
     cl = (cl + 3) & ~3ull;
-    chunks = (len + cl - 1) / cl;
+    if (cl == 0) cl = 4;                                      // len 0: one empty chunk
+    chunks = len ? (len + cl - 1) / cl : 1;
     p.chunks = (uint32_t)chunks;
     p.chunk_len = cl;
     const uint64_t warps = outer * chunks;
@@ -601,8 +602,8 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
       if (chunks > max_chunks) chunks = max_chunks;
       if (chunks > 65535) chunks = 65535;
     }
-    const uint64_t cl = (len + chunks - 1) / chunks;
-    chunks = (len + cl - 1) / cl;
+    const uint64_t cl = len ? (len + chunks - 1) / chunks : 1;   // len 0: one empty chunk
+    chunks = len ? (len + cl - 1) / cl : 1;
     p.chunks = (uint32_t)chunks;
     p.chunk_len = cl;
     p.grid = dim3((unsigned)tiles, (unsigned)gy, (unsigned)chunks);
@@ -732,7 +733,8 @@ cudaError_t run_fold_packed(const unsigned long long* parts, uint32_t nparts, ui
 size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,
                                uint64_t si) {
   // the plan depends on pointer alignment only through the vector choice;
-  // size for the larger of the two plans
+  // size for the larger of the two plans (an empty axis or output needs none)
+  if (len == 0 || outer == 0 || inner == 0) return 0;
   size_t best = 0;
   const float* probes[2] = {nullptr, reinterpret_cast<const float*>(4)};
   for (const float* pr : probes) {

@@ -15,6 +15,7 @@ for sums, means, losses and BatchNorm statistics).
 import datetime
 import multiprocessing as mp
 import os
+import queue
 import socket
 import time
 import traceback
@@ -275,6 +276,31 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _collect(q, procs, limit_s):
+    """Every rank's (ok, payload) from q.  A rank whose process ended without
+    posting (a crash) fails the test at once, with the others' reports."""
+    res, deadline = {}, time.monotonic() + limit_s
+    while len(res) < len(procs):
+        try:
+            r, ok, payload = q.get(timeout=5)
+            res[r] = (ok, payload)
+            continue
+        except queue.Empty:
+            pass
+        dead = [i for i, p in enumerate(procs) if i not in res and p.exitcode not in (None, 0)]
+        if dead or time.monotonic() > deadline:
+            while True:                          # reports already queued
+                try:
+                    r, ok, payload = q.get(timeout=1)
+                    res[r] = (ok, payload)
+                except queue.Empty:
+                    break
+            missing = [i for i in range(len(procs)) if i not in res]
+            raise AssertionError(f"ranks {missing} posted nothing (exit codes "
+                                 f"{[procs[i].exitcode for i in missing]}); reports: {res}")
+    return res
+
+
 def _worldn_worker(rank, world, port, q, transport="peer"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), DCT_DEVICE=str(rank),
                       NCCL_NVLS_ENABLE="0", DCT_PEER_EXCHANGE="0" if transport == "nccl" else "1")
@@ -317,6 +343,33 @@ def _worldn_worker(rank, world, port, q, transport="peer"):
                     want.astype(np.float32))))))
             dev.free(ho)
         dev.free(hx)
+        # small shards: a single-chunk plan (its record staged, then the separate
+        # put/wait/fold kernel) and, with fewer rows than ranks, an empty shard
+        for R2 in (2 * world, world - 1):
+            x2 = r.standard_normal((R2, 96)).astype(np.float32)
+            o5, c5 = shard_range(R2, world, rank)
+            hx2 = dev.buf(x2[o5:o5 + c5]) if c5 else dev.empty(1)
+            for op in ("sum", "max", "argmax"):
+                ho = dev.empty(96)
+                comm.reduce(op, hx2, 1, c5, 96, o5, R2, ho)
+                dev.sync()
+                got = dev.read(ho, np.int32 if op == "argmax" else np.float32)
+                if op == "sum":
+                    x64 = x2.astype(np.float64)
+                    want, mag = x64.sum(axis=0), np.abs(x64).sum(axis=0)
+                    err = np.maximum(np.abs(got - want) - 1e-12 * mag, 0.0) / np.abs(want)
+                    errs[f"small{R2}_sum"] = float(np.max(err))
+                else:
+                    errs[f"small{R2}_{op}"] = int(np.sum(got != O.reduce(op, x2, axis=0)))
+                dev.free(ho)
+            dev.free(hx2)
+            v2 = r.uniform(-1, 1, R2).astype(np.float32)
+            hv2, ho2 = (dev.buf(v2[o5:o5 + c5]) if c5 else dev.empty(1)), dev.empty(1)
+            s2 = comm.reduce_all("sum", hv2, c5, ho2, want_host=True)
+            want2 = float(v2.astype(np.float64).sum())
+            errs[f"small{R2}_full_sum"] = abs(s2 - want2) / max(abs(want2), 1e-30)
+            errs[f"small{R2}_full_max"] = int(comm.reduce_all("max", hv2, c5, ho2, want_host=True) != float(v2.max()))
+            dev.free(hv2, ho2)
         # full reduction of a flat vector
         n = (1 << 21) + 5
         v = r.uniform(-1, 1, n).astype(np.float32)
@@ -399,11 +452,8 @@ def test_worldn_sharded_ops_match_unsharded_oracle(transport):
     procs = [ctx.Process(target=_worldn_worker, args=(r, world, port, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
-    res = {}
     try:
-        for _ in range(world):
-            r, ok, payload = q.get(timeout=600)
-            res[r] = (ok, payload)
+        res = _collect(q, procs, 600)
     finally:
         for p in procs:
             p.join(timeout=60)
@@ -414,9 +464,12 @@ def test_worldn_sharded_ops_match_unsharded_oracle(transport):
         assert ok, e
         print(f"rank {r}: {e}")
         assert e["peer_exchange"] == (transport == "peer"), (r, transport)
-        for k in ("max", "argmax", "min", "argmin", "full_max", "dlogits", "bn_y", "bn_dx", "allreduce"):
+        small = [f"small{R2}_" for R2 in (2 * world, world - 1)]
+        for k in ("max", "argmax", "min", "argmin", "full_max", "dlogits", "bn_y", "bn_dx", "allreduce",
+                  *[p + q for p in small for q in ("max", "argmax", "full_max")]):
             assert e[k] == 0, (r, k, e[k])
-        for k in ("sum", "mean", "full_sum", "loss", "bn_mean", "bn_var", "bn_running", "bn_dgamma", "bn_dbeta"):
+        for k in ("sum", "mean", "full_sum", "loss", "bn_mean", "bn_var", "bn_running", "bn_dgamma", "bn_dbeta",
+                  *[p + q for p in small for q in ("sum", "full_sum")]):
             assert e[k] <= 1e-5, (r, k, e[k])
 
 
@@ -482,11 +535,8 @@ def test_worldn_peer_wait_times_out_when_a_rank_skips_an_exchange():
     procs = [ctx.Process(target=_skip_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = {}
     try:
-        for _ in range(world):
-            r, ok, payload = q.get(timeout=300)
-            res[r] = (ok, payload)
+        res = _collect(q, procs, 300)
     finally:
         for p in procs:
             p.join(timeout=60)
