@@ -423,6 +423,33 @@ def _worldn_worker(rank, world, port, q, transport="peer"):
         dx_o = _bn_dx_global(x[o4:o4 + c4], dy[o4:o4 + c4], mean, var, gamma, dg, db, C, S_, N * S_, 1e-5)
         errs["bn_dx"] = int(np.sum(dev.read(hdx).view(np.uint32) != dx_o.view(np.uint32)))
         dev.free(hx, hdy, hgm, hbt, hrm, hrv, hm, hvv, hy, hdg, hdb, hdx)
+        # an empty rank (fewer rows / samples than ranks): softmax-CE and BatchNorm
+        B2, K2 = world - 1, 64
+        lg2 = (3 * r.standard_normal((B2, K2))).astype(np.float32)
+        lab2 = r.integers(0, K2, B2)
+        o6, c6 = shard_range(B2, world, rank)
+        hl2 = dev.buf(lg2[o6:o6 + c6]) if c6 else dev.empty(1)
+        ht2 = dev.buf(lab2[o6:o6 + c6].astype(np.float32)) if c6 else dev.empty(1)
+        hp2, hg2, hs2 = dev.empty(max(c6, 1) * K2), dev.empty(max(c6, 1) * K2), dev.empty(1)
+        comm.softmax_ce(hl2, ht2, c6, K2, probs=hp2, dlogits=hg2, loss=hs2, global_rows=B2)
+        dev.sync()
+        _, l64, _ = O.softmax_ce_f64(lg2, lab2)
+        errs["small_loss"] = abs(float(dev.read(hs2)[0]) - float(l64)) / abs(float(l64))
+        dev.free(hl2, ht2, hp2, hg2, hs2)
+        shape2 = (world - 1, 4, 3, 3)
+        N2, C2 = shape2[0], shape2[1]
+        S2 = shape2[2] * shape2[3]
+        xb, dyb, gb, bb, rmb, rvb = _bn_inputs(shape2, 42)
+        o7, c7 = shard_range(N2, world, rank)
+        hx = dev.buf(xb[o7:o7 + c7]) if c7 else dev.empty(1)
+        hgm, hbt, hrm, hrv = dev.buf(gb), dev.buf(bb), dev.buf(rmb), dev.buf(rvb)
+        hm, hvv, hy = dev.empty(C2), dev.empty(C2), dev.empty(max(c7, 1) * C2 * S2)
+        comm.batchnorm_forward_train(hx, hgm, hbt, hrm, hrv, hm, hvv, hy, c7, C2, S2, 1e-5, 0.1)
+        dev.sync()
+        m64, v64 = S.batchnorm_mean_var(xb.ravel(), N2, C2, S2)
+        errs["small_bn_mean"] = float(np.max(np.abs(dev.read(hm) - m64) / np.maximum(np.abs(m64), 1e-3)))
+        errs["small_bn_var"] = float(np.max(np.abs(dev.read(hvv) - v64) / v64))
+        dev.free(hx, hgm, hbt, hrm, hrv, hm, hvv, hy)
         # fp32 all-reduce
         a = np.full(4099, rank + 1.0, np.float32)
         ha = dev.buf(a)
@@ -469,7 +496,8 @@ def test_worldn_sharded_ops_match_unsharded_oracle(transport):
                   *[p + q for p in small for q in ("max", "argmax", "full_max")]):
             assert e[k] == 0, (r, k, e[k])
         for k in ("sum", "mean", "full_sum", "loss", "bn_mean", "bn_var", "bn_running", "bn_dgamma", "bn_dbeta",
-                  *[p + q for p in small for q in ("sum", "full_sum")]):
+                  *[p + q for p in small for q in ("sum", "full_sum")], "small_loss", "small_bn_mean",
+                  "small_bn_var"):
             assert e[k] <= 1e-5, (r, k, e[k])
 
 
