@@ -1049,12 +1049,16 @@ def cpu_c2_sample(threads: int, rows: int = 1024, reps: int = 3, min_seconds: fl
 
 
 def cpu_other_configs(threads: int) -> dict:
-    """The oracle's arithmetic for C3, C4, C5a and C5b on bounded samples (about 2 s each)."""
+    """The oracle's arithmetic for C1 (whole, one thread), C3, C4, C5a and C5b (bounded
+    samples on `threads` threads), about 1-2 s each."""
     from oracle import threaded as T
     out = {}
-    for key, fn in (("c3", T.c3_sample), ("c4", T.c4_sample), ("c5a", T.c5a_sample), ("c5b", T.c5b_sample)):
+    for key, fn in (("c1", T.c1_sample), ("c3", T.c3_sample), ("c4", T.c4_sample), ("c5a", T.c5a_sample),
+                    ("c5b", T.c5b_sample)):
         gbs, secs, desc = fn(threads)
-        out[key] = {"gbs": round(gbs, 2), "s_per_pass": round(secs, 4), "sample": desc}
+        out[key] = {"gbs": round(gbs, 2), "s_per_pass": round(secs, 6 if key == "c1" else 4), "sample": desc}
+        if key == "c1":
+            out[key]["us_per_step"] = round(secs * 1e6, 1)
     return out
 
 

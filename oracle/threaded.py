@@ -90,6 +90,47 @@ def _timed(fn, reps: int, min_seconds: float, warmup: int = 1):
     return (time.perf_counter() - t0) / n, n
 
 
+def c1_sample(threads: int = 1, M: int = 256, N: int = 784, seed: int = 0, reps: int = 500,
+              min_seconds: float = 1.0):
+    """Config C1 whole, as NumPy runs it on the CPU (one thread: the arrays are 0.8 MB):
+    Y = relu(X + b), sum(Y, axis=0), sum(Y), dX = relu_grad(ones, Y), db = sum(dX, axis=0),
+    acc += db.  The vectorised forms are checked once against the oracle's formulas for
+    nn_bias_relu.hlsl, nn_bias_grad.hlsl, nn_relu_grad.hlsl and nn_grad_accum.hlsl (same
+    bits; the sums in float64), then timed.  `threads` is ignored.  Returns (GB/s over the
+    chain's algorithmic bytes, seconds per step, text)."""
+    from . import shaders as S
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((M, N), dtype=F32)
+    b = rng.uniform(-0.1, 0.1, N).astype(F32)
+    ones = np.ones((M, N), F32)
+    acc = np.zeros(N, F32)
+    zero = F32(0.0)
+
+    def chain(acc):
+        Y = np.maximum(X + b, zero)
+        s0 = Y.sum(axis=0, dtype=np.float64).astype(F32)
+        tot = Y.sum(dtype=np.float64)
+        dX = np.where(Y > 0, ones, zero)
+        db = dX.sum(axis=0, dtype=np.float64).astype(F32)
+        return Y, s0, tot, dX, db, acc + db
+
+    Y, s0, _, dX, db, acc1 = chain(acc)
+    assert np.array_equal(Y.ravel(), S.bias_relu(X.ravel(), b, M, N))
+    assert np.array_equal(s0, S.bias_grad(Y.ravel(), M, N, N, 1))
+    assert np.array_equal(dX.ravel(), S.relu_grad(ones.ravel(), Y.ravel(), M * N))
+    assert np.array_equal(db, S.bias_grad(dX.ravel(), M, N, N, 1))
+    assert np.array_equal(acc1, S.grad_accum(acc, db, N))
+
+    def step():
+        nonlocal acc
+        acc = chain(acc)[-1]
+    secs, n = _timed(step, reps, min_seconds)
+    nbytes = 4 * (3 * M * N + 2 * N + 1) + 4 * (3 * M * N + N)
+    desc = (f"C1 whole: X[{M},{N}] forward + backward chain (6 ops) per step, "
+            f"{secs * 1e6:.0f} us per step; {n} steps, 1 thread")
+    return nbytes / secs / 1e9, secs, desc
+
+
 def c3_sample(threads: int, rows: int = 2048, cols: int = 4096, seed: int = 2, reps: int = 2,
               min_seconds: float = 2.0):
     """Config C3's eight axis reductions (sum / mean / max / argmax along axis -1 and

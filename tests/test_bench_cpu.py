@@ -112,3 +112,12 @@ def test_compact_maps_and_parity_bookkeeping():
     q = bench.Parity(False)
     q.run("a", bad)
     assert q.finish(bench._OneRank()) == {}
+
+
+def test_cpu_c1_sample_matches_the_oracle_and_times_a_step():
+    """The C1 CPU baseline checks its vectorised NumPy chain against the oracle's
+    formulas (it asserts bit equality before timing) and reports seconds per step."""
+    from oracle import threaded as T
+    gbs, secs, desc = T.c1_sample(1, reps=3, min_seconds=0.0)
+    assert gbs > 0 and 0 < secs < 1.0
+    assert "C1 whole" in desc and "1 thread" in desc
