@@ -615,9 +615,10 @@ class Suite:
         nbytes = 4 * (3 * M * N + 2 * N + 1) + 4 * (3 * M * N + N)
         # kernels per step: bias_relu and grad_accum one each; each column sum (bias_grad)
         # and the full sum two (partials, then their fold); relu_grad one eager, while
-        # the graph runs relu_grad + bias_grad as one fused pass (+ its fold)
+        # the graph runs bias_relu + bias_grad and relu_grad + bias_grad + grad_accum
+        # each as one pass (+ its fold), and the full sum as two
         self.measure("c1_dense_step_eager", nbytes, eager, 9, it=200)
-        self.measure("c1_dense_step_graph", nbytes, graph, 8, it=200)
+        self.measure("c1_dense_step_graph", nbytes, graph, 6, it=200)
         for k in ("c1_dense_step_eager", "c1_dense_step_graph"):
             if k in self.res:
                 self.res[k]["us_per_step"] = round(self.res[k]["ms"] * 1e3, 2)

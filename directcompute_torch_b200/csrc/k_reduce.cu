@@ -55,6 +55,9 @@ struct RedOut {
   int32_t* idx = nullptr;
   unsigned long long* packed = nullptr;
   int32_t idx_off = 0;
+  // sums only: also acc[k] = acc[k] + out[k] in float32 (nn_grad_accum.hlsl:5-8
+  // on the stored value, as a grad_accum dispatch after the reduction would)
+  float* acc = nullptr;
 };
 
 // Partial accumulator of one reduction lane.
@@ -151,6 +154,9 @@ struct Acc {
       o.packed[k] = t.pack();
     } else {
       store(o.out, o.idx, k, len);
+      if constexpr (!kArg && !kExt) {
+        if (o.acc) o.acc[k] = __fadd_rn(o.acc[k], o.out[k]);
+      }
     }
   }
   DCT_DEV void store(float* out, int32_t* out_idx, uint64_t k, uint64_t len) const {
@@ -317,27 +323,38 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
 // order.  (A fold by the last block of each tile, found with an atomic counter,
 // was measured slower: its fence and serial fold sit on the kernel's tail.)
 //
-// GATE fuses the backward of bias + ReLU (nn_engine.py:1091-1106) into the
-// column sum: the reduced value is relu_grad(x, y) = y > 0 ? x : 0
-// (nn_relu_grad.hlsl:6-9), stored to dx as it streams by, and the column sums
-// of it are bias_grad (nn_bias_grad.hlsl:8-29) -- one read of the gradient and
-// of the forward output instead of two passes.  y and dx share x's layout.  The
-// per-lane order of the adds is the ungated kernel's, so for the same plan the
-// sums are bit-identical to relu_grad followed by bias_grad.
-struct ColGate {
-  const float* y = nullptr;
-  float* dx = nullptr;
+// MODE fuses an elementwise pass over the reduced matrix into the column sum,
+// storing the transformed value to `out` (x's layout) as it streams by:
+//  * COL_RELU_GRAD, the backward of bias + ReLU (nn_engine.py:1091-1106):
+//    v = aux > 0 ? x : 0 with aux the forward output (relu_grad,
+//    nn_relu_grad.hlsl:6-9), out = dx; the column sums are bias_grad
+//    (nn_bias_grad.hlsl:8-29) of dx;
+//  * COL_BIAS_RELU, the forward: v = max(0, x + aux[c]) with aux the bias row
+//    (bias_relu, nn_bias_relu.hlsl:8-12), out = y; the column sums are
+//    bias_grad of y.
+// One read of the operands instead of two passes.  The per-lane order of the
+// adds is the plain kernel's, so for the same plan the sums are bit-identical
+// to the elementwise dispatch followed by bias_grad.
+enum ColMode : int { COL_PLAIN = 0, COL_RELU_GRAD = 1, COL_BIAS_RELU = 2 };
+struct ColXform {
+  const float* aux = nullptr;   // COL_RELU_GRAD: the forward output; COL_BIAS_RELU: the bias row
+  float* out = nullptr;         // the transformed matrix
 };
 
 DCT_DEV float relu_gate(float g, float y) { return y > 0.0f ? g : 0.0f; }
+DCT_DEV float bias_relu1(float x, float b) {
+  const float o = __fadd_rn(x, b);
+  return o > 0.0f ? o : 0.0f;                           // HLSL max(0, x): NaN -> 0
+}
 
-template <int OP, int VEC, bool GATE = false>
+template <int OP, int VEC, int MODE = COL_PLAIN>
 __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __restrict__ x, uint64_t outer, uint64_t len,
                                                              uint64_t inner, uint64_t so, uint64_t sl,
                                                              uint32_t chunks, uint64_t chunk_len, RedOut ro,
-                                                             unsigned long long* part, ColGate gate) {
+                                                             unsigned long long* part, ColXform xf) {
   pdl_entry();
   constexpr int W = 32 * VEC;
+  constexpr bool GATE = MODE == COL_RELU_GRAD, BIAS = MODE == COL_BIAS_RELU, XF = MODE != COL_PLAIN;
   __shared__ unsigned long long sh[kRedWarps][W];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t c0 = (uint64_t)blockIdx.x * W + (uint64_t)lane * VEC;
@@ -347,12 +364,14 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
   for (uint64_t o = blockIdx.y; o < outer; o += gridDim.y) {
     Acc<OP> acc[VEC];
     const float* base = x + o * so;
-    const float* ybase = GATE ? gate.y + o * so : nullptr;
-    float* dbase = GATE ? gate.dx + o * so : nullptr;
+    const float* ybase = GATE ? xf.aux + o * so : nullptr;
+    float* dbase = XF ? xf.out + o * so : nullptr;
     if (VEC == 4 && c0 + 3 < inner) {
       // 8 rows (8 x 512 B per warp) in flight per batch: the loop is bound by
-      // memory latency, not by the per-element work (4 rows of two operands gated)
-      constexpr int U = GATE ? 4 : 8;
+      // memory latency, not by the per-element work.  With a fused elementwise
+      // pass, which also stores (and gated, loads a second operand), 4 rows.
+      constexpr int U = XF ? 4 : 8;
+      const float4 bv = BIAS ? ld_keep4(xf.aux + c0) : make_float4(0.f, 0.f, 0.f, 0.f);
       const uint64_t first = l0 + warp;
       ColLane<OP> ln[4];
 #pragma unroll
@@ -367,11 +386,19 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 #pragma unroll
           for (int k = 0; k < U; ++k) yv[k] = ld_stream4(ybase + (l + k * kRedWarps) * sl + c0);
 #pragma unroll
-          for (int k = 0; k < U; ++k) {
+          for (int k = 0; k < U; ++k)
             v[k] = make_float4(relu_gate(v[k].x, yv[k].x), relu_gate(v[k].y, yv[k].y), relu_gate(v[k].z, yv[k].z),
                                relu_gate(v[k].w, yv[k].w));
-            st_stream4(dbase + (l + k * kRedWarps) * sl + c0, v[k]);
-          }
+        }
+        if constexpr (BIAS) {
+#pragma unroll
+          for (int k = 0; k < U; ++k)
+            v[k] = make_float4(bias_relu1(v[k].x, bv.x), bias_relu1(v[k].y, bv.y), bias_relu1(v[k].z, bv.z),
+                               bias_relu1(v[k].w, bv.w));
+        }
+        if constexpr (XF) {
+#pragma unroll
+          for (int k = 0; k < U; ++k) st_stream4(dbase + (l + k * kRedWarps) * sl + c0, v[k]);
         }
 #pragma unroll
         for (int k = 0; k < U; ++k) {
@@ -384,8 +411,10 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
         if constexpr (GATE) {
           const float4 yv = ld_stream4(ybase + l * sl + c0);
           v = make_float4(relu_gate(v.x, yv.x), relu_gate(v.y, yv.y), relu_gate(v.z, yv.z), relu_gate(v.w, yv.w));
-          st_stream4(dbase + l * sl + c0, v);
         }
+        if constexpr (BIAS)
+          v = make_float4(bias_relu1(v.x, bv.x), bias_relu1(v.y, bv.y), bias_relu1(v.z, bv.z), bias_relu1(v.w, bv.w));
+        if constexpr (XF) st_stream4(dbase + l * sl + c0, v);
         const int32_t li = (int32_t)l;
         ln[0].add(v.x, li); ln[1].add(v.y, li); ln[2].add(v.z, li); ln[3].add(v.w, li);
       }
@@ -396,12 +425,12 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_cols(const float* __rest
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
         if (c0 + j >= inner) break;
+        const float bj = BIAS ? ld_keep(xf.aux + c0 + j) : 0.0f;
         for (uint64_t l = l0 + warp; l < l1; l += kRedWarps) {
           float v = ld_stream(base + l * sl + c0 + j);
-          if constexpr (GATE) {
-            v = relu_gate(v, ld_stream(ybase + l * sl + c0 + j));
-            st_stream(dbase + l * sl + c0 + j, v);
-          }
+          if constexpr (GATE) v = relu_gate(v, ld_stream(ybase + l * sl + c0 + j));
+          if constexpr (BIAS) v = bias_relu1(v, bj);
+          if constexpr (XF) st_stream(dbase + l * sl + c0 + j, v);
           acc[j].add(v, (int64_t)l);
         }
       }
@@ -632,8 +661,8 @@ int cols_occupancy(bool vec) {
   if (cols_occ[vi] == 0) {
     int b = 0;
     const cudaError_t e =
-        vi ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 4, false>, kRedThreads, 0)
-           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 1, false>, kRedThreads, 0);
+        vi ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 4, COL_PLAIN>, kRedThreads, 0)
+           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_reduce_cols<OP, 1, COL_PLAIN>, kRedThreads, 0);
     cols_occ[vi] = (e == cudaSuccess && b > 0) ? b : -1;
     cudaGetLastError();
   }
@@ -685,8 +714,8 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
     if (p.vec) launch_pdl(k_reduce_rows<OP, true>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
     else launch_pdl(k_reduce_rows<OP, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
   } else if (p.kind == 1) {
-    if (p.vec) launch_pdl(k_reduce_cols<OP, 4, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColGate{});
-    else launch_pdl(k_reduce_cols<OP, 1, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColGate{});
+    if (p.vec) launch_pdl(k_reduce_cols<OP, 4, COL_PLAIN>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColXform{});
+    else launch_pdl(k_reduce_cols<OP, 1, COL_PLAIN>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColXform{});
   } else {
     launch_pdl(k_reduce_generic<OP>, dim3(p.grid), dim3(256), 0, st, x, outer, len, inner, so, sl, si, ro);
   }
@@ -769,16 +798,21 @@ size_t relu_grad_colsum_ws_bytes(uint64_t rows, uint64_t cols) {
   return reduce_strided_ws_bytes(1, rows, cols, 0, cols, 1);
 }
 
-cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, float* db, uint64_t rows,
-                                    uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st) {
+namespace {
+// A column sum fused with the elementwise pass that produces its input (see
+// ColMode): bias_grad's column plan over the transformed [rows, cols] matrix,
+// made for the pointer bias_grad would read (`out`), so the same chunks and the
+// same sums as the two dispatches.  acc (optional): acc += the sums (grad_accum).
+template <int MODE>
+cudaError_t launch_xform_colsum(const float* x, const float* aux, float* out, float* db, float* acc, uint64_t rows,
+                                uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (cols == 0) return cudaSuccess;
-  if (rows == 0) return cudaMemsetAsync(db, 0, cols * sizeof(float), st);
-  // bias_grad's column plan over [rows, cols]: the same chunks, so the same sums
-  Plan p = make_plan(1, rows, cols, 0, cols, 1, g);
+  if (rows == 0) return cudaMemsetAsync(db, 0, cols * sizeof(float), st);   // acc + 0 = acc
+  Plan p = make_plan(1, rows, cols, 0, cols, 1, out);
   const int occ = cols_occupancy<RED_SUM>(p.vec);
-  if (occ > 0) p = make_plan(1, rows, cols, 0, cols, 1, g, occ);
-  // 128-bit loads need all three operands aligned; the chunking stays the plan's
-  const bool vec = p.vec && aligned16_h(y) && aligned16_h(dx);
+  if (occ > 0) p = make_plan(1, rows, cols, 0, cols, 1, out, occ);
+  // 128-bit accesses need every operand aligned; the chunking stays the plan's
+  const bool vec = p.vec && aligned16_h(x) && aligned16_h(aux);
   unsigned long long* part = (unsigned long long*)ws;
   if (p.chunks > 1) {
     const size_t need = (size_t)cols * p.chunks * sizeof(unsigned long long);
@@ -786,21 +820,33 @@ cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, f
   }
   RedOut ro;
   ro.out = db;
-  ColGate gate;
-  gate.y = y;
-  gate.dx = dx;
+  ro.acc = acc;
+  ColXform xf;
+  xf.aux = aux;
+  xf.out = out;
   if (vec) {
-    launch_pdl(k_reduce_cols<RED_SUM, 4, true>, dim3(p.grid), dim3(kRedThreads), 0, st, g, (uint64_t)1, rows, cols,
-               (uint64_t)0, cols, p.chunks, p.chunk_len, ro, part, gate);
+    launch_pdl(k_reduce_cols<RED_SUM, 4, MODE>, dim3(p.grid), dim3(kRedThreads), 0, st, x, (uint64_t)1, rows, cols,
+               (uint64_t)0, cols, p.chunks, p.chunk_len, ro, part, xf);
   } else {
     const dim3 grid((unsigned)((cols + 31) / 32), 1, p.grid.z);       // scalar tiles are 32 columns wide
-    launch_pdl(k_reduce_cols<RED_SUM, 1, true>, grid, dim3(kRedThreads), 0, st, g, (uint64_t)1, rows, cols,
-               (uint64_t)0, cols, p.chunks, p.chunk_len, ro, part, gate);
+    launch_pdl(k_reduce_cols<RED_SUM, 1, MODE>, grid, dim3(kRedThreads), 0, st, x, (uint64_t)1, rows, cols,
+               (uint64_t)0, cols, p.chunks, p.chunk_len, ro, part, xf);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.chunks == 1) return e;
   return launch_pdl(k_fold_chunks<RED_SUM>, dim3(grid_for(cols, 32)), dim3(256), 0, st,
                     (const unsigned long long*)part, cols, p.chunks, cols, rows, ro);
+}
+}  // namespace
+
+cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, float* db, uint64_t rows,
+                                    uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st, float* acc) {
+  return launch_xform_colsum<COL_RELU_GRAD>(g, y, dx, db, acc, rows, cols, ws, ws_bytes, st);
+}
+
+cudaError_t launch_bias_relu_colsum(const float* x, const float* b, float* y, float* col, uint64_t rows,
+                                    uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st) {
+  return launch_xform_colsum<COL_BIAS_RELU>(x, b, y, col, nullptr, rows, cols, ws, ws_bytes, st);
 }
 
 size_t reduce3d_ws_bytes(int op, uint64_t outer, uint64_t len, uint64_t inner) {

@@ -90,8 +90,16 @@ cudaError_t launch_sum_to_shape(const float* g, int ndim, const int64_t* gshape,
 // Backward of bias + ReLU over [rows, cols] in one pass: dx = y > 0 ? g : 0 and
 // db[c] = sum_r dx[r, c] (float64, rounded once), bit-identical to relu_grad
 // followed by bias_grad.  dx may alias g.  `ws` holds relu_grad_colsum_ws_bytes.
+// acc (optional): acc[c] = acc[c] + db[c] in float32, as a grad_accum after it.
 size_t relu_grad_colsum_ws_bytes(uint64_t rows, uint64_t cols);
 cudaError_t launch_relu_grad_colsum(const float* g, const float* y, float* dx, float* db, uint64_t rows,
+                                    uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st,
+                                    float* acc = nullptr);
+// Forward of bias + ReLU over [rows, cols] with its column sums in one pass:
+// y = max(0, x + b[c]) and col[c] = sum_r y[r, c], bit-identical to bias_relu
+// followed by bias_grad over y.  y may alias x.  `ws` holds
+// relu_grad_colsum_ws_bytes (the same plan).
+cudaError_t launch_bias_relu_colsum(const float* x, const float* b, float* y, float* col, uint64_t rows,
                                     uint64_t cols, void* ws, size_t ws_bytes, cudaStream_t st);
 // General strided form: out[o*inner + i] = reduce_l x[o*so + l*sl + i*si].
 size_t reduce_strided_ws_bytes(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64_t sl,

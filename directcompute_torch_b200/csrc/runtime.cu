@@ -1004,26 +1004,70 @@ static bool dispatch(Shader* s, void** srvs, uint32_t nsrv, void** uavs, uint32_
   return s->fn(d);
 }
 
-// relu_grad (grad, y -> dx) directly followed by bias_grad over that dx with
-// row strides (the backward of bias + ReLU, nn_engine.py:1091-1106): one pass
-// over grad and y writes dx and the column sums (launch_relu_grad_colsum),
-// with the same results as the two dispatches.  Returns false, launching
-// nothing, when the pair does not have that form.
-static bool try_fused_relu_bias_grad(const Disp& a, const Disp& b, bool& ok) {
-  if (strcmp(a.name, "relu_grad") != 0 || strcmp(b.name, "bias_grad") != 0) return false;
-  if (a.nsrv < 2 || a.nuav < 1 || b.nsrv < 1 || b.nuav < 1) return false;
-  if (!a.srv[0] || !a.srv[1] || !a.uav[0] || !b.srv[0] || !b.uav[0]) return false;
-  if (b.srv[0] != a.uav[0]) return false;                         // bias_grad reads the dx just written
+// Peepholes of RunSequence: an elementwise dispatch over a [B, K] row-major
+// matrix directly followed by bias_grad over its output (column sums, row
+// stride K) runs as one pass that writes the matrix and its column sums, with
+// the same results as the dispatches (the column kernel keeps bias_grad's
+// plan).  Each returns false, launching nothing, when the commands do not have
+// that form.
+
+// bias_grad (b) over the whole [B, K] matrix a just wrote to a.uav[0] (n floats).
+static bool colsum_of(const Disp& a, const Disp& b, uint64_t n, uint64_t& B, uint64_t& K) {
+  if (strcmp(b.name, "bias_grad") != 0 || b.nsrv < 1 || b.nuav < 1 || !b.srv[0] || !b.uav[0]) return false;
+  if (!a.uav[0] || b.srv[0] != a.uav[0]) return false;             // bias_grad reads what a just wrote
+  B = b.u[0];
+  K = std::min<uint64_t>(b.u[1], b.gx);
+  return K > 0 && B > 0 && b.u[3] == 1 && b.u[2] == K && B * K == n && b.uav[0]->count >= K;
+}
+
+// grad_accum (c) adding exactly the K column sums in db to its accumulator.
+static Buffer* accum_of(const Disp* c, const Buffer* db, uint64_t K) {
+  if (!c || strcmp(c->name, "grad_accum") != 0 || c->nsrv < 1 || c->nuav < 1) return nullptr;
+  if (c->srv[0] != db || !c->uav[0] || c->uav[0] == db) return nullptr;
+  if (lim(c->u[0], c->gx) != K || c->uav[0]->count < K) return nullptr;
+  return c->uav[0];
+}
+
+// relu_grad (grad, y -> dx), then bias_grad over dx (the backward of bias +
+// ReLU, nn_engine.py:1091-1106), and when c is grad_accum over those column
+// sums, that too (*used = 3).
+static bool try_fused_relu_bias_grad(const Disp& a, const Disp& b, const Disp* c, bool& ok, int* used) {
+  if (strcmp(a.name, "relu_grad") != 0 || a.nsrv < 2 || a.nuav < 1) return false;
+  if (!a.srv[0] || !a.srv[1] || !a.uav[0]) return false;
   const uint64_t n = lim(a.u[0], a.gx);
-  const uint64_t B = b.u[0], K = std::min<uint64_t>(b.u[1], b.gx);
-  if (K == 0 || B == 0 || b.u[3] != 1 || b.u[2] != K || B * K != n) return false;
+  uint64_t B, K;
+  if (!colsum_of(a, b, n, B, K)) return false;
   Buffer *bg = a.srv[0], *by = a.srv[1], *bdx = a.uav[0], *bdb = b.uav[0];
   if (bdb == bg || bdb == by || bdb == bdx) return false;
-  if (bg->count < n || by->count < n || bdx->count < n || bdb->count < K) return false;
+  if (bg->count < n || by->count < n || bdx->count < n) return false;
+  Buffer* acc = accum_of(c, bdb, K);
+  if (acc && (acc == bg || acc == by || acc == bdx)) acc = nullptr;
   const size_t ws = relu_grad_colsum_ws_bytes(B, K);
+  *used = acc ? 3 : 2;
   if (ws && !ensure_ws(ws)) { ok = false; return true; }
-  ok = cuda_ok(launch_relu_grad_colsum(bg->d, by->d, bdx->d, bdb->d, B, K, g.ws, g.ws_bytes, g.stream),
+  ok = cuda_ok(launch_relu_grad_colsum(bg->d, by->d, bdx->d, bdb->d, B, K, g.ws, g.ws_bytes, g.stream,
+                                       acc ? acc->d : nullptr),
                "relu_grad + bias_grad");
+  return true;
+}
+
+// bias_relu (x, b -> y) over whole rows, then bias_grad over y (column sums of
+// the layer's output, the C1 forward).
+static bool try_fused_bias_relu_colsum(const Disp& a, const Disp& b, bool& ok, int* used) {
+  if (strcmp(a.name, "bias_relu") != 0 || a.nsrv < 2 || a.nuav < 1) return false;
+  if (!a.srv[0] || !a.srv[1] || !a.uav[0]) return false;
+  const uint64_t M = a.u[0], N = a.u[1];
+  const uint64_t n = lim(M * N, a.gx);
+  uint64_t B, K;
+  if (N == 0 || n != M * N || !colsum_of(a, b, n, B, K) || B != M || K != N) return false;
+  Buffer *bx = a.srv[0], *bb = a.srv[1], *by = a.uav[0], *bc = b.uav[0];
+  if (bc == bx || bc == bb || bc == by || by == bb) return false;
+  if (bx->count < n || by->count < n || bb->count < N) return false;
+  const size_t ws = relu_grad_colsum_ws_bytes(B, K);
+  *used = 2;
+  if (ws && !ensure_ws(ws)) { ok = false; return true; }
+  ok = cuda_ok(launch_bias_relu_colsum(bx->d, bb->d, by->d, bc->d, B, K, g.ws, g.ws_bytes, g.stream),
+               "bias_relu + bias_grad");
   return true;
 }
 
@@ -1466,6 +1510,11 @@ static bool seq_key(const DctSeqCmd* cmds, uint32_t count, std::vector<uint8_t>&
 
 static bool seq_run(DctSeqCmd* cmds, uint32_t count) {
   bool ok = true;
+  auto disp_of = [](Disp& d, DctSeqCmd& c) {
+    return make_disp(d, static_cast<Shader*>(c.shader), c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs,
+                     std::min<uint32_t>(c.uavCount, 4), c.threads, c.cbSize ? c.cbData : nullptr,
+                     std::min<uint32_t>(c.cbSize, 64));
+  };
   for (uint32_t i = 0; i < count; ++i) {
     DctSeqCmd& c = cmds[i];
     if (!c.shader) continue;
@@ -1476,20 +1525,23 @@ static bool seq_run(DctSeqCmd* cmds, uint32_t count) {
     }
     Shader* s = static_cast<Shader*>(c.shader);
     if (i + 1 < count && cmds[i + 1].shader && is_shader_ptr(cmds[i + 1].shader) && ensure_init()) {
-      DctSeqCmd& c2 = cmds[i + 1];
-      Disp a, b;
+      Disp a, b, cc;
       bool fused_ok = true;
-      const int code0 = g.err_code;                  // a pair that does not fuse leaves no error behind
+      int used = 0;
+      const int code0 = g.err_code;                  // commands that do not fuse leave no error behind
       const std::string msg0 = g.err;
-      if (make_disp(a, s, c.srvs, std::min<uint32_t>(c.srvCount, 8), c.uavs, std::min<uint32_t>(c.uavCount, 4),
-                    c.threads, c.cbSize ? c.cbData : nullptr, std::min<uint32_t>(c.cbSize, 64)) &&
-          make_disp(b, static_cast<Shader*>(c2.shader), c2.srvs, std::min<uint32_t>(c2.srvCount, 8), c2.uavs,
-                    std::min<uint32_t>(c2.uavCount, 4), c2.threads, c2.cbSize ? c2.cbData : nullptr,
-                    std::min<uint32_t>(c2.cbSize, 64)) &&
-          try_fused_relu_bias_grad(a, b, fused_ok)) {
-        ok &= fused_ok;
-        ++i;
-        continue;
+      const bool have_c = i + 2 < count && cmds[i + 2].shader && is_shader_ptr(cmds[i + 2].shader);
+      if (disp_of(a, c) && disp_of(b, cmds[i + 1])) {
+        const Disp* pc = nullptr;
+        if (have_c) {
+          if (disp_of(cc, cmds[i + 2])) pc = &cc;
+          else { g.err_code = code0; g.err = msg0; }   // that command reports its own error when it runs
+        }
+        if (try_fused_relu_bias_grad(a, b, pc, fused_ok, &used) || try_fused_bias_relu_colsum(a, b, fused_ok, &used)) {
+          ok &= fused_ok;
+          i += used - 1;
+          continue;
+        }
       }
       g.err_code = code0;
       g.err = msg0;

@@ -107,3 +107,66 @@ def test_run_sequence_fuses_the_pair(dev, shape):
         lib.ClearBuffer(hdx)
         lib.ClearBuffer(hdb)
     dev.free(hg, hy, hdx, hdb, udx, udb)
+
+
+def _bias_inputs(M, N, seed):
+    r = np.random.default_rng(seed)
+    x = r.standard_normal((M, N)).astype(np.float32)
+    b = r.uniform(-0.1, 0.1, N).astype(np.float32)
+    if x.size > 8:
+        x.ravel()[:3] = [np.nan, -b[1], -0.0]                # NaN -> 0, an exact zero sum, -0 + b
+    return x, b
+
+
+@pytest.mark.parametrize("shape", [(256, 784), (64, 10), (300, 4099), (1, 5), (4097, 12)])
+def test_run_sequence_fuses_bias_relu_with_its_column_sums(dev, shape):
+    """bias_relu then bias_grad over its output (the C1 forward) runs as one pass
+    inside RunSequence: y and the column sums bit-identical to the two dispatches,
+    y bit-exact against the oracle, eager and as a graph."""
+    M, N = shape
+    x, b = _bias_inputs(M, N, 21)
+    hx, hb, hy, hc = dev.buf(x), dev.buf(b), dev.empty(M * N), dev.empty(N)
+    lib = dev.lib
+    g = ((M * N + 255) // 256, 1, 1)
+    arr = (SeqCmd * 2)(_cmd(lib, "bias_relu", [hx, hb], [hy], g, [M, N]),
+                       _cmd(lib, "bias_grad", [hy], [hc], (N, 1, 1), [M, N, N, 1]))
+    uy, uc = dev.empty(M * N), dev.empty(N)
+    dev.run("bias_relu", [hx, hb], [uy], g, [M, N])
+    dev.run("bias_grad", [uy], [uc], (N, 1, 1), [M, N, N, 1])
+    want_y, want_c = dev.read(uy), dev.read(uc)
+    assert np.array_equal(want_y.view(np.uint32), S.bias_relu(x.ravel(), b, M, N).view(np.uint32))
+    for _ in range(4):                                  # eager, capture, then graph launches
+        lib.RunSequence(ctypes.cast(arr, ctypes.c_void_p), 2)
+        dev.sync()
+        assert dev.error()[0] == 0, dev.error()
+        assert np.array_equal(dev.read(hy).view(np.uint32), want_y.view(np.uint32))
+        assert np.array_equal(dev.read(hc).view(np.uint32), want_c.view(np.uint32))
+        lib.ClearBuffer(hy)
+        lib.ClearBuffer(hc)
+    dev.free(hx, hb, hy, hc, uy, uc)
+
+
+@pytest.mark.parametrize("shape", [(256, 784), (300, 4099)])
+def test_run_sequence_fuses_the_backward_with_grad_accum(dev, shape):
+    """relu_grad, bias_grad and grad_accum over those column sums (the C1 backward)
+    run as one pass plus its fold: dx, db and the accumulator bit-identical to the
+    three dispatches after every replay."""
+    M, N = shape
+    g, y = _inputs(M, N, 31)
+    hg, hy, hdx, hdb, hacc = dev.buf(g), dev.buf(y), dev.empty(M * N), dev.empty(N), dev.empty(N)
+    lib = dev.lib
+    gr = ((M * N + 255) // 256, 1, 1)
+    arr = (SeqCmd * 3)(_cmd(lib, "relu_grad", [hg, hy], [hdx], gr, [M * N]),
+                       _cmd(lib, "bias_grad", [hdx], [hdb], (N, 1, 1), [M, N, N, 1]),
+                       _cmd(lib, "grad_accum", [hdb], [hacc], ((N + 255) // 256, 1, 1), [N]))
+    udx, udb, uacc = dev.empty(M * N), dev.empty(N), dev.empty(N)
+    for rep in range(4):                                # eager, capture, then graph launches
+        dev.run("relu_grad", [hg, hy], [udx], gr, [M * N])
+        dev.run("bias_grad", [udx], [udb], (N, 1, 1), [M, N, N, 1])
+        dev.run("grad_accum", [udb], [uacc], ((N + 255) // 256, 1, 1), [N])
+        lib.RunSequence(ctypes.cast(arr, ctypes.c_void_p), 3)
+        dev.sync()
+        assert dev.error()[0] == 0, dev.error()
+        for h, u in ((hdx, udx), (hdb, udb), (hacc, uacc)):
+            assert np.array_equal(dev.read(h).view(np.uint32), dev.read(u).view(np.uint32)), rep
+    dev.free(hg, hy, hdx, hdb, hacc, udx, udb, uacc)
