@@ -502,7 +502,8 @@ PER_OP_SECTIONS = {"c1": ("c1_dense_step_eager", "c1_dense_step_graph"),
                    "c5a": ("c5a_adam_1.5e9", "c5a_adam_1.5e8_small"),
                    "c5b": ("c5b_batchnorm_fwd", "c5b_batchnorm_bwd"),
                    "layout": ("f3_upsample2x_fwd", "f3_upsample2x_bwd", "f3_concat", "f3_slice", "f3_maxpool2x2_fwd",
-                              "f3_maxpool2x2_fused_fwd_bwd", "f4_conv_reshape_relu", "f4_conv_grad_reshape_relu")}
+                              "f3_maxpool2x2_fused_fwd_bwd", "f4_conv_reshape_relu", "f4_conv_grad_reshape_relu"),
+                   "dice": ("f1_dice_sums", "f1_dice_loss", "f1_dice_grad")}
 #: the configs whose global size BASELINE fixes, timed split N ways at N > 1
 STRONG_SECTIONS = ("c3", "c3f", "c4", "c5a", "c5b")
 
@@ -553,7 +554,8 @@ class Suite:
     def run(self, sections=None):
         sections = sections or tuple(PER_OP_SECTIONS)
         for key, fn in (("c1", self._c1), ("c3", self._c3), ("c3f", self._c3f), ("c4", self._c4),
-                        ("c5a", self._c5a), ("c5b", self._c5b), ("layout", self._layout)):
+                        ("c5a", self._c5a), ("c5b", self._c5b), ("layout", self._layout),
+                        ("dice", self._dice)):
             if key in sections and self.want(key):
                 fn()
         self.lib.DrainPool()
@@ -905,6 +907,50 @@ class Suite:
             lib.ReleaseBuffer(h)
 
     # -- layout ops ---------------------------------------------------------------------
+    def _dice(self):
+        """Dice loss beside the path (nn_dice_loss_sums.hlsl:19-55, nn_dice_loss.hlsl:19-53,
+        nn_dice_loss_grad.hlsl:17-34; nn_engine.py:1290-1317), dispatched by reference
+        shader name with the reference's cbuffer words, on a segmentation batch
+        pred / target [64, 1, 512, 512] ~ U(0, 1): 67 MB each, the pair larger than L2.
+        No reference config sizes it; the shape is synthetic.  Checks cover the first
+        and last sample."""
+        L, lib = self.L, self.lib
+        for name in ("dice_loss_sums", "dice_loss", "dice_loss_grad"):
+            lib.CompileShader(name.encode(), "")
+        B, S_ = 64, 512 * 512
+        n = B * S_
+        seed = 6 + 1000 * self.rank
+        p, t, sums, loss, dx = L.new(n), L.new(n), L.new(3 * B), L.new(B), L.new(n)
+        L.fill(p, seed, 30, 0, 0.0, 1.0)
+        L.fill(t, seed, 31, 0, 0.0, 1.0)
+        ends = (0, B - 1)
+        g1 = (B, 1, 1)
+        if self.measure("f1_dice_sums", 4 * (2 * n + 3 * B), lambda: L.run("dice_loss_sums", [p, t], [sums], g1, [B, S_]), 2):
+            def chk_sums():
+                got = L.read(sums, 0, 3 * B).reshape(B, 3)
+                for b in ends:
+                    want = _oracle_shaders().dice_sums(L.read(p, b * S_, S_), L.read(t, b * S_, S_), 1, S_)[0]
+                    _assert_rel(got[b], want, 1e-5, f"dice sums sample {b}")
+            self.check("f1_dice_sums", chk_sums)
+        if self.measure("f1_dice_loss", 4 * (2 * n + B), lambda: L.run("dice_loss", [p, t], [loss], g1, [B, S_]), 2):
+            def chk_loss():
+                got = L.read(loss, 0, B)
+                for b in ends:
+                    want = _oracle_shaders().dice_loss(L.read(p, b * S_, S_), L.read(t, b * S_, S_), 1, S_)
+                    _assert_rel(got[b:b + 1], want, 1e-5, f"dice loss sample {b}")
+            self.check("f1_dice_loss", chk_loss)
+        if self.measure("f1_dice_grad", 4 * (2 * n + 3 * B),
+                        lambda: L.run("dice_loss_grad", [p, t, sums], [dx], ((n + 255) // 256, 1, 1), [B, S_]), 1):
+            def chk_grad():
+                sm = L.read(sums, 0, 3 * B)
+                for b in ends:
+                    want = _oracle_shaders().dice_loss_grad(L.read(p, b * S_, S_), L.read(t, b * S_, S_),
+                                                            sm[3 * b:3 * b + 3], 1, S_, divisor=B)
+                    _assert_bits(L.read(dx, b * S_, S_), want, f"dice grad sample {b}")
+            self.check("f1_dice_grad", chk_grad)
+        for h in (p, t, sums, loss, dx):
+            lib.ReleaseBuffer(h)
+
     def _layout(self):
         """The layout ops beside the path at UNet-like sizes (every tensor larger than
         L2 or close to it), dispatched by reference shader name with the reference's
@@ -1097,7 +1143,8 @@ _SHORT = {"c1_dense_step_eager": "c1.eager", "c1_dense_step_graph": "c1.graph", 
           "c5b_batchnorm_bwd": "c5b.b", "f3_upsample2x_fwd": "f3.up", "f3_upsample2x_bwd": "f3.upb",
           "f3_concat": "f3.cat", "f3_slice": "f3.slice", "f3_maxpool2x2_fwd": "f3.pool",
           "f3_maxpool2x2_fused_fwd_bwd": "f3.poolfb", "f4_conv_reshape_relu": "f4.conv",
-          "f4_conv_grad_reshape_relu": "f4.convg"}
+          "f4_conv_grad_reshape_relu": "f4.convg", "f1_dice_sums": "f1.sums", "f1_dice_loss": "f1.loss",
+          "f1_dice_grad": "f1.grad"}
 
 
 def short(name: str) -> str:

@@ -640,27 +640,69 @@ cudaError_t launch_accumulate_scalar(const float* src, float* dst, cudaStream_t 
   return cudaGetLastError();
 }
 
-__global__ void __launch_bounds__(256) k_dice_grad(const float* pred, const float* target, const float* sums,
-                                                   float* dx, uint32_t batch, uint32_t size, uint64_t n) {
+// nn_dice_loss_grad.hlsl:17-34: dx[i] = -2 * (t[i] * denom - inter) / (denom * denom) / batch
+// with (inter, sum p, sum t) of sample b = i / size and denom = sum p + sum t + 1e-6
+// (the reference's gradient reads the target and the sums, not the prediction).
+DCT_DEV float dice_grad1(float t, float inter, float denom, float fb) {
+  const float num = __fmul_rn(-2.0f, __fsub_rn(__fmul_rn(t, denom), inter));
+  return __fdiv_rn(__fdiv_rn(num, __fmul_rn(denom, denom)), fb);
+}
+
+DCT_DEV void dice_sample(const float* sums, uint64_t b, float& inter, float& denom) {
+  inter = __ldg(sums + b * 3 + 0);
+  denom = __fadd_rn(__fadd_rn(__ldg(sums + b * 3 + 1), __ldg(sums + b * 3 + 2)), 1e-6f);
+}
+
+// scalar form: any size, any alignment
+__global__ void __launch_bounds__(256) k_dice_grad(const float* target, const float* sums, float* dx, uint32_t batch,
+                                                   uint32_t size, uint64_t n) {
   pdl_entry();
   const float fb = (float)batch;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const uint64_t b = i / size;
-    const float inter = sums[b * 3 + 0];
-    const float denom = __fadd_rn(__fadd_rn(sums[b * 3 + 1], sums[b * 3 + 2]), 1e-6f);
-    const float t = target[i];
-    const float num = __fmul_rn(-2.0f, __fsub_rn(__fmul_rn(t, denom), inter));
-    dx[i] = __fdiv_rn(__fdiv_rn(num, __fmul_rn(denom, denom)), fb);
+    float inter, denom;
+    dice_sample(sums, i / size, inter, denom);
+    dx[i] = dice_grad1(target[i], inter, denom, fb);
   }
-  (void)pred;
+}
+
+// the chunked float4 schedule (see the streaming kernels above) when size and n
+// are multiples of 4 (a vector never straddles two samples) and the float4
+// count fits 32 bits: the sample of float4 i is i / (size / 4), a fast division
+__global__ void __launch_bounds__(256) k_dice_grad_chunk(const float* target, const float* sums, float* dx,
+                                                         uint32_t batch, uint64_t n4, FastDiv per_sample4) {
+  pdl_entry();
+  const float fb = (float)batch;
+  const uint64_t base = (uint64_t)blockIdx.x * kChunk4 + threadIdx.x;
+  float4 v[kChunkU];
+#pragma unroll
+  for (int k = 0; k < kChunkU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) v[k] = ld_stream4(target + 4 * i);
+  }
+#pragma unroll
+  for (int k = 0; k < kChunkU; ++k) {
+    const uint64_t i = base + 256ull * k;
+    if (i < n4) {
+      float inter, denom;
+      dice_sample(sums, per_sample4.div((uint32_t)i), inter, denom);
+      st_stream4(dx + 4 * i, make_float4(dice_grad1(v[k].x, inter, denom, fb), dice_grad1(v[k].y, inter, denom, fb),
+                                         dice_grad1(v[k].z, inter, denom, fb), dice_grad1(v[k].w, inter, denom, fb)));
+    }
+  }
 }
 
 cudaError_t launch_dice_grad(const float* pred, const float* target, const float* sums, float* dx,
                              uint32_t batch, uint32_t size, uint64_t n, cudaStream_t st) {
+  (void)pred;
   if (n == 0) return cudaSuccess;
   if (size == 0 || batch == 0) return cudaErrorInvalidValue;
-  launch_pdl(k_dice_grad, dim3(grid_for(n, 256)), dim3(256), 0, st, pred, target, sums, dx, batch, size, n);
+  const uint64_t n4 = n >> 2;
+  if (size % 4 == 0 && n % 4 == 0 && n4 <= 0xffffffffull && aligned16_h(target) && aligned16_h(dx))
+    launch_pdl(k_dice_grad_chunk, dim3(std::max(1u, chunk_blocks(n4))), dim3(256), 0, st, target, sums, dx, batch,
+               n4, FastDiv(size / 4));
+  else
+    launch_pdl(k_dice_grad, dim3(grid_for(n, 256)), dim3(256), 0, st, target, sums, dx, batch, size, n);
   return cudaGetLastError();
 }
 

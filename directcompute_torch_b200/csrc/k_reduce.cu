@@ -1382,38 +1382,146 @@ cudaError_t launch_grad_norm_final(const float* partials, uint64_t n, float max_
 }
 
 // ---------------------------------------------------------------------------
-// dice sums: one block per sample
+// dice sums (nn_dice_loss_sums.hlsl:19-55, nn_dice_loss.hlsl:19-53): per
+// sample (sum p*t, sum p, sum t) in float64.  Block (b, c) streams chunk c of
+// sample b -- float4 loads when the samples are 16-byte aligned -- and leaves
+// three float64 partials; one warp per sample folds them in chunk order
+// (lane-strided, then a fixed shuffle tree), so the sums are the same on every
+// run.  A sample of one chunk is written by its block directly.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) k_dice_sums(const float* __restrict__ pred, const float* __restrict__ target,
-                                                   uint32_t size, float* out, int mode) {
+namespace {
+constexpr int kDiceThreads = 256;
+
+struct DicePlan {
+  uint32_t chunks = 1, chunk_len = 0;
+};
+
+// chunks per sample: about two waves of blocks over the batch, >= 4096
+// elements a chunk, chunk starts on a float4 boundary
+DicePlan dice_plan(uint32_t batch, uint32_t size) {
+  DicePlan p;
+  const DevInfo& d = dev_info();
+  const uint64_t want = (uint64_t)d.sm_count * (d.max_threads_per_sm / kDiceThreads) * 2;
+  uint64_t chunks = batch ? (want + batch - 1) / batch : 1;
+  const uint64_t max_chunks = ((uint64_t)size + 4095) / 4096;
+  if (chunks > max_chunks) chunks = max_chunks;
+  if (chunks < 1) chunks = 1;
+  uint64_t cl = ((uint64_t)size + chunks - 1) / chunks;
+  cl = (cl + 3) & ~3ull;
+  if (cl == 0) cl = 4;
+  p.chunks = (uint32_t)(size ? ((uint64_t)size + cl - 1) / cl : 1);
+  p.chunk_len = (uint32_t)cl;
+  return p;
+}
+
+DCT_DEV void dice_emit(double si, double sp, double st, float* out, uint64_t b, int mode) {
+  if (mode == 0) {
+    out[b * 3 + 0] = (float)si;
+    out[b * 3 + 1] = (float)sp;
+    out[b * 3 + 2] = (float)st;
+  } else {
+    out[b] = (float)(1.0 - 2.0 * si / (sp + st + (double)1e-6f));
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(kDiceThreads) k_dice_partials(const float* __restrict__ pred,
+                                                                const float* __restrict__ target, uint32_t size,
+                                                                uint32_t chunks, uint32_t chunk_len, double* part,
+                                                                float* out, int mode) {
   pdl_entry();
   __shared__ double sh[32];
-  const uint64_t base = (uint64_t)blockIdx.x * size;
-  double si = 0.0, sp = 0.0, stt = 0.0;
-  for (uint32_t i = threadIdx.x; i < size; i += blockDim.x) {
-    const double p = (double)pred[base + i], t = (double)target[base + i];
-    si += p * t; sp += p; stt += t;
+  const uint64_t b = blockIdx.x / chunks;
+  const uint32_t c = blockIdx.x - (uint32_t)b * chunks;
+  const uint64_t base = b * size;
+  const uint32_t l0 = c * chunk_len, l1 = min(size, l0 + chunk_len);
+  double si = 0.0, sp = 0.0, st = 0.0;
+  if (VEC) {                                    // size, chunk_len and the bases are float4 multiples
+    // 4 float4 pairs in flight per thread, loads first, then the adds in index order
+    constexpr int U = 4;
+    uint32_t i = l0 + 4 * threadIdx.x;
+    for (; i + 4 * kDiceThreads * (U - 1) < l1; i += 4 * kDiceThreads * U) {
+      float4 p[U], t[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        p[k] = ld_stream4(pred + base + i + 4 * kDiceThreads * k);
+        t[k] = ld_stream4(target + base + i + 4 * kDiceThreads * k);
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        si += (double)p[k].x * (double)t[k].x; sp += (double)p[k].x; st += (double)t[k].x;
+        si += (double)p[k].y * (double)t[k].y; sp += (double)p[k].y; st += (double)t[k].y;
+        si += (double)p[k].z * (double)t[k].z; sp += (double)p[k].z; st += (double)t[k].z;
+        si += (double)p[k].w * (double)t[k].w; sp += (double)p[k].w; st += (double)t[k].w;
+      }
+    }
+    for (; i < l1; i += 4 * kDiceThreads) {
+      const float4 p = ld_stream4(pred + base + i), t = ld_stream4(target + base + i);
+      si += (double)p.x * (double)t.x; sp += (double)p.x; st += (double)t.x;
+      si += (double)p.y * (double)t.y; sp += (double)p.y; st += (double)t.y;
+      si += (double)p.z * (double)t.z; sp += (double)p.z; st += (double)t.z;
+      si += (double)p.w * (double)t.w; sp += (double)p.w; st += (double)t.w;
+    }
+  } else {
+    for (uint32_t i = l0 + threadIdx.x; i < l1; i += kDiceThreads) {
+      const double p = (double)ld_stream(pred + base + i), t = (double)ld_stream(target + base + i);
+      si += p * t; sp += p; st += t;
+    }
   }
   si = block_sum(si, sh);
   __syncthreads();
   sp = block_sum(sp, sh);
   __syncthreads();
-  stt = block_sum(stt, sh);
+  st = block_sum(st, sh);
   if (threadIdx.x == 0) {
-    if (mode == 0) {
-      out[blockIdx.x * 3 + 0] = (float)si;
-      out[blockIdx.x * 3 + 1] = (float)sp;
-      out[blockIdx.x * 3 + 2] = (float)stt;
+    if (chunks == 1) {
+      dice_emit(si, sp, st, out, b, mode);
     } else {
-      out[blockIdx.x] = (float)(1.0 - 2.0 * si / (sp + stt + (double)1e-6f));
+      double* q = part + ((uint64_t)b * chunks + c) * 3;
+      q[0] = si; q[1] = sp; q[2] = st;
     }
   }
 }
 
+__global__ void __launch_bounds__(256) k_dice_fold(const double* __restrict__ part, uint32_t batch, uint32_t chunks,
+                                                   float* out, int mode) {
+  pdl_entry();
+  const int lane = threadIdx.x & 31;
+  const uint64_t b = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (b >= batch) return;
+  double si = 0.0, sp = 0.0, st = 0.0;
+  for (uint32_t c = lane; c < chunks; c += 32) {
+    const double* q = part + (b * chunks + c) * 3;
+    si += q[0]; sp += q[1]; st += q[2];
+  }
+  si = warp_sum(si);
+  sp = warp_sum(sp);
+  st = warp_sum(st);
+  if (lane == 0) dice_emit(si, sp, st, out, b, mode);
+}
+}  // namespace
+
+size_t dice_ws_bytes(uint32_t batch, uint32_t size) {
+  const DicePlan p = dice_plan(batch, size);
+  return p.chunks > 1 ? (size_t)batch * p.chunks * 3 * sizeof(double) : 0;
+}
+
 cudaError_t launch_dice_sums(const float* pred, const float* target, uint32_t batch, uint32_t size, float* out,
-                             int mode, cudaStream_t st) {
+                             int mode, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (batch == 0) return cudaSuccess;
-  launch_pdl(k_dice_sums, dim3(batch), dim3(512), 0, st, pred, target, size, out, mode);
+  const DicePlan p = dice_plan(batch, size);
+  if (p.chunks > 1 && (!ws || ws_bytes < dice_ws_bytes(batch, size))) return cudaErrorInvalidValue;
+  const bool vec = size % 4 == 0 && aligned16_h(pred) && aligned16_h(target);
+  const unsigned blocks = (unsigned)((uint64_t)batch * p.chunks);
+  double* part = (double*)ws;
+  if (vec) launch_pdl(k_dice_partials<true>, dim3(blocks), dim3(kDiceThreads), 0, st, pred, target, size, p.chunks,
+                      p.chunk_len, part, out, mode);
+  else launch_pdl(k_dice_partials<false>, dim3(blocks), dim3(kDiceThreads), 0, st, pred, target, size, p.chunks,
+                  p.chunk_len, part, out, mode);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || p.chunks == 1) return e;
+  launch_pdl(k_dice_fold, dim3((unsigned)(((uint64_t)batch * 32 + 255) / 256)), dim3(256), 0, st,
+             (const double*)part, batch, p.chunks, out, mode);
   return cudaGetLastError();
 }
 

@@ -125,9 +125,11 @@ cudaError_t launch_grad_norm_final(const float* partials, uint64_t n, float max_
                                    cudaStream_t st);
 // out[0] = sqrt(sum x^2 / n)
 cudaError_t launch_rms(const float* x, uint64_t n, float* out, void* ws, cudaStream_t st);
-// dice: per-sample (sum p*t, sum p, sum t); mode 0 -> sums[b*3+k], mode 1 -> loss[b]
+// dice: per-sample (sum p*t, sum p, sum t); mode 0 -> sums[b*3+k], mode 1 -> loss[b].
+// `ws` holds dice_ws_bytes (float64 chunk partials; 0 when a sample is one chunk).
+size_t dice_ws_bytes(uint32_t batch, uint32_t size);
 cudaError_t launch_dice_sums(const float* pred, const float* target, uint32_t batch, uint32_t size,
-                             float* out, int mode, cudaStream_t st);
+                             float* out, int mode, void* ws, size_t ws_bytes, cudaStream_t st);
 
 // ---- softmax / cross-entropy (k_softmax.cu) ---------------------------------
 struct SoftmaxCEArgs {

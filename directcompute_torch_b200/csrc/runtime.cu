@@ -519,14 +519,16 @@ static bool h_dice_loss(const Disp& d) {
   if (!need(d, 2, 1)) return false;
   const uint32_t b = std::min<uint32_t>(d.u[0], d.gx), size = d.u[1];
   FITS(d.srv[0], (uint64_t)b * size, "Pred"); FITS(d.srv[1], (uint64_t)b * size, "Target"); FITS(d.uav[0], b, "Out");
-  LAUNCH(launch_dice_sums(d.srv[0]->d, d.srv[1]->d, b, size, d.uav[0]->d, 1, g.stream));
+  if (!ensure_ws(dice_ws_bytes(b, size))) return false;
+  LAUNCH(launch_dice_sums(d.srv[0]->d, d.srv[1]->d, b, size, d.uav[0]->d, 1, g.ws, g.ws_bytes, g.stream));
 }
 static bool h_dice_loss_sums(const Disp& d) {
   if (!need(d, 2, 1)) return false;
   const uint32_t b = std::min<uint32_t>(d.u[0], d.gx), size = d.u[1];
   FITS(d.srv[0], (uint64_t)b * size, "Pred"); FITS(d.srv[1], (uint64_t)b * size, "Target");
   FITS(d.uav[0], 3ull * b, "Sums");
-  LAUNCH(launch_dice_sums(d.srv[0]->d, d.srv[1]->d, b, size, d.uav[0]->d, 0, g.stream));
+  if (!ensure_ws(dice_ws_bytes(b, size))) return false;
+  LAUNCH(launch_dice_sums(d.srv[0]->d, d.srv[1]->d, b, size, d.uav[0]->d, 0, g.ws, g.ws_bytes, g.stream));
 }
 static bool h_dice_loss_grad(const Disp& d) {
   if (!need(d, 3, 1)) return false;

@@ -228,15 +228,18 @@ def batchnorm_backward_dx(x, dy, mean, var, gamma, dgamma, dbeta, N, C, S, eps, 
     return ((gamma[c] * rstd[c]) * (dy[:n] - inner)).astype(F32)
 
 
-def dice_loss_grad(pred, target, sums, batch, size):
-    """nn_dice_loss_grad.hlsl:17-34 -- -2 * ((t*denom) - inter) / (denom*denom) / batch."""
+def dice_loss_grad(pred, target, sums, batch, size, divisor=None):
+    """nn_dice_loss_grad.hlsl:17-34 -- -2 * ((t*denom) - inter) / (denom*denom) / batch.
+
+    `divisor` (default: batch) is the shader's batch divisor, for checking a
+    slice of samples of a larger batch."""
     n = batch * size
     b = np.arange(n, dtype=np.int64) // size
     inter = sums[b * 3 + 0]
     denom = (sums[b * 3 + 1] + sums[b * 3 + 2] + F32(1e-6)).astype(F32)
     t = target[:n]
     num = (F32(-2.0) * (t * denom - inter)).astype(F32)
-    return ((num / (denom * denom)) / F32(batch)).astype(F32)
+    return ((num / (denom * denom)) / F32(batch if divisor is None else divisor)).astype(F32)
 
 
 # ---------------------------------------------------------------------------

@@ -168,9 +168,10 @@ def test_softmax_ce_grad_exact(dev, BK):
     dev.free(hp, hl, hg)
 
 
-def test_dice_grad_exact_given_sums(dev):
+# (3, 777): the scalar kernel; (4, 4096) and (5, 1000): the float4 chunked kernel
+@pytest.mark.parametrize("b,size", [(3, 777), (4, 4096), (5, 1000)])
+def test_dice_grad_exact_given_sums(dev, b, size):
     r = np.random.default_rng(13)
-    b, size = 3, 777
     p = r.random(b * size, dtype=np.float32)
     t = (r.random(b * size) > 0.5).astype(np.float32)
     sums = S.dice_sums(p, t, b, size).astype(np.float32).ravel()

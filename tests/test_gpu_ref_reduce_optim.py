@@ -215,9 +215,11 @@ def test_batchnorm_reference_shaders(dev, shape):
     dev.free(hx, hdy, hgm, hbt, hmean, hvar, hrm, hrv, hy, hdg, hdb, hdx)
 
 
-def test_dice_loss_and_sums(dev):
+# (4, 12288): float4 chunks + the chunk fold; (3, 777): scalar, one chunk a
+# sample; (2, 50001): scalar chunks + fold; (700, 4096): one float4 chunk a sample
+@pytest.mark.parametrize("b,size", [(4, 3 * 64 * 64), (3, 777), (2, 50001), (700, 4096)])
+def test_dice_loss_and_sums(dev, b, size):
     r = np.random.default_rng(10)
-    b, size = 4, 3 * 64 * 64
     p = r.random(b * size, dtype=np.float32)
     t = (r.random(b * size) > 0.5).astype(np.float32)
     hp, ht, ho, hs = dev.buf(p), dev.buf(t), dev.empty(b), dev.empty(3 * b)
