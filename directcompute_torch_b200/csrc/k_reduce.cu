@@ -1392,28 +1392,6 @@ cudaError_t launch_grad_norm_final(const float* partials, uint64_t n, float max_
 namespace {
 constexpr int kDiceThreads = 256;
 
-struct DicePlan {
-  uint32_t chunks = 1, chunk_len = 0;
-};
-
-// chunks per sample: about two waves of blocks over the batch, >= 4096
-// elements a chunk, chunk starts on a float4 boundary
-DicePlan dice_plan(uint32_t batch, uint32_t size) {
-  DicePlan p;
-  const DevInfo& d = dev_info();
-  const uint64_t want = (uint64_t)d.sm_count * (d.max_threads_per_sm / kDiceThreads) * 2;
-  uint64_t chunks = batch ? (want + batch - 1) / batch : 1;
-  const uint64_t max_chunks = ((uint64_t)size + 4095) / 4096;
-  if (chunks > max_chunks) chunks = max_chunks;
-  if (chunks < 1) chunks = 1;
-  uint64_t cl = ((uint64_t)size + chunks - 1) / chunks;
-  cl = (cl + 3) & ~3ull;
-  if (cl == 0) cl = 4;
-  p.chunks = (uint32_t)(size ? ((uint64_t)size + cl - 1) / cl : 1);
-  p.chunk_len = (uint32_t)cl;
-  return p;
-}
-
 DCT_DEV void dice_emit(double si, double sp, double st, float* out, uint64_t b, int mode) {
   if (mode == 0) {
     out[b * 3 + 0] = (float)si;
@@ -1498,6 +1476,34 @@ __global__ void __launch_bounds__(256) k_dice_fold(const double* __restrict__ pa
   sp = warp_sum(sp);
   st = warp_sum(st);
   if (lane == 0) dice_emit(si, sp, st, out, b, mode);
+}
+struct DicePlan {
+  uint32_t chunks = 1, chunk_len = 0;
+};
+
+// chunks per sample: two full waves of blocks over the batch (at the partials
+// kernel's own occupancy, so no partly filled last wave), >= 4096 elements a
+// chunk, chunk starts on a float4 boundary
+DicePlan dice_plan(uint32_t batch, uint32_t size) {
+  static int occ = 0;
+  if (occ == 0) {
+    int b = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_dice_partials<true>, kDiceThreads, 0);
+    occ = (e == cudaSuccess && b > 0) ? b : dev_info().max_threads_per_sm / kDiceThreads;
+    cudaGetLastError();
+  }
+  DicePlan p;
+  const uint64_t want = (uint64_t)dev_info().sm_count * (uint64_t)occ * 2;
+  uint64_t chunks = batch ? want / batch : 1;                  // rounded down: at most the two waves
+  const uint64_t max_chunks = ((uint64_t)size + 4095) / 4096;
+  if (chunks > max_chunks) chunks = max_chunks;
+  if (chunks < 1) chunks = 1;
+  uint64_t cl = ((uint64_t)size + chunks - 1) / chunks;
+  cl = (cl + 3) & ~3ull;
+  if (cl == 0) cl = 4;
+  p.chunks = (uint32_t)(size ? ((uint64_t)size + cl - 1) / cl : 1);
+  p.chunk_len = (uint32_t)cl;
+  return p;
 }
 }  // namespace
 
