@@ -159,6 +159,24 @@ DCT_DEV void warp_argbest(float& v, int64_t& i) {
   }
 }
 
+// This thread's share of a block's fold of n partials: p[t] + p[t + B] + ...
+// (t = threadIdx.x, B = blockDim.x), added in that order.  Four loads are
+// issued before their adds, so the partials' latency is paid once per four.
+DCT_DEV double strided_sum(const double* p, int n) {
+  double acc = 0.0;
+  const int B = blockDim.x;
+  int k = threadIdx.x;
+  for (; k + 3 * B < n; k += 4 * B) {
+    const double a0 = p[k], a1 = p[k + B], a2 = p[k + 2 * B], a3 = p[k + 3 * B];
+    acc += a0;
+    acc += a1;
+    acc += a2;
+    acc += a3;
+  }
+  for (; k < n; k += B) acc += p[k];
+  return acc;
+}
+
 // Sum a per-thread double across a block of blockDim.x threads (<= 1024) in a
 // fixed order.  Returns the total in thread 0.  `sh` needs 32 doubles.
 DCT_DEV double block_sum(double v, double* sh) {

@@ -260,9 +260,7 @@ cudaError_t run_mt(const MtTensor* t, int count, MtTable& tab, cudaStream_t st) 
 __global__ void k_norm_scale(const double* part, int n, float max_norm, float* ns) {
   pdl_entry();
   __shared__ double sh[32];
-  double acc = 0.0;
-  for (int k = threadIdx.x; k < n; k += blockDim.x) acc += part[k];
-  const double t = block_sum(acc, sh);
+  const double t = block_sum(strided_sum(part, n), sh);
   if (threadIdx.x == 0) {
     const float norm = (float)sqrt(t);
     ns[0] = norm;

@@ -1227,8 +1227,7 @@ DCT_DEV double full_pass2_value(const double* part, int nparts, double* sh) {
     return t;
   } else {
     // fixed assignment: thread t sums parts t, t+B, ... in order, then block tree
-    double acc = 0.0;
-    for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
+    const double acc = strided_sum(part, nparts);
     return block_sum(acc, sh);
   }
 }

@@ -423,8 +423,7 @@ __global__ void __launch_bounds__(kSmThreads) k_softmax_ce_block(const __grid_co
 __global__ void k_loss_final(const double* part, int nparts, double div, float* loss, double* raw) {
   pdl_entry();
   __shared__ double sh[32];
-  double acc = 0.0;
-  for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
+  const double acc = strided_sum(part, nparts);
   double t = block_sum(acc, sh);
   if (threadIdx.x == 0) {
     if (raw) raw[0] = t;
@@ -442,8 +441,7 @@ __global__ void k_loss_final_xchg(const double* part, int nparts, double div, fl
   __shared__ double sh[32];
   bool gave_up = false;
   peer_put_header(p);
-  double acc = 0.0;
-  for (int k = threadIdx.x; k < nparts; k += blockDim.x) acc += part[k];
+  const double acc = strided_sum(part, nparts);
   const double t = block_sum(acc, sh);
   if (threadIdx.x == 0) {
     peer_put_word(p, 0, (unsigned long long)__double_as_longlong(t));
