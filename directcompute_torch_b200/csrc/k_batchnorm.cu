@@ -86,14 +86,29 @@ __global__ void __launch_bounds__(256) k_bn_plane_sums(const float* __restrict__
 // chan[2c + j] = sum over n of ps[2 (n C + c) + j]: a warp per (c, j); lane l
 // adds n = l, l + 32, ... in order, then a fixed shuffle tree (deterministic,
 // and 32 loads in flight instead of one serial chain of N).
+// Lane l's share of a channel's plane sums: q[l * step] + q[(l + 32) * step] + ...
+// over n < N, added in that order with four loads issued ahead of their adds.
+DCT_DEV double lane_plane_sum(const double* __restrict__ q, uint64_t step, uint32_t N, int lane) {
+  double acc = 0.0;
+  uint32_t n = lane;
+  for (; n + 96 < N; n += 128) {
+    const double a0 = q[n * step], a1 = q[(n + 32) * step], a2 = q[(n + 64) * step], a3 = q[(n + 96) * step];
+    acc += a0;
+    acc += a1;
+    acc += a2;
+    acc += a3;
+  }
+  for (; n < N; n += 32) acc += q[n * step];
+  return acc;
+}
+
 __global__ void __launch_bounds__(256) k_bn_fold(const double* __restrict__ ps, uint32_t N, uint32_t C, double* chan) {
   pdl_entry();
   const uint32_t k = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;     // (c, j)
   const int lane = threadIdx.x & 31;
   if (k >= 2 * C) return;
   const uint32_t c = k >> 1, j = k & 1;
-  double acc = 0.0;
-  for (uint32_t n = lane; n < N; n += 32) acc += ps[2 * ((uint64_t)n * C + c) + j];
+  double acc = lane_plane_sum(ps + 2 * (uint64_t)c + j, 2ull * C, N, lane);
   acc = warp_sum(acc);
   if (lane == 0) chan[k] = acc;
 }
@@ -114,8 +129,7 @@ __global__ void __launch_bounds__(256) k_bn_fold_xchg(const double* __restrict__
   const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
   for (uint32_t k = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; k < nsum; k += warps) {
     const uint32_t c = k >> 1, j = k & 1;
-    double acc = 0.0;
-    for (uint32_t n = lane; n < N; n += 32) acc += ps[2 * ((uint64_t)n * C + c) + j];
+    double acc = lane_plane_sum(ps + 2 * (uint64_t)c + j, 2ull * C, N, lane);
     acc = warp_sum(acc);
     if (lane == 0) {
       peer_put_word(p, k, (unsigned long long)__double_as_longlong(acc));
