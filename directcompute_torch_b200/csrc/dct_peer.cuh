@@ -79,10 +79,12 @@ DCT_DEV void peer_put(const PeerXfer& p) {
   for (uint64_t i = w0 + threadIdx.x; i < w1; i += blockDim.x) peer_put_word(p, i, peer_word(p, i));
 }
 
-// Block 0 stores the header words (a kernel that puts its record words itself).
-DCT_DEV void peer_put_header(const PeerXfer& p) {
-  if (blockIdx.x == 0 && threadIdx.x < p.h.n) peer_put_word(p, p.h.off + threadIdx.x, p.h.v[threadIdx.x]);
+// The designated block (block 0 unless the kernel names another) stores the
+// header words (a kernel that puts its record words itself).
+DCT_DEV void peer_put_header(const PeerXfer& p, bool mine) {
+  if (mine && threadIdx.x < p.h.n) peer_put_word(p, p.h.off + threadIdx.x, p.h.v[threadIdx.x]);
 }
+DCT_DEV void peer_put_header(const PeerXfer& p) { peer_put_header(p, blockIdx.x == 0); }
 
 // Word i of rank r's record: this rank's from its record, a peer's once both of
 // its lines carry this exchange's tag.  `gave_up` is the calling thread's:
@@ -114,19 +116,21 @@ DCT_DEV double peer_get_f64(const PeerXfer& p, int r, uint64_t i, bool& gave_up)
   return __longlong_as_double((long long)peer_get(p, r, i, gave_up));
 }
 
-// Block 0: thread q waits for peer q's last word (the ordering the slot reuse
-// relies on, whatever the fold itself reads).
-DCT_DEV void peer_sync(const PeerXfer& p, bool& gave_up) {
-  if (blockIdx.x != 0) return;
+// The designated block: thread q waits for peer q's last word (the ordering the
+// slot reuse relies on, whatever the fold itself reads).
+DCT_DEV void peer_sync(const PeerXfer& p, bool& gave_up, bool mine) {
+  if (!mine) return;
   for (int q = threadIdx.x; q < p.world; q += blockDim.x)
     if (q != p.rank) (void)peer_get(p, q, peer_words(p) - 1, gave_up);
 }
+DCT_DEV void peer_sync(const PeerXfer& p, bool& gave_up) { peer_sync(p, gave_up, blockIdx.x == 0); }
 
-// Block 0 of an axis reduction (every thread of the block calls it): the
-// shards' headers [offset, len, len_total, valid] must tile [0, len_total) in
-// rank order.  The block fetches every rank's four header words at once.
-DCT_DEV void peer_check_axis(const PeerXfer& p, bool& gave_up) {
-  if (p.axis_nout < 0 || blockIdx.x != 0) return;
+// The designated block of an axis reduction (every thread of that block calls
+// it): the shards' headers [offset, len, len_total, valid] must tile
+// [0, len_total) in rank order.  The block fetches every rank's four header
+// words at once.
+DCT_DEV void peer_check_axis(const PeerXfer& p, bool& gave_up, bool mine) {
+  if (p.axis_nout < 0 || !mine) return;
   __shared__ unsigned long long hv[kPeerMaxWorld][4];
   const uint64_t nout = (uint64_t)p.axis_nout;
   for (int t = threadIdx.x; t < 4 * p.world; t += blockDim.x) hv[t >> 2][t & 3] = peer_get(p, t >> 2, nout + (t & 3), gave_up);
@@ -142,6 +146,7 @@ DCT_DEV void peer_check_axis(const PeerXfer& p, bool& gave_up) {
   ok &= (expect == total);
   if (!ok && p.err) atomicOr(p.err, DCT_DEVERR_PEER_INVALID);
 }
+DCT_DEV void peer_check_axis(const PeerXfer& p, bool& gave_up) { peer_check_axis(p, gave_up, blockIdx.x == 0); }
 
 // The start of every fold kernel over peer memory: put, then the ordering wait
 // and (axis records) the shard check.

@@ -505,8 +505,11 @@ __global__ void __launch_bounds__(256) k_fold_chunks(const unsigned long long* _
 // lane l of warp 0 folds column k's chunk partials as k_fold_chunks does,
 // stores this rank's packed partial (global index) into every peer's slot,
 // then merges every rank's partial for k in rank order as each arrives (ties
-// to the lower index; mean divides by len_total) and emits.  The launch keeps
-// every block resident, since each waits for the peers' puts.
+// to the lower index; mean divides by len_total) and emits.  The grid's last
+// block does no tile: it stores the header, waits for every peer's (the slot
+// reuse ordering) and checks that the shards tile the axis, off the tile
+// blocks' path (as block 0's tail it cost 1.2 us per call).  The launch keeps
+// the tile blocks resident, since each waits for the peers' puts.
 template <int OP>
 __global__ void __launch_bounds__(256) k_fold_chunks_xchg(const unsigned long long* __restrict__ part, uint64_t nout,
                                                           uint32_t chunks, uint64_t inner, uint64_t len_total,
@@ -514,10 +517,16 @@ __global__ void __launch_bounds__(256) k_fold_chunks_xchg(const unsigned long lo
                                                           const __grid_constant__ PeerXfer p) {
   pdl_entry();
   bool gave_up = false;
-  peer_put_header(p);
+  const unsigned tiles_grid = gridDim.x - 1;
+  if (blockIdx.x == tiles_grid) {
+    peer_put_header(p, true);
+    peer_sync(p, gave_up, true);
+    peer_check_axis(p, gave_up, true);
+    return;
+  }
   __shared__ unsigned long long sh[kRedWarps][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (uint64_t k0 = (uint64_t)blockIdx.x * 32; k0 < nout; k0 += (uint64_t)gridDim.x * 32) {
+  for (uint64_t k0 = (uint64_t)blockIdx.x * 32; k0 < nout; k0 += (uint64_t)tiles_grid * 32) {
     const uint64_t k = k0 + lane;
     Acc<OP> a;
     a.reset();
@@ -556,8 +565,6 @@ __global__ void __launch_bounds__(256) k_fold_chunks_xchg(const unsigned long lo
     }
     __syncthreads();
   }
-  peer_sync(p, gave_up);
-  peer_check_axis(p, gave_up);
 }
 
 // generic strided: one thread per output
@@ -670,7 +677,8 @@ int cols_occupancy(bool vec) {
 }
 
 // Blocks of k_fold_chunks_xchg that are resident at once (every block waits
-// for the peers' puts): at most the SMs times its occupancy.
+// for the peers' puts): at most the SMs times its occupancy, the header block
+// included.
 template <int OP>
 unsigned xchg_fold_blocks(uint64_t nout) {
   static int occ = 0;
@@ -680,9 +688,9 @@ unsigned xchg_fold_blocks(uint64_t nout) {
     occ = (e == cudaSuccess && b > 0) ? b : 1;
     cudaGetLastError();
   }
-  const uint64_t cap = (uint64_t)dev_info().sm_count * (uint64_t)occ;
+  const uint64_t cap = (uint64_t)dev_info().sm_count * (uint64_t)occ - 1;
   const uint64_t need = (nout + 31) / 32;
-  return (unsigned)(need < cap ? need : cap);
+  return (unsigned)(need < cap ? need : cap) + 1;             // + the header block
 }
 
 // The exchange a sharded axis reduction's last stage runs (null: none).
