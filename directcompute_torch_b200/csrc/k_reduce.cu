@@ -901,17 +901,26 @@ cudaError_t launch_reduce3d_packed(int op, const float* x, uint64_t outer, uint6
 
 namespace {
 // The rank fold of a sharded axis reduction, in the same launch as the exchange
-// over peer memory (dct_peer.cuh): after the put, thread k folds output k over
-// the ranks' packed partials in rank order as each arrives (ties to the lower
-// index; mean divides by len_total).
+// over peer memory (dct_peer.cuh): every block stores its slice of the staged
+// record, then thread k of the folding blocks folds output k over the ranks'
+// packed partials in rank order as each arrives (ties to the lower index; mean
+// divides by len_total).  The grid's last block folds nothing: it waits for
+// every peer's last word (the slot reuse ordering) and checks that the shards
+// tile the axis, off the folding blocks' path.
 template <int OP>
 __global__ void __launch_bounds__(256) k_peer_fold_axis(const __grid_constant__ PeerXfer p, uint64_t nout,
                                                         uint64_t len_total, RedOut ro) {
   pdl_entry();                                         // the record comes from the previous kernel
   bool gave_up = false;
-  peer_begin(p, gave_up);
+  peer_put(p);
+  const unsigned fold_grid = gridDim.x - 1;
+  if (blockIdx.x == fold_grid) {
+    peer_sync(p, gave_up, true);
+    peer_check_axis(p, gave_up, true);
+    return;
+  }
   if (!ro.out && !ro.idx) return;                      // an invalid rank only takes part in the exchange
-  const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t step = (uint64_t)fold_grid * blockDim.x;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nout; k += step) {
     Acc<OP> a;
     a.reset();
@@ -927,6 +936,7 @@ __global__ void __launch_bounds__(256) k_peer_fold_axis(const __grid_constant__ 
 
 cudaError_t launch_peer_fold_axis(int op, const PeerXfer& p, unsigned blocks, uint64_t nout, uint64_t len_total,
                                   float* out, int32_t* out_idx, cudaStream_t st) {
+  blocks += 1;                                           // + the check block
   RedOut ro;
   ro.out = out;
   ro.idx = out_idx;
