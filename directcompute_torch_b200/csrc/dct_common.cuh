@@ -162,18 +162,20 @@ DCT_DEV void warp_argbest(float& v, int64_t& i) {
 // This thread's share of a block's fold of n partials: p[t] + p[t + B] + ...
 // (t = threadIdx.x, B = blockDim.x), added in that order.  Four loads are
 // issued before their adds, so the partials' latency is paid once per four.
-DCT_DEV double strided_sum(const double* p, int n) {
+// (float partials are widened to double as they are added.)
+template <typename T, typename N>
+DCT_DEV double strided_sum(const T* p, N n) {
   double acc = 0.0;
-  const int B = blockDim.x;
-  int k = threadIdx.x;
+  const N B = blockDim.x;
+  N k = threadIdx.x;
   for (; k + 3 * B < n; k += 4 * B) {
-    const double a0 = p[k], a1 = p[k + B], a2 = p[k + 2 * B], a3 = p[k + 3 * B];
-    acc += a0;
-    acc += a1;
-    acc += a2;
-    acc += a3;
+    const T a0 = p[k], a1 = p[k + B], a2 = p[k + 2 * B], a3 = p[k + 3 * B];
+    acc += (double)a0;
+    acc += (double)a1;
+    acc += (double)a2;
+    acc += (double)a3;
   }
-  for (; k < n; k += B) acc += p[k];
+  for (; k < n; k += B) acc += (double)p[k];
   return acc;
 }
 

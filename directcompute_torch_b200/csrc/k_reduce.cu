@@ -1383,9 +1383,7 @@ cudaError_t launch_grad_sq_reduce(const float* g, uint64_t count, float* partial
 __global__ void __launch_bounds__(1024) k_grad_norm_final(const float* part, uint64_t n, float max_norm, float* ns) {
   pdl_entry();
   __shared__ double sh[32];
-  double acc = 0.0;
-  for (uint64_t k = threadIdx.x; k < n; k += blockDim.x) acc += (double)part[k];
-  double t = block_sum(acc, sh);
+  double t = block_sum(strided_sum(part, n), sh);
   if (threadIdx.x == 0) {
     const float norm = (float)sqrt(t);
     ns[0] = norm;
