@@ -1323,12 +1323,15 @@ def main():
             "per_op": per_op,
             "strong_detail": strong or None,
             "parity_notes": {**parity.msg, **{"strong " + k: v for k, v in parity_strong.msg.items()}} or None,
+            "parity": {short(k): v for k, v in par.items()},
+            # the compact tail (the driver keeps the line's last 1500 characters)
             "c1_us": {k.split("_")[-1]: per_op[k].get("us_per_step")
                       for k in ("c1_dense_step_eager", "c1_dense_step_graph") if k in per_op},
             "per_op_frac": {short(k): round(v["frac_of_measured_hbm"], 3) for k, v in per_op.items()
                             if not k.startswith("c1_")},
             "strong": strong_c,
-            "parity": {short(k): v for k, v in par.items()},
+            "parity_failed": sorted([short(k) for k, v in par.items() if not v] +
+                                    ["strong " + short(k) for k, v in par_strong.items() if not v]),
             "parity_all": (all(par.values()) if par else None),
             "parity_strong_all": (all(par_strong.values()) if par_strong else None),
         }
