@@ -234,7 +234,7 @@ struct ColLane {
     return a;
   }
   // Acc form for the row kernel's lanes: indices first + 128 t + q (q < 4), < end
-  DCT_DEV Acc<OP> finish_rows(const float* row, uint64_t first, uint64_t end) const {
+  DCT_DEV Acc<OP> finish_rows(const float* row, uint64_t first, uint64_t end, uint64_t step = 128) const {
     Acc<OP> a;
     a.reset();
     if (first >= end) return a;
@@ -242,7 +242,7 @@ struct ColLane {
       a.v = v;
       a.i = i;
       if (v != v) {                                       // rare: this lane's first NaN
-        for (uint64_t l = first; l < end; l += 128) {
+        for (uint64_t l = first; l < end; l += step) {
           bool found = false;
           for (int q = 0; q < 4 && l + q < end; ++q) {
             const float xq = row[l + q];
@@ -311,6 +311,67 @@ __global__ void __launch_bounds__(kRedThreads) k_reduce_rows(const float* __rest
       if (chunks == 1) acc.emit(ro, row, len);
       else part[pr] = acc.pack();
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// ROW kernel, one block per row: for rows that fill a quarter of the warp
+// slots or less (a one-warp-per-row grid would leave most SMs idle).  The
+// block's 256 threads stream the row -- thread t the float4s 4t, 4t + 1024, ...
+// in increasing order, so the lane-local state of the row kernel applies --
+// then each warp reduces its lanes and warp 0 merges the 8 warp results in
+// warp order: one launch, no chunk partials, no fold.
+// ---------------------------------------------------------------------------
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kRedThreads) k_reduce_rows_block(const float* __restrict__ x, uint64_t rows,
+                                                                   uint64_t len, uint64_t so, RedOut ro) {
+  pdl_entry();
+  __shared__ unsigned long long sh[kRedWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr uint64_t T = kRedThreads;
+  for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* p = x + row * so;
+    Acc<OP> acc;
+    acc.reset();
+    if (VEC) {
+      const uint64_t first = 4 * (uint64_t)threadIdx.x;
+      ColLane<OP> ln;
+      ln.reset((int32_t)first);
+      uint64_t l = first;
+      for (; l + 3 * 4 * T + 3 < len; l += 4 * 4 * T) {
+        float4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = ld_stream4(p + l + 4 * T * k);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int32_t b = (int32_t)(l + 4 * T * k);
+          ln.add(v[k].x, b); ln.add(v[k].y, b + 1); ln.add(v[k].z, b + 2); ln.add(v[k].w, b + 3);
+        }
+      }
+      for (; l + 3 < len; l += 4 * T) {
+        const float4 v = ld_stream4(p + l);
+        const int32_t b = (int32_t)l;
+        ln.add(v.x, b); ln.add(v.y, b + 1); ln.add(v.z, b + 2); ln.add(v.w, b + 3);
+      }
+      acc = ln.finish_rows(p, first, len, 4 * T);
+    } else {
+      for (uint64_t l = threadIdx.x; l < len; l += T) acc.add(ld_stream(p + l), (int64_t)l);
+    }
+    acc.warp_reduce();
+    if (lane == 0) sh[warp] = acc.pack();
+    __syncthreads();
+    if (warp == 0) {
+      Acc<OP> tot;
+      const unsigned long long mine = lane < kRedWarps ? sh[lane] : 0ull;
+#pragma unroll
+      for (int w = 0; w < kRedWarps; ++w) {
+        Acc<OP> t;
+        t.unpack(__shfl_sync(0xffffffffu, mine, w));
+        if (w == 0) tot = t; else tot.merge(t);
+      }
+      if (lane == 0) tot.emit(ro, row, len);
+    }
+    __syncthreads();
   }
 }
 
@@ -586,7 +647,7 @@ __global__ void __launch_bounds__(256) k_reduce_generic(const float* __restrict_
 }
 
 struct Plan {
-  int kind;           // 0 rows, 1 cols, 2 generic
+  int kind;           // 0 rows (a warp per row chunk), 1 cols, 2 generic, 3 rows (a block per row)
   bool vec;
   uint32_t chunks;
   uint64_t chunk_len;
@@ -613,13 +674,13 @@ Plan make_plan(uint64_t outer, uint64_t len, uint64_t inner, uint64_t so, uint64
       const uint64_t max_chunks = (len + 4095) / 4096;       // keep >= 4096 elements per chunk
       if (chunks > max_chunks) chunks = max_chunks;
     } else if (outer * 4 < target_warps && len >= 2048) {
-      // few rows (a quarter of the warp slots or less): split each row into
-      // chunks of >= 1024 elements and fold.  [4096, 4096] went from 12.0 to
-      // 9.3 us and [2048, 4096] from 11.8 to 6.5 us; at half the slots the
-      // fold cost more than the extra warps gave ([8192, 4096]: 22.4 -> 28.7 us).
-      chunks = (target_warps + outer - 1) / outer;
-      const uint64_t max_chunks = len / 1024;
-      if (chunks > max_chunks) chunks = max_chunks;
+      // few rows (a quarter of the warp slots or less): a block of 8 warps per
+      // row (k_reduce_rows_block), one launch and no fold
+      p.kind = 3;
+      p.chunks = 1;
+      p.chunk_len = len;
+      p.grid = dim3((unsigned)(outer < target_blocks * 4 ? outer : target_blocks * 4), 1, 1);
+      return p;
     }
     uint64_t cl = (len + chunks - 1) / chunks;
     cl = (cl + 3) & ~3ull;
@@ -721,6 +782,9 @@ cudaError_t run_reduce(const float* x, uint64_t outer, uint64_t len, uint64_t in
   if (p.kind == 0) {
     if (p.vec) launch_pdl(k_reduce_rows<OP, true>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
     else launch_pdl(k_reduce_rows<OP, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, p.chunks, p.chunk_len, ro, part);
+  } else if (p.kind == 3) {
+    if (p.vec) launch_pdl(k_reduce_rows_block<OP, true>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, ro);
+    else launch_pdl(k_reduce_rows_block<OP, false>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, so, ro);
   } else if (p.kind == 1) {
     if (p.vec) launch_pdl(k_reduce_cols<OP, 4, COL_PLAIN>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColXform{});
     else launch_pdl(k_reduce_cols<OP, 1, COL_PLAIN>, dim3(p.grid), dim3(kRedThreads), 0, st, x, outer, len, inner, so, sl, p.chunks, p.chunk_len, ro, part, ColXform{});
